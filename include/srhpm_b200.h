@@ -1,0 +1,120 @@
+/* srhpm_b200: B200 (sm_100a) kernels for SR-HPM's speculative-verification hot path, behind a plain C ABI.
+ *
+ * The path verifies 1 + k drafted tokens against a quantized dense decoder in one pass:
+ *   - small-batch quantized matmul (ggml_mul_mat with ne[1] = 1..16 on Q4_K / Q5_K / Q6_K / Q3_K / IQ4_XS / Q8_0)
+ *   - multi-query attention over an f16 or q8_0 KV cache (ggml_flash_attn_ext with 2..8 query rows)
+ *   - greedy longest-prefix acceptance over the target logits
+ *
+ * Conventions (all entry points):
+ *   - tensors are ggml-shaped views (srhpm_tensor: type, ne[4] in elements, nb[4] in bytes, data) of DEVICE memory,
+ *     unless an argument says otherwise; the caller owns every buffer, including the work buffer (wdata) whose size
+ *     the matching *_work_size call returns.
+ *   - calls are asynchronous and ordered on `stream` (a cudaStream_t; NULL = the legacy default stream).
+ *   - errors are returned as srhpm_status codes, never by aborting. SRHPM_UNSUPPORTED means "not handled here, run
+ *     the stock path", as the reference's compute_forward returning false does.
+ *   - one srhpm_ctx per device; a context may be used from several host threads only with external serialisation.
+ */
+#ifndef SRHPM_B200_H
+#define SRHPM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ggml_type numbering (GGUF) */
+enum srhpm_type {
+    SRHPM_TYPE_F32    = 0,
+    SRHPM_TYPE_F16    = 1,
+    SRHPM_TYPE_Q8_0   = 8,
+    SRHPM_TYPE_Q3_K   = 11,
+    SRHPM_TYPE_Q4_K   = 12,
+    SRHPM_TYPE_Q5_K   = 13,
+    SRHPM_TYPE_Q6_K   = 14,
+    SRHPM_TYPE_Q8_K   = 15,
+    SRHPM_TYPE_IQ4_XS = 23,
+    SRHPM_TYPE_I32    = 26,
+};
+
+enum srhpm_status {
+    SRHPM_OK             = 0,
+    SRHPM_UNSUPPORTED    = 1,  /* shape / type outside this path: use the stock path */
+    SRHPM_ERR_INVALID    = -1, /* inconsistent arguments */
+    SRHPM_ERR_ALIGN      = -2, /* a pointer or stride misses its required alignment */
+    SRHPM_ERR_WORKSPACE  = -3, /* wdata missing or smaller than *_work_size */
+    SRHPM_ERR_CUDA       = -4, /* a CUDA runtime call failed (srhpm_last_cuda_error has the code) */
+    SRHPM_ERR_DEVICE     = -5, /* a kernel reported an error through the context's status word */
+};
+
+/* q8_0 activation quantizer used for Q8_0 weights and for Q against a q8_0 KV cache (the upstream ggml-cpu quantizer
+ * is not in the reference; both variants are provided). SIMD: id = 127/amax, round half to even (ggml-cpu's x86
+ * path, the default). REF: id = 1/d, roundf (ggml's quantize_row_q8_0_ref). */
+enum srhpm_q8_0_act_mode { SRHPM_Q8_0_ACT_SIMD = 0, SRHPM_Q8_0_ACT_REF = 1 };
+
+typedef struct srhpm_tensor {
+    int32_t type;   /* enum srhpm_type */
+    int64_t ne[4];  /* elements per dimension, ggml order (ne[0] innermost) */
+    size_t  nb[4];  /* bytes per step in each dimension */
+    void *  data;   /* device pointer */
+} srhpm_tensor;
+
+typedef struct srhpm_ctx srhpm_ctx;
+
+/* Context of one device: options, a device status word for bounded-wait errors, launch counters.
+ * Replaces dgpu_init (dgpu/dgpu.cu:17-25); srhpm_ctx_destroy has no counterpart there. */
+int  srhpm_ctx_create(int device, srhpm_ctx ** out);
+int  srhpm_ctx_destroy(srhpm_ctx * ctx);
+int  srhpm_ctx_set_q8_0_act_mode(srhpm_ctx * ctx, int mode);
+/* kernels this context launched since creation (or the last reset) */
+int64_t srhpm_ctx_launch_count(const srhpm_ctx * ctx, int reset);
+/* reads (synchronously) and clears the device status word; SRHPM_ERR_DEVICE when a kernel reported an error */
+int  srhpm_ctx_check(srhpm_ctx * ctx, int32_t * device_code);
+int  srhpm_last_cuda_error(void);
+const char * srhpm_status_str(int status);
+
+/* ggml type facts (ggml_blck_size / ggml_type_size / ggml_row_size) */
+int    srhpm_blck_size(int type);
+size_t srhpm_type_size(int type);
+size_t srhpm_row_size(int type, int64_t n);
+
+/* ---- small-batch quantized matmul ------------------------------------------------------------------------------
+ * Y = W X in ggml_mul_mat semantics: W = src0 [K, rows] of a quantized type (rows contiguous, nb[1] = row size,
+ * data 16-byte aligned), X = src1 f32 [K, N] (any row stride, multiple of 4), Y = dst f32 [rows, N] (any row
+ * stride). 1 <= N <= 16, K a multiple of 256. Activations are quantized per row and 256 columns to int8 (bit-identical
+ * to the reference's srv_quantize_row, patch/srhpm.patch:5518-5575) or, for Q8_0 weights, to q8_0; each super-block
+ * is decoded once for all N rows and reduced with exact int32 sums on the tensor cores.
+ * Replaces tensor_traits_srv::work_size / compute_forward (patch/srhpm.patch:6366-6374, :6400-6611) and the dGPU's
+ * dgpu_launch + dgpu_collect (dgpu/dgpu.cu:244-312). A row range of W (a view with fewer rows and Y a matching view)
+ * is the reference's CPU/GPU row split (patch/srhpm.patch:6497-6529). */
+int srhpm_mul_mat_work_size(const srhpm_tensor * W, const srhpm_tensor * X, size_t * size);
+int srhpm_mul_mat(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, srhpm_tensor * Y, void * wdata,
+                  size_t wsize, void * stream);
+
+/* The integer part of srhpm_mul_mat, for bit-exact checks: per (token t, row r, block j) the int32 sum of
+ * (integer block scale) x (code . activation) over block j (super-block of 256, or the 32-block for Q8_0), written to
+ * isum[(t * rows + r) * nblk + j], and for Q4_K / Q5_K the sum of (integer min) x (activation sum) to imin (same
+ * layout; may be NULL otherwise). Same kernels and decoders as srhpm_mul_mat. No reference counterpart (test hook). */
+int srhpm_mul_mat_isums(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, int32_t * isum,
+                        int32_t * imin, void * wdata, size_t wsize, void * stream);
+
+/* Activation quantizer, row by row: X f32 [K, N] -> q int8 [N][K], d f32 [N][K/256], bsum32 int16 [N][K/32],
+ * bsum16 int16 [N][K/16] (dense, device; bsum pointers may be NULL). Bit-identical to srv_quantize_row
+ * (patch/srhpm.patch:5518-5575), which equals ggml's quantize_row_q8_K. */
+int srhpm_quantize_rows_q8_K(srhpm_ctx * ctx, const srhpm_tensor * X, int8_t * q, float * d, int16_t * bsum32,
+                             int16_t * bsum16, void * stream);
+/* X f32 [K, N] -> N rows of K/32 q8_0 blocks (34 bytes each, GGUF layout), with the context's q8_0 mode.
+ * ggml-cpu from_float of GGML_TYPE_Q8_0 (upstream; used by the reference at patch/srhpm.patch:670-673). */
+int srhpm_quantize_rows_q8_0(srhpm_ctx * ctx, const srhpm_tensor * X, void * blocks, void * stream);
+
+/* ---- host-side weight quantizer (CPU) -------------------------------------------------------------------------
+ * f32 rows -> GGUF blocks of `type` (Q4_K, Q5_K, Q6_K, Q3_K, IQ4_XS, Q8_0, F16). Host pointers. Returns the bytes
+ * written. ggml_quantize_chunk's contract (upstream); imatrix is accepted and ignored (uniform importance). */
+size_t srhpm_quantize_chunk(int type, const float * src, void * dst, int64_t start, int64_t nrows, int64_t n_per_row,
+                            const float * imatrix);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SRHPM_B200_H */

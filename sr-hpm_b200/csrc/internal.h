@@ -1,0 +1,44 @@
+// Internal declarations shared by the CUDA translation units of libsrhpm_b200 (not part of the C ABI).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+
+#include "srhpm_b200.h"
+
+struct srhpm_ctx {
+    int                  device        = 0;
+    int                  q8_0_act_mode = SRHPM_Q8_0_ACT_SIMD;
+    int                  num_sms       = 148;
+    int32_t *            d_status      = nullptr;  // device status word of the bounded waits
+    std::atomic<int64_t> launches{ 0 };
+};
+
+namespace srhpm {
+
+void set_last_cuda_error(cudaError_t e);
+
+inline int cuda_status(cudaError_t e) {
+    if (e != cudaSuccess) {
+        set_last_cuda_error(e);
+        return SRHPM_ERR_CUDA;
+    }
+    return SRHPM_OK;
+}
+
+// shape / type facts
+bool is_weight_type(int type);
+int  weight_block_bytes(int type);
+
+// srv_gemm.cu
+size_t gemm_work_size(int wtype, int64_t K, int64_t N);
+int    gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
+                const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
+                int32_t * isum, int32_t * imin, cudaStream_t stream);
+int    quantize_q8K_dense(srhpm_ctx * ctx, const float * X, int64_t ldx, int64_t N, int64_t K, int8_t * q, float * d,
+                          int16_t * b32, int16_t * b16, cudaStream_t stream);
+int    quantize_q8_0_dense(srhpm_ctx * ctx, const float * X, int64_t ldx, int64_t N, int64_t K, void * blocks,
+                           cudaStream_t stream);
+
+}  // namespace srhpm

@@ -1,0 +1,123 @@
+// Thin wrappers over the sm_100a PTX this library uses: mbarriers with bounded waits, 1-D bulk async copies
+// (global -> shared, completion counted on an mbarrier), int8 tensor-core MMA, programmatic dependent launch.
+#pragma once
+#include <cstdint>
+#include <cuda_fp16.h>
+
+namespace srhpm {
+
+// Spin limit of every mbarrier wait. A wait that runs out sets the kernel's error word and the kernel returns
+// instead of hanging (each probe of try_wait already blocks for a hardware-defined interval).
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+// error words written to the context's device status slot
+enum : int32_t { kErrNone = 0, kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3 };
+
+__device__ __forceinline__ uint32_t smem_u32(const void * p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t * bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t * bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t * bar, uint32_t tx) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(tx)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// bounded wait for the phase with the given parity to complete; false when the limit ran out
+__device__ __forceinline__ bool mbar_wait(uint64_t * bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kWaitLimit; i++) {
+        if (mbar_try_wait(bar, parity)) {
+            return true;
+        }
+    }
+    return false;
+}
+
+// 1-D bulk copy global -> shared of `bytes` (multiple of 16, both addresses 16-byte aligned), completion counted on bar
+__device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t bytes, uint64_t * bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// orders this thread's generic-proxy shared-memory writes before later async-proxy (bulk copy) accesses
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// programmatic dependent launch: wait for the preceding grid's writes / let the next grid start its prologue
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+// D = A(16x32, row) * B(32x8, col) + C, int8 operands, int32 accumulators. A unsigned (u8) or signed (s8), B signed.
+// Fragments (g = lane/4, t = lane%4): a0 = A[g][4t..4t+3], a1 = A[g+8][4t..], a2 = A[g][16+4t..], a3 = A[g+8][16+4t..];
+// b0 = B[4t..4t+3][g], b1 = B[16+4t..][g]; c0 = C[g][2t], c1 = C[g][2t+1], c2 = C[g+8][2t], c3 = C[g+8][2t+1].
+template <bool A_UNSIGNED>
+__device__ __forceinline__ void mma_k32(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+    if constexpr (A_UNSIGNED) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+            : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    }
+}
+
+// D = A(16x16, row) * B(16x8, col) + C, int8. a0 = A[g][4t..4t+3], a1 = A[g+8][4t..]; b0 = B[4t..4t+3][g].
+template <bool A_UNSIGNED>
+__device__ __forceinline__ void mma_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    if constexpr (A_UNSIGNED) {
+        asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+                     : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+                     : "r"(a0), "r"(a1), "r"(b0));
+    } else {
+        asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
+                     : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+                     : "r"(a0), "r"(a1), "r"(b0));
+    }
+}
+
+// 4 bytes from a 2-byte-aligned shared-memory address (two aligned 32-bit loads and a funnel shift when needed)
+__device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t * p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    if ((a & 3) == 0) {
+        return *reinterpret_cast<const uint32_t *>(p);
+    }
+    const uint32_t * q = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
+    return __funnelshift_r(q[0], q[1], 16);
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+__device__ __forceinline__ uint16_t lds_u16(const uint8_t * p) { return *reinterpret_cast<const uint16_t *>(p); }
+
+}  // namespace srhpm

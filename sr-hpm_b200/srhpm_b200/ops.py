@@ -1,0 +1,196 @@
+"""Host-side operator layer of the B200 verify path, shaped like the ggml operators it replaces.
+
+    Context.mul_mat(W, X)          ggml_mul_mat(W, X) with ne[1] = N = 1..16 on a GGUF-quantized W
+                                   (reference: tensor_traits_srv::compute_forward, patch/srhpm.patch:6400-6611)
+    Context.flash_attn_ext(...)    ggml_flash_attn_ext with 2..8 query rows over an f16 / q8_0 KV cache
+                                   (reference: ggml_compute_forward_flash_attn_ext_gqa_small, patch/srhpm.patch:581-824)
+    Context.sample_and_accept_n()  greedy longest-prefix acceptance (reference: common_sampler_sample_and_accept_n,
+                                   patch/srhpm.patch:1-37)
+
+Tensors are torch tensors in device memory; torch only provides allocation and streams. Every compute call goes to
+libsrhpm_b200.so through its C ABI; a missing library raises.
+"""
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _lib as L
+
+
+def _tensor_view(t, type_, ne, nb):
+    v = L.SrhpmTensor()
+    v.type = type_
+    for i in range(4):
+        v.ne[i] = ne[i] if i < len(ne) else 1
+    last = nb[-1] * (ne[len(nb) - 1] if len(nb) else 1)
+    for i in range(4):
+        v.nb[i] = nb[i] if i < len(nb) else last
+    v.data = t.data_ptr() if t is not None else 0
+    return v
+
+
+def f32_rows_view(x):
+    """ggml view of a 2-D f32 tensor [rows, cols] (cols innermost): ne = [cols, rows]."""
+    assert x.dtype == torch.float32 and x.dim() == 2 and x.stride(1) == 1
+    return _tensor_view(x, L.F32, [x.shape[1], x.shape[0]], [4, x.stride(0) * 4])
+
+
+def _stream_ptr(stream):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def quantize_chunk(w, qtype):
+    """Host weight quantizer: f32 [rows, K] (numpy or CPU torch) -> GGUF-packed bytes (numpy uint8, rows x row_size).
+    ggml_quantize_chunk's contract (srhpm_quantize_chunk)."""
+    lib = L.load()
+    w = np.ascontiguousarray(np.asarray(w, dtype=np.float32))
+    rows, K = w.shape
+    rs = lib.srhpm_row_size(qtype, K)
+    if rs == 0:
+        raise ValueError(f"K={K} is not a multiple of the block size of {L.TYPE_NAMES.get(qtype, qtype)}")
+    out = np.empty((rows, rs), dtype=np.uint8)
+    n = lib.srhpm_quantize_chunk(qtype, w.ctypes.data, out.ctypes.data, 0, rows, K, None)
+    if n != rows * rs:
+        raise RuntimeError("srhpm_quantize_chunk failed")
+    return out
+
+
+class QuantTensor:
+    """GGUF-packed weight rows in device memory: a ggml tensor of a quantized type with ne = [K, rows]."""
+
+    def __init__(self, data, qtype, rows, K):
+        lib = L.load()
+        self.qtype, self.rows, self.K = qtype, rows, K
+        self.row_bytes = lib.srhpm_row_size(qtype, K)
+        if self.row_bytes == 0:
+            raise ValueError("K is not a multiple of the block size")
+        assert data.dtype == torch.uint8 and data.is_cuda and data.numel() >= rows * self.row_bytes
+        self.data = data
+
+    @classmethod
+    def from_blocks(cls, blocks, qtype, rows, K, device="cuda"):
+        t = torch.from_numpy(np.ascontiguousarray(blocks).reshape(-1)).to(device)
+        return cls(t, qtype, rows, K)
+
+    @classmethod
+    def quantize(cls, w, qtype, device="cuda"):
+        w = np.asarray(w, dtype=np.float32)
+        return cls.from_blocks(quantize_chunk(w, qtype), qtype, w.shape[0], w.shape[1], device)
+
+    def view(self):
+        lib = L.load()
+        return _tensor_view(self.data, self.qtype, [self.K, self.rows], [lib.srhpm_type_size(self.qtype),
+                                                                         self.row_bytes])
+
+    def row_slice(self, r0, r1):
+        """Rows [r0, r1) as their own tensor (a view: the reference's CPU/GPU row split)."""
+        sub = self.data[r0 * self.row_bytes:r1 * self.row_bytes]
+        return QuantTensor(sub, self.qtype, r1 - r0, self.K)
+
+    @property
+    def nbytes(self):
+        return self.rows * self.row_bytes
+
+
+class Context:
+    """srhpm_ctx of one device plus a cached work buffer."""
+
+    def __init__(self, device=0):
+        self.lib = L.load()
+        self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
+        h = ctypes.c_void_p()
+        L.check(self.lib.srhpm_ctx_create(self.device.index or 0, ctypes.byref(h)), "srhpm_ctx_create")
+        self.handle = h
+        self._work = None
+
+    def close(self):
+        if self.handle:
+            self.lib.srhpm_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_q8_0_act_mode(self, mode):
+        L.check(self.lib.srhpm_ctx_set_q8_0_act_mode(self.handle, mode), "set_q8_0_act_mode")
+
+    def launch_count(self, reset=False):
+        return int(self.lib.srhpm_ctx_launch_count(self.handle, 1 if reset else 0))
+
+    def check(self):
+        code = ctypes.c_int32(0)
+        st = self.lib.srhpm_ctx_check(self.handle, ctypes.byref(code))
+        if st != L.OK:
+            raise L.SrhpmError(st, f"device status {code.value}", self.lib)
+
+    def work(self, nbytes):
+        if self._work is None or self._work.numel() < nbytes:
+            self._work = torch.empty(max(nbytes, 1 << 16), dtype=torch.uint8, device=self.device)
+        return self._work
+
+    # ---- small-batch quantized matmul -------------------------------------------------------------------------
+    def mul_mat_work_size(self, W, X):
+        wv, xv = W.view(), f32_rows_view(X)
+        sz = ctypes.c_size_t()
+        st = self.lib.srhpm_mul_mat_work_size(ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(sz))
+        return st, sz.value
+
+    def mul_mat(self, W, X, out=None, stream=None, work=None):
+        """Y[N, rows] = X[N, K] . W[rows, K]^T (ggml_mul_mat(W, X): dst ne = [rows, N])."""
+        X = X if X.stride(-1) == 1 else X.contiguous()
+        N = X.shape[0]
+        if out is None:
+            out = torch.empty((N, W.rows), dtype=torch.float32, device=X.device)
+        wv, xv, yv = W.view(), f32_rows_view(X), f32_rows_view(out)
+        st, ws = self.mul_mat_work_size(W, X)
+        L.check(st, "srhpm_mul_mat_work_size")
+        buf = work if work is not None else self.work(ws)
+        L.check(self.lib.srhpm_mul_mat(self.handle, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv),
+                                       ctypes.c_void_p(buf.data_ptr()), buf.numel(), _stream_ptr(stream)),
+                "srhpm_mul_mat")
+        return out
+
+    def mul_mat_isums(self, W, X, stream=None):
+        """Integer block sums of the matmul: isum, imin int32 [N, rows, nblk] (imin only for Q4_K / Q5_K)."""
+        X = X.contiguous()
+        N = X.shape[0]
+        nblk = W.K // (32 if W.qtype == L.Q8_0 else 256)
+        isum = torch.zeros((N, W.rows, nblk), dtype=torch.int32, device=X.device)
+        imin = torch.zeros_like(isum)
+        wv, xv = W.view(), f32_rows_view(X)
+        st, ws = self.mul_mat_work_size(W, X)
+        L.check(st, "srhpm_mul_mat_work_size")
+        buf = self.work(ws)
+        L.check(self.lib.srhpm_mul_mat_isums(self.handle, ctypes.byref(wv), ctypes.byref(xv),
+                                             ctypes.c_void_p(isum.data_ptr()), ctypes.c_void_p(imin.data_ptr()),
+                                             ctypes.c_void_p(buf.data_ptr()), buf.numel(), _stream_ptr(stream)),
+                "srhpm_mul_mat_isums")
+        return isum, imin
+
+    def quantize_rows_q8_K(self, X, stream=None):
+        X = X.contiguous()
+        N, K = X.shape
+        q = torch.empty((N, K), dtype=torch.int8, device=X.device)
+        d = torch.empty((N, K // 256), dtype=torch.float32, device=X.device)
+        b32 = torch.empty((N, K // 32), dtype=torch.int16, device=X.device)
+        b16 = torch.empty((N, K // 16), dtype=torch.int16, device=X.device)
+        xv = f32_rows_view(X)
+        L.check(self.lib.srhpm_quantize_rows_q8_K(self.handle, ctypes.byref(xv), ctypes.c_void_p(q.data_ptr()),
+                                                  ctypes.c_void_p(d.data_ptr()), ctypes.c_void_p(b32.data_ptr()),
+                                                  ctypes.c_void_p(b16.data_ptr()), _stream_ptr(stream)),
+                "srhpm_quantize_rows_q8_K")
+        return q, d, b32, b16
+
+    def quantize_rows_q8_0(self, X, stream=None):
+        X = X.contiguous()
+        N, K = X.shape
+        out = torch.empty((N, (K // 32) * 34), dtype=torch.uint8, device=X.device)
+        xv = f32_rows_view(X)
+        L.check(self.lib.srhpm_quantize_rows_q8_0(self.handle, ctypes.byref(xv), ctypes.c_void_p(out.data_ptr()),
+                                                  _stream_ptr(stream)), "srhpm_quantize_rows_q8_0")
+        return out
