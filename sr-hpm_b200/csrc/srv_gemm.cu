@@ -745,13 +745,15 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     a.SR                  = slot_stride(need);
     a.stage_bytes         = (kTileRows * a.SR + a.kc * RB + 127) / 128 * 128;
     const size_t smem     = kBarBytes + (size_t) kStages * a.stage_bytes;
+    if (smem > 200 * 1024) return SRHPM_ERR_INVALID;
     auto         kern     = srv_gemm_kernel<D, NG, DBG>;
     // the shared-memory opt-in is per kernel and per device
     static std::atomic<unsigned> attr_done{ 0 };
     int                          dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_done.load() & (1u << (dev & 31)))) {
-        const int st = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) smem));
+        // every configuration of this kernel needs well under 200 KB (checked below); the opt-in covers them all
+        const int st = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         if (st != SRHPM_OK) return st;
         attr_done.fetch_or(1u << (dev & 31));
     }
