@@ -9,12 +9,14 @@ the 20 matrices (864 MB) are far larger than L2, so no call reads another's weig
 value  = algorithmic bytes (weights + activations read + outputs written) / device time of the step, GB/s, summed
          over ranks. With N GPUs every matrix is sharded by output rows (each rank computes rows/N rows, then
          an all-gather of Y over NCCL): strong scaling.
-e2e    = the same products through the public API with host buffers: each call copies its activations from
-         pinned host memory to the device, runs, and copies Y back, all inside the timed region.
-roofline: the matmul op (activation quantizer + GEMM kernel, PDL-overlapped) timed per call with CUDA events on
-         its stream; achieved = algorithmic bytes / summed op time, against the measured HBM copy bandwidth.
+         The timed steps replay a CUDA graph of one step (1 GPU); --eager times the calls as issued.
+e2e    = the same products through the public API with host buffers, issued call by call: one H2D copy of the
+         step's activations from pinned host memory, the 60 products, one D2H copy of every output, all timed.
+roofline: the matmul op (activation quantizer + GEMM kernel, PDL-overlapped) timed per product with CUDA events
+         captured between the products; achieved = algorithmic bytes / summed op time, against the measured HBM
+         copy bandwidth.
 cpu_baseline: the reference's own SRV kernels (compiled from its patch into oracle/_ref; Q8_0 has no SRV kernel,
-         so its share runs the restated stock path) on the host cores, over a row sample of the same sweep.
+         so its share runs the restated stock path) on all host cores, full passes of the same workload.
 
 --impl reference runs that CPU implementation alone as the reference arm (rank 0 only).
 """
@@ -131,38 +133,53 @@ def make_host_acts():
     return {(N, K): rng.standard_normal((N, K), dtype=np.float32) for N in NS for K in sorted({k for _, k in SHAPES})}
 
 
-def sweep_ops():
+def sweep_ops(only=None):
+    """(N, type, rows, K) of one step. only = "TYPE:ROWSxK:N" restricts the step to that product."""
+    if only:
+        name, shape, n = only.split(":")
+        rows, K = (int(v) for v in shape.lower().split("x"))
+        return [(int(n), TYPE_IDS[name], rows, K)]
     return [(N, TYPE_IDS[name], rows, K) for N in NS for (rows, K) in SHAPES for name in TYPE_NAMES]
 
 
 # ------------------------------------------------------------------------------------------------------------------
 # CPU baseline: the reference's own kernels
 
-def cpu_sample(host_w, host_x, frac_rows, reps=1):
-    """Runs the sweep on the host cores over the first rows*frac_rows rows of every matrix; returns (GB/s, secs,
-    threads, kind)."""
+def cpu_pass(host_w, host_x, ops, nth, O, ref):
+    """One pass of `ops` on the host cores; returns (bytes, seconds, kinds)."""
+    total_b, total_t, kinds = 0.0, 0.0, set()
+    for N, t, rows, K in ops:
+        W = host_w[(t, rows, K)]
+        X = host_x[(N, K)]
+        t0 = time.perf_counter()
+        if t == TYPE_IDS["q8_0"]:
+            O.mul_mat_q8_0_f32(W, rows, K, X, nth=nth)
+            kinds.add("port")
+        elif ref is None:
+            raise RuntimeError("the reference kernels (oracle/_ref) are not built")
+        else:
+            O.ref_mul_mat(t, W, rows, K, X, nth=nth, off=1, paired=1, lib=ref)
+            kinds.add("reference")
+        total_t += time.perf_counter() - t0
+        total_b += op_bytes(t, rows, K, N)
+    return total_b, total_t, kinds
+
+
+def cpu_sample(host_w, host_x, ops, target_s):
+    """Full passes of the workload on all host cores until target_s seconds of CPU time; (GB/s, s, passes, threads,
+    kind, build)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     ref = O.load_ref()
     nth = os.cpu_count() or 1
-    total_b, total_t = 0.0, 0.0
-    kinds = set()
-    for _ in range(reps):
-        for N, t, rows, K in sweep_ops():
-            r = max(16, int(rows * frac_rows))
-            W = host_w[(t, rows, K)][:r]
-            X = host_x[(N, K)]
-            t0 = time.perf_counter()
-            if t == TYPE_IDS["q8_0"] or ref is None:
-                O.mul_mat_q8_0_f32(W, r, K, X, nth=nth) if t == TYPE_IDS["q8_0"] else O.mul_mat(t, W, r, K, X)
-                kinds.add("port" if t == TYPE_IDS["q8_0"] else "port-scalar")
-            else:
-                O.ref_mul_mat(t, W, r, K, X, nth=nth, off=1, paired=1, lib=ref)
-                kinds.add("reference")
-            total_t += time.perf_counter() - t0
-            total_b += op_bytes(t, r, K, N)
-    kind = "reference" if kinds == {"reference", "port"} or kinds == {"reference"} else "port"
-    return total_b / total_t / 1e9, total_t, nth, kind, (O.ref_variant() or "none")
+    cpu_pass(host_w, host_x, ops[:1], nth, O, ref)  # warm the thread pool / pages
+    b, t, kinds, passes = 0.0, 0.0, set(), 0
+    while t < target_s or passes == 0:
+        pb, pt, pk = cpu_pass(host_w, host_x, ops, nth, O, ref)
+        b, t, passes = b + pb, t + pt, passes + 1
+        kinds |= pk
+    kind = "reference" if "reference" in kinds else "port"
+    return b / t / 1e9, t, passes, nth, kind, (O.ref_variant() or "none")
 
 
 # ------------------------------------------------------------------------------------------------------------------
@@ -181,32 +198,51 @@ def dist_setup():
 
 
 def run_reference(args):
+    """The reference arm: the reference's own CPU kernels on all host cores, one full pass of the workload per step."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    ref = O.load_ref()
     host_w = make_host_weights()
     host_x = make_host_acts()
-    frac = args.cpu_frac
+    ops = sweep_ops(args.only)
+    nth = os.cpu_count() or 1
     for _ in range(args.warmup):
-        cpu_sample(host_w, host_x, frac / 4)
-    t0 = time.perf_counter()
-    gbs, secs, nth, kind, variant = cpu_sample(host_w, host_x, frac, reps=args.steps)
-    wall = time.perf_counter() - t0
+        cpu_pass(host_w, host_x, ops, nth, O, ref)
+    b, t, kinds = 0.0, 0.0, set()
+    for _ in range(args.steps):
+        pb, pt, pk = cpu_pass(host_w, host_x, ops, nth, O, ref)
+        b, t, kinds = b + pb, t + pt, kinds | pk
+    gbs = b / t / 1e9
+    kind = "reference" if "reference" in kinds else "port"
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs / args.steps * 1e3, 3),
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8xq", "data": "synthetic",
-        "config": {"workload": "verify-GEMM sweep (5 types x 4 shapes x N=2,4,8)", "sample_rows_frac": frac,
-                   "parallelism": "host threads"},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 x quantized (int32 sums)",
+        "data": "synthetic", "config": workload_config(ops, world),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": nth, "kind": kind,
-                         "sample": f"first {frac:.4f} of the rows of every product of the sweep, {args.steps} steps, "
-                                   f"srv kernels build {variant}"},
+                         "sample": f"{args.steps} full passes of the workload; reference srv kernels build "
+                                   f"{O.ref_variant() or 'none'} (Q8_0: restated stock path)"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "wall_s": round(wall, 2),
     }
     print(json.dumps(line))
     return 0
+
+
+def workload_config(ops, world):
+    if len(ops) == 1:
+        N, t, rows, K = ops[0]
+        name = [k for k, v in TYPE_IDS.items() if v == t][0]
+        wl = f"single product {name} {rows}x{K}, N={N}"
+    else:
+        wl = ("verify-GEMM sweep: Q4_K/Q5_K/Q6_K/Q8_0/IQ4_XS x [5120x5120, 6144x5120, 17408x5120, 5120x17408] x "
+              "N=2,4,8 (60 products per step)")
+    return {"workload": wl, "step_bytes": sum(op_bytes(t, rows, K, N) for N, t, rows, K in ops),
+            "parallelism": f"rows sharded x{world}" if world > 1 else "1 GPU",
+            "l2": "inputs larger than L2: every product in a step reads a different weight matrix (>= 300 MB rotated)"}
 
 
 def run_gpu(args):
@@ -218,43 +254,70 @@ def run_gpu(args):
     ctx = S.Context(local)
     host_w = make_host_weights()
     host_x = make_host_acts()
+    base_ops = sweep_ops(args.only)
+    # with a single product, rotate over copies of its matrix so that consecutive calls never hit L2
+    ncopy = 1
+    if len(base_ops) == 1:
+        N, t, rows, K = base_ops[0]
+        ncopy = max(2, -(-300_000_000 // (rows * row_bytes(t, K))))
+    ops = [op for op in base_ops for _ in range(ncopy)]
+    copy_of = [i % ncopy for i in range(len(ops))]
 
-    # device tensors: each rank holds its row shard of every matrix
     shards = {}
-    for (t, rows, K), blocks in host_w.items():
-        r0 = rows * rank // world
-        r1 = rows * (rank + 1) // world
-        shards[(t, rows, K)] = (S.QuantTensor.from_blocks(blocks[r0:r1], t, r1 - r0, K, dev), r0, r1)
-    xs = {key: torch.from_numpy(v).to(dev) for key, v in host_x.items()}
-    xs_pinned = {key: torch.from_numpy(v).pin_memory() for key, v in host_x.items()}
-    ops = sweep_ops()
-    ys = {}
+    for (N, t, rows, K), c in zip(ops, copy_of):
+        if (t, rows, K, c) in shards:
+            continue
+        r0, r1 = rows * rank // world, rows * (rank + 1) // world
+        shards[(t, rows, K, c)] = (S.QuantTensor.from_blocks(host_w[(t, rows, K)][r0:r1], t, r1 - r0, K, dev), r0, r1)
+    # activations of a step, packed in one buffer (one H2D per step in the end-to-end pass)
+    keys = sorted({(N, K) for N, t, rows, K in ops})
+    xoff, off = {}, 0
+    for key in keys:
+        xoff[key] = off
+        off += key[0] * key[1]
+    x_host = torch.empty(off, dtype=torch.float32).pin_memory()
+    for key in keys:
+        x_host[xoff[key]:xoff[key] + key[0] * key[1]].copy_(torch.from_numpy(host_x[key]).reshape(-1))
+    x_dev = x_host.to(dev)
+    xs = {key: x_dev[xoff[key]:xoff[key] + key[0] * key[1]].view(key[0], key[1]) for key in keys}
+    yoff, off = [], 0
     for N, t, rows, K in ops:
-        ys[(N, t, rows, K)] = torch.empty((N, rows), dtype=torch.float32, device=dev)
-    ws = max(ctx.mul_mat_work_size(shards[(t, rows, K)][0], xs[(N, K)])[1] for N, t, rows, K in ops)
+        yoff.append(off)
+        off += N * rows
+    y_dev = torch.zeros(off, dtype=torch.float32, device=dev)
+    y_host = torch.empty(off, dtype=torch.float32).pin_memory()
+    ys = [y_dev[o:o + N * rows].view(N, rows) for o, (N, t, rows, K) in zip(yoff, ops)]
+    ws = max(ctx.mul_mat_work_size(shards[(t, rows, K, c)][0], xs[(N, K)])[1]
+             for (N, t, rows, K), c in zip(ops, copy_of))
     work = torch.empty(ws, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream()
-
-    def one_op(N, t, rows, K, x=None):
-        W, r0, r1 = shards[(t, rows, K)]
-        y = ys[(N, t, rows, K)]
+    parts = []
+    runs = []
+    for i, ((N, t, rows, K), c) in enumerate(zip(ops, copy_of)):
+        W, r0, r1 = shards[(t, rows, K, c)]
         if world == 1:
-            ctx.mul_mat(W, xs[(N, K)] if x is None else x, out=y, work=work)
+            runs.append(ctx.prepare_mul_mat(W, xs[(N, K)], ys[i], work))
+            parts.append(None)
         else:
             part = torch.empty((N, r1 - r0), dtype=torch.float32, device=dev)
-            ctx.mul_mat(W, xs[(N, K)] if x is None else x, out=part, work=work)
-            gathered = [torch.empty((N, rows * (i + 1) // world - rows * i // world), dtype=torch.float32,
-                                    device=dev) for i in range(world)]
-            dist.all_gather(gathered, part)
-            torch.cat(gathered, dim=1, out=y)
+            runs.append(ctx.prepare_mul_mat(W, xs[(N, K)], part, work))
+            parts.append(part)
+
+    def gather(i):
+        N, t, rows, K = ops[i]
+        gathered = [torch.empty((N, rows * (j + 1) // world - rows * j // world), dtype=torch.float32, device=dev)
+                    for j in range(world)]
+        dist.all_gather(gathered, parts[i])
+        torch.cat(gathered, dim=1, out=ys[i])
 
     def step(events=None):
-        for i, op in enumerate(ops):
+        for i, run in enumerate(runs):
             if events is not None:
-                events[i][0].record(stream)
-            one_op(*op)
+                events[i][0].record()
+            run()
             if events is not None:
-                events[i][1].record(stream)
+                events[i][1].record()
+            if world > 1:
+                gather(i)
 
     def barrier():
         if world > 1:
@@ -265,23 +328,46 @@ def run_gpu(args):
     torch.cuda.synchronize()
     ctx.check()
 
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in ops]
-          for _ in range(args.steps)]
+    # the timed step is replayed from a CUDA graph (no host launch gaps between the 2 kernels of each product);
+    # with several ranks the NCCL all-gathers run eagerly
+    op_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in ops]
+    graph = None
+    if world == 1 and not args.eager:
+        graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()  # one more eager step on the capture stream before capturing
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        ctx.launch_count(reset=True)
+        with torch.cuda.graph(graph):
+            step(op_ev)
+        launches_per_step = ctx.launch_count(reset=True)
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        ctx.check()
+    stream = torch.cuda.current_stream()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = ClockSampler(local) if rank == 0 else None
     if clocks:
         clocks.start()
-        time.sleep(0.3)
+        time.sleep(0.5)
     barrier()
     torch.cuda.synchronize()
     ctx.launch_count(reset=True)
+    op_ms = [0.0] * len(ops)
     t_start.record(stream)
-    for s in range(args.steps):
-        step(ev[s])
+    for _ in range(args.steps):
+        if graph is not None:
+            graph.replay()
+        else:
+            step(op_ev)
     t_end.record(stream)
     torch.cuda.synchronize()
     barrier()
-    launches = ctx.launch_count()
+    launches = launches_per_step * args.steps if graph is not None else ctx.launch_count()
     clk = clocks.stop() if clocks else None
     ms = t_start.elapsed_time(t_end)
     if world > 1:
@@ -292,37 +378,35 @@ def run_gpu(args):
     step_bytes = sum(op_bytes(t, rows, K, N) for N, t, rows, K in ops)
     value = step_bytes / (ms_step * 1e-3) / 1e9
 
-    # roofline: per-op durations (quantize + GEMM) of this rank, summed over the timed steps
-    op_ms = [sum(ev[s][i][0].elapsed_time(ev[s][i][1]) for s in range(args.steps)) / args.steps
-             for i in range(len(ops))]
-    my_bytes = [shards[(t, rows, K)][0].nbytes + N * K * 4 + N * (shards[(t, rows, K)][2] - shards[(t, rows, K)][1]) * 4
-                for N, t, rows, K in ops]
-    achieved = sum(my_bytes) / (sum(op_ms) * 1e-3) / 1e9
+    # roofline: per-product op times of the last timed step (events captured between the products)
+    try:
+        op_ms = [a.elapsed_time(b) for a, b in op_ev]
+    except RuntimeError:
+        op_ms = None
+    my_bytes = [shards[(t, rows, K, c)][0].nbytes + N * K * 4 + N * (shards[(t, rows, K, c)][2] -
+                shards[(t, rows, K, c)][1]) * 4 for (N, t, rows, K), c in zip(ops, copy_of)]
+    if op_ms:
+        achieved = sum(my_bytes) / (sum(op_ms) * 1e-3) / 1e9
+    else:
+        achieved = sum(my_bytes) / (ms_step * 1e-3) / 1e9
     peak, peak_kind = peaks()
-    per_type = {}
-    for i, (N, t, rows, K) in enumerate(ops):
-        name = [k for k, v in TYPE_IDS.items() if v == t][0]
-        per_type.setdefault(name, [0.0, 0.0])
-        per_type[name][0] += my_bytes[i]
-        per_type[name][1] += op_ms[i]
-    per_n = {}
-    for i, (N, t, rows, K) in enumerate(ops):
-        per_n.setdefault(N, [0.0, 0.0])
-        per_n[N][0] += my_bytes[i]
-        per_n[N][1] += op_ms[i]
-    c1 = [i for i, (N, t, rows, K) in enumerate(ops) if (N, t, rows, K) == (4, 12, 17408, 5120)]
 
-    # e2e through the public API with host buffers (H2D of the activations, D2H of Y, per call)
-    host_y = {key: torch.empty(y.shape, dtype=torch.float32).pin_memory() for key, y in ys.items()}
-    h2d = sum(N * K * 4 for N, t, rows, K in ops)
-    d2h = sum(N * rows * 4 for N, t, rows, K in ops)
+    def group(keyf):
+        acc = {}
+        for i, op in enumerate(ops):
+            k = keyf(op)
+            b, m = acc.get(k, (0.0, 0.0))
+            acc[k] = (b + my_bytes[i], m + (op_ms[i] if op_ms else 0.0))
+        return {str(k): round(b / (m * 1e-3) / 1e9, 1) for k, (b, m) in acc.items() if m > 0}
+
+    # e2e through the public API with host buffers: one H2D of the step's activations, the products (issued
+    # call by call, no graph), one D2H of every output
+    h2d, d2h = x_host.numel() * 4, y_host.numel() * 4
 
     def e2e_step():
-        for N, t, rows, K in ops:
-            x = torch.empty((N, K), dtype=torch.float32, device=dev)
-            x.copy_(xs_pinned[(N, K)], non_blocking=True)
-            one_op(N, t, rows, K, x)
-            host_y[(N, t, rows, K)].copy_(ys[(N, t, rows, K)], non_blocking=True)
+        x_dev.copy_(x_host, non_blocking=True)
+        step()
+        y_host.copy_(y_dev, non_blocking=True)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
@@ -343,37 +427,41 @@ def run_gpu(args):
     e2e_value = step_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
     ctx.check()
 
-    line = None
     if rank == 0:
+        cfg = workload_config(base_ops, world)
+        cfg["timed"] = "CUDA graph of one step, replayed" if graph is not None else "eager calls"
+        if ncopy > 1:
+            cfg["copies_rotated"] = ncopy
+        cfg["per_type_gbs"] = group(lambda op: [k for k, v in TYPE_IDS.items() if v == op[1]][0])
+        cfg["per_N_gbs"] = group(lambda op: op[0])
+        cfg["per_shape_gbs"] = group(lambda op: f"{op[2]}x{op[3]}")
+        c1 = [i for i, op in enumerate(ops) if op == (4, 12, 17408, 5120)]
+        if op_ms and c1:
+            cfg["q4_K_17408x5120_N4_us"] = round(sum(op_ms[i] for i in c1) / len(c1) * 1e3, 2)
         cpu = None
         if world == 1 and not args.no_cpu:
-            gbs, secs, nth, kind, variant = cpu_sample(host_w, host_x, args.cpu_frac)
+            gbs, secs, passes, nth, kind, variant = cpu_sample(host_w, host_x, base_ops, args.cpu_seconds)
             cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": nth, "kind": kind,
-                   "sample": f"first {args.cpu_frac:.4f} of the rows of every product of the sweep (one pass, "
-                             f"{secs:.1f} s); reference srv kernels build {variant}; Q8_0 restated stock path"}
+                   "sample": f"{passes} full passes of the workload ({secs:.1f} s of CPU time); reference srv "
+                             f"kernels build {variant}; Q8_0 (no srv kernel) through the restated stock path"}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int8xq4..q8 (int32 exact sums, f32 scales)",
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8 x quantized (int32 exact sums, f32 scales)",
             "data": "synthetic (seeded N(0,0.02) weights quantized on the host, N(0,1) activations)",
-            "config": {"workload": "verify-GEMM sweep: Q4_K/Q5_K/Q6_K/Q8_0/IQ4_XS x [5120x5120, 6144x5120, "
-                                   "17408x5120, 5120x17408] x N=2,4,8 (60 products per step)",
-                       "step_bytes": step_bytes, "parallelism": f"row-sharded x{world}" if world > 1 else "1 GPU",
-                       "l2": "inputs larger than L2 (864 MB of weights rotated per step)",
-                       "config1_q4K_17408x5120_N4_gbs": round(
-                           sum(my_bytes[i] for i in c1) / (sum(op_ms[i] for i in c1) * 1e-3) / 1e9, 2) if c1 else None,
-                       "per_type_gbs": {k: round(b / (m * 1e-3) / 1e9, 1) for k, (b, m) in per_type.items()},
-                       "per_N_gbs": {str(k): round(b / (m * 1e-3) / 1e9, 1) for k, (b, m) in sorted(per_n.items())}},
+            "config": cfg,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "kernel": "srv_gemm_kernel (+ activation quantizer, PDL-overlapped)",
                          "traffic": args.traffic},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
             "gpu_launches": int(launches),
             "clocks": clk,
         }
         print(json.dumps(line))
+    graph = None
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -387,7 +475,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="srhpm", choices=["srhpm", "reference"])
-    ap.add_argument("--cpu-frac", type=float, default=1.0 / 32, help="row fraction of the CPU baseline sample")
+    ap.add_argument("--only", default=None, help='one product "TYPE:ROWSxK:N", e.g. q4_K:17408x5120:4')
+    ap.add_argument("--eager", action="store_true", help="time eager calls instead of a captured graph")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU time of the CPU-baseline sample")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--traffic", type=float, default=None, help="ncu dram bytes per launch, when captured")
     args = ap.parse_args()

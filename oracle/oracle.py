@@ -31,6 +31,14 @@ def _ptr(a):
     return ctypes.c_void_p(a.ctypes.data) if a is not None else None
 
 
+def _u8(a):
+    """The bytes of a as a contiguous uint8 vector (no copy when a already is one)."""
+    a = np.asarray(a)
+    if not a.flags.c_contiguous:
+        a = np.ascontiguousarray(a)
+    return a.reshape(-1).view(np.uint8)
+
+
 def load_oracle():
     global _orc
     if _orc is None:
@@ -123,14 +131,14 @@ def quantize_row_q8_0(x, mode=Q8_0_SIMD):
 
 
 def dequantize(qtype, blocks, n):
-    blocks = np.ascontiguousarray(np.frombuffer(np.asarray(blocks).tobytes(), np.uint8))
+    blocks = _u8(blocks)
     y = np.empty(n, np.float32)
     load_oracle().orc_dequantize(qtype, _ptr(blocks), _ptr(y), n)
     return y
 
 
 def row_isums(qtype, row, xq, bsum32, K):
-    row = np.ascontiguousarray(np.frombuffer(np.asarray(row).tobytes(), np.uint8))
+    row = _u8(row)
     xq = np.ascontiguousarray(xq, np.int8)
     b32 = np.ascontiguousarray(bsum32, np.int16) if bsum32 is not None else np.zeros(K // 32, np.int16)
     nblk = K // BLOCK_ELEMS[qtype]
@@ -142,7 +150,7 @@ def row_isums(qtype, row, xq, bsum32, K):
 
 def mul_mat(qtype, W, rows, K, X, q8_mode=Q8_0_SIMD):
     """Exact-integer oracle: double [N, rows]."""
-    W = np.ascontiguousarray(np.frombuffer(np.asarray(W).tobytes(), np.uint8))
+    W = _u8(W)
     X = np.ascontiguousarray(X, np.float32)
     N = X.shape[0]
     Y = np.empty((N, rows), np.float64)
@@ -152,7 +160,7 @@ def mul_mat(qtype, W, rows, K, X, q8_mode=Q8_0_SIMD):
 
 
 def mul_mat_q8_0_f32(W, rows, K, X, q8_mode=Q8_0_SIMD, nth=1):
-    W = np.ascontiguousarray(np.frombuffer(np.asarray(W).tobytes(), np.uint8))
+    W = _u8(W)
     X = np.ascontiguousarray(X, np.float32)
     N = X.shape[0]
     Y = np.empty((N, rows), np.float32)
@@ -166,8 +174,8 @@ def attention(q, kv_type, k, v, DV, L, Hkv, mask=None, sinks=None, scale=1.0, ma
     """q f32 [H, N, DK]; k, v bytes [Hkv, L, row]; mask f16-bits uint16 [N, L]; returns double [N, H, DV]."""
     q = np.ascontiguousarray(q, np.float32)
     H, N, DK = q.shape
-    k = np.ascontiguousarray(np.frombuffer(np.asarray(k).tobytes(), np.uint8))
-    v = np.ascontiguousarray(np.frombuffer(np.asarray(v).tobytes(), np.uint8))
+    k = _u8(k)
+    v = _u8(v)
     m = np.ascontiguousarray(mask, np.uint16) if mask is not None else None
     s = np.ascontiguousarray(sinks, np.float32) if sinks is not None else None
     dst = np.empty((N, H, DV), np.float64)
@@ -203,7 +211,7 @@ def ref_quantize_row(x, lib=None):
 def ref_mul_mat(qtype, W, rows, K, X, nth=1, off=1, paired=1, lib=None):
     """The reference's SRV kernels (srv_row via compute_forward's scheduling): f32 [N, rows]."""
     lib = lib or load_ref()
-    W = np.ascontiguousarray(np.frombuffer(np.asarray(W).tobytes(), np.uint8))
+    W = _u8(W)
     X = np.ascontiguousarray(X, np.float32)
     N = X.shape[0]
     Y = np.empty((N, rows), np.float32)
@@ -219,8 +227,8 @@ def ref_fa_gqa(q, kv_type, k, v, DV, L, Hkv, mask=None, sinks=None, scale=1.0, m
     lib.ref_set_q8_0_mode(q8_mode)
     q = np.ascontiguousarray(q, np.float32)
     H, N, DK = q.shape
-    k = np.ascontiguousarray(np.frombuffer(np.asarray(k).tobytes(), np.uint8))
-    v = np.ascontiguousarray(np.frombuffer(np.asarray(v).tobytes(), np.uint8))
+    k = _u8(k)
+    v = _u8(v)
     krow = DK // 32 * 34 if kv_type == Q8_0 else DK * 2
     vrow = DV // 32 * 34 if kv_type == Q8_0 else DV * 2
     nbq = (ctypes.c_size_t * 4)(4, DK * 4, N * DK * 4, H * N * DK * 4)

@@ -155,6 +155,28 @@ class Context:
                 "srhpm_mul_mat")
         return out
 
+    def prepare_mul_mat(self, W, X, Y, work):
+        """A zero-argument callable that issues srhpm_mul_mat(W, X) -> Y on the current stream with prebuilt
+        arguments (the per-call host cost is one ctypes call); usable under CUDA-graph capture, since the call
+        allocates nothing."""
+        wv, xv, yv = W.view(), f32_rows_view(X), f32_rows_view(Y)
+        st, ws = self.mul_mat_work_size(W, X)
+        L.check(st, "srhpm_mul_mat_work_size")
+        if work.numel() < ws:
+            raise ValueError("work buffer too small")
+        fn, lib = self.lib.srhpm_mul_mat, self.lib
+        args = [self.handle, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv), ctypes.c_void_p(work.data_ptr()),
+                work.numel()]
+        keep = (wv, xv, yv, W, X, Y, work)
+
+        def run():
+            st = fn(*args, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+            if st != L.OK:
+                raise L.SrhpmError(st, "srhpm_mul_mat", lib)
+
+        run.keep = keep
+        return run
+
     def mul_mat_isums(self, W, X, stream=None):
         """Integer block sums of the matmul: isum, imin int32 [N, rows, nblk] (imin only for Q4_K / Q5_K)."""
         X = X.contiguous()
