@@ -182,7 +182,7 @@ int srhpm_mul_mat_work_size(const srhpm_tensor * W, const srhpm_tensor * X, size
     if (!size) return SRHPM_ERR_INVALID;
     const int st = check_mul_mat(W, X, nullptr);
     if (st != SRHPM_OK) return st;
-    *size = gemm_work_size(W->type, W->ne[0], X->ne[1]);
+    *size = gemm_work_size(W->type, W->ne[1], W->ne[0], X->ne[1]);
     return SRHPM_OK;
 }
 

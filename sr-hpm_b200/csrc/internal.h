@@ -32,7 +32,7 @@ bool is_weight_type(int type);
 int  weight_block_bytes(int type);
 
 // srv_gemm.cu
-size_t gemm_work_size(int wtype, int64_t K, int64_t N);
+size_t gemm_work_size(int wtype, int64_t rows, int64_t K, int64_t N);
 int    gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                 const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
                 int32_t * isum, int32_t * imin, cudaStream_t stream);

@@ -64,6 +64,24 @@ __device__ __forceinline__ void bulk_g2s(void * dst, const void * src, uint32_t 
         : "memory");
 }
 
+// 2-D tiled TMA load of one box at element coordinates (x, y), completion counted on bar (no multicast)
+__device__ __forceinline__ void tma_load_2d(void * dst, const void * tmap, int x, int y, uint64_t * bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const void * tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// barrier among `count` threads (a multiple of 32) on hardware barrier `id` (id 0 is __syncthreads)
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // orders this thread's generic-proxy shared-memory writes before later async-proxy (bulk copy) accesses
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -21,6 +21,9 @@
 #include <algorithm>
 #include <atomic>
 
+#include <cuda.h>
+#include <cstring>
+
 #include "internal.h"
 #include "ptx.cuh"
 
@@ -39,25 +42,6 @@ __host__ __device__ constexpr int rec_nscales(bool q80, int NT) { return q80 ? 8
 __host__ __device__ constexpr int rec_bytes(bool q80, int NT) {
     return (NT * kTokStride + 4 * rec_nscales(q80, NT) + 15) / 16 * 16;
 }
-
-struct GemmArgs {
-    const uint8_t * W;
-    int64_t         rows;
-    int64_t         row_bytes;
-    int64_t         w_bytes;     // valid bytes of W (rows * row_bytes)
-    int             nsb;         // 256-column super-blocks per row
-    int             kc;          // super-blocks per stage
-    int             SR;          // shared-memory bytes per weight row slot
-    int             stage_bytes;
-    const uint8_t * recs;        // activation records, nsb of them
-    float *         Y;
-    int64_t         ldy;         // elements
-    int             N;
-    int32_t *       status;
-    int32_t *       isum;        // integer outputs (srhpm_mul_mat_isums), else null
-    int32_t *       imin;
-    int             nblk;        // blocks per row in the integer outputs
-};
 
 // ---------------------------------------------------------------------------------------------------------------
 // activation quantizers
@@ -89,8 +73,10 @@ template <bool DENSE>
 __global__ void __launch_bounds__(256) quant_q8K_kernel(const float * __restrict__ X, int64_t ldx, int N, int nsb,
                                                          int NT, uint8_t * __restrict__ recs, int8_t * __restrict__ q,
                                                          float * __restrict__ d, int16_t * __restrict__ b32,
-                                                         int16_t * __restrict__ b16) {
+                                                         int16_t * __restrict__ b16, int32_t * __restrict__ cnt,
+                                                         int ncnt) {
     pdl_launch_dependents();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncnt; i += gridDim.x * blockDim.x) cnt[i] = 0;
     const int     lane = threadIdx.x & 31;
     const int     TT   = DENSE ? N : NT;
     const int64_t wid  = (int64_t) blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -158,8 +144,10 @@ __global__ void __launch_bounds__(256) quant_q8K_kernel(const float * __restrict
 template <bool DENSE>
 __global__ void __launch_bounds__(256) quant_q80_kernel(const float * __restrict__ X, int64_t ldx, int N, int nsb,
                                                          int NT, int mode, uint8_t * __restrict__ recs,
-                                                         uint8_t * __restrict__ blocks) {
+                                                         uint8_t * __restrict__ blocks, int32_t * __restrict__ cnt,
+                                                         int ncnt) {
     pdl_launch_dependents();
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncnt; i += gridDim.x * blockDim.x) cnt[i] = 0;
     const int     lane = threadIdx.x & 31;
     const int     TT   = DENSE ? N : NT;
     const int64_t wid  = (int64_t) blockIdx.x * 8 + (threadIdx.x >> 5);
@@ -585,93 +573,169 @@ struct DecQ80 {
 
 // ---------------------------------------------------------------------------------------------------------------
 // the kernel
+//
+// Work unit = (block of 64 weight rows, K range). CTAs are persistent: CTA c takes units c, c + grid, ... and the
+// grid is a multiple of the number of K ranges, so a CTA keeps one K range. Each unit streams through the stage ring
+// in chunks of kc super-blocks; a stage holds the chunk's 64 row segments (TMA boxes) and its kc activation records.
+// With one K range the consumers write Y; otherwise each unit writes its partial sums to the work buffer and the
+// last of the unit's K ranges to arrive (an atomic counter, no waiting) adds them up in K order and writes Y.
+
+struct GemmArgs {
+    const uint8_t * W;           // weight rows, 16-byte aligned
+    int64_t         rows;
+    int64_t         row_bytes;
+    int64_t         w_bytes;     // rows * row_bytes
+    int64_t         rows_main;   // rows reachable through the tensor map: (rows / G) * G
+    int             nsb;         // 256-column super-blocks per row
+    int             kc;          // super-blocks per stage
+    int             G;           // weight rows per tensor-map row (G * row_bytes is a multiple of 16)
+    int             Wbox;        // bytes per row segment in a stage (TMA box width)
+    int             ksplit;      // K ranges
+    int             kr_sbs;      // super-blocks per K range (the last one may be shorter)
+    int             units;
+    int             stage_bytes;
+    int             left_off;    // leftover-row slots (rows >= rows_main) inside a stage
+    int             LSR;         // leftover slot stride
+    int             rec_off;     // activation records inside a stage
+    const uint8_t * recs;
+    float *         part;        // split-K partial sums [ksplit][N][rows]
+    int32_t *       cnt;         // split-K arrival counters, one per row block (zeroed by the quantizer kernel)
+    float *         Y;
+    int64_t         ldy;         // elements
+    int             N;
+    int32_t *       status;
+    int32_t *       isum;        // integer outputs (srhpm_mul_mat_isums), else null
+    int32_t *       imin;
+    int             nblk;        // blocks per row in the integer outputs
+};
+
+// 1-D copy of the row segment [start, end) of W into dst (16-byte aligned, holding the segment at its own 16-byte
+// phase): bulk bytes below the last 16-byte boundary of W, hand copy of the ragged end. Returns the bulk bytes.
+__device__ __forceinline__ uint32_t row_segment_copy(const GemmArgs & a, uint8_t * dst, int64_t start, int64_t end,
+                                                     uint64_t * bar, bool issue) {
+    const int64_t wlim = a.w_bytes & ~int64_t(15);
+    const int64_t a0 = start & ~int64_t(15), be = min((end + 15) & ~int64_t(15), wlim);
+    uint32_t      tx = 0;
+    if (be > a0) {
+        if (issue) bulk_g2s(dst, a.W + a0, (uint32_t) (be - a0), bar);
+        tx = (uint32_t) (be - a0);
+    }
+    if (!issue) {
+        for (int64_t p = max(a0, be); p < end; p++) dst[p - a0] = a.W[p];
+    }
+    return tx;
+}
 
 template <class D, int NG>
-__device__ __forceinline__ void producer(const GemmArgs & a, uint64_t * full, uint64_t * empty, uint8_t * stage0,
-                                         int64_t row0, int nchunks, int lane) {
-    constexpr int  RB   = rec_bytes(D::Q80, 8 * NG);
-    const int64_t  wlim = a.w_bytes & ~int64_t(15);  // bytes below this are reachable by 16-byte bulk copies
-    // weight part of chunk c: tail bytes by hand (issue = false, returns this lane's bulk bytes) or the bulk copies
-    auto w_part = [&](int c, uint8_t * st, uint64_t * bar, bool issue) -> uint32_t {
-        uint32_t      tx  = 0;
-        const int     sb0 = c * a.kc, kcc = min(a.kc, a.nsb - sb0);
-        for (int i = lane; i < kTileRows; i += 32) {
-            const int64_t r = row0 + i;
-            if (r >= a.rows) continue;
-            const int64_t start = r * a.row_bytes + (int64_t) sb0 * D::BS, end = start + (int64_t) kcc * D::BS;
-            const int64_t a0 = start & ~int64_t(15), be = min((end + 15) & ~int64_t(15), wlim);
-            uint8_t *     dst = st + i * a.SR;
-            if (be > a0) {
-                if (issue) bulk_g2s(dst, a.W + a0, (uint32_t) (be - a0), bar);
-                tx += (uint32_t) (be - a0);
-            }
-            if (!issue) {
-                for (int64_t p = max(a0, be); p < end; p++) dst[p - a0] = a.W[p];
-            }
-        }
-        return tx;
-    };
-    const int npre   = min(kStages, nchunks);
-    int       issued = 0;
-    bool      ok     = true;
-    // prologue: weight copies of the first stages go out before the activation records exist (PDL overlap)
-    for (int c = 0; c < npre; c++) {
-        uint8_t *      st  = stage0 + (size_t) c * a.stage_bytes;
-        const int      kcc = min(a.kc, a.nsb - c * a.kc);
-        const uint32_t tx  = __reduce_add_sync(0xffffffffu, w_part(c, st, &full[c], false)) + (uint32_t) (kcc * RB);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_expect_tx(&full[c], tx);
-        __syncwarp();
-        w_part(c, st, &full[c], true);
+__device__ __forceinline__ void produce_stage(const GemmArgs & a, const CUtensorMap * wmap, uint8_t * st,
+                                              uint64_t * bar, int64_t row0, int sb0, int kcc, int lane,
+                                              bool defer_records) {
+    constexpr int RB = rec_bytes(D::Q80, 8 * NG);
+    // leftover rows (at most G - 1, never reached by the tensor map): one lane each, 1-D copies
+    uint32_t      tx = 0;
+    const int64_t lr = row0 + lane;
+    const bool    left = lane < kTileRows && lr >= a.rows_main && lr < a.rows && lr < row0 + kTileRows;
+    if (left) {
+        const int64_t start = lr * a.row_bytes + (int64_t) sb0 * D::BS;
+        tx = row_segment_copy(a, st + a.left_off + (int) (lr - a.rows_main) * a.LSR, start,
+                              start + (int64_t) kcc * D::BS, bar, false);
     }
-    pdl_wait();
+    tx = __reduce_add_sync(0xffffffffu, tx);
+    const bool tma = a.rows_main > 0;
+    if (tma) tx += (uint32_t) (kTileRows * a.Wbox);
+    tx += (uint32_t) (kcc * RB);  // the records, issued here or (deferred) once the quantizer grid has finished
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_expect_tx(bar, tx);
+    __syncwarp();
+    if (left) {
+        const int64_t start = lr * a.row_bytes + (int64_t) sb0 * D::BS;
+        row_segment_copy(a, st + a.left_off + (int) (lr - a.rows_main) * a.LSR, start, start + (int64_t) kcc * D::BS,
+                         bar, true);
+    }
     if (lane == 0) {
-        for (int c = 0; c < npre; c++) {
-            const int kcc = min(a.kc, a.nsb - c * a.kc);
-            bulk_g2s(stage0 + (size_t) c * a.stage_bytes + kTileRows * a.SR, a.recs + (size_t) c * a.kc * RB,
-                     (uint32_t) (kcc * RB), &full[c]);
+        if (tma) {
+            const int rpb = kTileRows / a.G;  // tensor-map rows per box
+            for (int j = 0; j < a.G; j++) {
+                const int64_t xb = ((int64_t) j * a.row_bytes + (int64_t) sb0 * D::BS) & ~int64_t(15);
+                tma_load_2d(st + j * rpb * a.Wbox, wmap, (int) (xb >> 2), (int) (row0 / a.G), bar);
+            }
+        }
+        if (!defer_records) bulk_g2s(st + a.rec_off, a.recs + (size_t) sb0 * RB, (uint32_t) (kcc * RB), bar);
+    }
+}
+
+template <class D, int NG>
+__device__ __forceinline__ void producer(const GemmArgs & a, const CUtensorMap * wmap, uint64_t * full,
+                                         uint64_t * empty, uint8_t * stage0, int lane) {
+    constexpr int RB  = rec_bytes(D::Q80, 8 * NG);
+    const int     kr  = blockIdx.x % a.ksplit;
+    const int     sbA = kr * a.kr_sbs, sbB = min(a.nsb, sbA + a.kr_sbs);
+    const int     nck = (sbB - sbA + a.kc - 1) / a.kc;
+    if (lane == 0 && a.rows_main > 0) prefetch_tmap(wmap);
+    int  n = 0;  // stages issued
+    bool ok = true;
+    bool waited = false;
+    for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
+        const int64_t row0 = (int64_t) (u / a.ksplit) * kTileRows;
+        for (int c = 0; c < nck; c++, n++) {
+            const int s = n % kStages;
+            if (n >= kStages && !mbar_wait(&empty[s], ((n / kStages) - 1) & 1)) {
+                ok = false;
+                break;
+            }
+            const int sb0 = sbA + c * a.kc, kcc = min(a.kc, sbB - sb0);
+            // the first stages' weights go out before the activation records exist (programmatic dependent
+            // launch); their records follow once the quantizer grid has finished
+            const bool pre = !waited;
+            produce_stage<D, NG>(a, wmap, stage0 + (size_t) s * a.stage_bytes, &full[s], row0, sb0, kcc, lane, pre);
+            if (pre && (n + 1 == kStages || (c + 1 == nck && u + (int) gridDim.x >= a.units))) {
+                pdl_wait();
+                waited = true;
+                if (lane == 0) {
+                    for (int m = 0; m <= n; m++) {  // the records of every stage issued so far
+                        const int cm = m % nck;  // all prologue stages belong to the first unit(s)
+                        const int sbm = sbA + cm * a.kc, kcm = min(a.kc, sbB - sbm);
+                        bulk_g2s(stage0 + (size_t) (m % kStages) * a.stage_bytes + a.rec_off,
+                                 a.recs + (size_t) sbm * RB, (uint32_t) (kcm * RB), &full[m % kStages]);
+                    }
+                }
+            }
         }
     }
-    issued = npre;
-    for (int c = npre; c < nchunks; c++) {
-        const int s = c % kStages;
-        if (!mbar_wait(&empty[s], ((c / kStages) - 1) & 1)) {
-            ok = false;
-            break;
-        }
-        uint8_t *      st  = stage0 + (size_t) s * a.stage_bytes;
-        const int      kcc = min(a.kc, a.nsb - c * a.kc);
-        const uint32_t tx  = __reduce_add_sync(0xffffffffu, w_part(c, st, &full[s], false)) + (uint32_t) (kcc * RB);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_expect_tx(&full[s], tx);
-        __syncwarp();
-        w_part(c, st, &full[s], true);
-        if (lane == 0) {
-            bulk_g2s(st + kTileRows * a.SR, a.recs + (size_t) c * a.kc * RB, (uint32_t) (kcc * RB), &full[s]);
-        }
-        issued = c + 1;
-    }
+    if (!waited) pdl_wait();
     // drain: every copy this warp issued has landed before the CTA may exit
-    for (int c = max(0, issued - kStages); c < issued; c++) {
-        if (!mbar_wait(&full[c % kStages], (c / kStages) & 1)) {
-            ok = false;
-        }
+    for (int m = max(0, n - kStages); m < n; m++) {
+        if (!mbar_wait(&full[m % kStages], (m / kStages) & 1)) ok = false;
     }
     if (!ok && lane == 0) atomicExch(a.status, kErrWaitEmpty);
 }
 
+// shared-memory address of local row r (0..63) of the tile in a stage; rows past the matrix map to the stage base
+template <class D>
+__device__ __forceinline__ const uint8_t * row_ptr(const GemmArgs & a, const uint8_t * st, int64_t row0, int r,
+                                                   int sb0) {
+    const int64_t R = row0 + r;
+    if (R < a.rows_main) {
+        const int j = r % a.G, q = r / a.G;
+        const int ph = (int) (((int64_t) j * a.row_bytes + (int64_t) sb0 * D::BS) & 15);
+        return st + (j * (kTileRows / a.G) + q) * a.Wbox + ph;
+    }
+    if (R < a.rows) {
+        const int ph = (int) ((R * a.row_bytes + (int64_t) sb0 * D::BS) & 15);
+        return st + a.left_off + (int) (R - a.rows_main) * a.LSR + ph;
+    }
+    return st;
+}
+
 template <class D, int NG, bool DBG>
-__global__ void __launch_bounds__(kThreads) srv_gemm_kernel(const GemmArgs a) {
+__global__ void __launch_bounds__(kThreads) srv_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
+                                                            const GemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t *    full   = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *    empty  = full + kStages;
-    uint8_t *     stage0 = smem + kBarBytes;
-    constexpr int RB     = rec_bytes(D::Q80, 8 * NG);
-    const int     warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t row0    = (int64_t) blockIdx.x * kTileRows;
-    const int     nchunks = (a.nsb + a.kc - 1) / a.kc;
+    uint64_t * full   = reinterpret_cast<uint64_t *>(smem);
+    uint64_t * empty  = full + kStages;
+    uint8_t *  stage0 = smem + kBarBytes;
+    const int  warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
             mbar_init(&full[s], 1);
@@ -681,43 +745,90 @@ __global__ void __launch_bounds__(kThreads) srv_gemm_kernel(const GemmArgs a) {
     }
     __syncthreads();
     if (warp == kNCW) {
-        producer<D, NG>(a, full, empty, stage0, row0, nchunks, lane);
+        producer<D, NG>(a, &wmap, full, empty, stage0, lane);
         return;
     }
-    const int     g = lane >> 2, t = lane & 3;
-    const int     rl = warp * 16 + g;
-    const int64_t rg = row0 + rl;
-    float         acc[NG][4];
+    pdl_wait();  // the split-K counters and partials are written below; the quantizer grid zeroes the counters
+    constexpr int  RB  = rec_bytes(D::Q80, 8 * NG);
+    const int      g = lane >> 2, t = lane & 3;
+    const int      rl  = warp * 16 + g;
+    const int      kr  = blockIdx.x % a.ksplit;
+    const int      sbA = kr * a.kr_sbs, sbB = min(a.nsb, sbA + a.kr_sbs);
+    const int      nck = (sbB - sbA + a.kc - 1) / a.kc;
+    const DbgOut   dbg = { a.isum, a.imin, a.rows, a.N, a.nblk };
+    __shared__ int last_flag;
+    int            n   = 0;
+    bool           bad = false;  // a wait ran out: skip further waits and work, keep meeting the barriers
+    for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
+        const int64_t rb = u / a.ksplit, row0 = rb * kTileRows, rg = row0 + rl;
+        float         acc[NG][4];
 #pragma unroll
-    for (int grp = 0; grp < NG; grp++) acc[grp][0] = acc[grp][1] = acc[grp][2] = acc[grp][3] = 0.0f;
-    const DbgOut dbg = { a.isum, a.imin, a.rows, a.N, a.nblk };
-    for (int c = 0; c < nchunks; c++) {
-        const int s = c % kStages;
-        if (!mbar_wait(&full[s], (c / kStages) & 1)) {
-            if (lane == 0) atomicExch(a.status, kErrWaitFull);
-            return;
+        for (int grp = 0; grp < NG; grp++) acc[grp][0] = acc[grp][1] = acc[grp][2] = acc[grp][3] = 0.0f;
+        for (int c = 0; c < nck; c++, n++) {
+            const int s = n % kStages;
+            if (!bad && !mbar_wait(&full[s], (n / kStages) & 1)) {
+                if (lane == 0) atomicExch(a.status, kErrWaitFull);
+                bad = true;
+            }
+            if (bad) continue;
+            const uint8_t * st  = stage0 + (size_t) s * a.stage_bytes;
+            const int       sb0 = sbA + c * a.kc, kcc = min(a.kc, sbB - sb0);
+            const uint8_t * wa  = row_ptr<D>(a, st, row0, rl, sb0);
+            const uint8_t * wb  = row_ptr<D>(a, st, row0, rl + 8, sb0);
+            const uint8_t * xr  = st + a.rec_off;
+            for (int kb = 0; kb < kcc; kb++) {
+                D::template sb<NG, DBG>(wa + kb * D::BS, wb + kb * D::BS, xr + kb * RB, lane, acc, dbg, rg, sb0 + kb);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
         }
-        const uint8_t * st  = stage0 + (size_t) s * a.stage_bytes;
-        const int       sb0 = c * a.kc, kcc = min(a.kc, a.nsb - sb0);
-        const int       pa  = rg < a.rows ? (int) ((rg * a.row_bytes + (int64_t) sb0 * D::BS) & 15) : 0;
-        const int       pb  = rg + 8 < a.rows ? (int) (((rg + 8) * a.row_bytes + (int64_t) sb0 * D::BS) & 15) : 0;
-        const uint8_t * wa  = st + rl * a.SR + pa;
-        const uint8_t * wb  = st + (rl + 8) * a.SR + pb;
-        const uint8_t * xr  = st + kTileRows * a.SR;
-        for (int kb = 0; kb < kcc; kb++) {
-            D::template sb<NG, DBG>(wa + kb * D::BS, wb + kb * D::BS, xr + kb * RB, lane, acc, dbg, rg, sb0 + kb);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    if constexpr (!DBG) {
+        if constexpr (!DBG) {
+            if (a.ksplit == 1) {
+                if (bad) continue;
 #pragma unroll
-        for (int grp = 0; grp < NG; grp++) {
+                for (int grp = 0; grp < NG; grp++) {
 #pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int     tok = 8 * grp + 2 * t + (e & 1);
-                const int64_t row = e < 2 ? rg : rg + 8;
-                if (tok < a.N && row < a.rows) a.Y[(int64_t) tok * a.ldy + row] = acc[grp][e];
+                    for (int e = 0; e < 4; e++) {
+                        const int     tok = 8 * grp + 2 * t + (e & 1);
+                        const int64_t row = e < 2 ? rg : rg + 8;
+                        if (tok < a.N && row < a.rows) a.Y[(int64_t) tok * a.ldy + row] = acc[grp][e];
+                    }
+                }
+            } else {
+                // split K: partial sums out, then the last K range of this row block reduces them in K order
+#pragma unroll
+                for (int grp = 0; grp < NG; grp++) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int     tok = 8 * grp + 2 * t + (e & 1);
+                        const int64_t row = e < 2 ? rg : rg + 8;
+                        if (tok < a.N && row < a.rows && !bad) {
+                            a.part[((int64_t) kr * a.N + tok) * a.rows + row] = acc[grp][e];
+                        }
+                    }
+                }
+                __threadfence();
+                named_bar_sync(1, kNCW * 32);
+                if (threadIdx.x == 0) last_flag = atomicAdd(&a.cnt[rb], 1) == a.ksplit - 1;
+                named_bar_sync(1, kNCW * 32);
+                if (last_flag && !bad) {
+                    __threadfence();
+#pragma unroll
+                    for (int grp = 0; grp < NG; grp++) {
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const int     tok = 8 * grp + 2 * t + (e & 1);
+                            const int64_t row = e < 2 ? rg : rg + 8;
+                            if (tok < a.N && row < a.rows) {
+                                float sum = 0.0f;
+                                for (int k = 0; k < a.ksplit; k++) {
+                                    sum += __ldcg(&a.part[((int64_t) k * a.N + tok) * a.rows + row]);
+                                }
+                                a.Y[(int64_t) tok * a.ldy + row] = sum;
+                            }
+                        }
+                    }
+                }
             }
         }
     }
@@ -733,32 +844,87 @@ int slot_stride(int need) {
 }
 
 template <class D>
-int choose_kc() {
-    return std::max(1, 20000 / (kTileRows * D::BS));
+constexpr int kc_for() {
+    // stages of ~18-23 KB of weights, with a box width that spreads rows over the shared-memory banks
+    return D::BS == 144 ? 2 : D::BS == 176 ? 2 : D::BS == 210 ? 1 : D::BS == 110 ? 3 : D::BS == 136 ? 2 : 1;
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = [] {
+        void *                          p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            p = nullptr;
+        }
+        return reinterpret_cast<EncodeTiled>(p);
+    }();
+    return fn;
 }
 
 template <class D, int NG, bool DBG>
 int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
-    constexpr int RB      = rec_bytes(D::Q80, 8 * NG);
-    const bool    aligned = (a.row_bytes % 16 == 0) && ((a.kc * D::BS) % 16 == 0);
-    const int     need    = (aligned ? 0 : 14) + a.kc * D::BS;
-    a.SR                  = slot_stride(need);
-    a.stage_bytes         = (kTileRows * a.SR + a.kc * RB + 127) / 128 * 128;
-    const size_t smem     = kBarBytes + (size_t) kStages * a.stage_bytes;
-    if (smem > 200 * 1024) return SRHPM_ERR_INVALID;
-    auto         kern     = srv_gemm_kernel<D, NG, DBG>;
-    // the shared-memory opt-in is per kernel and per device
+    constexpr int RB = rec_bytes(D::Q80, 8 * NG);
+    a.kc             = std::min(kc_for<D>(), a.nsb);
+    a.G              = 1;
+    while ((a.G * a.row_bytes) % 16 != 0) a.G *= 2;  // row sizes are even, so G <= 8
+    a.rows_main        = (a.rows / a.G) * a.G;
+    const bool aligned = a.G == 1 && D::BS % 16 == 0;
+    a.Wbox             = ((aligned ? 0 : 14) + a.kc * D::BS + 15) / 16 * 16;
+    a.LSR              = slot_stride((aligned ? 0 : 14) + a.kc * D::BS);
+    a.left_off         = kTileRows * a.Wbox;
+    a.rec_off          = (a.left_off + (a.G > 1 ? (a.G - 1) * a.LSR : 0) + 127) / 128 * 128;
+    a.stage_bytes      = (a.rec_off + a.kc * RB + 127) / 128 * 128;
+    const size_t smem  = kBarBytes + (size_t) kStages * a.stage_bytes;
+    if (smem > 200 * 1024 || a.Wbox > 1024) return SRHPM_ERR_INVALID;
+
+    CUtensorMap wmap;
+    memset(&wmap, 0, sizeof(wmap));
+    if (a.rows_main > 0) {
+        EncodeTiled enc = encode_fn();
+        if (!enc) return SRHPM_ERR_CUDA;
+        const cuuint64_t dims[2]    = { (cuuint64_t) (a.G * a.row_bytes / 4), (cuuint64_t) (a.rows / a.G) };
+        const cuuint64_t strides[1] = { (cuuint64_t) (a.G * a.row_bytes) };
+        const cuuint32_t box[2]     = { (cuuint32_t) (a.Wbox / 4), (cuuint32_t) (kTileRows / a.G) };
+        const cuuint32_t estr[2]    = { 1, 1 };
+        const CUresult   r = enc(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t *>(a.W), dims, strides,
+                                 box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) return SRHPM_ERR_INVALID;
+    }
+
+    auto kern = srv_gemm_kernel<D, NG, DBG>;
+    // the shared-memory opt-in is per kernel and per device; every configuration needs under 200 KB
     static std::atomic<unsigned> attr_done{ 0 };
     int                          dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_done.load() & (1u << (dev & 31)))) {
-        // every configuration of this kernel needs well under 200 KB (checked below); the opt-in covers them all
         const int st = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
         if (st != SRHPM_OK) return st;
         attr_done.fetch_or(1u << (dev & 31));
     }
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+    const int     slots  = std::max(1, per_sm) * ctx->num_sms;
+    const int64_t nrb    = (a.rows + kTileRows - 1) / kTileRows;
+    // split K while the row blocks alone would leave the GPU short of resident work
+    a.ksplit = 1;
+    if (!DBG && a.part) {
+        while (nrb * a.ksplit < (int64_t) ctx->num_sms * 3 / 2 && a.ksplit < 8 && a.ksplit * 2 <= a.nsb) a.ksplit++;
+    }
+    a.kr_sbs = (a.nsb + a.ksplit - 1) / a.ksplit;
+    a.units  = (int) (nrb * a.ksplit);
+    // persistent grid: balanced rounds, a multiple of the K ranges
+    const int rounds = (a.units + slots - 1) / slots;
+    int       grid   = (a.units + rounds - 1) / rounds;
+    grid             = (grid + a.ksplit - 1) / a.ksplit * a.ksplit;
+
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim            = dim3((unsigned) ((a.rows + kTileRows - 1) / kTileRows));
+    cfg.gridDim            = dim3((unsigned) grid);
     cfg.blockDim           = dim3(kThreads);
     cfg.dynamicSmemBytes   = smem;
     cfg.stream             = stream;
@@ -768,7 +934,7 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     cfg.attrs                                          = attr;
     cfg.numAttrs                                       = 1;
     ctx->launches.fetch_add(1);
-    return cuda_status(cudaLaunchKernelEx(&cfg, kern, a));
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, wmap, a));
 }
 
 template <class D>
@@ -779,71 +945,76 @@ int dispatch_ng(srhpm_ctx * ctx, const GemmArgs & a, bool dbg, cudaStream_t stre
     return dbg ? launch_gemm<D, 2, true>(ctx, a, stream) : launch_gemm<D, 2, false>(ctx, a, stream);
 }
 
-template <class D>
-int kc_for() { return choose_kc<D>(); }
-
-int kc_of(int wtype) {
-    switch (wtype) {
-        case SRHPM_TYPE_Q4_K: return kc_for<DecK45<false>>();
-        case SRHPM_TYPE_Q5_K: return kc_for<DecK45<true>>();
-        case SRHPM_TYPE_Q6_K: return kc_for<DecQ6K>();
-        case SRHPM_TYPE_Q3_K: return kc_for<DecQ3K>();
-        case SRHPM_TYPE_IQ4_XS: return kc_for<DecIQ4XS>();
-        case SRHPM_TYPE_Q8_0: return kc_for<DecQ80>();
-        default: return 1;
-    }
-}
-
 uint8_t * align256(void * p) {
     return reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(p) + 255) & ~uintptr_t(255));
 }
 
+constexpr int kMaxSplit = 8;
+
 }  // namespace
 
-size_t gemm_work_size(int wtype, int64_t K, int64_t N) {
-    const int NT = N <= 8 ? 8 : 16;
-    return (size_t) (K / QK) * rec_bytes(wtype == SRHPM_TYPE_Q8_0, NT) + 256;
+// work buffer: [activation records][split-K partials][split-K counters]
+struct WorkLayout {
+    size_t recs, part, cnt, total;
+};
+
+WorkLayout work_layout(int wtype, int64_t rows, int64_t K, int64_t N) {
+    const int  NT  = N <= 8 ? 8 : 16;
+    WorkLayout w   = {};
+    w.recs         = 0;
+    w.part         = ((size_t) (K / QK) * rec_bytes(wtype == SRHPM_TYPE_Q8_0, NT) + 255) / 256 * 256;
+    w.cnt          = w.part + ((size_t) kMaxSplit * N * rows * 4 + 255) / 256 * 256;
+    const int64_t nrb = (rows + kTileRows - 1) / kTileRows;
+    w.total        = w.cnt + (size_t) nrb * 4 + 256;  // + 256: room to align the caller's pointer
+    return w;
 }
+
+size_t gemm_work_size(int wtype, int64_t rows, int64_t K, int64_t N) { return work_layout(wtype, rows, K, N).total; }
 
 int gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
              const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
              int32_t * isum, int32_t * imin, cudaStream_t stream) {
-    if (wsize < gemm_work_size(wtype, K, N) || !wdata) return SRHPM_ERR_WORKSPACE;
+    const WorkLayout wl = work_layout(wtype, rows, K, N);
+    if (wsize < wl.total || !wdata) return SRHPM_ERR_WORKSPACE;
     const int  nsb  = (int) (K / QK);
     const int  NT   = N <= 8 ? 8 : 16;
     const bool q80  = wtype == SRHPM_TYPE_Q8_0;
-    uint8_t *  recs = align256(wdata);
-    // 1. activation records
+    uint8_t *  base = align256(wdata);
+    uint8_t *  recs = base + wl.recs;
+    int32_t *  cnt  = reinterpret_cast<int32_t *>(base + wl.cnt);
+    const int  nrb  = (int) ((rows + kTileRows - 1) / kTileRows);
+    // 1. activation records (and zeroed split-K counters)
     {
         const int64_t warps  = (int64_t) nsb * NT;
         const int     blocks = (int) ((warps + 7) / 8);
         if (q80) {
             quant_q80_kernel<false><<<blocks, 256, 0, stream>>>(X, ldx, (int) N, nsb, NT, ctx->q8_0_act_mode, recs,
-                                                                nullptr);
+                                                                nullptr, cnt, nrb);
         } else {
             quant_q8K_kernel<false><<<blocks, 256, 0, stream>>>(X, ldx, (int) N, nsb, NT, recs, nullptr, nullptr,
-                                                                nullptr, nullptr);
+                                                                nullptr, nullptr, cnt, nrb);
         }
         ctx->launches.fetch_add(1);
         const int st = cuda_status(cudaGetLastError());
         if (st != SRHPM_OK) return st;
     }
     // 2. the matmul
-    GemmArgs a    = {};
-    a.W           = W;
-    a.rows        = rows;
-    a.row_bytes   = (int64_t) row_bytes;
-    a.w_bytes     = rows * (int64_t) row_bytes;
-    a.nsb         = nsb;
-    a.kc          = std::min(kc_of(wtype), nsb);
-    a.recs        = recs;
-    a.Y           = Y;
-    a.ldy         = ldy;
-    a.N           = (int) N;
-    a.status      = ctx->d_status;
-    a.isum        = isum;
-    a.imin        = imin;
-    a.nblk        = q80 ? nsb * 8 : nsb;
+    GemmArgs a  = {};
+    a.W         = W;
+    a.rows      = rows;
+    a.row_bytes = (int64_t) row_bytes;
+    a.w_bytes   = rows * (int64_t) row_bytes;
+    a.nsb       = nsb;
+    a.recs      = recs;
+    a.part      = reinterpret_cast<float *>(base + wl.part);
+    a.cnt       = cnt;
+    a.Y         = Y;
+    a.ldy       = ldy;
+    a.N         = (int) N;
+    a.status    = ctx->d_status;
+    a.isum      = isum;
+    a.imin      = imin;
+    a.nblk      = q80 ? nsb * 8 : nsb;
     const bool dbg = isum != nullptr;
     switch (wtype) {
         case SRHPM_TYPE_Q4_K: return dispatch_ng<DecK45<false>>(ctx, a, dbg, stream);
@@ -861,7 +1032,8 @@ int quantize_q8K_dense(srhpm_ctx * ctx, const float * X, int64_t ldx, int64_t N,
     const int     nsb    = (int) (K / QK);
     const int64_t warps  = (int64_t) nsb * N;
     const int     blocks = (int) ((warps + 7) / 8);
-    quant_q8K_kernel<true><<<blocks, 256, 0, stream>>>(X, ldx, (int) N, nsb, 0, nullptr, q, d, b32, b16);
+    quant_q8K_kernel<true><<<blocks, 256, 0, stream>>>(X, ldx, (int) N, nsb, 0, nullptr, q, d, b32, b16,
+                                                       nullptr, 0);
     ctx->launches.fetch_add(1);
     return cuda_status(cudaGetLastError());
 }
@@ -872,7 +1044,7 @@ int quantize_q8_0_dense(srhpm_ctx * ctx, const float * X, int64_t ldx, int64_t N
     const int64_t warps  = (int64_t) nsb * N;
     const int     nblk   = (int) ((warps + 7) / 8);
     quant_q80_kernel<true><<<nblk, 256, 0, stream>>>(X, ldx, (int) N, nsb, 0, ctx->q8_0_act_mode, nullptr,
-                                                     reinterpret_cast<uint8_t *>(blocks));
+                                                     reinterpret_cast<uint8_t *>(blocks), nullptr, 0);
     ctx->launches.fetch_add(1);
     return cuda_status(cudaGetLastError());
 }
