@@ -35,8 +35,8 @@ constexpr int     kNCW       = 4;                 // consumer warps
 constexpr int     kThreads   = (kNCW + 1) * 32;   // + 1 producer warp
 constexpr int     kTileRows  = 16 * kNCW;         // weight rows per CTA
 constexpr int     kTokStride = 288;               // bytes per token row inside an activation record
-constexpr int     kStages    = 4;
-constexpr int     kBarBytes  = 128;               // room for the 2 * kStages mbarriers
+constexpr int     kMaxStages = 6;
+constexpr int     kBarBytes  = 128;               // room for the 2 * kMaxStages mbarriers
 
 __host__ __device__ constexpr int rec_nscales(bool q80, int NT) { return q80 ? 8 * NT : NT; }
 __host__ __device__ constexpr int rec_bytes(bool q80, int NT) {
@@ -198,11 +198,19 @@ __global__ void __launch_bounds__(256) quant_q80_kernel(const float * __restrict
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// per-type super-block decoders. sb<NG>() consumes one super-block of rows (g, g+8) of the warp's 16-row slice:
-// wa / wb point at the two rows' blocks in shared memory, xr at the super-block's activation record.
+// per-type super-block decoders
+//
+// prep(): one lane unpacks the scales of one (row, super-block) into a "scale record" in shared memory (integer block
+//         scales as int32, Q4_K/Q5_K mins replicated over the 4 bytes of an MMA operand word, f32 super-block
+//         scales), so the four lanes that share a row read them instead of each unpacking them again.
+// sb():   consumes one super-block of rows (g, g+8) of the warp's 16-row slice: wa / wb point at the two rows'
+//         blocks in shared memory, ra / rb at their scale records, xr at the super-block's activation record.
 
 __device__ __forceinline__ uint32_t lds32(const uint8_t * p) { return *reinterpret_cast<const uint32_t *>(p); }
 __device__ __forceinline__ uint2    lds64(const uint8_t * p) { return *reinterpret_cast<const uint2 *>(p); }
+__device__ __forceinline__ int4     lds128i(const uint8_t * p) { return *reinterpret_cast<const int4 *>(p); }
+__device__ __forceinline__ uint4    lds128u(const uint8_t * p) { return *reinterpret_cast<const uint4 *>(p); }
+__device__ __forceinline__ float2   ldsf2(const uint8_t * p) { return *reinterpret_cast<const float2 *>(p); }
 __device__ __forceinline__ float    ldh(const uint8_t * p) { return half_bits_to_float(lds_u16(p)); }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -212,9 +220,15 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 }
 __device__ __forceinline__ int ubyte(uint32_t w, int j) { return (int) ((w >> (8 * j)) & 0xffu); }
 __device__ __forceinline__ int sbyte(uint32_t w, int j) { return ((int32_t) (w << (24 - 8 * j))) >> 24; }
+__device__ __forceinline__ uint32_t rep_byte(uint32_t w, int j) { return prmt(w, 0, 0x1111u * (uint32_t) j); }
 
 // per-byte a - k for bytes holding 0..127 (no borrow between bytes)
 __device__ __forceinline__ uint32_t vsub_small(uint32_t a, uint32_t k) { return ((a | 0x80808080u) - k) ^ 0x80808080u; }
+
+__device__ __forceinline__ int sel4(const int4 & v, int j) { return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w; }
+__device__ __forceinline__ uint32_t sel4(const uint4 & v, int j) {
+    return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
+}
 
 struct DbgOut {
     int32_t * isum;
@@ -241,89 +255,128 @@ __device__ __forceinline__ void dbg_store(const DbgOut & o, const int (&v)[NG][4
     }
 }
 
+template <int NG>
+__device__ __forceinline__ void zero(int (&v)[NG][4]) {
+#pragma unroll
+    for (int grp = 0; grp < NG; grp++) v[grp][0] = v[grp][1] = v[grp][2] = v[grp][3] = 0;
+}
+
 // f32 update of one super-block: acc += (d_row * x_tok) * isum  [- (dmin_row * x_tok) * imin]
 template <int NG, bool MIN>
 __device__ __forceinline__ void sb_update(float (&acc)[NG][4], const int (&im)[NG][4], const int (&in)[NG][4],
                                           float dA, float dB, float mA, float mB, const float * xs, int t) {
 #pragma unroll
     for (int grp = 0; grp < NG; grp++) {
-        const float x0 = xs[8 * grp + 2 * t], x1 = xs[8 * grp + 2 * t + 1];
-        acc[grp][0] += (dA * x0) * (float) im[grp][0];
-        acc[grp][1] += (dA * x1) * (float) im[grp][1];
-        acc[grp][2] += (dB * x0) * (float) im[grp][2];
-        acc[grp][3] += (dB * x1) * (float) im[grp][3];
+        const float2 x  = *reinterpret_cast<const float2 *>(xs + 8 * grp + 2 * t);
+        acc[grp][0] += (dA * x.x) * (float) im[grp][0];
+        acc[grp][1] += (dA * x.y) * (float) im[grp][1];
+        acc[grp][2] += (dB * x.x) * (float) im[grp][2];
+        acc[grp][3] += (dB * x.y) * (float) im[grp][3];
         if constexpr (MIN) {
-            acc[grp][0] -= (mA * x0) * (float) in[grp][0];
-            acc[grp][1] -= (mA * x1) * (float) in[grp][1];
-            acc[grp][2] -= (mB * x0) * (float) in[grp][2];
-            acc[grp][3] -= (mB * x1) * (float) in[grp][3];
+            acc[grp][0] -= (mA * x.x) * (float) in[grp][0];
+            acc[grp][1] -= (mA * x.y) * (float) in[grp][1];
+            acc[grp][2] -= (mB * x.x) * (float) in[grp][2];
+            acc[grp][3] -= (mB * x.y) * (float) in[grp][3];
         }
     }
 }
 
+// im += sA * c[0..1] (row g), sB * c[2..3] (row g + 8)
+template <int NG>
+__device__ __forceinline__ void scale_acc(int (&im)[NG][4], int grp, int sA, int sB, const int (&c)[4]) {
+    im[grp][0] += sA * c[0];
+    im[grp][1] += sA * c[1];
+    im[grp][2] += sB * c[2];
+    im[grp][3] += sB * c[3];
+}
+
 // Q4_K (144 B: d, dmin, 12 bytes of 6-bit scales/mins, 128 bytes of nibbles) and Q5_K (176 B: + 32 bytes of 5th
 // bits before the nibbles). Pair p of sub-blocks (2p, 2p+1) shares 32 code bytes: low nibble = sub-block 2p, high
-// nibble = sub-block 2p+1; the 5th bit of sub-block b, weight l is bit b of qh[l].
+// nibble = sub-block 2p+1; the 5th bit of sub-block b, weight l is bit b of qh[l]. Thread t holds weights 8t..8t+7
+// of each sub-block (one 8-byte load per row and pair). Q4_K feeds the high nibbles unshifted (16 x the code) into
+// the MMA and divides that accumulator by 16 once per super-block (exact: every term is a multiple of 16).
+// Scale record: int32 sc[8] | u32 min replicated x4 [8] | f32 d, dmin.
 template <bool Q5>
 struct DecK45 {
-    static constexpr int  BS  = Q5 ? 176 : 144;
-    static constexpr bool Q80 = false;
-    static constexpr int  QS  = Q5 ? 48 : 16;
+    static constexpr int  BS   = Q5 ? 176 : 144;
+    static constexpr int  KC   = 2;
+    static constexpr int  RECB = 80;
+    static constexpr bool Q80  = false;
+    static constexpr int  QS   = Q5 ? 48 : 16;
+
+    __device__ __forceinline__ static void prep(const uint8_t * blk, uint8_t * rec) {
+        const uint32_t s0 = lds32(blk + 4), s1 = lds32(blk + 8), s2 = lds32(blk + 12);
+        const uint32_t sl = s0 & 0x3F3F3F3Fu, sh = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
+        const uint32_t ml = s1 & 0x3F3F3F3Fu, mh = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
+        int4 *  ri = reinterpret_cast<int4 *>(rec);
+        uint4 * ru = reinterpret_cast<uint4 *>(rec);
+        ri[0] = make_int4(ubyte(sl, 0), ubyte(sl, 1), ubyte(sl, 2), ubyte(sl, 3));
+        ri[1] = make_int4(ubyte(sh, 0), ubyte(sh, 1), ubyte(sh, 2), ubyte(sh, 3));
+        ru[2] = make_uint4(rep_byte(ml, 0), rep_byte(ml, 1), rep_byte(ml, 2), rep_byte(ml, 3));
+        ru[3] = make_uint4(rep_byte(mh, 0), rep_byte(mh, 1), rep_byte(mh, 2), rep_byte(mh, 3));
+        *reinterpret_cast<float2 *>(rec + 64) = make_float2(ldh(blk), ldh(blk + 2));
+    }
 
     __device__ __forceinline__ static uint32_t hbit(uint32_t qh, int b) { return ((qh >> b) << 4) & 0x10101010u; }
 
     template <int NG, bool DBG>
-    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * xr, int lane,
-                                              float (&acc)[NG][4], const DbgOut & dbg, int64_t rg, int sbi) {
+    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * ra,
+                                              const uint8_t * rb, const uint8_t * xr, int lane, float (&acc)[NG][4],
+                                              const DbgOut & dbg, int64_t rg, int sbi) {
         constexpr int NT = 8 * NG;
         const int     t = lane & 3, g = lane >> 2;
-        const uint32_t a0w = lds32(wa + 4), a1w = lds32(wa + 8), a2w = lds32(wa + 12);
-        const uint32_t b0w = lds32(wb + 4), b1w = lds32(wb + 8), b2w = lds32(wb + 12);
-        // 6-bit scales of sub-blocks 0..3 / 4..7 and mins, one byte each
-        const uint32_t scA[2] = { a0w & 0x3F3F3F3Fu, (a2w & 0x0F0F0F0Fu) | ((a0w >> 2) & 0x30303030u) };
-        const uint32_t mnA[2] = { a1w & 0x3F3F3F3Fu, ((a2w >> 4) & 0x0F0F0F0Fu) | ((a1w >> 2) & 0x30303030u) };
-        const uint32_t scB[2] = { b0w & 0x3F3F3F3Fu, (b2w & 0x0F0F0F0Fu) | ((b0w >> 2) & 0x30303030u) };
-        const uint32_t mnB[2] = { b1w & 0x3F3F3F3Fu, ((b2w >> 4) & 0x0F0F0F0Fu) | ((b1w >> 2) & 0x30303030u) };
-        uint2 ha = make_uint2(0, 0), hb = make_uint2(0, 0);
+        const int4    scA[2] = { lds128i(ra), lds128i(ra + 16) }, scB[2] = { lds128i(rb), lds128i(rb + 16) };
+        const uint4   mnA[2] = { lds128u(ra + 32), lds128u(ra + 48) }, mnB[2] = { lds128u(rb + 32), lds128u(rb + 48) };
+        uint2         ha = make_uint2(0, 0), hb = make_uint2(0, 0);
         if constexpr (Q5) {
             ha = lds64(wa + 16 + 8 * t);
             hb = lds64(wb + 16 + 8 * t);
         }
-        int im[NG][4], in[NG][4];
-#pragma unroll
-        for (int grp = 0; grp < NG; grp++) {
-#pragma unroll
-            for (int e = 0; e < 4; e++) im[grp][e] = in[grp][e] = 0;
-        }
+        int im[NG][4], ih[NG][4], in[NG][4];
+        zero<NG>(im);
+        zero<NG>(ih);
+        zero<NG>(in);
 #pragma unroll
         for (int p = 0; p < 4; p++) {
             const uint2 va = lds64(wa + QS + 32 * p + 8 * t);
             const uint2 vb = lds64(wb + QS + 32 * p + 8 * t);
 #pragma unroll
             for (int h = 0; h < 2; h++) {
-                const int b  = 2 * p + h;
-                uint32_t  a0 = (va.x >> (4 * h)) & 0x0F0F0F0Fu, a2 = (va.y >> (4 * h)) & 0x0F0F0F0Fu;
-                uint32_t  a1 = (vb.x >> (4 * h)) & 0x0F0F0F0Fu, a3 = (vb.y >> (4 * h)) & 0x0F0F0F0Fu;
+                const int b = 2 * p + h;
+                uint32_t  a0, a1, a2, a3;
                 if constexpr (Q5) {
-                    a0 |= hbit(ha.x, b);
-                    a2 |= hbit(ha.y, b);
-                    a1 |= hbit(hb.x, b);
-                    a3 |= hbit(hb.y, b);
+                    a0 = ((va.x >> (4 * h)) & 0x0F0F0F0Fu) | hbit(ha.x, b);
+                    a2 = ((va.y >> (4 * h)) & 0x0F0F0F0Fu) | hbit(ha.y, b);
+                    a1 = ((vb.x >> (4 * h)) & 0x0F0F0F0Fu) | hbit(hb.x, b);
+                    a3 = ((vb.y >> (4 * h)) & 0x0F0F0F0Fu) | hbit(hb.y, b);
+                } else {
+                    const uint32_t m = h ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+                    a0 = va.x & m;
+                    a2 = va.y & m;
+                    a1 = vb.x & m;
+                    a3 = vb.y & m;
                 }
-                const int      sA = ubyte(scA[b >> 2], b & 3), sB = ubyte(scB[b >> 2], b & 3);
-                const uint32_t mA = prmt(mnA[b >> 2], 0, 0x1111u * (b & 3));
-                const uint32_t mB = prmt(mnB[b >> 2], 0, 0x1111u * (b & 3));
+                const int      sA = sel4(scA[b >> 2], b & 3), sB = sel4(scB[b >> 2], b & 3);
+                const uint32_t mA = sel4(mnA[b >> 2], b & 3), mB = sel4(mnB[b >> 2], b & 3);
 #pragma unroll
                 for (int grp = 0; grp < NG; grp++) {
                     const uint2 x = lds64(xr + (8 * grp + g) * kTokStride + 32 * b + 8 * t);
                     int         c[4] = { 0, 0, 0, 0 };
                     mma_k32<true>(c, a0, a1, a2, a3, x.x, x.y);
-                    im[grp][0] += sA * c[0];
-                    im[grp][1] += sA * c[1];
-                    im[grp][2] += sB * c[2];
-                    im[grp][3] += sB * c[3];
+                    if (!Q5 && h) {
+                        scale_acc<NG>(ih, grp, sA, sB, c);
+                    } else {
+                        scale_acc<NG>(im, grp, sA, sB, c);
+                    }
                     mma_k32<true>(in[grp], mA, mB, mA, mB, x.x, x.y);
                 }
+            }
+        }
+        if constexpr (!Q5) {
+#pragma unroll
+            for (int grp = 0; grp < NG; grp++) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) im[grp][e] += ih[grp][e] >> 4;
             }
         }
         if constexpr (DBG) {
@@ -331,37 +384,44 @@ struct DecK45 {
             dbg_store<NG>(dbg, in, true, rg, sbi, lane);
         } else {
             const float * xs = reinterpret_cast<const float *>(xr + NT * kTokStride);
-            sb_update<NG, true>(acc, im, in, ldh(wa), ldh(wb), ldh(wa + 2), ldh(wb + 2), xs, t);
+            const float2  dA = ldsf2(ra + 64), dB = ldsf2(rb + 64);
+            sb_update<NG, true>(acc, im, in, dA.x, dB.x, dA.y, dB.y, xs, t);
         }
     }
 };
 
 // Q6_K (210 B: 128 bytes low nibbles, 64 bytes of 2-bit highs, 16 int8 scales per 16 weights, d). Weight
 // 128n + 32j + l: nibble (j >> 1) of ql[64n + 32(j & 1) + l], bits 2j of qh[32n + l], minus 32; scale 8n + 2j + l/16.
-// One k16 MMA per 16-weight group.
+// One k16 MMA per 16-weight group. Scale record: int32 sc[16] | f32 d.
 struct DecQ6K {
-    static constexpr int  BS  = 210;
-    static constexpr bool Q80 = false;
+    static constexpr int  BS   = 210;
+    static constexpr int  KC   = 1;
+    static constexpr int  RECB = 80;
+    static constexpr bool Q80  = false;
 
-    template <int NG, bool DBG>
-    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * xr, int lane,
-                                              float (&acc)[NG][4], const DbgOut & dbg, int64_t rg, int sbi) {
-        constexpr int NT = 8 * NG;
-        const int     t = lane & 3, g = lane >> 2;
-        uint32_t      SA[4], SB[4];
+    __device__ __forceinline__ static void prep(const uint8_t * blk, uint8_t * rec) {
+        int4 * ri = reinterpret_cast<int4 *>(rec);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            SA[i] = lds_u32_a2(wa + 192 + 4 * i);
-            SB[i] = lds_u32_a2(wb + 192 + 4 * i);
+            const uint32_t w = lds_u32_a2(blk + 192 + 4 * i);
+            ri[i]            = make_int4(sbyte(w, 0), sbyte(w, 1), sbyte(w, 2), sbyte(w, 3));
         }
-        int im[NG][4], in[NG][4];
-#pragma unroll
-        for (int grp = 0; grp < NG; grp++) {
-#pragma unroll
-            for (int e = 0; e < 4; e++) im[grp][e] = in[grp][e] = 0;
-        }
+        *reinterpret_cast<float *>(rec + 64) = ldh(blk + 208);
+    }
+
+    template <int NG, bool DBG>
+    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * ra,
+                                              const uint8_t * rb, const uint8_t * xr, int lane, float (&acc)[NG][4],
+                                              const DbgOut & dbg, int64_t rg, int sbi) {
+        constexpr int NT = 8 * NG;
+        const int     t = lane & 3, g = lane >> 2;
+        int           im[NG][4], in[NG][4];
+        zero<NG>(im);
+        zero<NG>(in);
 #pragma unroll
         for (int n = 0; n < 2; n++) {
+            const int4 sA4[2] = { lds128i(ra + 32 * n), lds128i(ra + 32 * n + 16) };
+            const int4 sB4[2] = { lds128i(rb + 32 * n), lds128i(rb + 32 * n + 16) };
 #pragma unroll
             for (int h = 0; h < 2; h++) {
                 const int      off = 16 * h + 4 * t;
@@ -372,22 +432,19 @@ struct DecQ6K {
                 for (int j = 0; j < 4; j++) {
                     const uint32_t la = (j & 1) ? l1a : l0a, lb = (j & 1) ? l1b : l0b;
                     const int      sh = 4 * (j >> 1);
-                    uint32_t       ua = ((la >> sh) & 0x0F0F0F0Fu) | (((qha >> (2 * j)) & 0x03030303u) << 4);
-                    uint32_t       ub = ((lb >> sh) & 0x0F0F0F0Fu) | (((qhb >> (2 * j)) & 0x03030303u) << 4);
-                    ua                = vsub_small(ua, 0x20202020u);
-                    ub                = vsub_small(ub, 0x20202020u);
-                    const int is = 8 * n + 2 * j + h;
-                    const int sA = sbyte(SA[is >> 2], is & 3), sB = sbyte(SB[is >> 2], is & 3);
+                    const uint32_t ua = vsub_small(((la >> sh) & 0x0F0F0F0Fu) | (((qha >> (2 * j)) & 0x03030303u) << 4),
+                                                   0x20202020u);
+                    const uint32_t ub = vsub_small(((lb >> sh) & 0x0F0F0F0Fu) | (((qhb >> (2 * j)) & 0x03030303u) << 4),
+                                                   0x20202020u);
+                    const int is = 2 * j + h;  // scale index within this half
+                    const int sA = sel4(sA4[is >> 2], is & 3), sB = sel4(sB4[is >> 2], is & 3);
                     const int b  = 4 * n + j;
 #pragma unroll
                     for (int grp = 0; grp < NG; grp++) {
                         const uint32_t x    = lds32(xr + (8 * grp + g) * kTokStride + 32 * b + off);
                         int            c[4] = { 0, 0, 0, 0 };
                         mma_k16<false>(c, ua, ub, x);
-                        im[grp][0] += sA * c[0];
-                        im[grp][1] += sA * c[1];
-                        im[grp][2] += sB * c[2];
-                        im[grp][3] += sB * c[3];
+                        scale_acc<NG>(im, grp, sA, sB, c);
                     }
                 }
             }
@@ -396,40 +453,42 @@ struct DecQ6K {
             dbg_store<NG>(dbg, im, false, rg, sbi, lane);
         } else {
             const float * xs = reinterpret_cast<const float *>(xr + NT * kTokStride);
-            sb_update<NG, false>(acc, im, in, ldh(wa + 208), ldh(wb + 208), 0.f, 0.f, xs, t);
+            sb_update<NG, false>(acc, im, in, *reinterpret_cast<const float *>(ra + 64),
+                                 *reinterpret_cast<const float *>(rb + 64), 0.f, 0.f, xs, t);
         }
     }
 };
 
 // Q3_K (110 B: 32 bytes of high bits, 64 bytes of 2-bit codes, 12 bytes of 6-bit scales, d). Weight 128n + 32j + l:
 // bits 2j of qs[32n + l], high bit (4n + j) of hmask[l] (set = +0, clear = -4); scale index 8n + 2j + l/16, minus 32.
+// Scale record: int32 sc[16] | f32 d.
 struct DecQ3K {
-    static constexpr int  BS  = 110;
-    static constexpr bool Q80 = false;
+    static constexpr int  BS   = 110;
+    static constexpr int  KC   = 3;
+    static constexpr int  RECB = 80;
+    static constexpr bool Q80  = false;
+
+    __device__ __forceinline__ static void prep(const uint8_t * blk, uint8_t * rec) {
+        const uint32_t s0 = lds_u32_a2(blk + 96), s1 = lds_u32_a2(blk + 100), s2 = lds_u32_a2(blk + 104);
+        const uint32_t lo[4] = { s0 & 0x0F0F0F0Fu, s1 & 0x0F0F0F0Fu, (s0 >> 4) & 0x0F0F0F0Fu, (s1 >> 4) & 0x0F0F0F0Fu };
+        int4 *         ri    = reinterpret_cast<int4 *>(rec);
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t w = lo[i] | (((s2 >> (2 * i)) & 0x03030303u) << 4);
+            ri[i] = make_int4(ubyte(w, 0) - 32, ubyte(w, 1) - 32, ubyte(w, 2) - 32, ubyte(w, 3) - 32);
+        }
+        *reinterpret_cast<float *>(rec + 64) = ldh(blk + 108);
+    }
 
     template <int NG, bool DBG>
-    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * xr, int lane,
-                                              float (&acc)[NG][4], const DbgOut & dbg, int64_t rg, int sbi) {
+    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * ra,
+                                              const uint8_t * rb, const uint8_t * xr, int lane, float (&acc)[NG][4],
+                                              const DbgOut & dbg, int64_t rg, int sbi) {
         constexpr int NT = 8 * NG;
         const int     t = lane & 3, g = lane >> 2;
-        uint32_t      SA[4], SB[4];
-        {
-            const uint32_t s0 = lds_u32_a2(wa + 96), s1 = lds_u32_a2(wa + 100), s2 = lds_u32_a2(wa + 104);
-            const uint32_t r0 = lds_u32_a2(wb + 96), r1 = lds_u32_a2(wb + 100), r2 = lds_u32_a2(wb + 104);
-            const uint32_t loA[4] = { s0 & 0x0F0F0F0Fu, s1 & 0x0F0F0F0Fu, (s0 >> 4) & 0x0F0F0F0Fu, (s1 >> 4) & 0x0F0F0F0Fu };
-            const uint32_t loB[4] = { r0 & 0x0F0F0F0Fu, r1 & 0x0F0F0F0Fu, (r0 >> 4) & 0x0F0F0F0Fu, (r1 >> 4) & 0x0F0F0F0Fu };
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                SA[i] = vsub_small(loA[i] | (((s2 >> (2 * i)) & 0x03030303u) << 4), 0x20202020u);
-                SB[i] = vsub_small(loB[i] | (((r2 >> (2 * i)) & 0x03030303u) << 4), 0x20202020u);
-            }
-        }
-        int im[NG][4], in[NG][4];
-#pragma unroll
-        for (int grp = 0; grp < NG; grp++) {
-#pragma unroll
-            for (int e = 0; e < 4; e++) im[grp][e] = in[grp][e] = 0;
-        }
+        int           im[NG][4], in[NG][4];
+        zero<NG>(im);
+        zero<NG>(in);
 #pragma unroll
         for (int h = 0; h < 2; h++) {
             const int      off = 16 * h + 4 * t;
@@ -437,6 +496,8 @@ struct DecQ3K {
 #pragma unroll
             for (int n = 0; n < 2; n++) {
                 const uint32_t qa = lds_u32_a2(wa + 32 + 32 * n + off), qb = lds_u32_a2(wb + 32 + 32 * n + off);
+                const int4     sA4[2] = { lds128i(ra + 32 * n), lds128i(ra + 32 * n + 16) };
+                const int4     sB4[2] = { lds128i(rb + 32 * n), lds128i(rb + 32 * n + 16) };
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     const int      hs = 4 * n + j;
@@ -444,18 +505,15 @@ struct DecQ3K {
                                                    0x04040404u);
                     const uint32_t ub = vsub_small(((qb >> (2 * j)) & 0x03030303u) | (((hmb >> hs) & 0x01010101u) << 2),
                                                    0x04040404u);
-                    const int is = 8 * n + 2 * j + h;
-                    const int sA = sbyte(SA[is >> 2], is & 3), sB = sbyte(SB[is >> 2], is & 3);
+                    const int is = 2 * j + h;
+                    const int sA = sel4(sA4[is >> 2], is & 3), sB = sel4(sB4[is >> 2], is & 3);
                     const int b  = 4 * n + j;
 #pragma unroll
                     for (int grp = 0; grp < NG; grp++) {
                         const uint32_t x    = lds32(xr + (8 * grp + g) * kTokStride + 32 * b + off);
                         int            c[4] = { 0, 0, 0, 0 };
                         mma_k16<false>(c, ua, ub, x);
-                        im[grp][0] += sA * c[0];
-                        im[grp][1] += sA * c[1];
-                        im[grp][2] += sB * c[2];
-                        im[grp][3] += sB * c[3];
+                        scale_acc<NG>(im, grp, sA, sB, c);
                     }
                 }
             }
@@ -464,16 +522,20 @@ struct DecQ3K {
             dbg_store<NG>(dbg, im, false, rg, sbi, lane);
         } else {
             const float * xs = reinterpret_cast<const float *>(xr + NT * kTokStride);
-            sb_update<NG, false>(acc, im, in, ldh(wa + 108), ldh(wb + 108), 0.f, 0.f, xs, t);
+            sb_update<NG, false>(acc, im, in, *reinterpret_cast<const float *>(ra + 64),
+                                 *reinterpret_cast<const float *>(rb + 64), 0.f, 0.f, xs, t);
         }
     }
 };
 
 // IQ4_XS (136 B: d, 2 high bits of 8 scales, 4 bits of 8 scales, 128 bytes of code-book indices). Sub-block b,
 // weight l: index = nibble (l >= 16) of qs[16b + (l & 15)], value kvalues_iq4nl[index]; scale = 6 bits - 32.
+// Scale record: int32 sc[8] | f32 d.
 struct DecIQ4XS {
-    static constexpr int  BS  = 136;
-    static constexpr bool Q80 = false;
+    static constexpr int  BS   = 136;
+    static constexpr int  KC   = 2;
+    static constexpr int  RECB = 48;
+    static constexpr bool Q80  = false;
 
     // the 16-entry code book as four words of int8 lanes (GGUF constant kvalues_iq4nl)
     static constexpr uint32_t T0 = 0xBFAD9881u, T1 = 0xF6EADDCFu, T2 = 0x26190D01u, T3 = 0x71594535u;
@@ -482,29 +544,36 @@ struct DecIQ4XS {
     __device__ __forceinline__ static void lookup(uint32_t v, uint32_t & lo, uint32_t & hi) {
         const uint32_t v7  = v & 0x77777777u;
         const uint32_t sel = 0x32103210u | ((v & 0x88888888u) >> 1);  // bit 2 set: take the upper table's byte
-        const uint32_t r0  = prmt(prmt(T0, T1, v7), prmt(T2, T3, v7), sel & 0xffffu);
+        const uint32_t r0  = prmt(prmt(T0, T1, v7), prmt(T2, T3, v7), sel);
         const uint32_t r1  = prmt(prmt(T0, T1, v7 >> 16), prmt(T2, T3, v7 >> 16), sel >> 16);
         lo                 = prmt(r0, r1, 0x6420u);
         hi                 = prmt(r0, r1, 0x7531u);
     }
 
+    __device__ __forceinline__ static void prep(const uint8_t * blk, uint8_t * rec) {
+        const uint32_t H = lds_u16(blk + 2), L = lds32(blk + 4);
+        int4 *         ri = reinterpret_cast<int4 *>(rec);
+        int            v[8];
+#pragma unroll
+        for (int b = 0; b < 8; b++) v[b] = (int) (((L >> (4 * b)) & 0xFu) | (((H >> (2 * b)) & 3u) << 4)) - 32;
+        ri[0]                                = make_int4(v[0], v[1], v[2], v[3]);
+        ri[1]                                = make_int4(v[4], v[5], v[6], v[7]);
+        *reinterpret_cast<float *>(rec + 32) = ldh(blk);
+    }
+
     template <int NG, bool DBG>
-    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * xr, int lane,
-                                              float (&acc)[NG][4], const DbgOut & dbg, int64_t rg, int sbi) {
-        constexpr int  NT = 8 * NG;
-        const int      t = lane & 3, g = lane >> 2;
-        const uint32_t HA = lds_u16(wa + 2), HB = lds_u16(wb + 2);
-        const uint32_t LA = lds32(wa + 4), LB = lds32(wb + 4);
-        int            im[NG][4], in[NG][4];
-#pragma unroll
-        for (int grp = 0; grp < NG; grp++) {
-#pragma unroll
-            for (int e = 0; e < 4; e++) im[grp][e] = in[grp][e] = 0;
-        }
+    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * ra,
+                                              const uint8_t * rb, const uint8_t * xr, int lane, float (&acc)[NG][4],
+                                              const DbgOut & dbg, int64_t rg, int sbi) {
+        constexpr int NT = 8 * NG;
+        const int     t = lane & 3, g = lane >> 2;
+        const int4    sA4[2] = { lds128i(ra), lds128i(ra + 16) }, sB4[2] = { lds128i(rb), lds128i(rb + 16) };
+        int           im[NG][4], in[NG][4];
+        zero<NG>(im);
+        zero<NG>(in);
 #pragma unroll
         for (int b = 0; b < 8; b++) {
-            const int sA = (int) (((LA >> (4 * b)) & 0xFu) | (((HA >> (2 * b)) & 3u) << 4)) - 32;
-            const int sB = (int) (((LB >> (4 * b)) & 0xFu) | (((HB >> (2 * b)) & 3u) << 4)) - 32;
+            const int sA = sel4(sA4[b >> 2], b & 3), sB = sel4(sB4[b >> 2], b & 3);
             uint32_t  a0, a2, a1, a3;
             lookup(lds32(wa + 8 + 16 * b + 4 * t), a0, a2);
             lookup(lds32(wb + 8 + 16 * b + 4 * t), a1, a3);
@@ -513,33 +582,42 @@ struct DecIQ4XS {
                 const uint8_t * xp   = xr + (8 * grp + g) * kTokStride + 32 * b + 4 * t;
                 int             c[4] = { 0, 0, 0, 0 };
                 mma_k32<false>(c, a0, a1, a2, a3, lds32(xp), lds32(xp + 16));
-                im[grp][0] += sA * c[0];
-                im[grp][1] += sA * c[1];
-                im[grp][2] += sB * c[2];
-                im[grp][3] += sB * c[3];
+                scale_acc<NG>(im, grp, sA, sB, c);
             }
         }
         if constexpr (DBG) {
             dbg_store<NG>(dbg, im, false, rg, sbi, lane);
         } else {
             const float * xs = reinterpret_cast<const float *>(xr + NT * kTokStride);
-            sb_update<NG, false>(acc, im, in, ldh(wa), ldh(wb), 0.f, 0.f, xs, t);
+            sb_update<NG, false>(acc, im, in, *reinterpret_cast<const float *>(ra + 32),
+                                 *reinterpret_cast<const float *>(rb + 32), 0.f, 0.f, xs, t);
         }
     }
 };
 
 // Q8_0 (34 B per 32 weights: f16 d, 32 int8). A "super-block" here is 8 consecutive blocks (272 bytes); each block
-// has its own weight and activation scale, so the f32 update happens per block.
+// has its own weight and activation scale, so the f32 update happens per block. Scale record: f32 d[8].
 struct DecQ80 {
-    static constexpr int  BS  = 272;
-    static constexpr bool Q80 = true;
+    static constexpr int  BS   = 272;
+    static constexpr int  KC   = 1;
+    static constexpr int  RECB = 32;
+    static constexpr bool Q80  = true;
+
+    __device__ __forceinline__ static void prep(const uint8_t * blk, uint8_t * rec) {
+        float4 * rf = reinterpret_cast<float4 *>(rec);
+        rf[0]       = make_float4(ldh(blk), ldh(blk + 34), ldh(blk + 68), ldh(blk + 102));
+        rf[1]       = make_float4(ldh(blk + 136), ldh(blk + 170), ldh(blk + 204), ldh(blk + 238));
+    }
 
     template <int NG, bool DBG>
-    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * xr, int lane,
-                                              float (&acc)[NG][4], const DbgOut & dbg, int64_t rg, int sbi) {
+    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * ra,
+                                              const uint8_t * rb, const uint8_t * xr, int lane, float (&acc)[NG][4],
+                                              const DbgOut & dbg, int64_t rg, int sbi) {
         constexpr int NT = 8 * NG;
         const int     t = lane & 3, g = lane >> 2;
         const float * xsb = reinterpret_cast<const float *>(xr + NT * kTokStride);
+        const float4  dA4[2] = { *reinterpret_cast<const float4 *>(ra), *reinterpret_cast<const float4 *>(ra + 16) };
+        const float4  dB4[2] = { *reinterpret_cast<const float4 *>(rb), *reinterpret_cast<const float4 *>(rb + 16) };
 #pragma unroll
         for (int i = 0; i < 8; i++) {
             const uint8_t * ba = wa + 34 * i;
@@ -556,15 +634,18 @@ struct DecQ80 {
             if constexpr (DBG) {
                 dbg_store<NG>(dbg, c, false, rg, 8 * sbi + i, lane);
             } else {
-                const float   dA = ldh(ba), dB = ldh(bb);
-                const float * xs = xsb + i * NT;
+                const float4 & qa = dA4[i >> 2];
+                const float4 & qb = dB4[i >> 2];
+                const float    dA = (i & 3) == 0 ? qa.x : (i & 3) == 1 ? qa.y : (i & 3) == 2 ? qa.z : qa.w;
+                const float    dB = (i & 3) == 0 ? qb.x : (i & 3) == 1 ? qb.y : (i & 3) == 2 ? qb.z : qb.w;
+                const float *  xs = xsb + i * NT;
 #pragma unroll
                 for (int grp = 0; grp < NG; grp++) {
-                    const float x0 = xs[8 * grp + 2 * t], x1 = xs[8 * grp + 2 * t + 1];
-                    acc[grp][0] += (dA * x0) * (float) c[grp][0];
-                    acc[grp][1] += (dA * x1) * (float) c[grp][1];
-                    acc[grp][2] += (dB * x0) * (float) c[grp][2];
-                    acc[grp][3] += (dB * x1) * (float) c[grp][3];
+                    const float2 x = *reinterpret_cast<const float2 *>(xs + 8 * grp + 2 * t);
+                    acc[grp][0] += (dA * x.x) * (float) c[grp][0];
+                    acc[grp][1] += (dA * x.y) * (float) c[grp][1];
+                    acc[grp][2] += (dB * x.x) * (float) c[grp][2];
+                    acc[grp][3] += (dB * x.y) * (float) c[grp][3];
                 }
             }
         }
@@ -589,7 +670,10 @@ struct GemmArgs {
     int             nsb;         // 256-column super-blocks per row
     int             kc;          // super-blocks per stage
     int             G;           // weight rows per tensor-map row (G * row_bytes is a multiple of 16)
+    int             gshift;      // log2(G)
+    int             rbm16;       // row_bytes mod 16
     int             Wbox;        // bytes per row segment in a stage (TMA box width)
+    int             S;           // stages in the ring
     int             ksplit;      // K ranges
     int             kr_sbs;      // super-blocks per K range (the last one may be shorter)
     int             units;
@@ -597,6 +681,7 @@ struct GemmArgs {
     int             left_off;    // leftover-row slots (rows >= rows_main) inside a stage
     int             LSR;         // leftover slot stride
     int             rec_off;     // activation records inside a stage
+    int             scr_off;     // per-warp scale-record scratch (after the stages)
     const uint8_t * recs;
     float *         part;        // split-K partial sums [ksplit][N][rows]
     int32_t *       cnt;         // split-K arrival counters, one per row block (zeroed by the quantizer kernel)
@@ -655,10 +740,10 @@ __device__ __forceinline__ void produce_stage(const GemmArgs & a, const CUtensor
     }
     if (lane == 0) {
         if (tma) {
-            const int rpb = kTileRows / a.G;  // tensor-map rows per box
+            const int rpb = kTileRows >> a.gshift;  // tensor-map rows per box
             for (int j = 0; j < a.G; j++) {
                 const int64_t xb = ((int64_t) j * a.row_bytes + (int64_t) sb0 * D::BS) & ~int64_t(15);
-                tma_load_2d(st + j * rpb * a.Wbox, wmap, (int) (xb >> 2), (int) (row0 / a.G), bar);
+                tma_load_2d(st + j * rpb * a.Wbox, wmap, (int) (xb >> 2), (int) (row0 >> a.gshift), bar);
             }
         }
         if (!defer_records) bulk_g2s(st + a.rec_off, a.recs + (size_t) sb0 * RB, (uint32_t) (kcc * RB), bar);
@@ -673,14 +758,14 @@ __device__ __forceinline__ void producer(const GemmArgs & a, const CUtensorMap *
     const int     sbA = kr * a.kr_sbs, sbB = min(a.nsb, sbA + a.kr_sbs);
     const int     nck = (sbB - sbA + a.kc - 1) / a.kc;
     if (lane == 0 && a.rows_main > 0) prefetch_tmap(wmap);
-    int  n = 0;  // stages issued
-    bool ok = true;
+    int  n = 0, s = 0;  // stages issued; ring slot of the next one
+    int  ph     = 0;    // parity of the slot's next empty-barrier phase to wait for
+    bool ok     = true;
     bool waited = false;
     for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
         const int64_t row0 = (int64_t) (u / a.ksplit) * kTileRows;
-        for (int c = 0; c < nck; c++, n++) {
-            const int s = n % kStages;
-            if (n >= kStages && !mbar_wait(&empty[s], ((n / kStages) - 1) & 1)) {
+        for (int c = 0; c < nck; c++) {
+            if (n >= a.S && !mbar_wait(&empty[s], ph)) {
                 ok = false;
                 break;
             }
@@ -689,15 +774,20 @@ __device__ __forceinline__ void producer(const GemmArgs & a, const CUtensorMap *
             // launch); their records follow once the quantizer grid has finished
             const bool pre = !waited;
             produce_stage<D, NG>(a, wmap, stage0 + (size_t) s * a.stage_bytes, &full[s], row0, sb0, kcc, lane, pre);
-            if (pre && (n + 1 == kStages || (c + 1 == nck && u + (int) gridDim.x >= a.units))) {
+            n++;
+            if (++s == a.S) {
+                s = 0;
+                if (n > a.S) ph ^= 1;
+            }
+            if (n == a.S) ph = 0;
+            if (pre && (n == a.S || (c + 1 == nck && u + (int) gridDim.x >= a.units))) {
                 pdl_wait();
                 waited = true;
                 if (lane == 0) {
-                    for (int m = 0; m <= n; m++) {  // the records of every stage issued so far
-                        const int cm = m % nck;  // all prologue stages belong to the first unit(s)
-                        const int sbm = sbA + cm * a.kc, kcm = min(a.kc, sbB - sbm);
-                        bulk_g2s(stage0 + (size_t) (m % kStages) * a.stage_bytes + a.rec_off,
-                                 a.recs + (size_t) sbm * RB, (uint32_t) (kcm * RB), &full[m % kStages]);
+                    for (int m = 0; m < n; m++) {  // the records of the stages issued so far (slot m, first use)
+                        const int sbm = sbA + (m % nck) * a.kc, kcm = min(a.kc, sbB - sbm);
+                        bulk_g2s(stage0 + (size_t) m * a.stage_bytes + a.rec_off, a.recs + (size_t) sbm * RB,
+                                 (uint32_t) (kcm * RB), &full[m]);
                     }
                 }
             }
@@ -705,8 +795,8 @@ __device__ __forceinline__ void producer(const GemmArgs & a, const CUtensorMap *
     }
     if (!waited) pdl_wait();
     // drain: every copy this warp issued has landed before the CTA may exit
-    for (int m = max(0, n - kStages); m < n; m++) {
-        if (!mbar_wait(&full[m % kStages], (m / kStages) & 1)) ok = false;
+    for (int m = max(0, n - a.S); m < n; m++) {
+        if (!mbar_wait(&full[m % a.S], (m / a.S) & 1)) ok = false;
     }
     if (!ok && lane == 0) atomicExch(a.status, kErrWaitEmpty);
 }
@@ -717,9 +807,9 @@ __device__ __forceinline__ const uint8_t * row_ptr(const GemmArgs & a, const uin
                                                    int sb0) {
     const int64_t R = row0 + r;
     if (R < a.rows_main) {
-        const int j = r % a.G, q = r / a.G;
-        const int ph = (int) (((int64_t) j * a.row_bytes + (int64_t) sb0 * D::BS) & 15);
-        return st + (j * (kTileRows / a.G) + q) * a.Wbox + ph;
+        const int j = r & (a.G - 1), q = r >> a.gshift;
+        const int ph = (j * a.rbm16 + sb0 * (D::BS & 15)) & 15;
+        return st + (j * (kTileRows >> a.gshift) + q) * a.Wbox + ph;
     }
     if (R < a.rows) {
         const int ph = (int) ((R * a.row_bytes + (int64_t) sb0 * D::BS) & 15);
@@ -733,11 +823,11 @@ __global__ void __launch_bounds__(kThreads) srv_gemm_kernel(const __grid_constan
                                                             const GemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t * full   = reinterpret_cast<uint64_t *>(smem);
-    uint64_t * empty  = full + kStages;
+    uint64_t * empty  = full + kMaxStages;
     uint8_t *  stage0 = smem + kBarBytes;
     const int  warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; s++) {
+        for (int s = 0; s < a.S; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kNCW);
         }
@@ -756,31 +846,47 @@ __global__ void __launch_bounds__(kThreads) srv_gemm_kernel(const __grid_constan
     const int      sbA = kr * a.kr_sbs, sbB = min(a.nsb, sbA + a.kr_sbs);
     const int      nck = (sbB - sbA + a.kc - 1) / a.kc;
     const DbgOut   dbg = { a.isum, a.imin, a.rows, a.N, a.nblk };
+    uint8_t *      scr = smem + a.scr_off + warp * (D::KC * 16 * D::RECB);  // this warp's scale records
     __shared__ int last_flag;
-    int            n   = 0;
+    int            s = 0, ph = 0;
     bool           bad = false;  // a wait ran out: skip further waits and work, keep meeting the barriers
     for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
         const int64_t rb = u / a.ksplit, row0 = rb * kTileRows, rg = row0 + rl;
         float         acc[NG][4];
 #pragma unroll
         for (int grp = 0; grp < NG; grp++) acc[grp][0] = acc[grp][1] = acc[grp][2] = acc[grp][3] = 0.0f;
-        for (int c = 0; c < nck; c++, n++) {
-            const int s = n % kStages;
-            if (!bad && !mbar_wait(&full[s], (n / kStages) & 1)) {
+        for (int c = 0; c < nck; c++) {
+            const int slot = s, par = ph;
+            if (++s == a.S) {
+                s = 0;
+                ph ^= 1;
+            }
+            if (!bad && !mbar_wait(&full[slot], par)) {
                 if (lane == 0) atomicExch(a.status, kErrWaitFull);
                 bad = true;
             }
             if (bad) continue;
-            const uint8_t * st  = stage0 + (size_t) s * a.stage_bytes;
+            const uint8_t * st  = stage0 + (size_t) slot * a.stage_bytes;
             const int       sb0 = sbA + c * a.kc, kcc = min(a.kc, sbB - sb0);
-            const uint8_t * wa  = row_ptr<D>(a, st, row0, rl, sb0);
-            const uint8_t * wb  = row_ptr<D>(a, st, row0, rl + 8, sb0);
-            const uint8_t * xr  = st + a.rec_off;
-            for (int kb = 0; kb < kcc; kb++) {
-                D::template sb<NG, DBG>(wa + kb * D::BS, wb + kb * D::BS, xr + kb * RB, lane, acc, dbg, rg, sb0 + kb);
+            // scale records of this warp's 16 rows x kcc super-blocks, one (row, super-block) per lane
+            for (int it = lane; it < 16 * kcc; it += 32) {
+                const int kb = it >> 4, r = it & 15;
+                D::prep(row_ptr<D>(a, st, row0, warp * 16 + r, sb0) + kb * D::BS, scr + it * D::RECB);
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
+            const uint8_t * wa = row_ptr<D>(a, st, row0, rl, sb0);
+            const uint8_t * wb = row_ptr<D>(a, st, row0, rl + 8, sb0);
+            const uint8_t * xr = st + a.rec_off;
+#pragma unroll
+            for (int kb = 0; kb < D::KC; kb++) {
+                if (kb < kcc) {
+                    D::template sb<NG, DBG>(wa + kb * D::BS, wb + kb * D::BS, scr + (kb * 16 + g) * D::RECB,
+                                            scr + (kb * 16 + g + 8) * D::RECB, xr + kb * RB, lane, acc, dbg, rg,
+                                            sb0 + kb);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[slot]);
         }
         if constexpr (!DBG) {
             if (a.ksplit == 1) {
@@ -829,6 +935,7 @@ __global__ void __launch_bounds__(kThreads) srv_gemm_kernel(const __grid_constan
                         }
                     }
                 }
+                named_bar_sync(1, kNCW * 32);  // last_flag is rewritten by the next unit
             }
         }
     }
@@ -841,12 +948,6 @@ int slot_stride(int need) {
     int s = (need + 15) / 16 * 16;
     while (s % 128 != 32 && s % 128 != 96) s += 16;
     return s;
-}
-
-template <class D>
-constexpr int kc_for() {
-    // stages of ~18-23 KB of weights, with a box width that spreads rows over the shared-memory banks
-    return D::BS == 144 ? 2 : D::BS == 176 ? 2 : D::BS == 210 ? 1 : D::BS == 110 ? 3 : D::BS == 136 ? 2 : 1;
 }
 
 using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -869,9 +970,14 @@ EncodeTiled encode_fn() {
 template <class D, int NG, bool DBG>
 int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     constexpr int RB = rec_bytes(D::Q80, 8 * NG);
-    a.kc             = std::min(kc_for<D>(), a.nsb);
+    a.kc             = std::min(D::KC, a.nsb);
     a.G              = 1;
-    while ((a.G * a.row_bytes) % 16 != 0) a.G *= 2;  // row sizes are even, so G <= 8
+    a.gshift         = 0;
+    while ((a.G * a.row_bytes) % 16 != 0) {  // row sizes are even, so G <= 8
+        a.G *= 2;
+        a.gshift++;
+    }
+    a.rbm16            = (int) (a.row_bytes & 15);
     a.rows_main        = (a.rows / a.G) * a.G;
     const bool aligned = a.G == 1 && D::BS % 16 == 0;
     a.Wbox             = ((aligned ? 0 : 14) + a.kc * D::BS + 15) / 16 * 16;
@@ -879,7 +985,12 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     a.left_off         = kTileRows * a.Wbox;
     a.rec_off          = (a.left_off + (a.G > 1 ? (a.G - 1) * a.LSR : 0) + 127) / 128 * 128;
     a.stage_bytes      = (a.rec_off + a.kc * RB + 127) / 128 * 128;
-    const size_t smem  = kBarBytes + (size_t) kStages * a.stage_bytes;
+    const int scr      = kNCW * D::KC * 16 * D::RECB;
+    // as many stages (4..6) as keep two CTAs per SM; fewer when a stage is large
+    a.S = kMaxStages;
+    while (a.S > 3 && kBarBytes + (size_t) a.S * a.stage_bytes + scr > 110 * 1024) a.S--;
+    a.scr_off         = kBarBytes + a.S * a.stage_bytes;
+    const size_t smem = (size_t) a.scr_off + scr;
     if (smem > 200 * 1024 || a.Wbox > 1024) return SRHPM_ERR_INVALID;
 
     CUtensorMap wmap;
