@@ -330,7 +330,9 @@ def run_gpu(args):
 
     # the timed step is replayed from a CUDA graph (no host launch gaps between the 2 kernels of each product);
     # with several ranks the NCCL all-gathers run eagerly
-    op_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in ops]
+    # "external" events stay real timing events when recorded inside a captured graph
+    op_ev = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
+             for _ in ops]
     graph = None
     if world == 1 and not args.eager:
         graph = torch.cuda.CUDAGraph()

@@ -819,7 +819,7 @@ __device__ __forceinline__ const uint8_t * row_ptr(const GemmArgs & a, const uin
 }
 
 template <class D, int NG, bool DBG>
-__global__ void __launch_bounds__(kThreads) srv_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
+__global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
                                                             const GemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t * full   = reinterpret_cast<uint64_t *>(smem);
