@@ -31,9 +31,10 @@ namespace srhpm {
 namespace {
 
 constexpr int     QK         = 256;
-constexpr int     kNCW       = 4;                 // consumer warps
+constexpr int     kSlices    = 4;                 // 16-row slices of a 64-row tile
+constexpr int     kNCW       = 2 * kSlices;       // consumer warps: two per slice, splitting its super-blocks
 constexpr int     kThreads   = (kNCW + 1) * 32;   // + 1 producer warp
-constexpr int     kTileRows  = 16 * kNCW;         // weight rows per CTA
+constexpr int     kTileRows  = 16 * kSlices;      // weight rows per CTA tile
 constexpr int     kTokStride = 288;               // bytes per token row inside an activation record
 constexpr int     kMaxStages = 6;
 constexpr int     kBarBytes  = 128;               // room for the 2 * kMaxStages mbarriers
@@ -75,7 +76,10 @@ __global__ void __launch_bounds__(256) quant_q8K_kernel(const float * __restrict
                                                          float * __restrict__ d, int16_t * __restrict__ b32,
                                                          int16_t * __restrict__ b16, int32_t * __restrict__ cnt,
                                                          int ncnt) {
+    // launched early behind the previous call's GEMM: let the next GEMM get resident, then wait for the previous
+    // grid (it may still read the records and counters this kernel rewrites, or write the X it reads)
     pdl_launch_dependents();
+    pdl_wait();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncnt; i += gridDim.x * blockDim.x) cnt[i] = 0;
     const int     lane = threadIdx.x & 31;
     const int     TT   = DENSE ? N : NT;
@@ -146,7 +150,10 @@ __global__ void __launch_bounds__(256) quant_q80_kernel(const float * __restrict
                                                          int NT, int mode, uint8_t * __restrict__ recs,
                                                          uint8_t * __restrict__ blocks, int32_t * __restrict__ cnt,
                                                          int ncnt) {
+    // launched early behind the previous call's GEMM: let the next GEMM get resident, then wait for the previous
+    // grid (it may still read the records and counters this kernel rewrites, or write the X it reads)
     pdl_launch_dependents();
+    pdl_wait();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncnt; i += gridDim.x * blockDim.x) cnt[i] = 0;
     const int     lane = threadIdx.x & 31;
     const int     TT   = DENSE ? N : NT;
@@ -682,6 +689,7 @@ struct GemmArgs {
     int             LSR;         // leftover slot stride
     int             rec_off;     // activation records inside a stage
     int             scr_off;     // per-warp scale-record scratch (after the stages)
+    int             red_off;     // pair-reduction buffer (after the scratch)
     const uint8_t * recs;
     float *         part;        // split-K partial sums [ksplit][N][rows]
     int32_t *       cnt;         // split-K arrival counters, one per row block (zeroed by the quantizer kernel)
@@ -838,15 +846,18 @@ __global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_cons
         producer<D, NG>(a, &wmap, full, empty, stage0, lane);
         return;
     }
+    pdl_launch_dependents();  // the next call's quantizer may start; it waits for this grid before touching data
     pdl_wait();  // the split-K counters and partials are written below; the quantizer grid zeroes the counters
-    constexpr int  RB  = rec_bytes(D::Q80, 8 * NG);
+    constexpr int  RB   = rec_bytes(D::Q80, 8 * NG);
     const int      g = lane >> 2, t = lane & 3;
-    const int      rl  = warp * 16 + g;
-    const int      kr  = blockIdx.x % a.ksplit;
-    const int      sbA = kr * a.kr_sbs, sbB = min(a.nsb, sbA + a.kr_sbs);
-    const int      nck = (sbB - sbA + a.kc - 1) / a.kc;
-    const DbgOut   dbg = { a.isum, a.imin, a.rows, a.N, a.nblk };
-    uint8_t *      scr = smem + a.scr_off + warp * (D::KC * 16 * D::RECB);  // this warp's scale records
+    const int      slice = warp & (kSlices - 1), half = warp / kSlices;
+    const int      rl   = slice * 16 + g;
+    const int      kr   = blockIdx.x % a.ksplit;
+    const int      sbA  = kr * a.kr_sbs, sbB = min(a.nsb, sbA + a.kr_sbs);
+    const int      nck  = (sbB - sbA + a.kc - 1) / a.kc;
+    const DbgOut   dbg  = { a.isum, a.imin, a.rows, a.N, a.nblk };
+    uint8_t *      scr  = smem + a.scr_off + warp * (D::KC * 16 * D::RECB);  // this warp's scale records
+    float *        red  = reinterpret_cast<float *>(smem + a.red_off);        // pair reduction, [slice][lane][NG*4]
     __shared__ int last_flag;
     int            s = 0, ph = 0;
     bool           bad = false;  // a wait ran out: skip further waits and work, keep meeting the barriers
@@ -868,10 +879,12 @@ __global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_cons
             if (bad) continue;
             const uint8_t * st  = stage0 + (size_t) slot * a.stage_bytes;
             const int       sb0 = sbA + c * a.kc, kcc = min(a.kc, sbB - sb0);
-            // scale records of this warp's 16 rows x kcc super-blocks, one (row, super-block) per lane
+            // the two warps of a slice take alternate super-blocks of the unit: item c*KC + kb goes to half (i & 1)
+            // scale records of this warp's items, one (row, super-block) per lane
             for (int it = lane; it < 16 * kcc; it += 32) {
                 const int kb = it >> 4, r = it & 15;
-                D::prep(row_ptr<D>(a, st, row0, warp * 16 + r, sb0) + kb * D::BS, scr + it * D::RECB);
+                if (((c * D::KC + kb) & 1) != half) continue;
+                D::prep(row_ptr<D>(a, st, row0, slice * 16 + r, sb0) + kb * D::BS, scr + it * D::RECB);
             }
             __syncwarp();
             const uint8_t * wa = row_ptr<D>(a, st, row0, rl, sb0);
@@ -879,7 +892,7 @@ __global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_cons
             const uint8_t * xr = st + a.rec_off;
 #pragma unroll
             for (int kb = 0; kb < D::KC; kb++) {
-                if (kb < kcc) {
+                if (kb < kcc && ((c * D::KC + kb) & 1) == half) {
                     D::template sb<NG, DBG>(wa + kb * D::BS, wb + kb * D::BS, scr + (kb * 16 + g) * D::RECB,
                                             scr + (kb * 16 + g + 8) * D::RECB, xr + kb * RB, lane, acc, dbg, rg,
                                             sb0 + kb);
@@ -889,8 +902,26 @@ __global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_cons
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
         if constexpr (!DBG) {
+            // the pair's partial sums meet in warp half 0
+            float * mine = red + (slice * 32 + lane) * (NG * 4);
+            if (half == 1) {
+#pragma unroll
+                for (int grp = 0; grp < NG; grp++) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) mine[grp * 4 + e] = acc[grp][e];
+                }
+            }
+            named_bar_sync(1, kNCW * 32);
+            if (half == 0) {
+#pragma unroll
+                for (int grp = 0; grp < NG; grp++) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) acc[grp][e] += mine[grp * 4 + e];
+                }
+            }
+            named_bar_sync(1, kNCW * 32);  // red is rewritten at the end of the next unit
             if (a.ksplit == 1) {
-                if (bad) continue;
+                if (bad || half) continue;
 #pragma unroll
                 for (int grp = 0; grp < NG; grp++) {
 #pragma unroll
@@ -902,14 +933,16 @@ __global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_cons
                 }
             } else {
                 // split K: partial sums out, then the last K range of this row block reduces them in K order
+                if (half == 0 && !bad) {
 #pragma unroll
-                for (int grp = 0; grp < NG; grp++) {
+                    for (int grp = 0; grp < NG; grp++) {
 #pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const int     tok = 8 * grp + 2 * t + (e & 1);
-                        const int64_t row = e < 2 ? rg : rg + 8;
-                        if (tok < a.N && row < a.rows && !bad) {
-                            a.part[((int64_t) kr * a.N + tok) * a.rows + row] = acc[grp][e];
+                        for (int e = 0; e < 4; e++) {
+                            const int     tok = 8 * grp + 2 * t + (e & 1);
+                            const int64_t row = e < 2 ? rg : rg + 8;
+                            if (tok < a.N && row < a.rows) {
+                                a.part[((int64_t) kr * a.N + tok) * a.rows + row] = acc[grp][e];
+                            }
                         }
                     }
                 }
@@ -917,7 +950,7 @@ __global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_cons
                 named_bar_sync(1, kNCW * 32);
                 if (threadIdx.x == 0) last_flag = atomicAdd(&a.cnt[rb], 1) == a.ksplit - 1;
                 named_bar_sync(1, kNCW * 32);
-                if (last_flag && !bad) {
+                if (last_flag && !bad && half == 0) {
                     __threadfence();
 #pragma unroll
                     for (int grp = 0; grp < NG; grp++) {
@@ -988,9 +1021,11 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     const int scr      = kNCW * D::KC * 16 * D::RECB;
     // as many stages (4..6) as keep two CTAs per SM; fewer when a stage is large
     a.S = kMaxStages;
-    while (a.S > 3 && kBarBytes + (size_t) a.S * a.stage_bytes + scr > 110 * 1024) a.S--;
+    const int red = kSlices * 32 * NG * 4 * (int) sizeof(float);
+    while (a.S > 3 && kBarBytes + (size_t) a.S * a.stage_bytes + scr + red > 110 * 1024) a.S--;
     a.scr_off         = kBarBytes + a.S * a.stage_bytes;
-    const size_t smem = (size_t) a.scr_off + scr;
+    a.red_off         = a.scr_off + scr;
+    const size_t smem = (size_t) a.red_off + kSlices * 32 * NG * 4 * sizeof(float);
     if (smem > 200 * 1024 || a.Wbox > 1024) return SRHPM_ERR_INVALID;
 
     CUtensorMap wmap;
@@ -1098,15 +1133,25 @@ int gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_
     {
         const int64_t warps  = (int64_t) nsb * NT;
         const int     blocks = (int) ((warps + 7) / 8);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim            = dim3((unsigned) blocks);
+        cfg.blockDim           = dim3(256);
+        cfg.stream             = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs                                          = attr;
+        cfg.numAttrs                                       = 1;
+        cudaError_t e;
         if (q80) {
-            quant_q80_kernel<false><<<blocks, 256, 0, stream>>>(X, ldx, (int) N, nsb, NT, ctx->q8_0_act_mode, recs,
-                                                                nullptr, cnt, nrb);
+            e = cudaLaunchKernelEx(&cfg, quant_q80_kernel<false>, X, ldx, (int) N, nsb, NT, ctx->q8_0_act_mode, recs,
+                                   (uint8_t *) nullptr, cnt, nrb);
         } else {
-            quant_q8K_kernel<false><<<blocks, 256, 0, stream>>>(X, ldx, (int) N, nsb, NT, recs, nullptr, nullptr,
-                                                                nullptr, nullptr, cnt, nrb);
+            e = cudaLaunchKernelEx(&cfg, quant_q8K_kernel<false>, X, ldx, (int) N, nsb, NT, recs, (int8_t *) nullptr,
+                                   (float *) nullptr, (int16_t *) nullptr, (int16_t *) nullptr, cnt, nrb);
         }
         ctx->launches.fetch_add(1);
-        const int st = cuda_status(cudaGetLastError());
+        const int st = cuda_status(e);
         if (st != SRHPM_OK) return st;
     }
     // 2. the matmul
