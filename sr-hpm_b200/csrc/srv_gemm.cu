@@ -7,9 +7,10 @@
 //      scale (bit-identical to srv_quantize_row, patch/srhpm.patch:5518-5575) -- or per 32 columns to q8_0 for Q8_0
 //      weights -- into "activation records": for each super-block, NT = 8 or 16 token rows of 256 int8 values at a
 //      288-byte stride (so that consecutive tokens fall on different shared-memory banks), then the scales.
-//   2. srv_gemm_kernel: one CTA per 64-row tile. A producer warp streams the tile through a 4-stage shared-memory
-//      ring, kc super-blocks at a time: one 1-D bulk async copy per weight row (16-byte aligned, ragged bytes at the
-//      very end of the matrix copied by hand) plus one copy of the kc activation records, completion counted on an
+//   2. srv_gemm_kernel: persistent CTAs over (64-row block, K range) units. A producer warp streams each unit
+//      through a 3-4 stage shared-memory ring, one super-block column at a time: 2-D TMA boxes of the 64 row
+//      segments (rows grouped G at a time when the row stride is not a multiple of 16 bytes; the < G rows past
+//      the tensor map come by 1-D bulk copies) plus the column's activation record, completion counted on an
 //      mbarrier. Four consumer warps each own 16 rows. Every super-block is decoded once in registers into int8 MMA
 //      fragments (A = 16 rows x 32 (or 16) weights) and multiplied with all activation rows at once on the tensor
 //      cores (B = 32 x 8 tokens), int32 exact; the integer block scales multiply the int32 fragments, the Q4_K/Q5_K
@@ -31,12 +32,12 @@ namespace srhpm {
 namespace {
 
 constexpr int     QK         = 256;
-constexpr int     kSlices    = 4;                 // 16-row slices of a 64-row tile
-constexpr int     kNCW       = 2 * kSlices;       // consumer warps: two per slice, splitting its super-blocks
+constexpr int     kNCW       = 4;                 // consumer warps, one per 16-row slice
 constexpr int     kThreads   = (kNCW + 1) * 32;   // + 1 producer warp
-constexpr int     kTileRows  = 16 * kSlices;      // weight rows per CTA tile
+constexpr int     kTileRows  = 16 * kNCW;         // weight rows per CTA tile
 constexpr int     kTokStride = 288;               // bytes per token row inside an activation record
 constexpr int     kMaxStages = 6;
+constexpr int     kMaxSplit  = 8;                 // K ranges per product at most
 constexpr int     kBarBytes  = 128;               // room for the 2 * kMaxStages mbarriers
 
 __host__ __device__ constexpr int rec_nscales(bool q80, int NT) { return q80 ? 8 * NT : NT; }
@@ -306,7 +307,7 @@ __device__ __forceinline__ void scale_acc(int (&im)[NG][4], int grp, int sA, int
 template <bool Q5>
 struct DecK45 {
     static constexpr int  BS   = Q5 ? 176 : 144;
-    static constexpr int  KC   = 2;
+    static constexpr int  KC   = 1;
     static constexpr int  RECB = 80;
     static constexpr bool Q80  = false;
     static constexpr int  QS   = Q5 ? 48 : 16;
@@ -471,7 +472,7 @@ struct DecQ6K {
 // Scale record: int32 sc[16] | f32 d.
 struct DecQ3K {
     static constexpr int  BS   = 110;
-    static constexpr int  KC   = 3;
+    static constexpr int  KC   = 1;
     static constexpr int  RECB = 80;
     static constexpr bool Q80  = false;
 
@@ -540,7 +541,7 @@ struct DecQ3K {
 // Scale record: int32 sc[8] | f32 d.
 struct DecIQ4XS {
     static constexpr int  BS   = 136;
-    static constexpr int  KC   = 2;
+    static constexpr int  KC   = 1;
     static constexpr int  RECB = 48;
     static constexpr bool Q80  = false;
 
@@ -689,7 +690,6 @@ struct GemmArgs {
     int             LSR;         // leftover slot stride
     int             rec_off;     // activation records inside a stage
     int             scr_off;     // per-warp scale-record scratch (after the stages)
-    int             red_off;     // pair-reduction buffer (after the scratch)
     const uint8_t * recs;
     float *         part;        // split-K partial sums [ksplit][N][rows]
     int32_t *       cnt;         // split-K arrival counters, one per row block (zeroed by the quantizer kernel)
@@ -827,7 +827,7 @@ __device__ __forceinline__ const uint8_t * row_ptr(const GemmArgs & a, const uin
 }
 
 template <class D, int NG, bool DBG>
-__global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
+__global__ void __launch_bounds__(kThreads, 4) srv_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
                                                             const GemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t * full   = reinterpret_cast<uint64_t *>(smem);
@@ -848,21 +848,29 @@ __global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_cons
     }
     pdl_launch_dependents();  // the next call's quantizer may start; it waits for this grid before touching data
     pdl_wait();  // the split-K counters and partials are written below; the quantizer grid zeroes the counters
-    constexpr int  RB   = rec_bytes(D::Q80, 8 * NG);
+    constexpr int  RB  = rec_bytes(D::Q80, 8 * NG);
     const int      g = lane >> 2, t = lane & 3;
-    const int      slice = warp & (kSlices - 1), half = warp / kSlices;
-    const int      rl   = slice * 16 + g;
-    const int      kr   = blockIdx.x % a.ksplit;
-    const int      sbA  = kr * a.kr_sbs, sbB = min(a.nsb, sbA + a.kr_sbs);
-    const int      nck  = (sbB - sbA + a.kc - 1) / a.kc;
-    const DbgOut   dbg  = { a.isum, a.imin, a.rows, a.N, a.nblk };
-    uint8_t *      scr  = smem + a.scr_off + warp * (D::KC * 16 * D::RECB);  // this warp's scale records
-    float *        red  = reinterpret_cast<float *>(smem + a.red_off);        // pair reduction, [slice][lane][NG*4]
+    const int      rl  = warp * 16 + g;
+    const int      kr  = blockIdx.x % a.ksplit;
+    const int      sbA = kr * a.kr_sbs, sbB = min(a.nsb, sbA + a.kr_sbs);
+    const int      nck = (sbB - sbA + a.kc - 1) / a.kc;
+    const DbgOut   dbg = { a.isum, a.imin, a.rows, a.N, a.nblk };
+    uint8_t *      scr = smem + a.scr_off + warp * (D::KC * 16 * D::RECB);  // this warp's scale records
     __shared__ int last_flag;
     int            s = 0, ph = 0;
     bool           bad = false;  // a wait ran out: skip further waits and work, keep meeting the barriers
+    // a row's place in a stage: fixed offset + 16-byte phase (j * row_bytes + sb0 * BS) mod 16, j = row mod G
+    const int      bsm = D::BS & 15;
+    auto           row_off = [&](int r, int & jterm) -> int {
+        const int j = r & (a.G - 1), q = r >> a.gshift;
+        jterm       = j * a.rbm16;
+        return (j * (kTileRows >> a.gshift) + q) * a.Wbox;
+    };
+    int       ja, jb, jp;
+    const int offa = row_off(rl, ja), offb = row_off(rl + 8, jb), offp = row_off(warp * 16 + (lane & 15), jp);
     for (int u = blockIdx.x; u < a.units; u += gridDim.x) {
         const int64_t rb = u / a.ksplit, row0 = rb * kTileRows, rg = row0 + rl;
+        const bool    edge = row0 + kTileRows > a.rows_main;  // rows past the tensor map in this tile
         float         acc[NG][4];
 #pragma unroll
         for (int grp = 0; grp < NG; grp++) acc[grp][0] = acc[grp][1] = acc[grp][2] = acc[grp][3] = 0.0f;
@@ -879,20 +887,27 @@ __global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_cons
             if (bad) continue;
             const uint8_t * st  = stage0 + (size_t) slot * a.stage_bytes;
             const int       sb0 = sbA + c * a.kc, kcc = min(a.kc, sbB - sb0);
-            // the two warps of a slice take alternate super-blocks of the unit: item c*KC + kb goes to half (i & 1)
-            // scale records of this warp's items, one (row, super-block) per lane
-            for (int it = lane; it < 16 * kcc; it += 32) {
-                const int kb = it >> 4, r = it & 15;
-                if (((c * D::KC + kb) & 1) != half) continue;
-                D::prep(row_ptr<D>(a, st, row0, slice * 16 + r, sb0) + kb * D::BS, scr + it * D::RECB);
+            const uint8_t * wa;
+            const uint8_t * wb;
+            const uint8_t * wp;
+            if (!edge) {
+                const int sbt = sb0 * bsm;
+                wa            = st + offa + ((ja + sbt) & 15);
+                wb            = st + offb + ((jb + sbt) & 15);
+                wp            = st + offp + ((jp + sbt) & 15);
+            } else {
+                wa = row_ptr<D>(a, st, row0, rl, sb0);
+                wb = row_ptr<D>(a, st, row0, rl + 8, sb0);
+                wp = row_ptr<D>(a, st, row0, warp * 16 + (lane & 15), sb0);
             }
+            // scale records of this warp's 16 rows x kcc super-blocks, one (row, super-block) per lane
+            if (lane < 16) D::prep(wp, scr + lane * D::RECB);
+            for (int kb = 1 + (lane >> 4); kb < kcc; kb += 2) D::prep(wp + kb * D::BS, scr + (kb * 16 + (lane & 15)) * D::RECB);
             __syncwarp();
-            const uint8_t * wa = row_ptr<D>(a, st, row0, rl, sb0);
-            const uint8_t * wb = row_ptr<D>(a, st, row0, rl + 8, sb0);
             const uint8_t * xr = st + a.rec_off;
 #pragma unroll
             for (int kb = 0; kb < D::KC; kb++) {
-                if (kb < kcc && ((c * D::KC + kb) & 1) == half) {
+                if (kb < kcc) {
                     D::template sb<NG, DBG>(wa + kb * D::BS, wb + kb * D::BS, scr + (kb * 16 + g) * D::RECB,
                                             scr + (kb * 16 + g + 8) * D::RECB, xr + kb * RB, lane, acc, dbg, rg,
                                             sb0 + kb);
@@ -902,26 +917,8 @@ __global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_cons
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
         if constexpr (!DBG) {
-            // the pair's partial sums meet in warp half 0
-            float * mine = red + (slice * 32 + lane) * (NG * 4);
-            if (half == 1) {
-#pragma unroll
-                for (int grp = 0; grp < NG; grp++) {
-#pragma unroll
-                    for (int e = 0; e < 4; e++) mine[grp * 4 + e] = acc[grp][e];
-                }
-            }
-            named_bar_sync(1, kNCW * 32);
-            if (half == 0) {
-#pragma unroll
-                for (int grp = 0; grp < NG; grp++) {
-#pragma unroll
-                    for (int e = 0; e < 4; e++) acc[grp][e] += mine[grp * 4 + e];
-                }
-            }
-            named_bar_sync(1, kNCW * 32);  // red is rewritten at the end of the next unit
             if (a.ksplit == 1) {
-                if (bad || half) continue;
+                if (bad) continue;
 #pragma unroll
                 for (int grp = 0; grp < NG; grp++) {
 #pragma unroll
@@ -933,7 +930,7 @@ __global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_cons
                 }
             } else {
                 // split K: partial sums out, then the last K range of this row block reduces them in K order
-                if (half == 0 && !bad) {
+                if (!bad) {
 #pragma unroll
                     for (int grp = 0; grp < NG; grp++) {
 #pragma unroll
@@ -950,7 +947,7 @@ __global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_cons
                 named_bar_sync(1, kNCW * 32);
                 if (threadIdx.x == 0) last_flag = atomicAdd(&a.cnt[rb], 1) == a.ksplit - 1;
                 named_bar_sync(1, kNCW * 32);
-                if (last_flag && !bad && half == 0) {
+                if (last_flag && !bad) {
                     __threadfence();
 #pragma unroll
                     for (int grp = 0; grp < NG; grp++) {
@@ -1013,19 +1010,18 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     a.rbm16            = (int) (a.row_bytes & 15);
     a.rows_main        = (a.rows / a.G) * a.G;
     const bool aligned = a.G == 1 && D::BS % 16 == 0;
-    a.Wbox             = ((aligned ? 0 : 14) + a.kc * D::BS + 15) / 16 * 16;
+    // box width: the segment (plus its 16-byte phase) widened to 32 or 96 mod 128, so that the rows of a quad
+    // group land on different shared-memory banks (the extra bytes are the next segment's, read from L2)
+    a.Wbox             = slot_stride((aligned ? 0 : 14) + a.kc * D::BS);
     a.LSR              = slot_stride((aligned ? 0 : 14) + a.kc * D::BS);
     a.left_off         = kTileRows * a.Wbox;
     a.rec_off          = (a.left_off + (a.G > 1 ? (a.G - 1) * a.LSR : 0) + 127) / 128 * 128;
     a.stage_bytes      = (a.rec_off + a.kc * RB + 127) / 128 * 128;
     const int scr      = kNCW * D::KC * 16 * D::RECB;
-    // as many stages (4..6) as keep two CTAs per SM; fewer when a stage is large
-    a.S = kMaxStages;
-    const int red = kSlices * 32 * NG * 4 * (int) sizeof(float);
-    while (a.S > 3 && kBarBytes + (size_t) a.S * a.stage_bytes + scr + red > 110 * 1024) a.S--;
+    // 4 stages while that keeps 4 CTAs per SM resident, else 3
+    a.S = kBarBytes + 4 * a.stage_bytes + scr <= 56 * 1024 ? 4 : 3;
     a.scr_off         = kBarBytes + a.S * a.stage_bytes;
-    a.red_off         = a.scr_off + scr;
-    const size_t smem = (size_t) a.red_off + kSlices * 32 * NG * 4 * sizeof(float);
+    const size_t smem = (size_t) a.scr_off + scr;
     if (smem > 200 * 1024 || a.Wbox > 1024) return SRHPM_ERR_INVALID;
 
     CUtensorMap wmap;
@@ -1057,10 +1053,11 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
     const int     slots  = std::max(1, per_sm) * ctx->num_sms;
     const int64_t nrb    = (a.rows + kTileRows - 1) / kTileRows;
-    // split K while the row blocks alone would leave the GPU short of resident work
+    // split K so that the units fill the resident CTA slots (about one round), K ranges of >= 2 super-blocks
     a.ksplit = 1;
     if (!DBG && a.part) {
-        while (nrb * a.ksplit < (int64_t) ctx->num_sms * 3 / 2 && a.ksplit < 8 && a.ksplit * 2 <= a.nsb) a.ksplit++;
+        const int want = (int) ((slots + nrb / 2) / nrb);
+        a.ksplit       = std::max(1, std::min({ want, kMaxSplit, a.nsb / 2 }));
     }
     a.kr_sbs = (a.nsb + a.ksplit - 1) / a.ksplit;
     a.units  = (int) (nrb * a.ksplit);
@@ -1095,7 +1092,6 @@ uint8_t * align256(void * p) {
     return reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(p) + 255) & ~uintptr_t(255));
 }
 
-constexpr int kMaxSplit = 8;
 
 }  // namespace
 
