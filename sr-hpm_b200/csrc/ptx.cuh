@@ -6,9 +6,11 @@
 
 namespace srhpm {
 
-// Spin limit of every mbarrier wait. A wait that runs out sets the kernel's error word and the kernel returns
-// instead of hanging (each probe of try_wait already blocks for a hardware-defined interval).
-constexpr uint32_t kWaitLimit = 1u << 22;
+// Bound of every mbarrier wait: kWaitLimit probes of try_wait, each suspending the thread for up to kSuspendNs
+// (it wakes as soon as the phase completes), about 2 s in all. A wait that runs out sets the kernel's error word
+// and the kernel finishes without hanging.
+constexpr uint32_t kWaitLimit = 20000;
+constexpr uint32_t kSuspendNs = 100000;
 
 // error words written to the context's device status slot
 enum : int32_t { kErrNone = 0, kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3 };
@@ -38,10 +40,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendNs)
         : "memory");
     return ok != 0;
 }
@@ -107,6 +109,39 @@ __device__ __forceinline__ void mma_k32(int (&c)[4], uint32_t a0, uint32_t a1, u
             "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
             : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
             : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    }
+}
+
+// D = A(16x32) * B(32x8) with a zero accumulator input (no per-call register zeroing)
+template <bool A_UNSIGNED>
+__device__ __forceinline__ void mma_k32_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    const int z = 0;
+    if constexpr (A_UNSIGNED) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(z));
+    } else {
+        asm volatile(
+            "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+            : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+            : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(z));
+    }
+}
+
+// D = A(16x16) * B(16x8) with a zero accumulator input
+template <bool A_UNSIGNED>
+__device__ __forceinline__ void mma_k16_z(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    const int z = 0;
+    if constexpr (A_UNSIGNED) {
+        asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+                     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                     : "r"(a0), "r"(a1), "r"(b0), "r"(z));
+    } else {
+        asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+                     : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                     : "r"(a0), "r"(a1), "r"(b0), "r"(z));
     }
 }
 

@@ -369,8 +369,8 @@ struct DecK45 {
 #pragma unroll
                 for (int grp = 0; grp < NG; grp++) {
                     const uint2 x = lds64(xr + (8 * grp + g) * kTokStride + 32 * b + 8 * t);
-                    int         c[4] = { 0, 0, 0, 0 };
-                    mma_k32<true>(c, a0, a1, a2, a3, x.x, x.y);
+                    int         c[4];
+                    mma_k32_z<true>(c, a0, a1, a2, a3, x.x, x.y);
                     if (!Q5 && h) {
                         scale_acc<NG>(ih, grp, sA, sB, c);
                     } else {
@@ -450,8 +450,8 @@ struct DecQ6K {
 #pragma unroll
                     for (int grp = 0; grp < NG; grp++) {
                         const uint32_t x    = lds32(xr + (8 * grp + g) * kTokStride + 32 * b + off);
-                        int            c[4] = { 0, 0, 0, 0 };
-                        mma_k16<false>(c, ua, ub, x);
+                        int            c[4];
+                        mma_k16_z<false>(c, ua, ub, x);
                         scale_acc<NG>(im, grp, sA, sB, c);
                     }
                 }
@@ -519,8 +519,8 @@ struct DecQ3K {
 #pragma unroll
                     for (int grp = 0; grp < NG; grp++) {
                         const uint32_t x    = lds32(xr + (8 * grp + g) * kTokStride + 32 * b + off);
-                        int            c[4] = { 0, 0, 0, 0 };
-                        mma_k16<false>(c, ua, ub, x);
+                        int            c[4];
+                        mma_k16_z<false>(c, ua, ub, x);
                         scale_acc<NG>(im, grp, sA, sB, c);
                     }
                 }
@@ -588,8 +588,8 @@ struct DecIQ4XS {
 #pragma unroll
             for (int grp = 0; grp < NG; grp++) {
                 const uint8_t * xp   = xr + (8 * grp + g) * kTokStride + 32 * b + 4 * t;
-                int             c[4] = { 0, 0, 0, 0 };
-                mma_k32<false>(c, a0, a1, a2, a3, lds32(xp), lds32(xp + 16));
+                int             c[4];
+                mma_k32_z<false>(c, a0, a1, a2, a3, lds32(xp), lds32(xp + 16));
                 scale_acc<NG>(im, grp, sA, sB, c);
             }
         }
@@ -636,8 +636,7 @@ struct DecQ80 {
 #pragma unroll
             for (int grp = 0; grp < NG; grp++) {
                 const uint8_t * xp = xr + (8 * grp + g) * kTokStride + 32 * i + 4 * t;
-                c[grp][0] = c[grp][1] = c[grp][2] = c[grp][3] = 0;
-                mma_k32<false>(c[grp], a0, a1, a2, a3, lds32(xp), lds32(xp + 16));
+                mma_k32_z<false>(c[grp], a0, a1, a2, a3, lds32(xp), lds32(xp + 16));
             }
             if constexpr (DBG) {
                 dbg_store<NG>(dbg, c, false, rg, 8 * sbi + i, lane);
