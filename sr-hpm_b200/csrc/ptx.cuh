@@ -6,11 +6,10 @@
 
 namespace srhpm {
 
-// Bound of every mbarrier wait: kWaitLimit probes of try_wait, each suspending the thread for up to kSuspendNs
-// (it wakes as soon as the phase completes), about 2 s in all. A wait that runs out sets the kernel's error word
-// and the kernel finishes without hanging.
-constexpr uint32_t kWaitLimit = 20000;
-constexpr uint32_t kSuspendNs = 100000;
+// Bound of every mbarrier wait: kWaitLimit probes of try_wait (each blocks for a hardware-defined interval while
+// the phase is incomplete). A wait that runs out sets the kernel's error word and the kernel finishes without
+// hanging.
+constexpr uint32_t kWaitLimit = 1u << 22;
 
 // error words written to the context's device status slot
 enum : int32_t { kErrNone = 0, kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3 };
@@ -40,10 +39,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendNs)
+        : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     return ok != 0;
 }
@@ -87,6 +86,25 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
 // orders this thread's generic-proxy shared-memory writes before later async-proxy (bulk copy) accesses
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// streaming global loads of read-once data: non-coherent path, no L1 allocation
+__device__ __forceinline__ uint4 ldg_stream128(const void * p) {
+    uint4 v;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ldg_stream64(const void * p) {
+    uint2 v;
+    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldg_stream32(const void * p) {
+    uint32_t v;
+    asm("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
 }
 
 // programmatic dependent launch: wait for the preceding grid's writes / let the next grid start its prologue

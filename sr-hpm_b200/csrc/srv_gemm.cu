@@ -141,6 +141,17 @@ __global__ void __launch_bounds__(256) quant_q8K_kernel(const float * __restrict
         uint8_t * rec = recs + (size_t) sb * rec_bytes(false, NT);
         *reinterpret_cast<uint2 *>(rec + t * kTokStride + 8 * lane) = pk;
         if (lane == 0) reinterpret_cast<float *>(rec + NT * kTokStride)[t] = dv;
+        // per-32 sums of the quantized row, split into int8 halves s = 128 * hi + lo (lo in 0..127), in the token
+        // row's padding: hi at 256 + sub-block, lo at 264 + sub-block (the Q4_K / Q5_K minimum term)
+        int s32 = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) s32 += qv[j];
+        s32 += __shfl_xor_sync(0xffffffffu, s32, 1);
+        s32 += __shfl_xor_sync(0xffffffffu, s32, 2);
+        if ((lane & 3) == 0) {
+            rec[t * kTokStride + 256 + lane / 4] = (uint8_t) (int8_t) (s32 >> 7);
+            rec[t * kTokStride + 264 + lane / 4] = (uint8_t) (s32 & 127);
+        }
     }
 }
 
@@ -971,6 +982,286 @@ __global__ void __launch_bounds__(kThreads, 4) srv_gemm_kernel(const __grid_cons
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// direct-load kernel for the types whose blocks keep 8- or 16-byte alignment (Q4_K, Q5_K, IQ4_XS)
+//
+// No shared-memory ring: each warp streams its 16 weight rows straight into registers with non-allocating 64/128-bit
+// loads, two super-blocks ahead of the one it multiplies (the register file is the staging buffer). The activation
+// records of the CTA's K range sit in shared memory for the whole kernel. Work units, split K and the fix-up are those
+// of srv_gemm_kernel.
+
+// Q4_K / Q5_K minimum term of one super-block through one MMA pair over k = sub-block index: A = the 8 6-bit mins
+// of each row (thread t = 0 holds sub-blocks 0..3, t = 1 holds 4..7, others zero), B = the per-sub-block activation
+// sums split as s = 128 hi + lo (int8 each, from the record's padding). Returns sum_b m_b * s_b.
+template <int NG>
+__device__ __forceinline__ void mins_mma(int (&in)[NG][4], uint32_t mlA, uint32_t mhA, uint32_t mlB, uint32_t mhB,
+                                         const uint8_t * xr, int lane) {
+    const int      t  = lane & 3, g = lane >> 2;
+    const uint32_t a0 = t == 0 ? mlA : t == 1 ? mhA : 0u;
+    const uint32_t a1 = t == 0 ? mlB : t == 1 ? mhB : 0u;
+#pragma unroll
+    for (int grp = 0; grp < NG; grp++) {
+        const uint8_t * tok = xr + (8 * grp + g) * kTokStride;
+        const uint32_t  bh  = t < 2 ? lds32(tok + 256 + 4 * t) : 0u;
+        const uint32_t  bl  = t < 2 ? lds32(tok + 264 + 4 * t) : 0u;
+        int             ch[4], cl[4];
+        mma_k32_z<true>(ch, a0, a1, 0u, 0u, bh, 0u);
+        mma_k32_z<true>(cl, a0, a1, 0u, 0u, bl, 0u);
+#pragma unroll
+        for (int e = 0; e < 4; e++) in[grp][e] = ch[e] * 128 + cl[e];
+    }
+}
+
+template <bool Q5>
+struct DirK45 {
+    static constexpr int  BS  = Q5 ? 176 : 144;
+    static constexpr int  QS  = Q5 ? 48 : 16;
+    static constexpr bool Q80 = false;
+    struct Frag {
+        uint4 h[2];     // d | dmin, 12 bytes of scales / mins (rows g, g + 8)
+        uint2 q[2][4];  // code bytes 8t..8t+7 of each sub-block pair
+        uint2 qh[2];    // Q5_K: 5th-bit bytes 8t..8t+7
+    };
+
+    __device__ __forceinline__ static void load(Frag & f, const uint8_t * ra, const uint8_t * rb, int t) {
+        f.h[0] = ldg_stream128(ra);
+        f.h[1] = ldg_stream128(rb);
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+            f.q[0][p] = ldg_stream64(ra + QS + 32 * p + 8 * t);
+            f.q[1][p] = ldg_stream64(rb + QS + 32 * p + 8 * t);
+        }
+        if constexpr (Q5) {
+            f.qh[0] = ldg_stream64(ra + 16 + 8 * t);
+            f.qh[1] = ldg_stream64(rb + 16 + 8 * t);
+        }
+    }
+
+    template <int NG, bool DBG>
+    __device__ __forceinline__ static void compute(const Frag & f, const uint8_t * xr, int lane, float (&acc)[NG][4],
+                                                   const DbgOut & dbg, int64_t rg, int sbi) {
+        constexpr int NT = 8 * NG;
+        const int     t = lane & 3, g = lane >> 2;
+        uint32_t      sl[2], sh[2], ml[2], mh[2];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const uint32_t w1 = f.h[r].y, w2 = f.h[r].z, w3 = f.h[r].w;
+            sl[r] = w1 & 0x3F3F3F3Fu;
+            sh[r] = (w3 & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u);
+            ml[r] = w2 & 0x3F3F3F3Fu;
+            mh[r] = ((w3 >> 4) & 0x0F0F0F0Fu) | ((w2 >> 2) & 0x30303030u);
+        }
+        int im[NG][4], ih[NG][4], in[NG][4];
+        zero<NG>(im);
+        zero<NG>(ih);
+        mins_mma<NG>(in, ml[0], mh[0], ml[1], mh[1], xr, lane);
+#pragma unroll
+        for (int p = 0; p < 4; p++) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int b = 2 * p + h;
+                uint32_t  a0, a1, a2, a3;
+                if constexpr (Q5) {
+                    a0 = ((f.q[0][p].x >> (4 * h)) & 0x0F0F0F0Fu) | DecK45<true>::hbit(f.qh[0].x, b);
+                    a2 = ((f.q[0][p].y >> (4 * h)) & 0x0F0F0F0Fu) | DecK45<true>::hbit(f.qh[0].y, b);
+                    a1 = ((f.q[1][p].x >> (4 * h)) & 0x0F0F0F0Fu) | DecK45<true>::hbit(f.qh[1].x, b);
+                    a3 = ((f.q[1][p].y >> (4 * h)) & 0x0F0F0F0Fu) | DecK45<true>::hbit(f.qh[1].y, b);
+                } else {
+                    const uint32_t m = h ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+                    a0 = f.q[0][p].x & m;
+                    a2 = f.q[0][p].y & m;
+                    a1 = f.q[1][p].x & m;
+                    a3 = f.q[1][p].y & m;
+                }
+                const int sA = ubyte(b < 4 ? sl[0] : sh[0], b & 3), sB = ubyte(b < 4 ? sl[1] : sh[1], b & 3);
+#pragma unroll
+                for (int grp = 0; grp < NG; grp++) {
+                    const uint2 x = lds64(xr + (8 * grp + g) * kTokStride + 32 * b + 8 * t);
+                    int         c[4];
+                    mma_k32_z<true>(c, a0, a1, a2, a3, x.x, x.y);
+                    if (!Q5 && h) {
+                        scale_acc<NG>(ih, grp, sA, sB, c);
+                    } else {
+                        scale_acc<NG>(im, grp, sA, sB, c);
+                    }
+                }
+            }
+        }
+        if constexpr (!Q5) {
+#pragma unroll
+            for (int grp = 0; grp < NG; grp++) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) im[grp][e] += ih[grp][e] >> 4;
+            }
+        }
+        if constexpr (DBG) {
+            dbg_store<NG>(dbg, im, false, rg, sbi, lane);
+            dbg_store<NG>(dbg, in, true, rg, sbi, lane);
+        } else {
+            const float * xs = reinterpret_cast<const float *>(xr + NT * kTokStride);
+            const float2  dA = __half22float2(*reinterpret_cast<const __half2 *>(&f.h[0].x));
+            const float2  dB = __half22float2(*reinterpret_cast<const __half2 *>(&f.h[1].x));
+            sb_update<NG, true>(acc, im, in, dA.x, dB.x, dA.y, dB.y, xs, t);
+        }
+    }
+};
+
+struct DirIQ4XS {
+    static constexpr int  BS  = 136;
+    static constexpr bool Q80 = false;
+    struct Frag {
+        uint2    h[2];     // d | scales_h, scales_l
+        uint32_t q[2][8];  // code bytes 4t..4t+3 of each sub-block
+    };
+
+    __device__ __forceinline__ static void load(Frag & f, const uint8_t * ra, const uint8_t * rb, int t) {
+        f.h[0] = ldg_stream64(ra);
+        f.h[1] = ldg_stream64(rb);
+#pragma unroll
+        for (int b = 0; b < 8; b++) {
+            f.q[0][b] = ldg_stream32(ra + 8 + 16 * b + 4 * t);
+            f.q[1][b] = ldg_stream32(rb + 8 + 16 * b + 4 * t);
+        }
+    }
+
+    template <int NG, bool DBG>
+    __device__ __forceinline__ static void compute(const Frag & f, const uint8_t * xr, int lane, float (&acc)[NG][4],
+                                                   const DbgOut & dbg, int64_t rg, int sbi) {
+        constexpr int NT = 8 * NG;
+        const int     t = lane & 3, g = lane >> 2;
+        const uint32_t HA = f.h[0].x >> 16, LA = f.h[0].y, HB = f.h[1].x >> 16, LB = f.h[1].y;
+        int            im[NG][4], in[NG][4];
+        zero<NG>(im);
+        zero<NG>(in);
+#pragma unroll
+        for (int b = 0; b < 8; b++) {
+            const int sA = (int) (((LA >> (4 * b)) & 0xFu) | (((HA >> (2 * b)) & 3u) << 4)) - 32;
+            const int sB = (int) (((LB >> (4 * b)) & 0xFu) | (((HB >> (2 * b)) & 3u) << 4)) - 32;
+            uint32_t  a0, a2, a1, a3;
+            DecIQ4XS::lookup(f.q[0][b], a0, a2);
+            DecIQ4XS::lookup(f.q[1][b], a1, a3);
+#pragma unroll
+            for (int grp = 0; grp < NG; grp++) {
+                const uint8_t * xp = xr + (8 * grp + g) * kTokStride + 32 * b + 4 * t;
+                int             c[4];
+                mma_k32_z<false>(c, a0, a1, a2, a3, lds32(xp), lds32(xp + 16));
+                scale_acc<NG>(im, grp, sA, sB, c);
+            }
+        }
+        if constexpr (DBG) {
+            dbg_store<NG>(dbg, im, false, rg, sbi, lane);
+        } else {
+            const float * xs = reinterpret_cast<const float *>(xr + NT * kTokStride);
+            const float   dA = __half2float(__ushort_as_half((unsigned short) (f.h[0].x & 0xffffu)));
+            const float   dB = __half2float(__ushort_as_half((unsigned short) (f.h[1].x & 0xffffu)));
+            sb_update<NG, false>(acc, im, in, dA, dB, 0.f, 0.f, xs, t);
+        }
+    }
+};
+
+template <class D, int NG, bool DBG>
+__global__ void __launch_bounds__(128, 4) srv_gemm_direct(const GemmArgs a) {
+    extern __shared__ __align__(16) uint8_t xsm[];  // activation records of this CTA's K range
+    constexpr int  RB   = rec_bytes(D::Q80, 8 * NG);
+    const int      warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    const int      kr   = blockIdx.x % a.ksplit;
+    const int      sbA  = kr * a.kr_sbs, sbB = min(a.nsb, sbA + a.kr_sbs), nk = sbB - sbA;
+    const DbgOut   dbg  = { a.isum, a.imin, a.rows, a.N, a.nblk };
+    __shared__ int last_flag;
+    typename D::Frag f0, f1, f2;
+    auto rowp = [&](int64_t row0, int r) -> const uint8_t * {
+        const int64_t R = min(row0 + warp * 16 + r, a.rows - 1);  // rows past the matrix re-read the last one
+        return a.W + R * a.row_bytes + (int64_t) sbA * D::BS;
+    };
+    auto load = [&](typename D::Frag & f, int64_t row0, int k) {
+        if (k < nk) D::load(f, rowp(row0, g) + k * D::BS, rowp(row0, g + 8) + k * D::BS, t);
+    };
+    // the first unit's first super-blocks are requested before the quantizer grid has finished
+    int u = blockIdx.x;
+    if (u < a.units) {
+        const int64_t row0 = (int64_t) (u / a.ksplit) * kTileRows;
+        load(f0, row0, 0);
+        load(f1, row0, 1);
+    }
+    pdl_launch_dependents();
+    pdl_wait();
+    {
+        const uint4 * src = reinterpret_cast<const uint4 *>(a.recs + (size_t) sbA * RB);
+        uint4 *       dst = reinterpret_cast<uint4 *>(xsm);
+        for (int i = threadIdx.x; i < nk * RB / 16; i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+    bool first = true;
+    for (; u < a.units; u += gridDim.x) {
+        const int64_t rb = u / a.ksplit, row0 = rb * kTileRows, rg = row0 + warp * 16 + g;
+        if (!first) {
+            load(f0, row0, 0);
+            load(f1, row0, 1);
+        }
+        first = false;
+        float acc[NG][4];
+#pragma unroll
+        for (int grp = 0; grp < NG; grp++) acc[grp][0] = acc[grp][1] = acc[grp][2] = acc[grp][3] = 0.0f;
+        // three-slot register ring, two super-blocks in flight
+        for (int k = 0; k < nk; k += 3) {
+            load(f2, row0, k + 2);
+            D::template compute<NG, DBG>(f0, xsm + k * RB, lane, acc, dbg, rg, sbA + k);
+            if (k + 1 >= nk) break;
+            load(f0, row0, k + 3);
+            D::template compute<NG, DBG>(f1, xsm + (k + 1) * RB, lane, acc, dbg, rg, sbA + k + 1);
+            if (k + 2 >= nk) break;
+            load(f1, row0, k + 4);
+            D::template compute<NG, DBG>(f2, xsm + (k + 2) * RB, lane, acc, dbg, rg, sbA + k + 2);
+        }
+        if constexpr (!DBG) {
+            if (a.ksplit == 1) {
+#pragma unroll
+                for (int grp = 0; grp < NG; grp++) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int     tok = 8 * grp + 2 * t + (e & 1);
+                        const int64_t row = e < 2 ? rg : rg + 8;
+                        if (tok < a.N && row < a.rows) a.Y[(int64_t) tok * a.ldy + row] = acc[grp][e];
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int grp = 0; grp < NG; grp++) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int     tok = 8 * grp + 2 * t + (e & 1);
+                        const int64_t row = e < 2 ? rg : rg + 8;
+                        if (tok < a.N && row < a.rows) a.part[((int64_t) kr * a.N + tok) * a.rows + row] = acc[grp][e];
+                    }
+                }
+                __threadfence();
+                __syncthreads();
+                if (threadIdx.x == 0) last_flag = atomicAdd(&a.cnt[rb], 1) == a.ksplit - 1;
+                __syncthreads();
+                if (last_flag) {
+                    __threadfence();
+#pragma unroll
+                    for (int grp = 0; grp < NG; grp++) {
+#pragma unroll
+                        for (int e = 0; e < 4; e++) {
+                            const int     tok = 8 * grp + 2 * t + (e & 1);
+                            const int64_t row = e < 2 ? rg : rg + 8;
+                            if (tok < a.N && row < a.rows) {
+                                float sum = 0.0f;
+                                for (int k = 0; k < a.ksplit; k++) {
+                                    sum += __ldcg(&a.part[((int64_t) k * a.N + tok) * a.rows + row]);
+                                }
+                                a.Y[(int64_t) tok * a.ldy + row] = sum;
+                            }
+                        }
+                    }
+                }
+                __syncthreads();  // last_flag is rewritten by the next unit
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // host side
 
 int slot_stride(int need) {
@@ -1079,6 +1370,62 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, wmap, a));
 }
 
+template <class D, int NG, bool DBG>
+int launch_direct(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
+    constexpr int RB   = rec_bytes(D::Q80, 8 * NG);
+    auto          kern = srv_gemm_direct<D, NG, DBG>;
+    static std::atomic<unsigned> attr_done{ 0 };
+    int                          dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_done.load() & (1u << (dev & 31)))) {
+        const int st = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        if (st != SRHPM_OK) return st;
+        attr_done.fetch_or(1u << (dev & 31));
+    }
+    const int64_t nrb = (a.rows + kTileRows - 1) / kTileRows;
+    // K ranges: the resident records of a range stay within ~50 KB (4 CTAs per SM), and the units fill the slots
+    const int max_sbs = std::max(1, (50 * 1024) / RB);
+    const int min_split = (a.nsb + max_sbs - 1) / max_sbs;
+    const int slots     = 4 * ctx->num_sms;
+    a.ksplit            = 1;
+    if (!DBG && a.part) {
+        const int want = (int) ((slots + nrb / 2) / nrb);
+        a.ksplit       = std::max(min_split, std::max(1, std::min({ want, kMaxSplit, a.nsb / 2 })));
+    } else {
+        a.ksplit = min_split;
+    }
+    a.kr_sbs          = (a.nsb + a.ksplit - 1) / a.ksplit;
+    a.ksplit          = (a.nsb + a.kr_sbs - 1) / a.kr_sbs;
+    a.units           = (int) (nrb * a.ksplit);
+    const size_t smem = (size_t) a.kr_sbs * RB;
+    int          per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem);
+    const int s2     = std::max(1, per_sm) * ctx->num_sms;
+    const int rounds = (a.units + s2 - 1) / s2;
+    int       grid   = (a.units + rounds - 1) / rounds;
+    grid             = (grid + a.ksplit - 1) / a.ksplit * a.ksplit;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim            = dim3((unsigned) grid);
+    cfg.blockDim           = dim3(128);
+    cfg.dynamicSmemBytes   = smem;
+    cfg.stream             = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs                                          = attr;
+    cfg.numAttrs                                       = 1;
+    ctx->launches.fetch_add(1);
+    return cuda_status(cudaLaunchKernelEx(&cfg, kern, a));
+}
+
+template <class D>
+int dispatch_direct(srhpm_ctx * ctx, const GemmArgs & a, bool dbg, cudaStream_t stream) {
+    if (a.N <= 8) {
+        return dbg ? launch_direct<D, 1, true>(ctx, a, stream) : launch_direct<D, 1, false>(ctx, a, stream);
+    }
+    return dbg ? launch_direct<D, 2, true>(ctx, a, stream) : launch_direct<D, 2, false>(ctx, a, stream);
+}
+
 template <class D>
 int dispatch_ng(srhpm_ctx * ctx, const GemmArgs & a, bool dbg, cudaStream_t stream) {
     if (a.N <= 8) {
@@ -1104,7 +1451,11 @@ WorkLayout work_layout(int wtype, int64_t rows, int64_t K, int64_t N) {
     WorkLayout w   = {};
     w.recs         = 0;
     w.part         = ((size_t) (K / QK) * rec_bytes(wtype == SRHPM_TYPE_Q8_0, NT) + 255) / 256 * 256;
-    w.cnt          = w.part + ((size_t) kMaxSplit * N * rows * 4 + 255) / 256 * 256;
+    // the most K ranges a product can be split into: kMaxSplit, or more when the direct kernel's resident records of
+    // a K range would exceed ~50 KB
+    const int     max_sbs = std::max(1, (50 * 1024) / rec_bytes(wtype == SRHPM_TYPE_Q8_0, NT));
+    const int64_t splits  = std::max<int64_t>(kMaxSplit, (K / QK + max_sbs - 1) / max_sbs);
+    w.cnt          = w.part + ((size_t) splits * N * rows * 4 + 255) / 256 * 256;
     const int64_t nrb = (rows + kTileRows - 1) / kTileRows;
     w.total        = w.cnt + (size_t) nrb * 4 + 256;  // + 256: room to align the caller's pointer
     return w;
@@ -1168,11 +1519,11 @@ int gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_
     a.nblk      = q80 ? nsb * 8 : nsb;
     const bool dbg = isum != nullptr;
     switch (wtype) {
-        case SRHPM_TYPE_Q4_K: return dispatch_ng<DecK45<false>>(ctx, a, dbg, stream);
-        case SRHPM_TYPE_Q5_K: return dispatch_ng<DecK45<true>>(ctx, a, dbg, stream);
+        case SRHPM_TYPE_Q4_K: return dispatch_direct<DirK45<false>>(ctx, a, dbg, stream);
+        case SRHPM_TYPE_Q5_K: return dispatch_direct<DirK45<true>>(ctx, a, dbg, stream);
         case SRHPM_TYPE_Q6_K: return dispatch_ng<DecQ6K>(ctx, a, dbg, stream);
         case SRHPM_TYPE_Q3_K: return dispatch_ng<DecQ3K>(ctx, a, dbg, stream);
-        case SRHPM_TYPE_IQ4_XS: return dispatch_ng<DecIQ4XS>(ctx, a, dbg, stream);
+        case SRHPM_TYPE_IQ4_XS: return dispatch_direct<DirIQ4XS>(ctx, a, dbg, stream);
         case SRHPM_TYPE_Q8_0: return dispatch_ng<DecQ80>(ctx, a, dbg, stream);
         default: return SRHPM_UNSUPPORTED;
     }
