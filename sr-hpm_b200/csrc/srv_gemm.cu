@@ -237,7 +237,7 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
     return r;
 }
-__device__ __forceinline__ int ubyte(uint32_t w, int j) { return (int) ((w >> (8 * j)) & 0xffu); }
+__device__ __forceinline__ int ubyte(uint32_t w, int j) { return (int) __byte_perm(w, 0u, 0x4440u | (uint32_t) j); }
 __device__ __forceinline__ int sbyte(uint32_t w, int j) { return ((int32_t) (w << (24 - 8 * j))) >> 24; }
 __device__ __forceinline__ uint32_t rep_byte(uint32_t w, int j) { return prmt(w, 0, 0x1111u * (uint32_t) j); }
 
