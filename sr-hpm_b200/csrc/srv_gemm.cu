@@ -309,17 +309,39 @@ __device__ __forceinline__ void scale_acc(int (&im)[NG][4], int grp, int sA, int
     im[grp][3] += sB * c[3];
 }
 
+// Q4_K / Q5_K minimum term of one super-block through one MMA pair over k = sub-block index: A = the 8 6-bit mins
+// of each row (thread t = 0 holds sub-blocks 0..3, t = 1 holds 4..7, others zero), B = the per-sub-block activation
+// sums split as s = 128 hi + lo (int8 each, from the record's padding). Returns sum_b m_b * s_b.
+template <int NG>
+__device__ __forceinline__ void mins_mma(int (&in)[NG][4], uint32_t mlA, uint32_t mhA, uint32_t mlB, uint32_t mhB,
+                                         const uint8_t * xr, int lane) {
+    const int      t  = lane & 3, g = lane >> 2;
+    const uint32_t a0 = t == 0 ? mlA : t == 1 ? mhA : 0u;
+    const uint32_t a1 = t == 0 ? mlB : t == 1 ? mhB : 0u;
+#pragma unroll
+    for (int grp = 0; grp < NG; grp++) {
+        const uint8_t * tok = xr + (8 * grp + g) * kTokStride;
+        const uint32_t  bh  = t < 2 ? lds32(tok + 256 + 4 * t) : 0u;
+        const uint32_t  bl  = t < 2 ? lds32(tok + 264 + 4 * t) : 0u;
+        int             ch[4], cl[4];
+        mma_k32_z<true>(ch, a0, a1, 0u, 0u, bh, 0u);
+        mma_k32_z<true>(cl, a0, a1, 0u, 0u, bl, 0u);
+#pragma unroll
+        for (int e = 0; e < 4; e++) in[grp][e] = ch[e] * 128 + cl[e];
+    }
+}
+
 // Q4_K (144 B: d, dmin, 12 bytes of 6-bit scales/mins, 128 bytes of nibbles) and Q5_K (176 B: + 32 bytes of 5th
 // bits before the nibbles). Pair p of sub-blocks (2p, 2p+1) shares 32 code bytes: low nibble = sub-block 2p, high
 // nibble = sub-block 2p+1; the 5th bit of sub-block b, weight l is bit b of qh[l]. Thread t holds weights 8t..8t+7
 // of each sub-block (one 8-byte load per row and pair). Q4_K feeds the high nibbles unshifted (16 x the code) into
 // the MMA and divides that accumulator by 16 once per super-block (exact: every term is a multiple of 16).
-// Scale record: int32 sc[8] | u32 min replicated x4 [8] | f32 d, dmin.
+// Scale record: int32 sc[8] | the 8 mins as bytes (2 words) | f32 d, dmin.
 template <bool Q5>
 struct DecK45 {
     static constexpr int  BS   = Q5 ? 176 : 144;
-    static constexpr int  KC   = 1;
-    static constexpr int  RECB = 80;
+    static constexpr int  KC   = 2;
+    static constexpr int  RECB = 48;
     static constexpr bool Q80  = false;
     static constexpr int  QS   = Q5 ? 48 : 16;
 
@@ -327,13 +349,11 @@ struct DecK45 {
         const uint32_t s0 = lds32(blk + 4), s1 = lds32(blk + 8), s2 = lds32(blk + 12);
         const uint32_t sl = s0 & 0x3F3F3F3Fu, sh = (s2 & 0x0F0F0F0Fu) | ((s0 >> 2) & 0x30303030u);
         const uint32_t ml = s1 & 0x3F3F3F3Fu, mh = ((s2 >> 4) & 0x0F0F0F0Fu) | ((s1 >> 2) & 0x30303030u);
-        int4 *  ri = reinterpret_cast<int4 *>(rec);
-        uint4 * ru = reinterpret_cast<uint4 *>(rec);
-        ri[0] = make_int4(ubyte(sl, 0), ubyte(sl, 1), ubyte(sl, 2), ubyte(sl, 3));
-        ri[1] = make_int4(ubyte(sh, 0), ubyte(sh, 1), ubyte(sh, 2), ubyte(sh, 3));
-        ru[2] = make_uint4(rep_byte(ml, 0), rep_byte(ml, 1), rep_byte(ml, 2), rep_byte(ml, 3));
-        ru[3] = make_uint4(rep_byte(mh, 0), rep_byte(mh, 1), rep_byte(mh, 2), rep_byte(mh, 3));
-        *reinterpret_cast<float2 *>(rec + 64) = make_float2(ldh(blk), ldh(blk + 2));
+        int4 * ri = reinterpret_cast<int4 *>(rec);
+        ri[0]     = make_int4(ubyte(sl, 0), ubyte(sl, 1), ubyte(sl, 2), ubyte(sl, 3));
+        ri[1]     = make_int4(ubyte(sh, 0), ubyte(sh, 1), ubyte(sh, 2), ubyte(sh, 3));
+        const float2 dd = make_float2(ldh(blk), ldh(blk + 2));
+        ri[2] = make_int4((int) ml, (int) mh, __float_as_int(dd.x), __float_as_int(dd.y));
     }
 
     __device__ __forceinline__ static uint32_t hbit(uint32_t qh, int b) { return ((qh >> b) << 4) & 0x10101010u; }
@@ -345,7 +365,7 @@ struct DecK45 {
         constexpr int NT = 8 * NG;
         const int     t = lane & 3, g = lane >> 2;
         const int4    scA[2] = { lds128i(ra), lds128i(ra + 16) }, scB[2] = { lds128i(rb), lds128i(rb + 16) };
-        const uint4   mnA[2] = { lds128u(ra + 32), lds128u(ra + 48) }, mnB[2] = { lds128u(rb + 32), lds128u(rb + 48) };
+        const int4    tA = lds128i(ra + 32), tB = lds128i(rb + 32);  // mins (2 words), d, dmin
         uint2         ha = make_uint2(0, 0), hb = make_uint2(0, 0);
         if constexpr (Q5) {
             ha = lds64(wa + 16 + 8 * t);
@@ -354,7 +374,7 @@ struct DecK45 {
         int im[NG][4], ih[NG][4], in[NG][4];
         zero<NG>(im);
         zero<NG>(ih);
-        zero<NG>(in);
+        mins_mma<NG>(in, (uint32_t) tA.x, (uint32_t) tA.y, (uint32_t) tB.x, (uint32_t) tB.y, xr, lane);
 #pragma unroll
         for (int p = 0; p < 4; p++) {
             const uint2 va = lds64(wa + QS + 32 * p + 8 * t);
@@ -375,8 +395,7 @@ struct DecK45 {
                     a1 = vb.x & m;
                     a3 = vb.y & m;
                 }
-                const int      sA = sel4(scA[b >> 2], b & 3), sB = sel4(scB[b >> 2], b & 3);
-                const uint32_t mA = sel4(mnA[b >> 2], b & 3), mB = sel4(mnB[b >> 2], b & 3);
+                const int sA = sel4(scA[b >> 2], b & 3), sB = sel4(scB[b >> 2], b & 3);
 #pragma unroll
                 for (int grp = 0; grp < NG; grp++) {
                     const uint2 x = lds64(xr + (8 * grp + g) * kTokStride + 32 * b + 8 * t);
@@ -387,7 +406,6 @@ struct DecK45 {
                     } else {
                         scale_acc<NG>(im, grp, sA, sB, c);
                     }
-                    mma_k32<true>(in[grp], mA, mB, mA, mB, x.x, x.y);
                 }
             }
         }
@@ -403,8 +421,8 @@ struct DecK45 {
             dbg_store<NG>(dbg, in, true, rg, sbi, lane);
         } else {
             const float * xs = reinterpret_cast<const float *>(xr + NT * kTokStride);
-            const float2  dA = ldsf2(ra + 64), dB = ldsf2(rb + 64);
-            sb_update<NG, true>(acc, im, in, dA.x, dB.x, dA.y, dB.y, xs, t);
+            sb_update<NG, true>(acc, im, in, __int_as_float(tA.z), __int_as_float(tB.z), __int_as_float(tA.w),
+                                __int_as_float(tB.w), xs, t);
         }
     }
 };
@@ -483,7 +501,7 @@ struct DecQ6K {
 // Scale record: int32 sc[16] | f32 d.
 struct DecQ3K {
     static constexpr int  BS   = 110;
-    static constexpr int  KC   = 1;
+    static constexpr int  KC   = 2;
     static constexpr int  RECB = 80;
     static constexpr bool Q80  = false;
 
@@ -552,7 +570,7 @@ struct DecQ3K {
 // Scale record: int32 sc[8] | f32 d.
 struct DecIQ4XS {
     static constexpr int  BS   = 136;
-    static constexpr int  KC   = 1;
+    static constexpr int  KC   = 2;
     static constexpr int  RECB = 48;
     static constexpr bool Q80  = false;
 
@@ -837,7 +855,7 @@ __device__ __forceinline__ const uint8_t * row_ptr(const GemmArgs & a, const uin
 }
 
 template <class D, int NG, bool DBG>
-__global__ void __launch_bounds__(kThreads, 4) srv_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
+__global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
                                                             const GemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t * full   = reinterpret_cast<uint64_t *>(smem);
@@ -847,7 +865,7 @@ __global__ void __launch_bounds__(kThreads, 4) srv_gemm_kernel(const __grid_cons
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.S; s++) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kNCW);
+            mbar_init(&empty[s], kNCW * 32);
         }
         fence_mbar_init();
     }
@@ -894,7 +912,10 @@ __global__ void __launch_bounds__(kThreads, 4) srv_gemm_kernel(const __grid_cons
                 if (lane == 0) atomicExch(a.status, kErrWaitFull);
                 bad = true;
             }
-            if (bad) continue;
+            if (bad) {
+                mbar_arrive(&empty[slot]);
+                continue;
+            }
             const uint8_t * st  = stage0 + (size_t) slot * a.stage_bytes;
             const int       sb0 = sbA + c * a.kc, kcc = min(a.kc, sbB - sb0);
             const uint8_t * wa;
@@ -910,9 +931,12 @@ __global__ void __launch_bounds__(kThreads, 4) srv_gemm_kernel(const __grid_cons
                 wb = row_ptr<D>(a, st, row0, rl + 8, sb0);
                 wp = row_ptr<D>(a, st, row0, warp * 16 + (lane & 15), sb0);
             }
-            // scale records of this warp's 16 rows x kcc super-blocks, one (row, super-block) per lane
-            if (lane < 16) D::prep(wp, scr + lane * D::RECB);
-            for (int kb = 1 + (lane >> 4); kb < kcc; kb += 2) D::prep(wp + kb * D::BS, scr + (kb * 16 + (lane & 15)) * D::RECB);
+            // scale records of this warp's 16 rows x kcc super-blocks, one (row, super-block) per lane: lane l takes
+            // row l & 15 of super-block l >> 4 (clamped to the chunk, so every lane runs the same code)
+            {
+                const int kb = min(lane >> 4, kcc - 1);
+                D::prep(wp + kb * D::BS, scr + (kb * 16 + (lane & 15)) * D::RECB);
+            }
             __syncwarp();
             const uint8_t * xr = st + a.rec_off;
 #pragma unroll
@@ -923,8 +947,7 @@ __global__ void __launch_bounds__(kThreads, 4) srv_gemm_kernel(const __grid_cons
                                             sb0 + kb);
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
+            mbar_arrive(&empty[slot]);  // every consumer thread arrives: no divergent branch per stage
         }
         if constexpr (!DBG) {
             if (a.ksplit == 1) {
@@ -982,286 +1005,6 @@ __global__ void __launch_bounds__(kThreads, 4) srv_gemm_kernel(const __grid_cons
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// direct-load kernel for the types whose blocks keep 8- or 16-byte alignment (Q4_K, Q5_K, IQ4_XS)
-//
-// No shared-memory ring: each warp streams its 16 weight rows straight into registers with non-allocating 64/128-bit
-// loads, two super-blocks ahead of the one it multiplies (the register file is the staging buffer). The activation
-// records of the CTA's K range sit in shared memory for the whole kernel. Work units, split K and the fix-up are those
-// of srv_gemm_kernel.
-
-// Q4_K / Q5_K minimum term of one super-block through one MMA pair over k = sub-block index: A = the 8 6-bit mins
-// of each row (thread t = 0 holds sub-blocks 0..3, t = 1 holds 4..7, others zero), B = the per-sub-block activation
-// sums split as s = 128 hi + lo (int8 each, from the record's padding). Returns sum_b m_b * s_b.
-template <int NG>
-__device__ __forceinline__ void mins_mma(int (&in)[NG][4], uint32_t mlA, uint32_t mhA, uint32_t mlB, uint32_t mhB,
-                                         const uint8_t * xr, int lane) {
-    const int      t  = lane & 3, g = lane >> 2;
-    const uint32_t a0 = t == 0 ? mlA : t == 1 ? mhA : 0u;
-    const uint32_t a1 = t == 0 ? mlB : t == 1 ? mhB : 0u;
-#pragma unroll
-    for (int grp = 0; grp < NG; grp++) {
-        const uint8_t * tok = xr + (8 * grp + g) * kTokStride;
-        const uint32_t  bh  = t < 2 ? lds32(tok + 256 + 4 * t) : 0u;
-        const uint32_t  bl  = t < 2 ? lds32(tok + 264 + 4 * t) : 0u;
-        int             ch[4], cl[4];
-        mma_k32_z<true>(ch, a0, a1, 0u, 0u, bh, 0u);
-        mma_k32_z<true>(cl, a0, a1, 0u, 0u, bl, 0u);
-#pragma unroll
-        for (int e = 0; e < 4; e++) in[grp][e] = ch[e] * 128 + cl[e];
-    }
-}
-
-template <bool Q5>
-struct DirK45 {
-    static constexpr int  BS  = Q5 ? 176 : 144;
-    static constexpr int  QS  = Q5 ? 48 : 16;
-    static constexpr bool Q80 = false;
-    struct Frag {
-        uint4 h[2];     // d | dmin, 12 bytes of scales / mins (rows g, g + 8)
-        uint2 q[2][4];  // code bytes 8t..8t+7 of each sub-block pair
-        uint2 qh[2];    // Q5_K: 5th-bit bytes 8t..8t+7
-    };
-
-    __device__ __forceinline__ static void load(Frag & f, const uint8_t * ra, const uint8_t * rb, int t) {
-        f.h[0] = ldg_stream128(ra);
-        f.h[1] = ldg_stream128(rb);
-#pragma unroll
-        for (int p = 0; p < 4; p++) {
-            f.q[0][p] = ldg_stream64(ra + QS + 32 * p + 8 * t);
-            f.q[1][p] = ldg_stream64(rb + QS + 32 * p + 8 * t);
-        }
-        if constexpr (Q5) {
-            f.qh[0] = ldg_stream64(ra + 16 + 8 * t);
-            f.qh[1] = ldg_stream64(rb + 16 + 8 * t);
-        }
-    }
-
-    template <int NG, bool DBG>
-    __device__ __forceinline__ static void compute(const Frag & f, const uint8_t * xr, int lane, float (&acc)[NG][4],
-                                                   const DbgOut & dbg, int64_t rg, int sbi) {
-        constexpr int NT = 8 * NG;
-        const int     t = lane & 3, g = lane >> 2;
-        uint32_t      sl[2], sh[2], ml[2], mh[2];
-#pragma unroll
-        for (int r = 0; r < 2; r++) {
-            const uint32_t w1 = f.h[r].y, w2 = f.h[r].z, w3 = f.h[r].w;
-            sl[r] = w1 & 0x3F3F3F3Fu;
-            sh[r] = (w3 & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u);
-            ml[r] = w2 & 0x3F3F3F3Fu;
-            mh[r] = ((w3 >> 4) & 0x0F0F0F0Fu) | ((w2 >> 2) & 0x30303030u);
-        }
-        int im[NG][4], ih[NG][4], in[NG][4];
-        zero<NG>(im);
-        zero<NG>(ih);
-        mins_mma<NG>(in, ml[0], mh[0], ml[1], mh[1], xr, lane);
-#pragma unroll
-        for (int p = 0; p < 4; p++) {
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const int b = 2 * p + h;
-                uint32_t  a0, a1, a2, a3;
-                if constexpr (Q5) {
-                    a0 = ((f.q[0][p].x >> (4 * h)) & 0x0F0F0F0Fu) | DecK45<true>::hbit(f.qh[0].x, b);
-                    a2 = ((f.q[0][p].y >> (4 * h)) & 0x0F0F0F0Fu) | DecK45<true>::hbit(f.qh[0].y, b);
-                    a1 = ((f.q[1][p].x >> (4 * h)) & 0x0F0F0F0Fu) | DecK45<true>::hbit(f.qh[1].x, b);
-                    a3 = ((f.q[1][p].y >> (4 * h)) & 0x0F0F0F0Fu) | DecK45<true>::hbit(f.qh[1].y, b);
-                } else {
-                    const uint32_t m = h ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
-                    a0 = f.q[0][p].x & m;
-                    a2 = f.q[0][p].y & m;
-                    a1 = f.q[1][p].x & m;
-                    a3 = f.q[1][p].y & m;
-                }
-                const int sA = ubyte(b < 4 ? sl[0] : sh[0], b & 3), sB = ubyte(b < 4 ? sl[1] : sh[1], b & 3);
-#pragma unroll
-                for (int grp = 0; grp < NG; grp++) {
-                    const uint2 x = lds64(xr + (8 * grp + g) * kTokStride + 32 * b + 8 * t);
-                    int         c[4];
-                    mma_k32_z<true>(c, a0, a1, a2, a3, x.x, x.y);
-                    if (!Q5 && h) {
-                        scale_acc<NG>(ih, grp, sA, sB, c);
-                    } else {
-                        scale_acc<NG>(im, grp, sA, sB, c);
-                    }
-                }
-            }
-        }
-        if constexpr (!Q5) {
-#pragma unroll
-            for (int grp = 0; grp < NG; grp++) {
-#pragma unroll
-                for (int e = 0; e < 4; e++) im[grp][e] += ih[grp][e] >> 4;
-            }
-        }
-        if constexpr (DBG) {
-            dbg_store<NG>(dbg, im, false, rg, sbi, lane);
-            dbg_store<NG>(dbg, in, true, rg, sbi, lane);
-        } else {
-            const float * xs = reinterpret_cast<const float *>(xr + NT * kTokStride);
-            const float2  dA = __half22float2(*reinterpret_cast<const __half2 *>(&f.h[0].x));
-            const float2  dB = __half22float2(*reinterpret_cast<const __half2 *>(&f.h[1].x));
-            sb_update<NG, true>(acc, im, in, dA.x, dB.x, dA.y, dB.y, xs, t);
-        }
-    }
-};
-
-struct DirIQ4XS {
-    static constexpr int  BS  = 136;
-    static constexpr bool Q80 = false;
-    struct Frag {
-        uint2    h[2];     // d | scales_h, scales_l
-        uint32_t q[2][8];  // code bytes 4t..4t+3 of each sub-block
-    };
-
-    __device__ __forceinline__ static void load(Frag & f, const uint8_t * ra, const uint8_t * rb, int t) {
-        f.h[0] = ldg_stream64(ra);
-        f.h[1] = ldg_stream64(rb);
-#pragma unroll
-        for (int b = 0; b < 8; b++) {
-            f.q[0][b] = ldg_stream32(ra + 8 + 16 * b + 4 * t);
-            f.q[1][b] = ldg_stream32(rb + 8 + 16 * b + 4 * t);
-        }
-    }
-
-    template <int NG, bool DBG>
-    __device__ __forceinline__ static void compute(const Frag & f, const uint8_t * xr, int lane, float (&acc)[NG][4],
-                                                   const DbgOut & dbg, int64_t rg, int sbi) {
-        constexpr int NT = 8 * NG;
-        const int     t = lane & 3, g = lane >> 2;
-        const uint32_t HA = f.h[0].x >> 16, LA = f.h[0].y, HB = f.h[1].x >> 16, LB = f.h[1].y;
-        int            im[NG][4], in[NG][4];
-        zero<NG>(im);
-        zero<NG>(in);
-#pragma unroll
-        for (int b = 0; b < 8; b++) {
-            const int sA = (int) (((LA >> (4 * b)) & 0xFu) | (((HA >> (2 * b)) & 3u) << 4)) - 32;
-            const int sB = (int) (((LB >> (4 * b)) & 0xFu) | (((HB >> (2 * b)) & 3u) << 4)) - 32;
-            uint32_t  a0, a2, a1, a3;
-            DecIQ4XS::lookup(f.q[0][b], a0, a2);
-            DecIQ4XS::lookup(f.q[1][b], a1, a3);
-#pragma unroll
-            for (int grp = 0; grp < NG; grp++) {
-                const uint8_t * xp = xr + (8 * grp + g) * kTokStride + 32 * b + 4 * t;
-                int             c[4];
-                mma_k32_z<false>(c, a0, a1, a2, a3, lds32(xp), lds32(xp + 16));
-                scale_acc<NG>(im, grp, sA, sB, c);
-            }
-        }
-        if constexpr (DBG) {
-            dbg_store<NG>(dbg, im, false, rg, sbi, lane);
-        } else {
-            const float * xs = reinterpret_cast<const float *>(xr + NT * kTokStride);
-            const float   dA = __half2float(__ushort_as_half((unsigned short) (f.h[0].x & 0xffffu)));
-            const float   dB = __half2float(__ushort_as_half((unsigned short) (f.h[1].x & 0xffffu)));
-            sb_update<NG, false>(acc, im, in, dA, dB, 0.f, 0.f, xs, t);
-        }
-    }
-};
-
-template <class D, int NG, bool DBG>
-__global__ void __launch_bounds__(128, 4) srv_gemm_direct(const GemmArgs a) {
-    extern __shared__ __align__(16) uint8_t xsm[];  // activation records of this CTA's K range
-    constexpr int  RB   = rec_bytes(D::Q80, 8 * NG);
-    const int      warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int      kr   = blockIdx.x % a.ksplit;
-    const int      sbA  = kr * a.kr_sbs, sbB = min(a.nsb, sbA + a.kr_sbs), nk = sbB - sbA;
-    const DbgOut   dbg  = { a.isum, a.imin, a.rows, a.N, a.nblk };
-    __shared__ int last_flag;
-    typename D::Frag f0, f1, f2;
-    auto rowp = [&](int64_t row0, int r) -> const uint8_t * {
-        const int64_t R = min(row0 + warp * 16 + r, a.rows - 1);  // rows past the matrix re-read the last one
-        return a.W + R * a.row_bytes + (int64_t) sbA * D::BS;
-    };
-    auto load = [&](typename D::Frag & f, int64_t row0, int k) {
-        if (k < nk) D::load(f, rowp(row0, g) + k * D::BS, rowp(row0, g + 8) + k * D::BS, t);
-    };
-    // the first unit's first super-blocks are requested before the quantizer grid has finished
-    int u = blockIdx.x;
-    if (u < a.units) {
-        const int64_t row0 = (int64_t) (u / a.ksplit) * kTileRows;
-        load(f0, row0, 0);
-        load(f1, row0, 1);
-    }
-    pdl_launch_dependents();
-    pdl_wait();
-    {
-        const uint4 * src = reinterpret_cast<const uint4 *>(a.recs + (size_t) sbA * RB);
-        uint4 *       dst = reinterpret_cast<uint4 *>(xsm);
-        for (int i = threadIdx.x; i < nk * RB / 16; i += blockDim.x) dst[i] = src[i];
-    }
-    __syncthreads();
-    bool first = true;
-    for (; u < a.units; u += gridDim.x) {
-        const int64_t rb = u / a.ksplit, row0 = rb * kTileRows, rg = row0 + warp * 16 + g;
-        if (!first) {
-            load(f0, row0, 0);
-            load(f1, row0, 1);
-        }
-        first = false;
-        float acc[NG][4];
-#pragma unroll
-        for (int grp = 0; grp < NG; grp++) acc[grp][0] = acc[grp][1] = acc[grp][2] = acc[grp][3] = 0.0f;
-        // three-slot register ring, two super-blocks in flight
-        for (int k = 0; k < nk; k += 3) {
-            load(f2, row0, k + 2);
-            D::template compute<NG, DBG>(f0, xsm + k * RB, lane, acc, dbg, rg, sbA + k);
-            if (k + 1 >= nk) break;
-            load(f0, row0, k + 3);
-            D::template compute<NG, DBG>(f1, xsm + (k + 1) * RB, lane, acc, dbg, rg, sbA + k + 1);
-            if (k + 2 >= nk) break;
-            load(f1, row0, k + 4);
-            D::template compute<NG, DBG>(f2, xsm + (k + 2) * RB, lane, acc, dbg, rg, sbA + k + 2);
-        }
-        if constexpr (!DBG) {
-            if (a.ksplit == 1) {
-#pragma unroll
-                for (int grp = 0; grp < NG; grp++) {
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const int     tok = 8 * grp + 2 * t + (e & 1);
-                        const int64_t row = e < 2 ? rg : rg + 8;
-                        if (tok < a.N && row < a.rows) a.Y[(int64_t) tok * a.ldy + row] = acc[grp][e];
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int grp = 0; grp < NG; grp++) {
-#pragma unroll
-                    for (int e = 0; e < 4; e++) {
-                        const int     tok = 8 * grp + 2 * t + (e & 1);
-                        const int64_t row = e < 2 ? rg : rg + 8;
-                        if (tok < a.N && row < a.rows) a.part[((int64_t) kr * a.N + tok) * a.rows + row] = acc[grp][e];
-                    }
-                }
-                __threadfence();
-                __syncthreads();
-                if (threadIdx.x == 0) last_flag = atomicAdd(&a.cnt[rb], 1) == a.ksplit - 1;
-                __syncthreads();
-                if (last_flag) {
-                    __threadfence();
-#pragma unroll
-                    for (int grp = 0; grp < NG; grp++) {
-#pragma unroll
-                        for (int e = 0; e < 4; e++) {
-                            const int     tok = 8 * grp + 2 * t + (e & 1);
-                            const int64_t row = e < 2 ? rg : rg + 8;
-                            if (tok < a.N && row < a.rows) {
-                                float sum = 0.0f;
-                                for (int k = 0; k < a.ksplit; k++) {
-                                    sum += __ldcg(&a.part[((int64_t) k * a.N + tok) * a.rows + row]);
-                                }
-                                a.Y[(int64_t) tok * a.ldy + row] = sum;
-                            }
-                        }
-                    }
-                }
-                __syncthreads();  // last_flag is rewritten by the next unit
-            }
-        }
-    }
-}
-
-// ---------------------------------------------------------------------------------------------------------------
 // host side
 
 int slot_stride(int need) {
@@ -1308,8 +1051,8 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     a.rec_off          = (a.left_off + (a.G > 1 ? (a.G - 1) * a.LSR : 0) + 127) / 128 * 128;
     a.stage_bytes      = (a.rec_off + a.kc * RB + 127) / 128 * 128;
     const int scr      = kNCW * D::KC * 16 * D::RECB;
-    // 4 stages while that keeps 4 CTAs per SM resident, else 3
-    a.S = kBarBytes + 4 * a.stage_bytes + scr <= 56 * 1024 ? 4 : 3;
+    // 4 stages while that keeps 2 CTAs per SM resident, else 3
+    a.S = kBarBytes + 4 * a.stage_bytes + scr <= 110 * 1024 ? 4 : 3;
     a.scr_off         = kBarBytes + a.S * a.stage_bytes;
     const size_t smem = (size_t) a.scr_off + scr;
     if (smem > 200 * 1024 || a.Wbox > 1024) return SRHPM_ERR_INVALID;
@@ -1368,62 +1111,6 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     cfg.numAttrs                                       = 1;
     ctx->launches.fetch_add(1);
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, wmap, a));
-}
-
-template <class D, int NG, bool DBG>
-int launch_direct(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
-    constexpr int RB   = rec_bytes(D::Q80, 8 * NG);
-    auto          kern = srv_gemm_direct<D, NG, DBG>;
-    static std::atomic<unsigned> attr_done{ 0 };
-    int                          dev = 0;
-    cudaGetDevice(&dev);
-    if (!(attr_done.load() & (1u << (dev & 31)))) {
-        const int st = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        if (st != SRHPM_OK) return st;
-        attr_done.fetch_or(1u << (dev & 31));
-    }
-    const int64_t nrb = (a.rows + kTileRows - 1) / kTileRows;
-    // K ranges: the resident records of a range stay within ~50 KB (4 CTAs per SM), and the units fill the slots
-    const int max_sbs = std::max(1, (50 * 1024) / RB);
-    const int min_split = (a.nsb + max_sbs - 1) / max_sbs;
-    const int slots     = 4 * ctx->num_sms;
-    a.ksplit            = 1;
-    if (!DBG && a.part) {
-        const int want = (int) ((slots + nrb / 2) / nrb);
-        a.ksplit       = std::max(min_split, std::max(1, std::min({ want, kMaxSplit, a.nsb / 2 })));
-    } else {
-        a.ksplit = min_split;
-    }
-    a.kr_sbs          = (a.nsb + a.ksplit - 1) / a.ksplit;
-    a.ksplit          = (a.nsb + a.kr_sbs - 1) / a.kr_sbs;
-    a.units           = (int) (nrb * a.ksplit);
-    const size_t smem = (size_t) a.kr_sbs * RB;
-    int          per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 128, smem);
-    const int s2     = std::max(1, per_sm) * ctx->num_sms;
-    const int rounds = (a.units + s2 - 1) / s2;
-    int       grid   = (a.units + rounds - 1) / rounds;
-    grid             = (grid + a.ksplit - 1) / a.ksplit * a.ksplit;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim            = dim3((unsigned) grid);
-    cfg.blockDim           = dim3(128);
-    cfg.dynamicSmemBytes   = smem;
-    cfg.stream             = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs                                          = attr;
-    cfg.numAttrs                                       = 1;
-    ctx->launches.fetch_add(1);
-    return cuda_status(cudaLaunchKernelEx(&cfg, kern, a));
-}
-
-template <class D>
-int dispatch_direct(srhpm_ctx * ctx, const GemmArgs & a, bool dbg, cudaStream_t stream) {
-    if (a.N <= 8) {
-        return dbg ? launch_direct<D, 1, true>(ctx, a, stream) : launch_direct<D, 1, false>(ctx, a, stream);
-    }
-    return dbg ? launch_direct<D, 2, true>(ctx, a, stream) : launch_direct<D, 2, false>(ctx, a, stream);
 }
 
 template <class D>
@@ -1519,11 +1206,11 @@ int gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_
     a.nblk      = q80 ? nsb * 8 : nsb;
     const bool dbg = isum != nullptr;
     switch (wtype) {
-        case SRHPM_TYPE_Q4_K: return dispatch_direct<DirK45<false>>(ctx, a, dbg, stream);
-        case SRHPM_TYPE_Q5_K: return dispatch_direct<DirK45<true>>(ctx, a, dbg, stream);
+        case SRHPM_TYPE_Q4_K: return dispatch_ng<DecK45<false>>(ctx, a, dbg, stream);
+        case SRHPM_TYPE_Q5_K: return dispatch_ng<DecK45<true>>(ctx, a, dbg, stream);
         case SRHPM_TYPE_Q6_K: return dispatch_ng<DecQ6K>(ctx, a, dbg, stream);
         case SRHPM_TYPE_Q3_K: return dispatch_ng<DecQ3K>(ctx, a, dbg, stream);
-        case SRHPM_TYPE_IQ4_XS: return dispatch_direct<DirIQ4XS>(ctx, a, dbg, stream);
+        case SRHPM_TYPE_IQ4_XS: return dispatch_ng<DecIQ4XS>(ctx, a, dbg, stream);
         case SRHPM_TYPE_Q8_0: return dispatch_ng<DecQ80>(ctx, a, dbg, stream);
         default: return SRHPM_UNSUPPORTED;
     }
