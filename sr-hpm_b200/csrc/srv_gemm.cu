@@ -855,7 +855,7 @@ __device__ __forceinline__ const uint8_t * row_ptr(const GemmArgs & a, const uin
 }
 
 template <class D, int NG, bool DBG>
-__global__ void __launch_bounds__(kThreads, 3) srv_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
+__global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
                                                             const GemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t * full   = reinterpret_cast<uint64_t *>(smem);
@@ -1051,9 +1051,9 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     a.rec_off          = (a.left_off + (a.G > 1 ? (a.G - 1) * a.LSR : 0) + 127) / 128 * 128;
     a.stage_bytes      = (a.rec_off + a.kc * RB + 127) / 128 * 128;
     const int scr      = kNCW * D::KC * 16 * D::RECB;
-    // ring depth: 3 stages when that keeps 3 CTAs per SM resident (more warps to hide latency), else 4 stages at
-    // 2 CTAs per SM (228 KB of shared memory per SM, 1 KB of it reserved per CTA)
-    a.S = kBarBytes + 3 * a.stage_bytes + scr <= 75 * 1024 ? 3 : 4;
+    // 4 stages while that keeps 2 CTAs per SM resident, else 3 (228 KB of shared memory per SM, 1 KB of it reserved
+    // per CTA). A measured alternative, 3 CTAs per SM with 3 stages, streamed slower.
+    a.S = kBarBytes + 4 * a.stage_bytes + scr <= 110 * 1024 ? 4 : 3;
     a.scr_off         = kBarBytes + a.S * a.stage_bytes;
     const size_t smem = (size_t) a.scr_off + scr;
     if (smem > 200 * 1024 || a.Wbox > 1024) return SRHPM_ERR_INVALID;
