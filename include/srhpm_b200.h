@@ -46,6 +46,7 @@ enum srhpm_status {
     SRHPM_ERR_WORKSPACE  = -3, /* wdata missing or smaller than *_work_size */
     SRHPM_ERR_CUDA       = -4, /* a CUDA runtime call failed (srhpm_last_cuda_error has the code) */
     SRHPM_ERR_DEVICE     = -5, /* a kernel reported an error through the context's status word */
+    SRHPM_ERR_TOO_LARGE  = -6, /* the product needs more scratch than srhpm_mul_mat_static's fixed buffer holds */
 };
 
 /* q8_0 activation quantizer used for Q8_0 weights and for Q against a q8_0 KV cache (the upstream ggml-cpu quantizer
@@ -98,6 +99,17 @@ int srhpm_mul_mat(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * 
  * layout; may be NULL otherwise). Same kernels and decoders as srhpm_mul_mat. No reference counterpart (test hook). */
 int srhpm_mul_mat_isums(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, int32_t * isum,
                         int32_t * imin, void * wdata, size_t wsize, void * stream);
+
+/* srhpm_mul_mat without a work buffer, for callers that cannot allocate device memory: a host framework that hands
+ * out only the tensors it owns (no scratch per operation), or a latency-critical decode loop where a cudaMalloc
+ * would synchronise the device. The scratch is a fixed 1 MiB array inside the library on every device that loads
+ * it, kept until the process exits; products are not split along K here. Limit: the activation records and row-block
+ * counters of the product must fit 1 MiB (for K up to 32768 and N up to 16 that leaves room for 6 million weight
+ * rows); beyond that the call returns SRHPM_ERR_TOO_LARGE and does nothing. The first call on a device looks up the array's device address
+ * (make it before any stream capture). All calls share the array: calls whose work overlaps on the GPU race.
+ * Allocates nothing. No counterpart in the reference. */
+int srhpm_mul_mat_static(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, srhpm_tensor * Y,
+                         void * stream);
 
 /* Activation quantizer, row by row: X f32 [K, N] -> q int8 [N][K], d f32 [N][K/256], bsum32 int16 [N][K/32],
  * bsum16 int16 [N][K/16] (dense, device; bsum pointers may be NULL). Bit-identical to srv_quantize_row

@@ -136,6 +136,7 @@ const char * srhpm_status_str(int status) {
         case SRHPM_ERR_WORKSPACE: return "work buffer missing or too small";
         case SRHPM_ERR_CUDA: return "CUDA runtime error";
         case SRHPM_ERR_DEVICE: return "a kernel reported an error";
+        case SRHPM_ERR_TOO_LARGE: return "product too large for the static work buffer";
         default: return "unknown status";
     }
 }
@@ -194,6 +195,16 @@ int srhpm_mul_mat(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * 
     return gemm_run(ctx, W->type, (const uint8_t *) W->data, W->ne[1], W->ne[0], W->nb[1], (const float *) X->data,
                     (int64_t) (X->nb[1] / 4), X->ne[1], (float *) Y->data, (int64_t) (Y->nb[1] / 4), wdata, wsize,
                     nullptr, nullptr, (cudaStream_t) stream);
+}
+
+int srhpm_mul_mat_static(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, srhpm_tensor * Y,
+                         void * stream) {
+    if (!ctx || !Y) return SRHPM_ERR_INVALID;
+    const int st = check_mul_mat(W, X, Y);
+    if (st != SRHPM_OK) return st;
+    return gemm_run_static(ctx, W->type, (const uint8_t *) W->data, W->ne[1], W->ne[0], W->nb[1],
+                           (const float *) X->data, (int64_t) (X->nb[1] / 4), X->ne[1], (float *) Y->data,
+                           (int64_t) (Y->nb[1] / 4), (cudaStream_t) stream);
 }
 
 int srhpm_mul_mat_isums(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, int32_t * isum,

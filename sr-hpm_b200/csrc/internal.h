@@ -36,9 +36,18 @@ size_t gemm_work_size(int wtype, int64_t rows, int64_t K, int64_t N);
 int    gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                 const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
                 int32_t * isum, int32_t * imin, cudaStream_t stream);
+size_t gemm_work_size_unsplit(int wtype, int64_t rows, int64_t K, int64_t N);
+int    gemm_run_unsplit(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
+                        const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
+                        cudaStream_t stream);
 int    quantize_q8K_dense(srhpm_ctx * ctx, const float * X, int64_t ldx, int64_t N, int64_t K, int8_t * q, float * d,
                           int16_t * b32, int16_t * b16, cudaStream_t stream);
 int    quantize_q8_0_dense(srhpm_ctx * ctx, const float * X, int64_t ldx, int64_t N, int64_t K, void * blocks,
                            cudaStream_t stream);
+
+// static_work.cu
+size_t static_work_bytes();
+int    gemm_run_static(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
+                       const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, cudaStream_t stream);
 
 }  // namespace srhpm

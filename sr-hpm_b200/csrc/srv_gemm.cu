@@ -228,8 +228,6 @@ __global__ void __launch_bounds__(256) quant_q80_kernel(const float * __restrict
 __device__ __forceinline__ uint32_t lds32(const uint8_t * p) { return *reinterpret_cast<const uint32_t *>(p); }
 __device__ __forceinline__ uint2    lds64(const uint8_t * p) { return *reinterpret_cast<const uint2 *>(p); }
 __device__ __forceinline__ int4     lds128i(const uint8_t * p) { return *reinterpret_cast<const int4 *>(p); }
-__device__ __forceinline__ uint4    lds128u(const uint8_t * p) { return *reinterpret_cast<const uint4 *>(p); }
-__device__ __forceinline__ float2   ldsf2(const uint8_t * p) { return *reinterpret_cast<const float2 *>(p); }
 __device__ __forceinline__ float    ldh(const uint8_t * p) { return half_bits_to_float(lds_u16(p)); }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -239,15 +237,11 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 }
 __device__ __forceinline__ int ubyte(uint32_t w, int j) { return (int) __byte_perm(w, 0u, 0x4440u | (uint32_t) j); }
 __device__ __forceinline__ int sbyte(uint32_t w, int j) { return ((int32_t) (w << (24 - 8 * j))) >> 24; }
-__device__ __forceinline__ uint32_t rep_byte(uint32_t w, int j) { return prmt(w, 0, 0x1111u * (uint32_t) j); }
 
 // per-byte a - k for bytes holding 0..127 (no borrow between bytes)
 __device__ __forceinline__ uint32_t vsub_small(uint32_t a, uint32_t k) { return ((a | 0x80808080u) - k) ^ 0x80808080u; }
 
 __device__ __forceinline__ int sel4(const int4 & v, int j) { return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w; }
-__device__ __forceinline__ uint32_t sel4(const uint4 & v, int j) {
-    return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
-}
 
 struct DbgOut {
     int32_t * isum;
@@ -1149,12 +1143,27 @@ WorkLayout work_layout(int wtype, int64_t rows, int64_t K, int64_t N) {
     return w;
 }
 
+// the same buffer without split-K partials (products are not split along K)
+WorkLayout work_layout_unsplit(int wtype, int64_t rows, int64_t K, int64_t N) {
+    WorkLayout w      = work_layout(wtype, rows, K, N);
+    const size_t cnts = w.total - w.cnt;
+    w.cnt             = w.part;
+    w.total           = w.cnt + cnts;
+    return w;
+}
+
 size_t gemm_work_size(int wtype, int64_t rows, int64_t K, int64_t N) { return work_layout(wtype, rows, K, N).total; }
 
-int gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
-             const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
-             int32_t * isum, int32_t * imin, cudaStream_t stream) {
-    const WorkLayout wl = work_layout(wtype, rows, K, N);
+size_t gemm_work_size_unsplit(int wtype, int64_t rows, int64_t K, int64_t N) {
+    return work_layout_unsplit(wtype, rows, K, N).total;
+}
+
+namespace {
+
+int gemm_run_impl(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
+                  const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
+                  int32_t * isum, int32_t * imin, bool split, cudaStream_t stream) {
+    const WorkLayout wl = split ? work_layout(wtype, rows, K, N) : work_layout_unsplit(wtype, rows, K, N);
     if (wsize < wl.total || !wdata) return SRHPM_ERR_WORKSPACE;
     const int  nsb  = (int) (K / QK);
     const int  NT   = N <= 8 ? 8 : 16;
@@ -1196,7 +1205,7 @@ int gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_
     a.w_bytes   = rows * (int64_t) row_bytes;
     a.nsb       = nsb;
     a.recs      = recs;
-    a.part      = reinterpret_cast<float *>(base + wl.part);
+    a.part      = split ? reinterpret_cast<float *>(base + wl.part) : nullptr;  // null: one K range
     a.cnt       = cnt;
     a.Y         = Y;
     a.ldy       = ldy;
@@ -1215,6 +1224,21 @@ int gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_
         case SRHPM_TYPE_Q8_0: return dispatch_ng<DecQ80>(ctx, a, dbg, stream);
         default: return SRHPM_UNSUPPORTED;
     }
+}
+
+}  // namespace
+
+int gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
+             const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
+             int32_t * isum, int32_t * imin, cudaStream_t stream) {
+    return gemm_run_impl(ctx, wtype, W, rows, K, row_bytes, X, ldx, N, Y, ldy, wdata, wsize, isum, imin, true, stream);
+}
+
+int gemm_run_unsplit(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
+                     const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
+                     cudaStream_t stream) {
+    return gemm_run_impl(ctx, wtype, W, rows, K, row_bytes, X, ldx, N, Y, ldy, wdata, wsize, nullptr, nullptr, false,
+                         stream);
 }
 
 int quantize_q8K_dense(srhpm_ctx * ctx, const float * X, int64_t ldx, int64_t N, int64_t K, int8_t * q, float * d,

@@ -18,7 +18,7 @@ TYPE_NAMES = {F32: "f32", F16: "f16", Q8_0: "q8_0", Q3_K: "q3_K", Q4_K: "q4_K", 
 TYPE_BY_NAME = {v.lower(): k for k, v in TYPE_NAMES.items()}
 
 OK, UNSUPPORTED = 0, 1
-ERR_INVALID, ERR_ALIGN, ERR_WORKSPACE, ERR_CUDA, ERR_DEVICE = -1, -2, -3, -4, -5
+ERR_INVALID, ERR_ALIGN, ERR_WORKSPACE, ERR_CUDA, ERR_DEVICE, ERR_TOO_LARGE = -1, -2, -3, -4, -5, -6
 Q8_0_ACT_SIMD, Q8_0_ACT_REF = 0, 1
 
 
@@ -54,6 +54,7 @@ _SIGNATURES = {
     "srhpm_mul_mat_work_size": (ctypes.c_int, [_T, _T, ctypes.POINTER(ctypes.c_size_t)]),
     "srhpm_mul_mat": (ctypes.c_int, [_P, _T, _T, _T, _P, ctypes.c_size_t, _P]),
     "srhpm_mul_mat_isums": (ctypes.c_int, [_P, _T, _T, _P, _P, _P, ctypes.c_size_t, _P]),
+    "srhpm_mul_mat_static": (ctypes.c_int, [_P, _T, _T, _T, _P]),
     "srhpm_quantize_rows_q8_K": (ctypes.c_int, [_P, _T, _P, _P, _P, _P, _P]),
     "srhpm_quantize_rows_q8_0": (ctypes.c_int, [_P, _T, _P, _P]),
     "srhpm_quantize_chunk": (ctypes.c_size_t, [ctypes.c_int, _P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
