@@ -63,6 +63,69 @@ int check_act(const srhpm_tensor * X) {
     return SRHPM_OK;
 }
 
+// ggml_flash_attn_ext(q, k, v, mask, sinks) contract of the reference's grouped path (patch/srhpm.patch:833-841) and
+// of this kernel: q f32 [DK, N, H], k / v q8_0 [256, L, Hkv] (token and head strides multiples of 16 bytes), mask f16
+// [>= L, >= N, ne2] broadcast over heads (h % ne2), sinks f32 [H], dst f32 [DV, H, N]
+int check_fa(const srhpm_tensor * q, const srhpm_tensor * k, const srhpm_tensor * v, const srhpm_tensor * mask,
+             const srhpm_tensor * sinks, const srhpm_tensor * dst, FaView * fv) {
+    if (!q || !k || !v) return SRHPM_ERR_INVALID;
+    if (q->type != SRHPM_TYPE_F32 || k->type != v->type) return SRHPM_UNSUPPORTED;
+    if (k->type != SRHPM_TYPE_Q8_0) return SRHPM_UNSUPPORTED;
+    if (q->ne[3] != 1 || k->ne[3] != 1 || v->ne[3] != 1) return SRHPM_UNSUPPORTED;
+    const int64_t DK = k->ne[0], DV = v->ne[0], L = k->ne[1], Hkv = k->ne[2], N = q->ne[1], H = q->ne[2];
+    if (q->ne[0] != DK) return SRHPM_ERR_INVALID;
+    if (DK != 256 || DV != 256) return SRHPM_UNSUPPORTED;
+    if (N < 1 || N > 16) return SRHPM_UNSUPPORTED;
+    if (L < 1 || L > INT32_MAX || Hkv < 1 || H < 1 || H > 65536 || H % Hkv != 0) return SRHPM_ERR_INVALID;
+    if (v->ne[1] != L || v->ne[2] != Hkv) return SRHPM_ERR_INVALID;
+    const size_t rowb = srhpm_row_size(SRHPM_TYPE_Q8_0, 256);
+    if (k->nb[0] != srhpm_type_size(k->type) || v->nb[0] != srhpm_type_size(v->type)) return SRHPM_ERR_INVALID;
+    if (k->nb[1] < rowb || v->nb[1] < rowb || k->nb[2] < rowb || v->nb[2] < rowb) return SRHPM_ERR_INVALID;
+    if (k->nb[1] % 16 || k->nb[2] % 16 || v->nb[1] % 16 || v->nb[2] % 16) return SRHPM_ERR_ALIGN;
+    if (!k->data || !v->data || !q->data) return SRHPM_ERR_INVALID;
+    if (!aligned(k->data, 16) || !aligned(v->data, 16) || !aligned(q->data, 4)) return SRHPM_ERR_ALIGN;
+    if (q->nb[0] != 4 || q->nb[1] % 4 || q->nb[2] % 4) return SRHPM_ERR_INVALID;
+    if (!dst || dst->type != SRHPM_TYPE_F32 || !dst->data) return SRHPM_ERR_INVALID;
+    if (dst->ne[0] != DV || dst->ne[1] != H || dst->ne[2] != N || dst->ne[3] != 1) return SRHPM_ERR_INVALID;
+    if (dst->nb[0] != 4 || dst->nb[1] % 4 || dst->nb[2] % 4 || !aligned(dst->data, 4)) return SRHPM_ERR_INVALID;
+    fv->mask = nullptr;
+    fv->mnb1 = fv->mnb2 = 0;
+    fv->mne2 = 1;
+    if (mask) {
+        if (mask->type != SRHPM_TYPE_F16 || !mask->data || mask->nb[0] != 2) return SRHPM_ERR_INVALID;
+        if (mask->ne[0] < L || mask->ne[1] < N || mask->ne[2] < 1 || mask->ne[3] != 1) return SRHPM_ERR_INVALID;
+        if (mask->nb[1] % 2 || mask->nb[2] % 2 || !aligned(mask->data, 2)) return SRHPM_ERR_ALIGN;
+        fv->mask = (const uint8_t *) mask->data;
+        fv->mnb1 = (int64_t) mask->nb[1];
+        fv->mnb2 = (int64_t) mask->nb[2];
+        fv->mne2 = (int) mask->ne[2];
+    }
+    fv->sinks = nullptr;
+    if (sinks) {
+        if (sinks->type != SRHPM_TYPE_F32 || sinks->ne[0] != H || sinks->nb[0] != 4 || !sinks->data) {
+            return SRHPM_ERR_INVALID;
+        }
+        fv->sinks = (const float *) sinks->data;
+    }
+    fv->q    = (const float *) q->data;
+    fv->qnb1 = (int64_t) q->nb[1];
+    fv->qnb2 = (int64_t) q->nb[2];
+    fv->N    = (int) N;
+    fv->H    = (int) H;
+    fv->k    = (const uint8_t *) k->data;
+    fv->knb1 = (int64_t) k->nb[1];
+    fv->knb2 = (int64_t) k->nb[2];
+    fv->v    = (const uint8_t *) v->data;
+    fv->vnb1 = (int64_t) v->nb[1];
+    fv->vnb2 = (int64_t) v->nb[2];
+    fv->L    = (int) L;
+    fv->Hkv  = (int) Hkv;
+    fv->dst  = (float *) dst->data;
+    fv->dnb1 = (int64_t) dst->nb[1];
+    fv->dnb2 = (int64_t) dst->nb[2];
+    return SRHPM_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -233,6 +296,37 @@ int srhpm_quantize_rows_q8_0(srhpm_ctx * ctx, const srhpm_tensor * X, void * blo
     if (!aligned(blocks, 2)) return SRHPM_ERR_ALIGN;
     return quantize_q8_0_dense(ctx, (const float *) X->data, (int64_t) (X->nb[1] / 4), X->ne[1], X->ne[0], blocks,
                                (cudaStream_t) stream);
+}
+
+int srhpm_flash_attn_ext_work_size(const srhpm_ctx * ctx, const srhpm_tensor * q, const srhpm_tensor * k,
+                                   const srhpm_tensor * v, size_t * size) {
+    if (!ctx || !size || !q || !k || !v) return SRHPM_ERR_INVALID;
+    FaView             fv;
+    srhpm_tensor       d = {};
+    d.type               = SRHPM_TYPE_F32;
+    d.ne[0]              = v->ne[0];
+    d.ne[1]              = q->ne[2];
+    d.ne[2]              = q->ne[1];
+    d.ne[3]              = 1;
+    d.nb[0]              = 4;
+    d.nb[1]              = 4 * (size_t) d.ne[0];
+    d.nb[2]              = d.nb[1] * (size_t) d.ne[1];
+    d.nb[3]              = d.nb[2] * (size_t) d.ne[2];
+    d.data               = (void *) 16;  // shape check only
+    const int st         = check_fa(q, k, v, nullptr, nullptr, &d, &fv);
+    if (st != SRHPM_OK) return st;
+    *size = fa_work_size(ctx->num_sms, (fv.H / fv.Hkv) * fv.N, fv.L, fv.Hkv);
+    return SRHPM_OK;
+}
+
+int srhpm_flash_attn_ext(srhpm_ctx * ctx, const srhpm_tensor * q, const srhpm_tensor * k, const srhpm_tensor * v,
+                         const srhpm_tensor * mask, const srhpm_tensor * sinks, float scale, float max_bias,
+                         float softcap, srhpm_tensor * dst, void * wdata, size_t wsize, void * stream) {
+    if (!ctx) return SRHPM_ERR_INVALID;
+    FaView    fv;
+    const int st = check_fa(q, k, v, mask, sinks, dst, &fv);
+    if (st != SRHPM_OK) return st;
+    return fa_run(ctx, fv, scale, max_bias, softcap, wdata, wsize, (cudaStream_t) stream);
 }
 
 }  // extern "C"

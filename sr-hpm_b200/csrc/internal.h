@@ -50,4 +50,25 @@ size_t static_work_bytes();
 int    gemm_run_static(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                        const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, cudaStream_t stream);
 
+// fa_decode.cu: multi-query attention over a q8_0 KV cache, DK = DV = 256 (byte strides)
+struct FaView {
+    const float *   q;
+    int64_t         qnb1, qnb2;  // token, head
+    int             N, H;
+    const uint8_t * k;
+    int64_t         knb1, knb2;  // token, KV head
+    const uint8_t * v;
+    int64_t         vnb1, vnb2;
+    int             L, Hkv;
+    const uint8_t * mask;  // f16 [L..][N..][mne2] or null
+    int64_t         mnb1, mnb2;
+    int             mne2;
+    const float *   sinks;  // f32 [H] or null
+    float *         dst;    // f32 [DV][H][N]
+    int64_t         dnb1, dnb2;
+};
+size_t fa_work_size(int num_sms, int R, int L, int Hkv);
+int    fa_run(srhpm_ctx * ctx, const FaView & v, float scale, float max_bias, float softcap, void * wdata,
+              size_t wsize, cudaStream_t stream);
+
 }  // namespace srhpm

@@ -57,6 +57,9 @@ _SIGNATURES = {
     "srhpm_mul_mat_static": (ctypes.c_int, [_P, _T, _T, _T, _P]),
     "srhpm_quantize_rows_q8_K": (ctypes.c_int, [_P, _T, _P, _P, _P, _P, _P]),
     "srhpm_quantize_rows_q8_0": (ctypes.c_int, [_P, _T, _P, _P]),
+    "srhpm_flash_attn_ext_work_size": (ctypes.c_int, [_P, _T, _T, _T, ctypes.POINTER(ctypes.c_size_t)]),
+    "srhpm_flash_attn_ext": (ctypes.c_int, [_P, _T, _T, _T, _T, _T, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                            _T, _P, ctypes.c_size_t, _P]),
     "srhpm_quantize_chunk": (ctypes.c_size_t, [ctypes.c_int, _P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                                 _P]),
 }

@@ -194,6 +194,60 @@ class Context:
                 "srhpm_mul_mat_isums")
         return isum, imin
 
+    # ---- multi-query attention (ggml_flash_attn_ext) -------------------------------------------------------------
+    @staticmethod
+    def _fa_views(q, k, v, kv_type, mask, sinks, out):
+        """ggml views: q f32 [H, N, D] -> ne [D, N, H]; k / v uint8 [Hkv, L, row bytes] (any strides, rows
+        contiguous) -> ne [D, L, Hkv]; mask f16 [N', L'] or [ne2, N', L'] -> ne [L', N', ne2]; sinks f32 [H];
+        out f32 [N, H, DV] -> ne [DV, H, N]."""
+        assert q.dtype == torch.float32 and q.dim() == 3 and q.stride(2) == 1
+        H, N, D = q.shape
+        tsz, blk = (34, 32) if kv_type == L.Q8_0 else (2, 1)
+        views = [_tensor_view(q, L.F32, [D, N, H], [4, q.stride(1) * 4, q.stride(0) * 4])]
+        for t in (k, v):
+            assert t.dtype == torch.uint8 and t.dim() == 3 and t.stride(2) == 1
+            Hkv, Lk, rowb = t.shape
+            views.append(_tensor_view(t, kv_type, [rowb // tsz * blk, Lk, Hkv], [tsz, t.stride(1), t.stride(0)]))
+        mv = None
+        if mask is not None:
+            assert mask.dtype == torch.float16 and mask.stride(-1) == 1
+            m3 = mask if mask.dim() == 3 else mask.unsqueeze(0)
+            mv = _tensor_view(m3, L.F16, [m3.shape[2], m3.shape[1], m3.shape[0]], [2, m3.stride(1) * 2, m3.stride(0) * 2])
+        sv = None
+        if sinks is not None:
+            assert sinks.dtype == torch.float32 and sinks.dim() == 1 and sinks.stride(0) == 1
+            sv = _tensor_view(sinks, L.F32, [sinks.shape[0]], [4])
+        ov = None
+        if out is not None:
+            Nn, Hh, DV = out.shape
+            ov = _tensor_view(out, L.F32, [DV, Hh, Nn], [4, out.stride(1) * 4, out.stride(0) * 4])
+        return views[0], views[1], views[2], mv, sv, ov
+
+    def flash_attn_ext_work_size(self, q, k, v, kv_type):
+        qv, kvv, vv, _, _, _ = self._fa_views(q, k, v, kv_type, None, None, None)
+        sz = ctypes.c_size_t()
+        st = self.lib.srhpm_flash_attn_ext_work_size(self.handle, ctypes.byref(qv), ctypes.byref(kvv),
+                                                     ctypes.byref(vv), ctypes.byref(sz))
+        return st, sz.value
+
+    def flash_attn_ext(self, q, k, v, kv_type, mask=None, sinks=None, scale=1.0, max_bias=0.0, softcap=0.0,
+                       out=None, stream=None, work=None):
+        """ggml_flash_attn_ext(q, k, v, mask, scale, max_bias, softcap) + sinks: out f32 [N, H, DV]."""
+        H, N, D = q.shape
+        DV = v.shape[2] // 34 * 32 if kv_type == L.Q8_0 else v.shape[2] // 2
+        if out is None:
+            out = torch.empty((N, H, DV), dtype=torch.float32, device=q.device)
+        qv, kvv, vv, mv, sv, ov = self._fa_views(q, k, v, kv_type, mask, sinks, out)
+        st, ws = self.flash_attn_ext_work_size(q, k, v, kv_type)
+        L.check(st, "srhpm_flash_attn_ext_work_size")
+        buf = work if work is not None else self.work(ws)
+        L.check(self.lib.srhpm_flash_attn_ext(self.handle, ctypes.byref(qv), ctypes.byref(kvv), ctypes.byref(vv),
+                                              ctypes.byref(mv) if mv is not None else None,
+                                              ctypes.byref(sv) if sv is not None else None, scale, max_bias, softcap,
+                                              ctypes.byref(ov), ctypes.c_void_p(buf.data_ptr()), buf.numel(),
+                                              _stream_ptr(stream)), "srhpm_flash_attn_ext")
+        return out
+
     def quantize_rows_q8_K(self, X, stream=None):
         X = X.contiguous()
         N, K = X.shape
