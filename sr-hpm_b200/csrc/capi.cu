@@ -91,6 +91,7 @@ int check_fa(const srhpm_tensor * q, const srhpm_tensor * k, const srhpm_tensor 
     fv->mask = nullptr;
     fv->mnb1 = fv->mnb2 = 0;
     fv->mne2 = 1;
+    fv->mne0 = 0;
     if (mask) {
         if (mask->type != SRHPM_TYPE_F16 || !mask->data || mask->nb[0] != 2) return SRHPM_ERR_INVALID;
         if (mask->ne[0] < L || mask->ne[1] < N || mask->ne[2] < 1 || mask->ne[3] != 1) return SRHPM_ERR_INVALID;
@@ -99,6 +100,7 @@ int check_fa(const srhpm_tensor * q, const srhpm_tensor * k, const srhpm_tensor 
         fv->mnb1 = (int64_t) mask->nb[1];
         fv->mnb2 = (int64_t) mask->nb[2];
         fv->mne2 = (int) mask->ne[2];
+        fv->mne0 = mask->ne[0];
     }
     fv->sinks = nullptr;
     if (sinks) {

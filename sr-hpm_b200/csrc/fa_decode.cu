@@ -41,10 +41,9 @@ constexpr int   kPlane   = kT * 128;            // one SWIZZLE_128B plane of a K
 constexpr int   kKTile   = 2 * kPlane + kT * 32;  // 36864: planes of row bytes 0-127, 128-255, 256-287
 constexpr int   kVTile   = kT * kRowB;          // 34816
 constexpr int   kSlot    = kKTile;
-constexpr int   kNSlot   = 3;
-constexpr int   kVC      = (kD / 8) * kT * 16;  // V^T operand: [dv group of 8][token][8 f16]
+constexpr int   kNSlot   = 5;                  // ring slots (a K or a V tile each)
 constexpr int   kRG      = 48;                  // rows per row group (tensor memory: 8 * 48 + 2 * 48 columns)
-constexpr int   kCW      = 4;                   // compute warps
+constexpr int   kCW      = 16;                  // compute warps (4 token quarters x 4 row quarters)
 constexpr int   kFaThreads = (kCW + 2) * 32;    // + producer warp + MMA warp
 constexpr float kLog2e   = 1.4426950408889634f;
 constexpr float kLazy    = 8.0f;                // raise the running maximum only beyond 2^8
@@ -57,7 +56,8 @@ struct FaArgs {
     int             chunk_len, n_chunks;
     const uint8_t * mask;  // f16 or null
     int64_t         mnb1, mnb2;
-    int             mne2;
+    int             mne2, mne0;
+    int             mask_mode;   // 0 none, 1 one mask row per query token (staged per tile), 2 per-head rows
     float           qscale;      // folded into the Q block scales: scale*log2e, or scale/softcap with a softcap
     float           softcap_l2;  // softcap*log2e, 0 = none
     float           max_bias, m0, m1;
@@ -74,20 +74,21 @@ struct FaArgs {
 // shared-memory layout (bytes from a 1024-aligned base)
 template <int RP> struct Smem {
     static constexpr int ring = 0;
-    static constexpr int vc   = ring + kNSlot * kSlot;
-    static constexpr int p    = vc + kVC;
-    static constexpr int qop  = p + RP * kT * 2;      // 16 Q operands of [2][RP][16]
-    static constexpr int qopb = 2 * RP * 16;          // bytes per Q operand
-    static constexpr int dq   = qop + 16 * qopb;      // f32 [8][RP]
-    static constexpr int red  = dq + 8 * RP * 4;      // f32 [4][RP]
-    static constexpr int mu   = red + kCW * RP * 4;   // f32 [RP] running maximum (log2 units)
+    static constexpr int p    = ring + kNSlot * kSlot;
+    static constexpr int qop  = p + RP * kT * 2;      // Q operands of the 9 K windows, [2][rows][16] each
+    static constexpr int qopb = 16 * RP * 32;         // their bytes
+    static constexpr int dq   = qop + qopb;           // f32 [8][RP]
+    static constexpr int red  = dq + 8 * RP * 4;      // f32 [2][4][RP] (per tile parity, per token quarter)
+    static constexpr int mu   = red + 2 * 4 * RP * 4; // f32 [RP] running maximum (log2 units)
     static constexpr int al   = mu + RP * 4;          // f32 [RP] rescale factor of this tile
     static constexpr int fac  = al + RP * 4;          // f32 [RP] final factor
     static constexpr int slope = fac + RP * 4;        // f32 [RP] ALiBi slope * log2e
     static constexpr int moff = slope + RP * 4;       // int64 [RP] mask row offsets
-    static constexpr int bar  = (moff + RP * 8 + 7) / 8 * 8;
-    static constexpr int nbar = 2 * kNSlot + 4;       // full[3], empty[3], s_full, s_free, pv_ready, pv_done
-    static constexpr int misc = bar + nbar * 8;       // tmem base, flags[2]
+    static constexpr int mslot = moff + RP * 8;       // int32 [RP] staged mask row of each row (its query token)
+    static constexpr int mbuf = (mslot + RP * 4 + 15) / 16 * 16;  // f16 [2][8][kT] staged mask tiles
+    static constexpr int bar  = mbuf + 2 * 8 * kT * 2;
+    static constexpr int nbar = 2 * kNSlot + 4;       // full[], empty[], s_full, s_free, pv_ready, pv_done
+    static constexpr int misc = bar + nbar * 8;       // tmem base, flags[3]
     static constexpr int total = misc + 16;
     static constexpr int alloc = total + 1024;
 };
@@ -102,7 +103,7 @@ __device__ __forceinline__ void tma3(uint8_t * dst, const CUtensorMap * m, int x
 
 __device__ __forceinline__ float redux_max(float v) {
     float r;
-    asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
+    asm("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));
     return r;
 }
 
@@ -127,18 +128,76 @@ template <int HI> __device__ __forceinline__ uint32_t magic_pair(uint32_t wx) {
     return prmt(wx, 0x64u, HI ? 0x4342u : 0x4140u);
 }
 
-// 1 thread = 1 KV token of the tile; V row (272 bytes, [d | 32 q] x 8) -> 256 f16 = d * q into the V^T operand
-__device__ __forceinline__ void convert_v_row(const uint8_t * row, uint8_t * vc, int t) {
-    uint32_t w[68];
+// packed f32 pairs (sm_100 f32x2 instructions: one issue for two lanes of arithmetic)
+typedef unsigned long long f2;
+__device__ __forceinline__ f2 f2_pack(float a, float b) {
+    f2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_unpack(f2 r, float & a, float & b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ f2 f2_add(f2 a, f2 b) {
+    f2 r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 f2_mul(f2 a, f2 b) {
+    f2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 f2_fma(f2 a, f2 b, f2 c) {
+    f2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ float ex2(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// The Q.K accumulators start at kMagic: an int32 sum i (|i| <= 32 * 127 * 127 < 2^22) then reads as the float
+// 12582912 + i exactly, and one subtraction gives i as a float (no integer-to-float conversion instruction).
+constexpr uint32_t kMagic  = 0x4B400000u;
+constexpr float    kMagicF = 12582912.0f;
+
+// K window w (row bytes 32w..32w+31) holds quant bytes of blocks w-1 and w (w = 1..7), of block 0 (w = 0) or of
+// block 7 (w = 8); its Q operand has the rows of those blocks (RP or 2 RP rows), so one MMA per window fills the score
+// columns of both blocks (block b at columns RP * b)
+template <int RP> __host__ __device__ constexpr int qwin_rows(int w) { return (w == 0 || w == 8) ? RP : 2 * RP; }
+template <int RP> __host__ __device__ constexpr int qwin_off(int w) {
+    return w == 0 ? 0 : RP * 32 + (w - 1) * 2 * RP * 32;
+}
+
+template <int RP> __device__ __forceinline__ void arm_scores(uint32_t tS, int q, int rbase) {
+    constexpr int RH = RP / 4;
+    uint32_t      m[RH];
 #pragma unroll
-    for (int c = 0; c < 17; c++) {
-        const uint4 u = *reinterpret_cast<const uint4 *>(row + 16 * c);
+    for (int j = 0; j < RH; j++) m[j] = kMagic;
+#pragma unroll
+    for (int b = 0; b < 8; b++) tc::st_cols<RH>(tc::taddr(tS, q, RP * b + rbase), m);
+}
+
+// 1 thread = a quarter of one KV token's V row: blocks 2*qr, 2*qr+1 ([d | 32 q] each, row bytes 68*qr..68*qr+67).
+// load_v_part reads the 80 bytes from 64*qr (16-byte loads, conflict-free across consecutive tokens); the quarter
+// starts WS = qr words into them. convert_v_part writes 64 f16 = d * q into the V^T operand of the dv half the blocks
+// belong to ([dv group of 8 (16 per half)][token][8 f16]).
+__device__ __forceinline__ void load_v_part(const uint8_t * row, int qr, uint32_t (&w)[20]) {
+    const uint4 * src = reinterpret_cast<const uint4 *>(row + 64 * qr);
+#pragma unroll
+    for (int c = 0; c < 5; c++) {
+        const uint4 u = src[c];
         w[4 * c] = u.x; w[4 * c + 1] = u.y; w[4 * c + 2] = u.z; w[4 * c + 3] = u.w;
     }
+}
+template <int WS> __device__ __forceinline__ void convert_v_part(const uint32_t (&w)[20], uint8_t * vch, int t) {
     const __half2 bias = __halves2half2(__ushort_as_half(0x6480u), __ushort_as_half(0x6480u));  // 1152
 #pragma unroll
-    for (int b = 0; b < 8; b++) {
-        const int      od = 34 * b;
+    for (int bb = 0; bb < 2; bb++) {
+        const int      od    = 4 * WS + 34 * bb;
         const uint32_t dbits = (w[od >> 2] >> (8 * (od & 3))) & 0xffffu;
         const __half2  dd    = __halves2half2(__ushort_as_half((unsigned short) dbits),
                                               __ushort_as_half((unsigned short) dbits));
@@ -152,19 +211,42 @@ __device__ __forceinline__ void convert_v_row(const uint8_t * row, uint8_t * vc,
             h                 = __hmul2(h, dd);
             f[m]              = *reinterpret_cast<const uint32_t *>(&h);
         }
+        const int jb = 4 * ((2 * WS + bb) & 3);  // dv group of block 2 qr + bb inside its half (qr = WS)
 #pragma unroll
         for (int qd = 0; qd < 4; qd++) {
-            *reinterpret_cast<uint4 *>(vc + ((4 * b + qd) * kT + t) * 16) =
+            *reinterpret_cast<uint4 *>(vch + ((jb + qd) * kT + t) * 16) =
                 make_uint4(f[4 * qd], f[4 * qd + 1], f[4 * qd + 2], f[4 * qd + 3]);
         }
     }
+}
+
+// P^T rows rbase..rbase+RH-1 (f16 pairs in pk) of token t: MN-major [row group of 8][token][8 f16], 4 rows per store
+template <int RH> __device__ __forceinline__ void store_p(uint8_t * pbase, int rbase, int t, const uint32_t * pk) {
+#pragma unroll
+    for (int u = 0; u < RH / 4; u++) {
+        const int row = rbase + 4 * u;
+        *reinterpret_cast<uint2 *>(pbase + ((row >> 3) * kT + t) * 16 + (row & 7) * 2) = make_uint2(pk[2 * u], pk[2 * u + 1]);
+    }
+}
+
+// staged mask tile (mask_mode 1, N <= 8): row tq, tokens tok0..tok0+127 -> f16 [8][kT]; thread p < N * 16 moves 8 tokens
+__device__ __forceinline__ uint4 mask_piece(const FaArgs & a, int p, int tok0) {
+    const int  tq = p >> 4, e0 = tok0 + 8 * (p & 15);
+    const uint8_t * src = a.mask + (int64_t) tq * a.mnb1 + 2 * (int64_t) e0;
+    if (e0 + 8 <= a.mne0) return __ldg(reinterpret_cast<const uint4 *>(src));
+    uint16_t v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] = e0 + e < a.mne0 ? __ldg(reinterpret_cast<const unsigned short *>(src) + e) : 0;
+    return make_uint4(v[0] | (uint32_t) v[1] << 16, v[2] | (uint32_t) v[3] << 16, v[4] | (uint32_t) v[5] << 16,
+                      v[6] | (uint32_t) v[7] << 16);
 }
 
 template <int RP>
 __global__ void __launch_bounds__(kFaThreads, 1)
     fa_q80_kernel(const __grid_constant__ CUtensorMap mk128, const __grid_constant__ CUtensorMap mk32,
                   const __grid_constant__ CUtensorMap mv, const FaArgs a) {
-    using S = Smem<RP>;
+    using S           = Smem<RP>;
+    constexpr int RH  = RP / 4;  // rows per compute thread
     extern __shared__ uint8_t smem_raw[];
     uint8_t * sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t * full    = reinterpret_cast<uint64_t *>(sm + S::bar);
@@ -182,37 +264,43 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     float *    fac     = reinterpret_cast<float *>(sm + S::fac);
     float *    slope2  = reinterpret_cast<float *>(sm + S::slope);
     int64_t *  moff    = reinterpret_cast<int64_t *>(sm + S::moff);
+    int *      mslot   = reinterpret_cast<int *>(sm + S::mslot);
+    uint16_t * mbuf    = reinterpret_cast<uint16_t *>(sm + S::mbuf);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int chunk = blockIdx.x;
     const int g = blockIdx.y / a.nrg, rg = blockIdx.y % a.nrg;
     const int t0 = chunk * a.chunk_len, t1 = min(a.L, t0 + a.chunk_len);
     const int nt = (t1 - t0 + kT - 1) / kT;
-    const int row0 = rg * kRG;                       // first row (of the KV head's R) of this group
-    const int rows = min(RP, a.R - row0);            // valid rows
-    bool      bad  = false;
+    const int row0 = rg * kRG;              // first row (of the KV head's R) of this group
+    const int rows = min(RP, a.R - row0);   // valid rows
+    // compute threads: lane quarter q (KV token t = 32 q + lane of the tile), row quarter qr (rows rbase..rbase+RH-1)
+    const int q = warp & 3, qr = (warp >> 2) & 3, t = 32 * q + lane, rbase = qr * RH;
+    bool      bad = false;
 
     if (tid == 0) {
         for (int i = 0; i < kNSlot; i++) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], kCW);
+            mbar_init(&empty[i], 1);  // released by the commit of the tile's P.V
         }
         mbar_init(s_full, 1);
         mbar_init(s_free, kCW);
         mbar_init(pv_rdy, kCW);
         mbar_init(pv_done, 1);
         fence_mbar_init();
-        flags[0] = flags[1] = 0;
+        flags[0] = flags[1] = flags[2] = 0;
     }
     if (warp == 0) tc::tmem_alloc(tptr, 512);
     if (tid < kCW * 32) {
         uint4 * z = reinterpret_cast<uint4 *>(sm + S::qop);
-        for (int i = tid; i < 16 * S::qopb / 16; i += kCW * 32) z[i] = make_uint4(0, 0, 0, 0);
+        for (int i = tid; i < S::qopb / 16; i += kCW * 32) z[i] = make_uint4(0, 0, 0, 0);
     }
     tc::fence_before();
     __syncthreads();
     tc::fence_after();
     const uint32_t tbase = *tptr;
+    const uint32_t tS    = tbase;           // S_b at columns RP * b
+    const uint32_t tO    = tbase + 8 * RP;  // O^T halves at tO, tO + RP
 
     // producer: the first loads of the ring need no empty-slot wait
     auto produce = [&](int n) {
@@ -238,15 +326,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     }
     __syncwarp();
 
-    // Q rows -> q8_0 (the cache type's vec_dot type), scattered into the 16 window operands; per-row constants
-    if (tid < kCW * 32) {
+    // Q rows -> q8_0 (the cache type's vec_dot type), scattered into the 16 window operands; per-row constants;
+    // the score accumulators armed with the magic offset
+    if (warp < kCW) {
         for (int u = tid; u < 8 * RP; u += kCW * 32) {
             const int r = u >> 3, b = u & 7;
             int8_t    qv[32];
             float     dqs = 0.0f;
             if (r < rows) {
-                const int     rr = row0 + r;
-                const int     h  = g * a.G + rr / a.N, tq = rr % a.N;
+                const int     rr  = row0 + r;
+                const int     h   = g * a.G + rr / a.N, tq = rr % a.N;
                 const float * src = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.q) +
                                                                      tq * a.qnb1 + h * a.qnb2) + 32 * b;
                 float x[32], amax = 0.0f;
@@ -271,12 +360,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 #pragma unroll
                 for (int j = 0; j < 32; j++) qv[j] = 0;
             }
-            dq[b * RP + r]   = dqs;
-            const int w0     = (34 * b + 2) >> 5;
+            dq[b * RP + r] = dqs;
 #pragma unroll
             for (int j = 0; j < 32; j++) {
-                const int pos = 34 * b + 2 + j, x = pos & 31, s = (pos >> 5) - w0;
-                sm[S::qop + (2 * b + s) * S::qopb + (x >> 4) * RP * 16 + r * 16 + (x & 15)] = (uint8_t) qv[j];
+                const int pos = 34 * b + 2 + j, x = pos & 31, w = pos >> 5;
+                const int row = (w >= 1 && w <= 7 && b == w) ? RP + r : r;  // second block of a shared window
+                sm[S::qop + qwin_off<RP>(w) + (x >> 4) * qwin_rows<RP>(w) * 16 + row * 16 + (x & 15)] =
+                    (uint8_t) qv[j];
             }
         }
         if (tid < RP) {
@@ -288,8 +378,14 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             }
             slope2[r] = sl * kLog2e;
             moff[r]   = a.mask ? (int64_t) tq * a.mnb1 + (int64_t) (h % a.mne2) * a.mnb2 : 0;
+            mslot[r]  = tq;
             mu[r]     = -INFINITY;
         }
+        if (a.mask_mode == 1 && tid < a.N * 16) {  // N <= 8
+            *reinterpret_cast<uint4 *>(mbuf + (tid >> 4) * kT + 8 * (tid & 15)) = mask_piece(a, tid, t0);
+        }
+        arm_scores<RP>(tS, q, rbase);
+        tc::wait_st();
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc::fence_before();
@@ -297,10 +393,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     tc::fence_after();
 
     const uint32_t qop_s = smem_u32(sm + S::qop);
-    const uint32_t vc_s  = smem_u32(sm + S::vc);
     const uint32_t p_s   = smem_u32(sm + S::p);
-    const uint32_t tS    = tbase;             // S_b at columns RP * b
-    const uint32_t tO    = tbase + 8 * RP;    // O^T halves at tO, tO + RP
 
     if (warp == kCW) {
         // ---------------- producer ----------------
@@ -316,6 +409,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t id8  = tc::idesc(tc::kD_S32, tc::kAB_S8, tc::kAB_S8, tc::kKMajor, tc::kKMajor, RP, 128);
+            constexpr uint32_t id8w = tc::idesc(tc::kD_S32, tc::kAB_S8, tc::kAB_S8, tc::kKMajor, tc::kKMajor, 2 * RP,
+                                                128);
             constexpr uint32_t id16 = tc::idesc(tc::kD_F32, tc::kAB_F16, tc::kAB_F16, tc::kMNMajor, tc::kMNMajor, RP,
                                                 128);
             auto issue_qk = [&](int i) {
@@ -324,20 +419,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 tc::fence_after();
                 const uint32_t kb = smem_u32(sm + S::ring + slot * kSlot);
 #pragma unroll
-                for (int b = 0; b < 8; b++) {
-                    const int w0 = (34 * b + 2) >> 5;
-#pragma unroll
-                    for (int s = 0; s < 2; s++) {
-                        const int j = w0 + s;
-                        uint64_t  ad;
-                        if (j < 8) {
-                            ad = tc::sdesc(kb + (j >> 2) * kPlane + (j & 3) * 32, 16, 1024) | (2ull << 61);
-                        } else {
-                            ad = tc::sdesc(kb + 2 * kPlane, 16, 256) | (6ull << 61);
-                        }
-                        const uint64_t bd = tc::sdesc(qop_s + (2 * b + s) * S::qopb, RP * 16, 128);
-                        tc::mma_i8(tS + RP * b, ad, bd, id8, (uint32_t) s);
+                for (int w = 0; w < 9; w++) {
+                    uint64_t ad;
+                    if (w < 8) {
+                        ad = tc::sdesc(kb + (w >> 2) * kPlane + (w & 3) * 32, 16, 1024) | (2ull << 61);
+                    } else {
+                        ad = tc::sdesc(kb + 2 * kPlane, 16, 256) | (6ull << 61);
                     }
+                    const uint64_t bd = tc::sdesc(qop_s + qwin_off<RP>(w), qwin_rows<RP>(w) * 16, 128);
+                    tc::mma_i8(tS + (w == 0 ? 0 : RP * (w - 1)), ad, bd, (w == 0 || w == 8) ? id8 : id8w,
+                               1u);  // onto the armed magic offset
                 }
                 tc::commit(s_full);
             };
@@ -349,26 +440,43 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 }
                 wait_or_flag(pv_rdy, i & 1, a.status, bad);
                 tc::fence_after();
+                const int ks = (2 * i) % kNSlot, vs = (2 * i + 1) % kNSlot;  // V^T halves live in these slots
 #pragma unroll
                 for (int hf = 0; hf < 2; hf++) {
+                    const uint32_t vb = smem_u32(sm + S::ring + (hf ? vs : ks) * kSlot);
 #pragma unroll
                     for (int k = 0; k < kT / 16; k++) {
-                        const uint64_t ad = tc::sdesc(vc_s + hf * 16 * kT * 16 + k * 256, 128, kT * 16);
+                        const uint64_t ad = tc::sdesc(vb + k * 256, 128, kT * 16);
                         const uint64_t bd = tc::sdesc(p_s + k * 256, 128, kT * 16);
                         tc::mma_f16(tO + hf * RP, ad, bd, id16, (uint32_t) (i > 0 || k > 0));
                     }
                 }
                 tc::commit(pv_done);
+                tc::commit(&empty[ks]);
+                tc::commit(&empty[vs]);
             }
         }
         __syncwarp();
     } else {
-        // ---------------- compute warps: thread = KV token of the tile ----------------
-        float l[RP];
+        // ---------------- compute warps ----------------
+        const f2 negC = f2_pack(-kMagicF, -kMagicF);
+        float    l[RH];  // row sums of this thread's token
 #pragma unroll
-        for (int r = 0; r < RP; r++) l[r] = 0.0f;
+        for (int r = 0; r < RH; r++) l[r] = 0.0f;
+        uint32_t msl[RH / 4];  // staged mask row of each of this thread's rows, 4 per word
+#pragma unroll
+        for (int j = 0; j < RH / 4; j++) {
+            msl[j] = 0;
+#pragma unroll
+            for (int e = 0; e < 4; e++) msl[j] |= (uint32_t) (mslot[rbase + 4 * j + e] & 0xff) << (8 * e);
+        }
         for (int i = 0; i < nt; i++) {
             const int n = 2 * i, kslot = n % kNSlot, vslot = (n + 1) % kNSlot;
+            // next tile's staged mask piece: loaded now, stored before this tile's first barrier (which orders it before
+            // the next tile's reads)
+            uint4      mnext = make_uint4(0, 0, 0, 0);
+            const bool stage = a.mask_mode == 1 && i + 1 < nt && tid < a.N * 16;  // N <= 8
+            if (stage) mnext = mask_piece(a, tid, t0 + (i + 1) * kT);
             wait_or_flag(s_full, i & 1, a.status, bad);
             wait_or_flag(&full[kslot], (n / kNSlot) & 1, a.status, bad);  // (complete already) the d bytes
             tc::fence_after();
@@ -376,116 +484,165 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             float           dk[8];
 #pragma unroll
             for (int b = 0; b < 8; b++) {
-                const int o = 34 * b, oo = o & 127;
-                const uint8_t * pr = kb + (o >> 7) * kPlane + tid * 128 + ((((oo >> 4) ^ (tid & 7))) << 4) + (oo & 15);
-                dk[b] = half_bits_to_float(*reinterpret_cast<const uint16_t *>(pr));
+                const int       o  = 34 * b, oo = o & 127;
+                const uint8_t * pr = kb + (o >> 7) * kPlane + t * 128 + ((((oo >> 4) ^ (t & 7))) << 4) + (oo & 15);
+                dk[b]              = half_bits_to_float(*reinterpret_cast<const uint16_t *>(pr));
             }
-            float s[RP];
+            // s[r] = sum_b d_k[b] * d_q[b][r] * isum_b[r] (d_q carries scale * log2e)
+            f2 s2[RH / 2];
 #pragma unroll
-            for (int r = 0; r < RP; r++) s[r] = 0.0f;
+            for (int j = 0; j < RH / 2; j++) s2[j] = 0ull;
+            {
+                // two blocks per tensor-memory round trip, the next pair loading while this one is scaled
+                uint32_t v[2][2 * RH];
+                tc::ld_cols<RH>(tc::taddr(tS, q, rbase), v[0]);
+                tc::ld_cols<RH>(tc::taddr(tS, q, RP + rbase), v[0] + RH);
 #pragma unroll
-            for (int b = 0; b < 8; b++) {
-                uint32_t v[RP];
+                for (int bp = 0; bp < 4; bp++) {
+                    tc::wait_ld();
+                    if (bp < 3) {
+                        tc::ld_cols<RH>(tc::taddr(tS, q, RP * (2 * bp + 2) + rbase), v[(bp + 1) & 1]);
+                        tc::ld_cols<RH>(tc::taddr(tS, q, RP * (2 * bp + 3) + rbase), v[(bp + 1) & 1] + RH);
+                    }
 #pragma unroll
-                for (int c = 0; c < RP / 16; c++) {
-                    tc::ld16(tc::taddr(tS, warp, RP * b + 16 * c), *reinterpret_cast<uint32_t(*)[16]>(&v[16 * c]));
+                    for (int e = 0; e < 2; e++) {
+                        const int        b   = 2 * bp + e;
+                        const float4 *   dqc = reinterpret_cast<const float4 *>(dq + b * RP + rbase);
+                        const f2         dk2 = f2_pack(dk[b], dk[b]);
+                        const uint32_t * vb  = v[bp & 1] + e * RH;
+#pragma unroll
+                        for (int j4 = 0; j4 < RH / 4; j4++) {
+                            const float4 d4 = dqc[j4];
+                            const f2 x0 = f2_add(f2_pack(__uint_as_float(vb[4 * j4]), __uint_as_float(vb[4 * j4 + 1])), negC);
+                            const f2 x1 = f2_add(f2_pack(__uint_as_float(vb[4 * j4 + 2]), __uint_as_float(vb[4 * j4 + 3])), negC);
+                            s2[2 * j4]     = f2_fma(x0, f2_mul(f2_pack(d4.x, d4.y), dk2), s2[2 * j4]);
+                            s2[2 * j4 + 1] = f2_fma(x1, f2_mul(f2_pack(d4.z, d4.w), dk2), s2[2 * j4 + 1]);
+                        }
+                    }
                 }
-                tc::wait_ld();
-                const float * dqb = dq + b * RP;
-#pragma unroll
-                for (int r = 0; r < RP; r++) s[r] = fmaf((float) (int) v[r], dqb[r] * dk[b], s[r]);
             }
+            // re-arm the accumulators, then release them (next Q.K) and the K slot
+            arm_scores<RP>(tS, q, rbase);
+            tc::wait_st();
             tc::fence_before();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(s_free);
-                mbar_arrive(&empty[kslot]);
-            }
+            if (lane == 0) mbar_arrive(s_free);
+            float s[RH];
+#pragma unroll
+            for (int j = 0; j < RH / 2; j++) f2_unpack(s2[j], s[2 * j], s[2 * j + 1]);
 
-            const int  tok   = t0 + i * kT + tid;
+            const int  tok   = t0 + i * kT + t;
             const bool valid = tok < t1;
             if (a.softcap_l2 != 0.0f) {
 #pragma unroll
-                for (int r = 0; r < RP; r++) s[r] = a.softcap_l2 * tanhf(s[r]);
+                for (int r = 0; r < RH; r++) s[r] = a.softcap_l2 * tanhf(s[r]);
             }
-            if (a.mask != nullptr && valid) {
+            if (a.mask_mode == 1) {
+                const uint16_t * mb = mbuf + (i & 1) * 8 * kT + t;
 #pragma unroll
-                for (int r = 0; r < RP; r++) {
-                    const uint16_t mb = __ldg(reinterpret_cast<const unsigned short *>(a.mask + moff[r] + 2 * (int64_t) tok));
-                    s[r] = fmaf(slope2[r], half_bits_to_float(mb), s[r]);
+                for (int r = 0; r < RH; r++) {
+                    const float sl = a.max_bias > 0.0f ? slope2[rbase + r] : kLog2e;
+                    const int   sl_r = (msl[r >> 2] >> (8 * (r & 3))) & 0xff;
+                    s[r] = fmaf(sl, half_bits_to_float(mb[sl_r * kT]), s[r]);
+                }
+            } else if (a.mask_mode == 2 && valid) {
+#pragma unroll
+                for (int r = 0; r < RH; r++) {
+                    const uint16_t mv16 = __ldg(reinterpret_cast<const unsigned short *>(a.mask + moff[rbase + r] +
+                                                                                         2 * (int64_t) tok));
+                    s[r] = fmaf(slope2[rbase + r], half_bits_to_float(mv16), s[r]);
                 }
             }
             if (!valid) {
 #pragma unroll
-                for (int r = 0; r < RP; r++) s[r] = -INFINITY;
+                for (int r = 0; r < RH; r++) s[r] = -INFINITY;
             }
+            // tile maxima; the running maximum rises (second barrier) only when some row's tile maximum exceeds it
+            // by more than 2^8
+            float * redb = red + (i & 1) * 4 * RP;
+            bool    up   = false;
+            float   mx[RH];
 #pragma unroll
-            for (int r = 0; r < RP; r++) {
-                const float m = redux_max(s[r]);
-                if (lane == 0) red[warp * RP + r] = m;
+            for (int r = 0; r < RH; r++) mx[r] = redux_max(s[r]);  // independent: all in flight together
+#pragma unroll
+            for (int r = 0; r < RH; r++) {
+                if (lane == 0) redb[q * RP + rbase + r] = mx[r];
+                up |= mx[r] > mu[rbase + r] + kLazy;
+            }
+            if (lane == 0 && up) flags[i % 3] = 1;
+            // this thread's half of the tile's raw V row, read before the barrier: after it, the K and V slots are
+            // rewritten with the f16 V^T halves
+            uint32_t vw[20];
+            wait_or_flag(&full[vslot], ((n + 1) / kNSlot) & 1, a.status, bad);
+            load_v_part(sm + S::ring + vslot * kSlot + t * kRowB, qr, vw);
+            if (stage) {
+                *reinterpret_cast<uint4 *>(mbuf + ((i + 1) & 1) * 8 * kT + (tid >> 4) * kT + 8 * (tid & 15)) = mnext;
             }
             named_bar_sync(1, kCW * 32);
-            if (tid < RP) {
-                float mt = red[tid];
+            if (tid == 0) flags[(i + 2) % 3] = 0;
+            const bool resc = flags[i % 3] != 0;
+            if (resc) {
+                if (tid < RP) {
+                    float mt = redb[tid];
 #pragma unroll
-                for (int w = 1; w < kCW; w++) mt = fmaxf(mt, red[w * RP + tid]);
-                const float mo = mu[tid];
-                if (mt > mo + kLazy) {
-                    mu[tid]         = mt;
-                    al[tid]         = exp2f(mo - mt);
-                    flags[i & 1]    = 1;
-                } else {
-                    al[tid] = 1.0f;
+                    for (int w = 1; w < 4; w++) mt = fmaxf(mt, redb[w * RP + tid]);
+                    const float mo = mu[tid];
+                    if (mt > mo + kLazy) {
+                        mu[tid] = mt;
+                        al[tid] = exp2f(mo - mt);
+                    } else {
+                        al[tid] = 1.0f;
+                    }
                 }
+                named_bar_sync(1, kCW * 32);
             }
-            named_bar_sync(1, kCW * 32);
-            const bool resc = flags[i & 1] != 0;
-            if (tid == 0) flags[(i + 1) & 1] = 0;
             if (i > 0) {
                 wait_or_flag(pv_done, (i - 1) & 1, a.status, bad);
                 tc::fence_after();
             }
             if (resc) {
 #pragma unroll
-                for (int r = 0; r < RP; r++) l[r] *= al[r];
+                for (int r = 0; r < RH; r++) l[r] *= al[rbase + r];
                 if (i > 0) {
 #pragma unroll
                     for (int hf = 0; hf < 2; hf++) {
+                        uint32_t       o[RH];
+                        const uint32_t ta = tc::taddr(tO + hf * RP, q, rbase);
+                        tc::ld_cols<RH>(ta, o);
+                        tc::wait_ld();
 #pragma unroll
-                        for (int c = 0; c < RP / 16; c++) {
-                            uint32_t o[16];
-                            const uint32_t ta = tc::taddr(tO + hf * RP, warp, 16 * c);
-                            tc::ld16(ta, o);
-                            tc::wait_ld();
-#pragma unroll
-                            for (int j = 0; j < 16; j++) o[j] = __float_as_uint(__uint_as_float(o[j]) * al[16 * c + j]);
-                            tc::st16(ta, o);
-                        }
+                        for (int j = 0; j < RH; j++) o[j] = __float_as_uint(__uint_as_float(o[j]) * al[rbase + j]);
+                        tc::st_cols<RH>(ta, o);
                     }
                     tc::wait_st();
                 }
             }
             // P^T (MN-major: [row group of 8][token][8 f16])
+            {
+                uint32_t pk[RH / 2];
 #pragma unroll
-            for (int rg8 = 0; rg8 < RP / 8; rg8++) {
-                uint32_t pk[4];
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const int   r0 = 8 * rg8 + 2 * j;
-                    const float p0 = s[r0] == -INFINITY ? 0.0f : exp2f(s[r0] - mu[r0]);
-                    const float p1 = s[r0 + 1] == -INFINITY ? 0.0f : exp2f(s[r0 + 1] - mu[r0 + 1]);
-                    l[r0] += p0;
-                    l[r0 + 1] += p1;
+                for (int j = 0; j < RH / 2; j++) {
+                    const int   r  = 2 * j, row = rbase + r;
+                    const float m0 = mu[row], m1 = mu[row + 1];
+                    const float p0 = ex2(s[r] - (m0 == -INFINITY ? 0.0f : m0));
+                    const float p1 = ex2(s[r + 1] - (m1 == -INFINITY ? 0.0f : m1));
+                    l[r] += p0;
+                    l[r + 1] += p1;
                     const __half2 hp = __floats2half2_rn(p0, p1);
                     pk[j]            = *reinterpret_cast<const uint32_t *>(&hp);
                 }
-                *reinterpret_cast<uint4 *>(sm + S::p + (rg8 * kT + tid) * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                store_p<RH>(sm + S::p, rbase, t, pk);
             }
-            // V^T
-            wait_or_flag(&full[vslot], ((n + 1) / kNSlot) & 1, a.status, bad);
-            convert_v_row(sm + S::ring + vslot * kSlot + tid * kRowB, sm + S::vc, tid);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[vslot]);
+            // V^T of blocks 2qr, 2qr+1: dv half 0 into the tile's K slot, half 1 into its V slot
+            {
+                uint8_t * vch = sm + S::ring + (qr >= 2 ? vslot : kslot) * kSlot;
+                switch (qr) {
+                    case 0: convert_v_part<0>(vw, vch, t); break;
+                    case 1: convert_v_part<1>(vw, vch, t); break;
+                    case 2: convert_v_part<2>(vw, vch, t); break;
+                    default: convert_v_part<3>(vw, vch, t); break;
+                }
+            }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             tc::fence_before();
             __syncwarp();
@@ -496,18 +653,19 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         wait_or_flag(pv_done, (nt - 1) & 1, a.status, bad);
         tc::fence_after();
 #pragma unroll
-        for (int r = 0; r < RP; r++) {
+        for (int r = 0; r < RH; r++) {
             float v = l[r];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) red[warp * RP + r] = v;
+            if (lane == 0) red[(nt & 1) * 4 * RP + q * RP + rbase + r] = v;
         }
         named_bar_sync(1, kCW * 32);
         const bool single = a.n_chunks == 1;
         if (tid < rows) {
-            float Ssum = red[tid];
+            const float * rs = red + (nt & 1) * 4 * RP;
+            float Ssum = rs[tid];
 #pragma unroll
-            for (int w = 1; w < kCW; w++) Ssum += red[w * RP + tid];
+            for (int w = 1; w < 4; w++) Ssum += rs[w * RP + tid];
             const int rr = row0 + tid;
             float     M  = mu[tid];
             if (single) {
@@ -531,26 +689,23 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         named_bar_sync(1, kCW * 32);
 #pragma unroll
         for (int hf = 0; hf < 2; hf++) {
-            const int dv = hf * 128 + warp * 32 + lane;
+            const int dv = hf * 128 + 32 * q + lane;
+            uint32_t  o[RH];
+            tc::ld_cols<RH>(tc::taddr(tO + hf * RP, q, rbase), o);
+            tc::wait_ld();
 #pragma unroll
-            for (int c = 0; c < RP / 16; c++) {
-                uint32_t o[16];
-                tc::ld16(tc::taddr(tO + hf * RP, warp, 16 * c), o);
-                tc::wait_ld();
-#pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    const int r = 16 * c + j;
-                    if (r < rows) {
-                        const int rr = row0 + r;
-                        const float val = __uint_as_float(o[j]);
-                        if (single) {
-                            const int h = g * a.G + rr / a.N, tq = rr % a.N;
-                            float * out = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(a.dst) + h * a.dnb1 +
-                                                                    tq * a.dnb2);
-                            out[dv] = val * fac[r];
-                        } else {
-                            a.part_acc[((int64_t) (g * a.R + rr) * a.n_chunks + chunk) * kD + dv] = val;
-                        }
+            for (int j = 0; j < RH; j++) {
+                const int r = rbase + j;
+                if (r < rows) {
+                    const int   rr  = row0 + r;
+                    const float val = __uint_as_float(o[j]);
+                    if (single) {
+                        const int h = g * a.G + rr / a.N, tq = rr % a.N;
+                        float * out = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(a.dst) + h * a.dnb1 +
+                                                                tq * a.dnb2);
+                        out[dv] = val * fac[r];
+                    } else {
+                        a.part_acc[((int64_t) (g * a.R + rr) * a.n_chunks + chunk) * kD + dv] = val;
                     }
                 }
             }
@@ -696,6 +851,12 @@ int fa_run(srhpm_ctx * ctx, const FaView & v, float scale, float max_bias, float
     a.mnb1     = v.mnb1;
     a.mnb2     = v.mnb2;
     a.mne2     = v.mne2;
+    a.mne0     = v.mne0;
+    a.mask_mode = 0;
+    if (v.mask) {
+        const bool staged = v.mne2 == 1 && v.N <= 8 && reinterpret_cast<uintptr_t>(v.mask) % 16 == 0 && v.mnb1 % 16 == 0;
+        a.mask_mode = staged ? 1 : 2;
+    }
     if (softcap != 0.0f) {
         a.qscale     = scale / softcap;
         a.softcap_l2 = softcap * kLog2e;

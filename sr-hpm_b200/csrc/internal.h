@@ -63,6 +63,7 @@ struct FaView {
     const uint8_t * mask;  // f16 [L..][N..][mne2] or null
     int64_t         mnb1, mnb2;
     int             mne2;
+    int64_t         mne0;
     const float *   sinks;  // f32 [H] or null
     float *         dst;    // f32 [DV][H][N]
     int64_t         dnb1, dnb2;

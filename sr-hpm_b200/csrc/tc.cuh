@@ -95,6 +95,32 @@ __device__ __forceinline__ void st16(uint32_t taddr, const uint32_t (&r)[16]) {
         "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
 }
+__device__ __forceinline__ void st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+__device__ __forceinline__ void ld4(uint32_t taddr, uint32_t (&r)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
+}
+__device__ __forceinline__ void st4(uint32_t taddr, const uint32_t (&r)[4]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3])
+                 : "memory");
+}
+// NC (a multiple of 4, at most 28) consecutive columns of this warp's lane quarter
+template <int NC> __device__ __forceinline__ void ld_cols(uint32_t taddr, uint32_t * r) {
+    if constexpr (NC >= 16) ld16(taddr, *reinterpret_cast<uint32_t(*)[16]>(r));
+    if constexpr ((NC & 8) != 0) ld8(taddr + (NC & 16), *reinterpret_cast<uint32_t(*)[8]>(r + (NC & 16)));
+    if constexpr ((NC & 4) != 0) ld4(taddr + (NC & 24), *reinterpret_cast<uint32_t(*)[4]>(r + (NC & 24)));
+}
+template <int NC> __device__ __forceinline__ void st_cols(uint32_t taddr, const uint32_t * r) {
+    if constexpr (NC >= 16) st16(taddr, *reinterpret_cast<const uint32_t(*)[16]>(r));
+    if constexpr ((NC & 8) != 0) st8(taddr + (NC & 16), *reinterpret_cast<const uint32_t(*)[8]>(r + (NC & 16)));
+    if constexpr ((NC & 4) != 0) st4(taddr + (NC & 24), *reinterpret_cast<const uint32_t(*)[4]>(r + (NC & 24)));
+}
 __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
