@@ -138,6 +138,36 @@ int srhpm_flash_attn_ext(srhpm_ctx * ctx, const srhpm_tensor * q, const srhpm_te
                          const srhpm_tensor * mask, const srhpm_tensor * sinks, float scale, float max_bias,
                          float softcap, srhpm_tensor * dst, void * wdata, size_t wsize, void * stream);
 
+/* ---- greedy acceptance -----------------------------------------------------------------------------------------
+ * Target logits f32 [n_vocab, >= n_draft + 1] (row i scores the token after draft position i; row stride nb[1]) and
+ * the drafted ids int32 [n_draft] (device): for i < n_draft, id_i = argmax of row i (the first maximum, as the
+ * sequential greedy scan finds it); with relax > 0 a drafted token whose logit is within relax of row i's maximum is
+ * taken instead; id_i is emitted and the scan stops at the first id_i != draft[i]; when all n_draft tokens are
+ * accepted, the argmax of row n_draft is emitted as well. out_ids int32 [n_draft + 1] and out_n int32 (device) receive
+ * the emitted ids and their count (accepted drafted tokens + 1; n_rollback = n_draft + 1 - out_n). 0 <= n_draft <= 16.
+ * Replaces common_sampler_sample_and_accept_n with a greedy sampler (upstream) and the reference's relaxed acceptance
+ * (patch/srhpm.patch:9-35). wdata: srhpm_verify_accept_work_size bytes. */
+int srhpm_verify_accept_work_size(const srhpm_ctx * ctx, const srhpm_tensor * logits, size_t * size);
+int srhpm_verify_accept(srhpm_ctx * ctx, const srhpm_tensor * logits, const int32_t * draft, int n_draft, float relax,
+                        int32_t * out_ids, int32_t * out_n, void * wdata, size_t wsize, void * stream);
+
+/* Acceptance over a vocabulary sharded across devices: each shard (logits [shard size, n_rows], global ids starting
+ * at vocab_offset) writes one record per row with srhpm_argmax_shard; srhpm_accept_merge takes the records of all
+ * shards ([n_shards][n_rows], in vocabulary order, gathered to one device) and emits what srhpm_verify_accept would
+ * for the whole vocabulary. imax = -1 marks a shard that starts the vocabulary with a NaN logit (argmax 0), -2 a row
+ * of the shard without a non-NaN value. No counterpart in the reference (its head is not sharded). */
+typedef struct srhpm_argmax_record {
+    float   vmax;       /* maximum over the shard's non-NaN logits of the row */
+    int32_t imax;       /* its first (global) index */
+    float   vdraft;     /* logit of the drafted token of this row, when the shard holds it */
+    int32_t has_draft;  /* 1 when it does */
+} srhpm_argmax_record;
+int srhpm_argmax_shard(srhpm_ctx * ctx, const srhpm_tensor * logits, int64_t vocab_offset, const int32_t * draft,
+                       int n_draft, srhpm_argmax_record * out, void * wdata, size_t wsize, void * stream);
+int srhpm_accept_merge(srhpm_ctx * ctx, const srhpm_argmax_record * recs, int n_shards, int n_rows,
+                       const int32_t * draft, int n_draft, float relax, int32_t * out_ids, int32_t * out_n,
+                       void * stream);
+
 /* ---- host-side weight quantizer (CPU) -------------------------------------------------------------------------
  * f32 rows -> GGUF blocks of `type` (Q4_K, Q5_K, Q6_K, Q3_K, IQ4_XS, Q8_0, F16). Host pointers. Returns the bytes
  * written. ggml_quantize_chunk's contract (upstream); imatrix is accepted and ignored (uniform importance). */

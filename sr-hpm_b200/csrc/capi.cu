@@ -128,6 +128,18 @@ int check_fa(const srhpm_tensor * q, const srhpm_tensor * k, const srhpm_tensor 
     return SRHPM_OK;
 }
 
+// logits f32 [n_vocab, rows], rows contiguous in the vocabulary (nb[0] = 4), any row stride
+int check_logits(const srhpm_tensor * lg, int min_rows) {
+    if (!lg || lg->type != SRHPM_TYPE_F32 || !lg->data) return SRHPM_ERR_INVALID;
+    if (lg->ne[0] < 1 || lg->ne[0] > INT32_MAX || lg->ne[1] < min_rows || lg->ne[2] != 1 || lg->ne[3] != 1) {
+        return SRHPM_ERR_INVALID;
+    }
+    if (lg->nb[0] != 4 || lg->nb[1] % 4 || lg->nb[1] < (size_t) lg->ne[0] * 4 || !aligned(lg->data, 4)) {
+        return SRHPM_ERR_INVALID;
+    }
+    return SRHPM_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -329,6 +341,47 @@ int srhpm_flash_attn_ext(srhpm_ctx * ctx, const srhpm_tensor * q, const srhpm_te
     const int st = check_fa(q, k, v, mask, sinks, dst, &fv);
     if (st != SRHPM_OK) return st;
     return fa_run(ctx, fv, scale, max_bias, softcap, wdata, wsize, (cudaStream_t) stream);
+}
+
+int srhpm_verify_accept_work_size(const srhpm_ctx * ctx, const srhpm_tensor * logits, size_t * size) {
+    if (!ctx || !size) return SRHPM_ERR_INVALID;
+    const int st = check_logits(logits, 1);
+    if (st != SRHPM_OK) return st;
+    if (logits->ne[1] > 17) return SRHPM_UNSUPPORTED;
+    *size = argmax_work_size(ctx->num_sms, (int) logits->ne[0], (int) logits->ne[1]);
+    return SRHPM_OK;
+}
+
+int srhpm_verify_accept(srhpm_ctx * ctx, const srhpm_tensor * logits, const int32_t * draft, int n_draft, float relax,
+                        int32_t * out_ids, int32_t * out_n, void * wdata, size_t wsize, void * stream) {
+    if (!ctx || !out_ids || !out_n || n_draft < 0 || (n_draft > 0 && !draft)) return SRHPM_ERR_INVALID;
+    if (n_draft > 16) return SRHPM_UNSUPPORTED;
+    const int st = check_logits(logits, n_draft + 1);
+    if (st != SRHPM_OK) return st;
+    return accept_run(ctx, (const uint8_t *) logits->data, (int64_t) logits->nb[1], (int) logits->ne[0], n_draft + 1,
+                      draft, n_draft, relax, out_ids, out_n, 0, nullptr, wdata, wsize, (cudaStream_t) stream);
+}
+
+int srhpm_argmax_shard(srhpm_ctx * ctx, const srhpm_tensor * logits, int64_t vocab_offset, const int32_t * draft,
+                       int n_draft, srhpm_argmax_record * out, void * wdata, size_t wsize, void * stream) {
+    if (!ctx || !out || vocab_offset < 0 || n_draft < 0 || (n_draft > 0 && !draft)) return SRHPM_ERR_INVALID;
+    const int st = check_logits(logits, 1);
+    if (st != SRHPM_OK) return st;
+    if (logits->ne[1] > 17 || n_draft > 16) return SRHPM_UNSUPPORTED;
+    return accept_run(ctx, (const uint8_t *) logits->data, (int64_t) logits->nb[1], (int) logits->ne[0],
+                      (int) logits->ne[1], draft, n_draft, 0.0f, nullptr, nullptr, vocab_offset, out, wdata, wsize,
+                      (cudaStream_t) stream);
+}
+
+int srhpm_accept_merge(srhpm_ctx * ctx, const srhpm_argmax_record * recs, int n_shards, int n_rows,
+                       const int32_t * draft, int n_draft, float relax, int32_t * out_ids, int32_t * out_n,
+                       void * stream) {
+    if (!ctx || !recs || !out_ids || !out_n || n_shards < 1 || n_draft < 0 || n_rows < n_draft + 1) {
+        return SRHPM_ERR_INVALID;
+    }
+    if (n_draft > 0 && !draft) return SRHPM_ERR_INVALID;
+    if (n_rows > 17) return SRHPM_UNSUPPORTED;
+    return accept_merge_run(ctx, recs, n_shards, n_rows, draft, n_draft, relax, out_ids, out_n, (cudaStream_t) stream);
 }
 
 }  // extern "C"

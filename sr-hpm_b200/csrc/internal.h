@@ -72,4 +72,13 @@ size_t fa_work_size(int num_sms, int R, int L, int Hkv);
 int    fa_run(srhpm_ctx * ctx, const FaView & v, float scale, float max_bias, float softcap, void * wdata,
               size_t wsize, cudaStream_t stream);
 
+// accept.cu: greedy acceptance (argmax of the target logits, longest accepted prefix)
+size_t argmax_work_size(int num_sms, int n_vocab, int n_rows);
+int    accept_run(srhpm_ctx * ctx, const uint8_t * logits, int64_t ldb, int n_vocab, int n_rows, const int32_t * draft,
+                  int n_draft, float relax, int32_t * out_ids, int32_t * out_n, int64_t vocab_offset,
+                  srhpm_argmax_record * out_recs, void * wdata, size_t wsize, cudaStream_t stream);
+int    accept_merge_run(srhpm_ctx * ctx, const srhpm_argmax_record * recs, int n_shards, int n_rows,
+                        const int32_t * draft, int n_draft, float relax, int32_t * out_ids, int32_t * out_n,
+                        cudaStream_t stream);
+
 }  // namespace srhpm

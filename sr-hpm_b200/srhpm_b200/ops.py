@@ -248,6 +248,61 @@ class Context:
                                               _stream_ptr(stream)), "srhpm_flash_attn_ext")
         return out
 
+    # ---- greedy acceptance ------------------------------------------------------------------------------------------
+    def sample_and_accept_n(self, logits, draft, relax=0.0, stream=None, work=None):
+        """common_sampler_sample_and_accept_n (greedy): logits f32 [>= n_draft + 1, n_vocab] (rows = positions),
+        draft int32 [n_draft] on the device -> (ids int32 [n_draft + 1], n int32 [1]) on the device; the emitted ids
+        are ids[:n]."""
+        assert logits.dtype == torch.float32 and logits.dim() == 2 and logits.stride(1) == 1
+        n_draft = int(draft.numel())
+        lv = _tensor_view(logits, L.F32, [logits.shape[1], logits.shape[0]], [4, logits.stride(0) * 4])
+        sz = ctypes.c_size_t()
+        L.check(self.lib.srhpm_verify_accept_work_size(self.handle, ctypes.byref(lv), ctypes.byref(sz)),
+                "srhpm_verify_accept_work_size")
+        buf = work if work is not None else self.work(sz.value)
+        ids = torch.empty(n_draft + 1, dtype=torch.int32, device=logits.device)
+        n = torch.empty(1, dtype=torch.int32, device=logits.device)
+        d = draft.to(torch.int32).contiguous() if n_draft else None
+        L.check(self.lib.srhpm_verify_accept(self.handle, ctypes.byref(lv),
+                                             ctypes.c_void_p(d.data_ptr()) if d is not None else None, n_draft,
+                                             relax, ctypes.c_void_p(ids.data_ptr()), ctypes.c_void_p(n.data_ptr()),
+                                             ctypes.c_void_p(buf.data_ptr()), buf.numel(), _stream_ptr(stream)),
+                "srhpm_verify_accept")
+        return ids, n
+
+    def argmax_shard(self, logits, vocab_offset, draft=None, stream=None, work=None):
+        """Per-row record of a vocabulary shard: uint8 [rows, 16] (srhpm_argmax_record) on the device."""
+        assert logits.dtype == torch.float32 and logits.dim() == 2 and logits.stride(1) == 1
+        rows = logits.shape[0]
+        lv = _tensor_view(logits, L.F32, [logits.shape[1], rows], [4, logits.stride(0) * 4])
+        sz = ctypes.c_size_t()
+        L.check(self.lib.srhpm_verify_accept_work_size(self.handle, ctypes.byref(lv), ctypes.byref(sz)),
+                "srhpm_verify_accept_work_size")
+        buf = work if work is not None else self.work(sz.value)
+        rec = torch.empty((rows, 16), dtype=torch.uint8, device=logits.device)
+        n_draft = int(draft.numel()) if draft is not None else 0
+        d = draft.to(torch.int32).contiguous() if n_draft else None
+        L.check(self.lib.srhpm_argmax_shard(self.handle, ctypes.byref(lv), vocab_offset,
+                                            ctypes.c_void_p(d.data_ptr()) if d is not None else None, n_draft,
+                                            ctypes.c_void_p(rec.data_ptr()), ctypes.c_void_p(buf.data_ptr()),
+                                            buf.numel(), _stream_ptr(stream)), "srhpm_argmax_shard")
+        return rec
+
+    def accept_merge(self, recs, draft, relax=0.0, stream=None):
+        """recs uint8 [n_shards, rows, 16] (argmax_shard outputs in vocabulary order) -> (ids, n) as
+        sample_and_accept_n."""
+        recs = recs.contiguous()
+        n_shards, rows = recs.shape[0], recs.shape[1]
+        n_draft = int(draft.numel())
+        ids = torch.empty(n_draft + 1, dtype=torch.int32, device=recs.device)
+        n = torch.empty(1, dtype=torch.int32, device=recs.device)
+        d = draft.to(torch.int32).contiguous() if n_draft else None
+        L.check(self.lib.srhpm_accept_merge(self.handle, ctypes.c_void_p(recs.data_ptr()), n_shards, rows,
+                                            ctypes.c_void_p(d.data_ptr()) if d is not None else None, n_draft, relax,
+                                            ctypes.c_void_p(ids.data_ptr()), ctypes.c_void_p(n.data_ptr()),
+                                            _stream_ptr(stream)), "srhpm_accept_merge")
+        return ids, n
+
     def quantize_rows_q8_K(self, X, stream=None):
         X = X.contiguous()
         N, K = X.shape
