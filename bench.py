@@ -453,6 +453,9 @@ def run_gpu(args):
         c1 = [i for i, op in enumerate(ops) if op == (4, 12, 17408, 5120)]
         if op_ms and c1:
             cfg["q4_K_17408x5120_N4_us"] = round(sum(op_ms[i] for i in c1) / len(c1) * 1e3, 2)
+        if world == 1 and not args.no_attn:
+            cfg["attention_q8_0"] = measure_attention(ctx, dev, peak)
+            cfg["accept_k8_vocab151936"] = measure_accept(ctx, dev)
         cpu = None
         if world == 1 and not args.no_cpu:
             gbs, secs, passes, nth, kind, variant = cpu_sample(host_w, host_x, base_ops, args.cpu_seconds)
@@ -484,6 +487,98 @@ def run_gpu(args):
     return 0
 
 
+def measure_attention(ctx, dev, peak, reps=20, lengths=(8192, 32768, 131072)):
+    """8 query rows, 24 query heads, 4 KV heads, head_dim 256, causal mask among the draft rows,
+    q8_0 K/V (N(0,1) before quantization) of L past tokens, Q N(0,1) / 16. Timed as CUDA-graph replays over copies
+    of the KV cache that together exceed L2."""
+    import torch
+    import srhpm_b200 as S
+    H, Hkv, N, D = 24, 4, 8, 256
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    out = {}
+    for L in lengths:
+        nbytes = 2176 * L + 2 * H * N * D * 4
+        ncopy = max(2, -(-400_000_000 // nbytes))
+        q = torch.randn((H, N, D), device=dev, generator=g) / 16
+        kv = []
+        for _ in range(ncopy):
+            pair = []
+            for _ in range(2):
+                x = torch.randn((Hkv * L, D), device=dev, generator=g)
+                pair.append(ctx.quantize_rows_q8_0(x).view(Hkv, L, 272))
+                del x
+            kv.append(pair)
+        mask = torch.zeros((N, L), dtype=torch.float16, device=dev)
+        for t in range(N):
+            mask[t, L - N + t + 1:] = float("-inf")
+        o = torch.empty((N, H, D), device=dev)
+        st, ws = ctx.flash_attn_ext_work_size(q, kv[0][0], kv[0][1], S.Q8_0)
+        work = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+        for i in range(3):
+            ctx.flash_attn_ext(q, *kv[i % ncopy], S.Q8_0, mask=mask, out=o, work=work)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                for i in range(ncopy):
+                    ctx.flash_attn_ext(q, *kv[i], S.Q8_0, mask=mask, out=o, work=work)
+        torch.cuda.synchronize()
+        graph.replay()
+        torch.cuda.synchronize()
+        rounds = max(1, reps // ncopy)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(rounds):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ctx.check()
+        us = e0.elapsed_time(e1) * 1e3 / (rounds * ncopy)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[str(L)] = {"us": round(us, 2), "GBps": round(gbs, 1), "frac": round(gbs / peak, 4), "bytes": nbytes}
+        del graph, kv
+        torch.cuda.empty_cache()
+    return out
+
+
+def measure_accept(ctx, dev, reps=50):
+    """Greedy acceptance over the BASELINE 27B head: logits f32 [9, 151936] (k = 8), all drafted tokens accepted
+    (the longest scan)."""
+    import torch
+    V, k = 151936, 8
+    g = torch.Generator(device=dev)
+    g.manual_seed(4)
+    ncopy = max(2, -(-400_000_000 // ((k + 1) * V * 4)))
+    lgs = [torch.randn((k + 1, V), device=dev, generator=g) for _ in range(ncopy)]
+    drafts = [lg[:k].argmax(dim=1).to(torch.int32) for lg in lgs]
+    for i in range(3):
+        ctx.sample_and_accept_n(lgs[i % ncopy], drafts[i % ncopy])
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            for i in range(ncopy):
+                ctx.sample_and_accept_n(lgs[i], drafts[i])
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    rounds = max(1, reps // ncopy)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(rounds):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ctx.check()
+    us = e0.elapsed_time(e1) * 1e3 / (rounds * ncopy)
+    nbytes = (k + 1) * V * 4
+    return {"us": round(us, 2), "GBps": round(nbytes / (us * 1e-6) / 1e9, 1), "logits_bytes": nbytes, "draft": k}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -494,8 +589,18 @@ def main():
     ap.add_argument("--eager", action="store_true", help="time eager calls instead of a captured graph")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU time of the CPU-baseline sample")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-attn", action="store_true", help="skip the attention and acceptance measurements")
+    ap.add_argument("--attn", type=int, default=None, help="time only the attention at this KV length (profiling)")
     ap.add_argument("--traffic", type=float, default=None, help="ncu dram bytes per launch, when captured")
     args = ap.parse_args()
+    if args.attn:
+        import torch
+        import srhpm_b200 as S
+        ctx = S.Context(0)
+        peak, kind = peaks()
+        print(json.dumps({"attention_q8_0": measure_attention(ctx, torch.device("cuda", 0), peak, lengths=(args.attn,)),
+                          "peak_kind": kind}))
+        return 0
     if args.warmup < 3 and args.impl == "srhpm":
         args.warmup = 3
     if args.impl == "reference":
