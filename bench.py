@@ -34,6 +34,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "sr-hpm_b200"))
 
+JSON_OUT = sys.stdout  # replaced in main() by a private handle on the real stdout
 METRIC = "quantized verify-GEMM HBM GB/s (% peak) at k=2–8; 27B verify steps/sec"
 SHAPES = [(5120, 5120), (6144, 5120), (17408, 5120), (5120, 17408)]
 TYPE_NAMES = ["q4_K", "q5_K", "q6_K", "q8_0", "iq4_xs"]
@@ -228,7 +229,7 @@ def run_reference(args):
                                    f"{O.ref_variant() or 'none'} (Q8_0: restated stock path)"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line))
+    print(json.dumps(line), file=JSON_OUT, flush=True)
     return 0
 
 
@@ -249,6 +250,7 @@ def run_gpu(args):
     import torch
     import torch.distributed as dist
     import srhpm_b200 as S
+    from srhpm_b200 import shard
     world, rank, local = dist_setup()
     dev = torch.device("cuda", local)
     ctx = S.Context(local)
@@ -267,7 +269,7 @@ def run_gpu(args):
     for (N, t, rows, K), c in zip(ops, copy_of):
         if (t, rows, K, c) in shards:
             continue
-        r0, r1 = rows * rank // world, rows * (rank + 1) // world
+        r0, r1 = shard.row_range(rows, world, rank)
         shards[(t, rows, K, c)] = (S.QuantTensor.from_blocks(host_w[(t, rows, K)][r0:r1], t, r1 - r0, K, dev), r0, r1)
     # activations of a step, packed in one buffer (one H2D per step in the end-to-end pass)
     keys = sorted({(N, K) for N, t, rows, K in ops})
@@ -290,24 +292,21 @@ def run_gpu(args):
     ws = max(ctx.mul_mat_work_size(shards[(t, rows, K, c)][0], xs[(N, K)])[1]
              for (N, t, rows, K), c in zip(ops, copy_of))
     work = torch.empty(ws, dtype=torch.uint8, device=dev)
-    parts = []
     runs = []
+    # several ranks: every product writes its row slice into one packed buffer (slices padded to ceil(rows / world)
+    # rows so that all ranks' buffers have one size) and one all-gather per step hands every rank all the slices;
+    # y_dev is then the gathered buffer [world][packed slices]
+    if world > 1:
+        packed = shard.PackedSlices([(N, rows) for N, t, rows, K in ops], world)
+        y_local = torch.zeros(packed.size, dtype=torch.float32, device=dev)
+        y_dev = torch.zeros(world * packed.size, dtype=torch.float32, device=dev)
+        y_host = torch.empty(world * packed.size, dtype=torch.float32).pin_memory()
     for i, ((N, t, rows, K), c) in enumerate(zip(ops, copy_of)):
         W, r0, r1 = shards[(t, rows, K, c)]
         if world == 1:
             runs.append(ctx.prepare_mul_mat(W, xs[(N, K)], ys[i], work))
-            parts.append(None)
         else:
-            part = torch.empty((N, r1 - r0), dtype=torch.float32, device=dev)
-            runs.append(ctx.prepare_mul_mat(W, xs[(N, K)], part, work))
-            parts.append(part)
-
-    def gather(i):
-        N, t, rows, K = ops[i]
-        gathered = [torch.empty((N, rows * (j + 1) // world - rows * j // world), dtype=torch.float32, device=dev)
-                    for j in range(world)]
-        dist.all_gather(gathered, parts[i])
-        torch.cat(gathered, dim=1, out=ys[i])
+            runs.append(ctx.prepare_mul_mat(W, xs[(N, K)], packed.local_view(y_local, i, rank), work))
 
     def step(events=None):
         for i, run in enumerate(runs):
@@ -316,8 +315,8 @@ def run_gpu(args):
             run()
             if events is not None:
                 events[i][1].record()
-            if world > 1:
-                gather(i)
+        if world > 1:
+            dist.all_gather_into_tensor(y_dev, y_local)
 
     def barrier():
         if world > 1:
@@ -328,13 +327,13 @@ def run_gpu(args):
     torch.cuda.synchronize()
     ctx.check()
 
-    # the timed step is replayed from a CUDA graph (no host launch gaps between the 2 kernels of each product);
-    # with several ranks the NCCL all-gathers run eagerly
+    # the timed step is replayed from a CUDA graph (no host launch gaps between the 2 kernels of each product; with
+    # several ranks the graph holds the step's NCCL all-gather too)
     # "external" events stay real timing events when recorded inside a captured graph
     op_ev = [(torch.cuda.Event(enable_timing=True, external=True), torch.cuda.Event(enable_timing=True, external=True))
              for _ in ops]
     graph = None
-    if world == 1 and not args.eager:
+    if not args.eager:
         graph = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
@@ -478,7 +477,7 @@ def run_gpu(args):
             "gpu_launches": int(launches),
             "clocks": clk,
         }
-        print(json.dumps(line))
+        print(json.dumps(line), file=JSON_OUT, flush=True)
     graph = graph_ev = None
     if world > 1:
         dist.barrier()
@@ -580,6 +579,12 @@ def measure_accept(ctx, dev, reps=50):
 
 
 def main():
+    # stdout carries exactly one JSON line: keep a private handle on it and send everything else that libraries
+    # write to file descriptor 1 (NCCL prints its version line there) to stderr
+    global JSON_OUT
+    JSON_OUT = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -599,7 +604,7 @@ def main():
         ctx = S.Context(0)
         peak, kind = peaks()
         print(json.dumps({"attention_q8_0": measure_attention(ctx, torch.device("cuda", 0), peak, lengths=(args.attn,)),
-                          "peak_kind": kind}))
+                          "peak_kind": kind}), file=JSON_OUT, flush=True)
         return 0
     if args.warmup < 3 and args.impl == "srhpm":
         args.warmup = 3

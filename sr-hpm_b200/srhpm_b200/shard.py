@@ -1,0 +1,73 @@
+"""Sharding of the verify path across the GPUs of one box (one process per GPU).
+
+Output rows of a weight matrix are independent, so the verify GEMM shards by rows exactly as the reference splits a
+matrix between its CPU and GPU (patch/srhpm.patch:6497-6529): rank j computes rows [rows*j/world, rows*(j+1)/world)
+and the slices are all-gathered. Row-parallel layers (attention output, FFN down) shard K on 256-column super-block
+boundaries and sum the partial products. The head shards the vocabulary; the acceptance merges per-shard argmax
+records (srhpm_argmax_shard / srhpm_accept_merge). Attention shards by KV head.
+
+This module holds the index arithmetic and the gather layout; the collectives are torch.distributed calls made by the
+caller (NCCL on GPUs, gloo in the CPU tests).
+"""
+
+QK = 256  # columns per K-quant super-block
+
+
+def row_range(rows, world, rank):
+    """Rows [r0, r1) of `rows` owned by `rank` (balanced; sizes differ by at most one)."""
+    return rows * rank // world, rows * (rank + 1) // world
+
+
+def k_range(K, world, rank):
+    """Columns [k0, k1) of a K-split (row-parallel) shard, on super-block boundaries (sizes differ by at most one
+    super-block: 68 super-blocks over 8 ranks give 9 or 8)."""
+    nsb = K // QK
+    return nsb * rank // world * QK, nsb * (rank + 1) // world * QK
+
+
+def vocab_range(n_vocab, world, rank):
+    """Vocabulary ids [v0, v1) of a head shard."""
+    return n_vocab * rank // world, n_vocab * (rank + 1) // world
+
+
+def kv_heads(n_kv, world, rank):
+    """KV heads [g0, g1) of an attention shard (world must divide n_kv)."""
+    if n_kv % world:
+        raise ValueError(f"{n_kv} KV heads do not split over {world} ranks")
+    per = n_kv // world
+    return per * rank, per * (rank + 1)
+
+
+class PackedSlices:
+    """Layout of the row slices of several products in one buffer per rank, for one all-gather per step.
+
+    Product i (N_i rows of activations, rows_i output rows) owns N_i * ceil(rows_i / world) floats of every rank's
+    buffer (the slice of rank j fills N_i * (r1 - r0) of them, as an [N_i, r1 - r0] row-major block), so that all ranks'
+    buffers have one size. After all-gathering into [world][size], `unpack` rebuilds each product's [N_i, rows_i]."""
+
+    def __init__(self, shapes, world):
+        self.shapes = list(shapes)  # (N, rows)
+        self.world = world
+        self.offsets = []
+        off = 0
+        for N, rows in self.shapes:
+            self.offsets.append(off)
+            off += N * (-(-rows // world))
+        self.size = off
+
+    def local_view(self, buf, i, rank):
+        """The [N, r1 - r0] block of product i in rank `rank`'s buffer (a torch view or numpy view)."""
+        N, rows = self.shapes[i]
+        r0, r1 = row_range(rows, self.world, rank)
+        o = self.offsets[i]
+        return buf[o:o + N * (r1 - r0)].reshape(N, r1 - r0)
+
+    def unpack(self, gathered, i):
+        """Product i as [N, rows] from the gathered buffer ([world * size], ranks in order), concatenated along rows."""
+        N, rows = self.shapes[i]
+        parts = [self.local_view(gathered[j * self.size:(j + 1) * self.size], i, j) for j in range(self.world)]
+        if hasattr(parts[0], "new_empty"):  # torch
+            import torch
+            return torch.cat(parts, dim=1)
+        import numpy as np
+        return np.concatenate(parts, axis=1)
