@@ -123,12 +123,13 @@ int srhpm_quantize_rows_q8_0(srhpm_ctx * ctx, const srhpm_tensor * X, void * blo
 /* ---- multi-query attention -------------------------------------------------------------------------------------
  * dst = softmax(scale * Q K^T [softcap] + slope * mask [+ sink]) V in ggml_flash_attn_ext semantics, for the few query
  * tokens of a verification pass: q f32 [DK, N, H] (token stride nb[1], head stride nb[2]), k / v [256, L, Hkv] of type
- * q8_0 (DK = DV = 256; token stride nb[1] and KV-head stride nb[2] multiples of 16 bytes, data 16-byte aligned, so
+ * q8_0 or f16 (DK = DV = 256; token stride nb[1] and KV-head stride nb[2] multiples of 16 bytes, data 16-byte aligned, so
  * both the [Hkv][L] layout and llama.cpp's [L][Hkv] cache view are accepted), mask f16 [>= L, >= N, ne2] applied to
  * head h from slice h % ne2 (may be NULL), sinks f32 [H] (may be NULL), dst f32 [DV, H, N] (dst row of head h and
  * token t at h * nb[1] + t * nb[2]). H a multiple of Hkv, 1 <= N <= 16. Q is quantized per row to q8_0 with the
- * context's q8_0 mode and Q.K is the exact q8_0 integer dot product, as the reference's grouped path computes it.
- * Other types / head sizes: SRHPM_UNSUPPORTED. wdata: srhpm_flash_attn_ext_work_size bytes (0 when the KV range is
+ * context's q8_0 mode and Q.K is the exact q8_0 integer dot product, as the reference's grouped path computes it;
+ * with an f16 cache Q stays f32 (split into two f16 parts on the tensor cores). Other types / head sizes:
+ * SRHPM_UNSUPPORTED. wdata: srhpm_flash_attn_ext_work_size bytes (0 when the KV range is
  * not split), ordered on `stream` like every call.
  * Replaces ggml_fa_gqa_small_work_size / ggml_compute_forward_flash_attn_ext_gqa_small (patch/srhpm.patch:555-824)
  * behind the gate at patch/srhpm.patch:833-841. */

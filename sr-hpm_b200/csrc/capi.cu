@@ -70,7 +70,7 @@ int check_fa(const srhpm_tensor * q, const srhpm_tensor * k, const srhpm_tensor 
              const srhpm_tensor * sinks, const srhpm_tensor * dst, FaView * fv) {
     if (!q || !k || !v) return SRHPM_ERR_INVALID;
     if (q->type != SRHPM_TYPE_F32 || k->type != v->type) return SRHPM_UNSUPPORTED;
-    if (k->type != SRHPM_TYPE_Q8_0) return SRHPM_UNSUPPORTED;
+    if (k->type != SRHPM_TYPE_Q8_0 && k->type != SRHPM_TYPE_F16) return SRHPM_UNSUPPORTED;
     if (q->ne[3] != 1 || k->ne[3] != 1 || v->ne[3] != 1) return SRHPM_UNSUPPORTED;
     const int64_t DK = k->ne[0], DV = v->ne[0], L = k->ne[1], Hkv = k->ne[2], N = q->ne[1], H = q->ne[2];
     if (q->ne[0] != DK) return SRHPM_ERR_INVALID;
@@ -78,7 +78,7 @@ int check_fa(const srhpm_tensor * q, const srhpm_tensor * k, const srhpm_tensor 
     if (N < 1 || N > 16) return SRHPM_UNSUPPORTED;
     if (L < 1 || L > INT32_MAX || Hkv < 1 || H < 1 || H > 65536 || H % Hkv != 0) return SRHPM_ERR_INVALID;
     if (v->ne[1] != L || v->ne[2] != Hkv) return SRHPM_ERR_INVALID;
-    const size_t rowb = srhpm_row_size(SRHPM_TYPE_Q8_0, 256);
+    const size_t rowb = srhpm_row_size(k->type, 256);
     if (k->nb[0] != srhpm_type_size(k->type) || v->nb[0] != srhpm_type_size(v->type)) return SRHPM_ERR_INVALID;
     if (k->nb[1] < rowb || v->nb[1] < rowb || k->nb[2] < rowb || v->nb[2] < rowb) return SRHPM_ERR_INVALID;
     if (k->nb[1] % 16 || k->nb[2] % 16 || v->nb[1] % 16 || v->nb[2] % 16) return SRHPM_ERR_ALIGN;
@@ -120,8 +120,9 @@ int check_fa(const srhpm_tensor * q, const srhpm_tensor * k, const srhpm_tensor 
     fv->v    = (const uint8_t *) v->data;
     fv->vnb1 = (int64_t) v->nb[1];
     fv->vnb2 = (int64_t) v->nb[2];
-    fv->L    = (int) L;
-    fv->Hkv  = (int) Hkv;
+    fv->L       = (int) L;
+    fv->Hkv     = (int) Hkv;
+    fv->kv_type = k->type;
     fv->dst  = (float *) dst->data;
     fv->dnb1 = (int64_t) dst->nb[1];
     fv->dnb2 = (int64_t) dst->nb[2];

@@ -717,6 +717,415 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     if (warp == 0) tc::tmem_free(tbase, 512);
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// f16 KV cache: the same pipeline without per-block scales. Q.K on kind::f16 with Q split into f16 hi + lo parts
+// (exact to ~2^-22 of Q, so the scores carry f32-level accuracy as the reference's f32 GEMM does); the K tile arrives
+// as SWIZZLE_128B planes of 64 dims (K-major operand), the V tile likewise and is the MN-major V^T operand as it lands
+// (no conversion). Ring: 4 slots of 32 KB per tile (K dims 0-127, 128-255, V dims 0-127, 128-255); K slots return to
+// the producer when Q.K completes, V slots when P.V does.
+
+constexpr int kSlotF = kT * 256;  // 32768: 128 tokens x 128 dims of f16
+
+template <int RP> struct SmemF {
+    static constexpr int ring  = 0;                   // 4 slots
+    static constexpr int p     = ring + 4 * kSlotF;
+    static constexpr int qop   = p + RP * kT * 2;     // 16 dim-steps x {hi, lo} x [2][RP][16]
+    static constexpr int red   = qop + 32 * RP * 32;  // f32 [2][4][RP]
+    static constexpr int mu    = red + 2 * 4 * RP * 4;
+    static constexpr int al    = mu + RP * 4;
+    static constexpr int fac   = al + RP * 4;
+    static constexpr int slope = fac + RP * 4;
+    static constexpr int moff  = slope + RP * 4;      // int64 [RP]
+    static constexpr int mslot = moff + RP * 8;       // int32 [RP]
+    static constexpr int mbuf  = (mslot + RP * 4 + 15) / 16 * 16;  // f16 [2][8][kT]
+    static constexpr int bar   = mbuf + 2 * 8 * kT * 2;
+    static constexpr int misc  = bar + 12 * 8;        // tmem base, flags[3]
+    static constexpr int total = misc + 16;
+    static constexpr int alloc = total + 1024;
+};
+
+__device__ __forceinline__ void tma3h(uint8_t * dst, const CUtensorMap * m, int x, int y, int z, uint64_t * bar) {
+    tma3(dst, m, x, y, z, bar);
+}
+
+template <int RP>
+__global__ void __launch_bounds__(kFaThreads, 1)
+    fa_f16_kernel(const __grid_constant__ CUtensorMap mk, const __grid_constant__ CUtensorMap mv, const FaArgs a) {
+    using S          = SmemF<RP>;
+    constexpr int RH = RP / 4;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t * sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t * full    = reinterpret_cast<uint64_t *>(sm + S::bar);
+    uint64_t * empty   = full + 4;
+    uint64_t * s_full  = empty + 4;
+    uint64_t * s_free  = s_full + 1;
+    uint64_t * pv_rdy  = s_full + 2;
+    uint64_t * pv_done = s_full + 3;
+    uint32_t * tptr    = reinterpret_cast<uint32_t *>(sm + S::misc);
+    int *      flags   = reinterpret_cast<int *>(sm + S::misc + 4);
+    float *    red     = reinterpret_cast<float *>(sm + S::red);
+    float *    mu      = reinterpret_cast<float *>(sm + S::mu);
+    float *    al      = reinterpret_cast<float *>(sm + S::al);
+    float *    fac     = reinterpret_cast<float *>(sm + S::fac);
+    float *    slope2  = reinterpret_cast<float *>(sm + S::slope);
+    int64_t *  moff    = reinterpret_cast<int64_t *>(sm + S::moff);
+    int *      mslot   = reinterpret_cast<int *>(sm + S::mslot);
+    uint16_t * mbuf    = reinterpret_cast<uint16_t *>(sm + S::mbuf);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int chunk = blockIdx.x;
+    const int g = blockIdx.y / a.nrg, rg = blockIdx.y % a.nrg;
+    const int t0 = chunk * a.chunk_len, t1 = min(a.L, t0 + a.chunk_len);
+    const int nt = (t1 - t0 + kT - 1) / kT;
+    const int row0 = rg * kRG;
+    const int rows = min(RP, a.R - row0);
+    const int q = warp & 3, qr = (warp >> 2) & 3, t = 32 * q + lane, rbase = qr * RH;
+    bool      bad = false;
+
+    if (tid == 0) {
+        for (int i = 0; i < 4; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);  // released by a tcgen05.commit
+        }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, kCW);
+        mbar_init(pv_rdy, kCW);
+        mbar_init(pv_done, 1);
+        fence_mbar_init();
+        flags[0] = flags[1] = flags[2] = 0;
+    }
+    if (warp == 0) tc::tmem_alloc(tptr, 256);
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+    const uint32_t tbase = *tptr;
+    const uint32_t tS    = tbase;        // S^T [token][row] at columns 0..RP-1 (f32)
+    const uint32_t tO    = tbase + RP;   // O^T halves at tO, tO + RP
+
+    // tile i uses slot s for: K dims 128 s.. (s = 0, 1), V dims 128 (s - 2).. (s = 2, 3); two 64-dim planes each
+    auto produce = [&](int i, int sl) {
+        uint8_t * dst = sm + S::ring + sl * kSlotF;
+        const int tok = t0 + i * kT;
+        mbar_arrive_expect_tx(&full[sl], kSlotF);
+        const CUtensorMap * m  = sl < 2 ? &mk : &mv;
+        const int           x0 = 128 * (sl & 1);
+        tma3h(dst, m, x0, tok, g, &full[sl]);
+        tma3h(dst + kPlane, m, x0 + 64, tok, g, &full[sl]);
+    };
+    if (warp == kCW && lane == 0) {
+        prefetch_tmap(&mk);
+        prefetch_tmap(&mv);
+        for (int sl = 0; sl < 4; sl++) produce(0, sl);
+    }
+    __syncwarp();
+
+    // Q rows -> f16 hi + lo parts into the 16 dim-step operands; per-row constants
+    if (warp < kCW) {
+        for (int u = tid; u < RP * 64; u += kCW * 32) {  // 4 dims per unit
+            const int r = u >> 6, d0 = (u & 63) * 4;
+            float     x[4] = { 0.0f, 0.0f, 0.0f, 0.0f };
+            if (r < rows) {
+                const int     rr  = row0 + r;
+                const int     h   = g * a.G + rr / a.N, tq = rr % a.N;
+                const float * src = reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(a.q) +
+                                                                     tq * a.qnb1 + h * a.qnb2);
+#pragma unroll
+                for (int e = 0; e < 4; e++) x[e] = src[d0 + e];
+            }
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int    d = d0 + e, j = d >> 4, xx = d & 15;
+                const __half hi = __float2half_rn(x[e]);
+                const __half lo = __float2half_rn(x[e] - __half2float(hi));
+                const int    o  = (xx >> 3) * RP * 16 + r * 16 + (xx & 7) * 2;
+                *reinterpret_cast<__half *>(sm + S::qop + (2 * j) * RP * 32 + o)     = hi;
+                *reinterpret_cast<__half *>(sm + S::qop + (2 * j + 1) * RP * 32 + o) = lo;
+            }
+        }
+        if (tid < RP) {
+            const int r = tid, rr = row0 + min(r, rows - 1);
+            const int h = g * a.G + rr / a.N, tq = rr % a.N;
+            float     sl = 1.0f;
+            if (a.max_bias > 0.0f) {
+                sl = h < a.n_head_log2 ? powf(a.m0, (float) (h + 1)) : powf(a.m1, (float) (2 * (h - a.n_head_log2) + 1));
+            }
+            slope2[r] = sl * kLog2e;
+            moff[r]   = a.mask ? (int64_t) tq * a.mnb1 + (int64_t) (h % a.mne2) * a.mnb2 : 0;
+            mslot[r]  = tq;
+            mu[r]     = -INFINITY;
+        }
+        if (a.mask_mode == 1 && tid < a.N * 16) {  // N <= 8
+            *reinterpret_cast<uint4 *>(mbuf + (tid >> 4) * kT + 8 * (tid & 15)) = mask_piece(a, tid, t0);
+        }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc::fence_before();
+    __syncthreads();
+    tc::fence_after();
+
+    const uint32_t qop_s = smem_u32(sm + S::qop);
+    const uint32_t p_s   = smem_u32(sm + S::p);
+
+    if (warp == kCW) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            for (int i = 1; i < nt && !bad; i++) {
+                for (int sl = 0; sl < 4; sl++) {
+                    if (!wait_or_flag(&empty[sl], (i - 1) & 1, a.status, bad)) break;
+                    produce(i, sl);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == kCW + 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idqk = tc::idesc(tc::kD_F32, tc::kAB_F16, tc::kAB_F16, tc::kKMajor, tc::kKMajor, RP, 128);
+            constexpr uint32_t idpv = tc::idesc(tc::kD_F32, tc::kAB_F16, tc::kAB_F16, tc::kMNMajor, tc::kMNMajor, RP,
+                                                128);
+            auto issue_qk = [&](int i) {
+                wait_or_flag(&full[0], i & 1, a.status, bad);
+                wait_or_flag(&full[1], i & 1, a.status, bad);
+                tc::fence_after();
+                const uint32_t kb = smem_u32(sm + S::ring);
+#pragma unroll
+                for (int j = 0; j < 16; j++) {  // 16 dims per MMA: 32 bytes of a 128-byte swizzled row
+                    const int      jj = j & 7;
+                    const uint64_t ad = tc::sdesc(kb + (j >> 3) * kSlotF + (jj >> 2) * kPlane + (jj & 3) * 32, 16,
+                                                  1024) | (2ull << 61);
+                    tc::mma_f16(tS, ad, tc::sdesc(qop_s + (2 * j) * RP * 32, RP * 16, 128), idqk, (uint32_t) (j > 0));
+                    tc::mma_f16(tS, ad, tc::sdesc(qop_s + (2 * j + 1) * RP * 32, RP * 16, 128), idqk, 1u);
+                }
+                tc::commit(s_full);
+                tc::commit(&empty[0]);
+                tc::commit(&empty[1]);
+            };
+            issue_qk(0);
+            for (int i = 0; i < nt; i++) {
+                if (i + 1 < nt) {
+                    wait_or_flag(s_free, i & 1, a.status, bad);
+                    issue_qk(i + 1);
+                }
+                wait_or_flag(pv_rdy, i & 1, a.status, bad);
+                wait_or_flag(&full[2], i & 1, a.status, bad);
+                wait_or_flag(&full[3], i & 1, a.status, bad);
+                tc::fence_after();
+#pragma unroll
+                for (int hf = 0; hf < 2; hf++) {
+                    const uint32_t vb = smem_u32(sm + S::ring + (2 + hf) * kSlotF);
+#pragma unroll
+                    for (int k = 0; k < kT / 16; k++) {  // 16 tokens = two 8-row groups of the swizzled planes
+                        const uint64_t ad = tc::sdesc(vb + k * 2048, kPlane, 1024) | (2ull << 61);
+                        const uint64_t bd = tc::sdesc(p_s + k * 256, 128, kT * 16);
+                        tc::mma_f16(tO + hf * RP, ad, bd, idpv, (uint32_t) (i > 0 || k > 0));
+                    }
+                }
+                tc::commit(pv_done);
+                tc::commit(&empty[2]);
+                tc::commit(&empty[3]);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- compute warps ----------------
+        float l[RH];
+#pragma unroll
+        for (int r = 0; r < RH; r++) l[r] = 0.0f;
+        uint32_t msl[RH / 4];
+#pragma unroll
+        for (int j = 0; j < RH / 4; j++) {
+            msl[j] = 0;
+#pragma unroll
+            for (int e = 0; e < 4; e++) msl[j] |= (uint32_t) (mslot[rbase + 4 * j + e] & 0xff) << (8 * e);
+        }
+        for (int i = 0; i < nt; i++) {
+            uint4      mnext = make_uint4(0, 0, 0, 0);
+            const bool stage = a.mask_mode == 1 && i + 1 < nt && tid < a.N * 16;
+            if (stage) mnext = mask_piece(a, tid, t0 + (i + 1) * kT);
+            wait_or_flag(s_full, i & 1, a.status, bad);
+            tc::fence_after();
+            float s[RH];
+            {
+                uint32_t v[RH];
+                tc::ld_cols<RH>(tc::taddr(tS, q, rbase), v);
+                tc::wait_ld();
+#pragma unroll
+                for (int r = 0; r < RH; r++) s[r] = __uint_as_float(v[r]);
+            }
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(s_free);
+            if (a.softcap_l2 != 0.0f) {
+#pragma unroll
+                for (int r = 0; r < RH; r++) s[r] = a.softcap_l2 * tanhf(s[r] * a.qscale);
+            } else {
+#pragma unroll
+                for (int r = 0; r < RH; r++) s[r] *= a.qscale;
+            }
+            const int  tok   = t0 + i * kT + t;
+            const bool valid = tok < t1;
+            if (a.mask_mode == 1) {
+                const uint16_t * mb = mbuf + (i & 1) * 8 * kT + t;
+#pragma unroll
+                for (int r = 0; r < RH; r++) {
+                    const float sl   = a.max_bias > 0.0f ? slope2[rbase + r] : kLog2e;
+                    const int   sl_r = (msl[r >> 2] >> (8 * (r & 3))) & 0xff;
+                    s[r] = fmaf(sl, half_bits_to_float(mb[sl_r * kT]), s[r]);
+                }
+            } else if (a.mask_mode == 2 && valid) {
+#pragma unroll
+                for (int r = 0; r < RH; r++) {
+                    const uint16_t mv16 = __ldg(reinterpret_cast<const unsigned short *>(a.mask + moff[rbase + r] +
+                                                                                         2 * (int64_t) tok));
+                    s[r] = fmaf(slope2[rbase + r], half_bits_to_float(mv16), s[r]);
+                }
+            }
+            if (!valid) {
+#pragma unroll
+                for (int r = 0; r < RH; r++) s[r] = -INFINITY;
+            }
+            float * redb = red + (i & 1) * 4 * RP;
+            bool    up   = false;
+            float   mx[RH];
+#pragma unroll
+            for (int r = 0; r < RH; r++) mx[r] = redux_max(s[r]);
+#pragma unroll
+            for (int r = 0; r < RH; r++) {
+                if (lane == 0) redb[q * RP + rbase + r] = mx[r];
+                up |= mx[r] > mu[rbase + r] + kLazy;
+            }
+            if (lane == 0 && up) flags[i % 3] = 1;
+            if (stage) {
+                *reinterpret_cast<uint4 *>(mbuf + ((i + 1) & 1) * 8 * kT + (tid >> 4) * kT + 8 * (tid & 15)) = mnext;
+            }
+            named_bar_sync(1, kCW * 32);
+            if (tid == 0) flags[(i + 2) % 3] = 0;
+            const bool resc = flags[i % 3] != 0;
+            if (resc) {
+                if (tid < RP) {
+                    float mt = redb[tid];
+#pragma unroll
+                    for (int w = 1; w < 4; w++) mt = fmaxf(mt, redb[w * RP + tid]);
+                    const float mo = mu[tid];
+                    if (mt > mo + kLazy) {
+                        mu[tid] = mt;
+                        al[tid] = exp2f(mo - mt);
+                    } else {
+                        al[tid] = 1.0f;
+                    }
+                }
+                named_bar_sync(1, kCW * 32);
+            }
+            if (i > 0) {
+                wait_or_flag(pv_done, (i - 1) & 1, a.status, bad);
+                tc::fence_after();
+            }
+            if (resc) {
+#pragma unroll
+                for (int r = 0; r < RH; r++) l[r] *= al[rbase + r];
+                if (i > 0) {
+#pragma unroll
+                    for (int hf = 0; hf < 2; hf++) {
+                        uint32_t       o[RH];
+                        const uint32_t ta = tc::taddr(tO + hf * RP, q, rbase);
+                        tc::ld_cols<RH>(ta, o);
+                        tc::wait_ld();
+#pragma unroll
+                        for (int j = 0; j < RH; j++) o[j] = __float_as_uint(__uint_as_float(o[j]) * al[rbase + j]);
+                        tc::st_cols<RH>(ta, o);
+                    }
+                    tc::wait_st();
+                }
+            }
+            {
+                uint32_t pk[RH / 2];
+#pragma unroll
+                for (int j = 0; j < RH / 2; j++) {
+                    const int   r  = 2 * j, row = rbase + r;
+                    const float m0 = mu[row], m1 = mu[row + 1];
+                    const float p0 = ex2(s[r] - (m0 == -INFINITY ? 0.0f : m0));
+                    const float p1 = ex2(s[r + 1] - (m1 == -INFINITY ? 0.0f : m1));
+                    l[r] += p0;
+                    l[r + 1] += p1;
+                    const __half2 hp = __floats2half2_rn(p0, p1);
+                    pk[j]            = *reinterpret_cast<const uint32_t *>(&hp);
+                }
+                store_p<RH>(sm + S::p, rbase, t, pk);
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc::fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(pv_rdy);
+        }
+
+        // ---------------- epilogue ----------------
+        wait_or_flag(pv_done, (nt - 1) & 1, a.status, bad);
+        tc::fence_after();
+#pragma unroll
+        for (int r = 0; r < RH; r++) {
+            float v = l[r];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) red[(nt & 1) * 4 * RP + q * RP + rbase + r] = v;
+        }
+        named_bar_sync(1, kCW * 32);
+        const bool single = a.n_chunks == 1;
+        if (tid < rows) {
+            const float * rs   = red + (nt & 1) * 4 * RP;
+            float         Ssum = rs[tid];
+#pragma unroll
+            for (int w = 1; w < 4; w++) Ssum += rs[w * RP + tid];
+            const int rr = row0 + tid;
+            float     M  = mu[tid];
+            if (single) {
+                if (Ssum == 0.0f) M = -INFINITY;
+                float ms = 1.0f;
+                if (a.sinks) {
+                    const int   h   = g * a.G + rr / a.N;
+                    const float sk2 = a.sinks[h] * kLog2e;
+                    if (sk2 > M) {
+                        ms   = exp2f(M - sk2);
+                        Ssum = Ssum * ms + 1.0f;
+                    } else {
+                        Ssum += exp2f(sk2 - M);
+                    }
+                }
+                fac[tid] = Ssum == 0.0f ? 0.0f : ms / Ssum;
+            } else {
+                a.part_ms[(int64_t) (g * a.R + rr) * a.n_chunks + chunk] = make_float2(M, Ssum);
+            }
+        }
+        named_bar_sync(1, kCW * 32);
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++) {
+            const int dv = hf * 128 + 32 * q + lane;
+            uint32_t  o[RH];
+            tc::ld_cols<RH>(tc::taddr(tO + hf * RP, q, rbase), o);
+            tc::wait_ld();
+#pragma unroll
+            for (int j = 0; j < RH; j++) {
+                const int r = rbase + j;
+                if (r < rows) {
+                    const int   rr  = row0 + r;
+                    const float val = __uint_as_float(o[j]);
+                    if (single) {
+                        const int h = g * a.G + rr / a.N, tq = rr % a.N;
+                        float * out = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(a.dst) + h * a.dnb1 +
+                                                                tq * a.dnb2);
+                        out[dv] = val * fac[r];
+                    } else {
+                        a.part_acc[((int64_t) (g * a.R + rr) * a.n_chunks + chunk) * kD + dv] = val;
+                    }
+                }
+            }
+        }
+    }
+
+    tc::fence_before();
+    __syncthreads();
+    if (warp == 0) tc::tmem_free(tbase, 256);
+}
+
 // merge of the chunk records of one row (P:787-823), then sinks and normalization; one CTA per (KV head, row)
 __global__ void __launch_bounds__(256) fa_combine_kernel(const FaArgs a) {
     pdl_wait();
@@ -786,35 +1195,55 @@ Plan fa_plan(int num_sms, int R, int L, int Hkv) {
     return p;
 }
 
-template <int RP>
-int launch_fa(srhpm_ctx * ctx, const FaArgs & a, const CUtensorMap & mk128, const CUtensorMap & mk32,
-              const CUtensorMap & mv, cudaStream_t stream) {
-    auto                         kern = fa_q80_kernel<RP>;
-    static std::atomic<unsigned> attr_done{ 0 };
-    if (!(attr_done.load() & (1u << ctx->device))) {
-        const int st = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                        Smem<RP>::alloc));
-        if (st != SRHPM_OK) return st;
-        attr_done.fetch_or(1u << ctx->device);
-    }
-    kern<<<dim3(a.n_chunks, a.Hkv * a.nrg), kFaThreads, Smem<RP>::alloc, stream>>>(mk128, mk32, mv, a);
-    ctx->launches.fetch_add(1);
-    int st = cuda_status(cudaGetLastError());
-    if (st != SRHPM_OK || a.n_chunks == 1) return st;
-
-    cudaLaunchConfig_t   cfg = {};
-    cudaLaunchAttribute  attr[1];
-    cfg.gridDim          = dim3(a.Hkv * a.R);
-    cfg.blockDim         = dim3(kD);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream           = stream;
+int launch_combine(srhpm_ctx * ctx, const FaArgs & a, cudaStream_t stream) {
+    cudaLaunchConfig_t  cfg = {};
+    cudaLaunchAttribute attr[1];
+    cfg.gridDim                                        = dim3(a.Hkv * a.R);
+    cfg.blockDim                                       = dim3(kD);
+    cfg.dynamicSmemBytes                               = 0;
+    cfg.stream                                         = stream;
     attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs                                          = attr;
     cfg.numAttrs                                       = 1;
-    st = cuda_status(cudaLaunchKernelEx(&cfg, fa_combine_kernel, a));
+    const int st = cuda_status(cudaLaunchKernelEx(&cfg, fa_combine_kernel, a));
     ctx->launches.fetch_add(1);
     return st;
+}
+
+template <class K> int set_smem(srhpm_ctx * ctx, K kern, int bytes, std::atomic<unsigned> & done) {
+    if (!(done.load() & (1u << ctx->device))) {
+        const int st = cuda_status(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+        if (st != SRHPM_OK) return st;
+        done.fetch_or(1u << ctx->device);
+    }
+    return SRHPM_OK;
+}
+
+template <int RP>
+int launch_fa(srhpm_ctx * ctx, const FaArgs & a, const CUtensorMap & mk128, const CUtensorMap & mk32,
+              const CUtensorMap & mv, cudaStream_t stream) {
+    static std::atomic<unsigned> done{ 0 };
+    int st = set_smem(ctx, fa_q80_kernel<RP>, Smem<RP>::alloc, done);
+    if (st != SRHPM_OK) return st;
+    fa_q80_kernel<RP><<<dim3(a.n_chunks, a.Hkv * a.nrg), kFaThreads, Smem<RP>::alloc, stream>>>(mk128, mk32, mv, a);
+    ctx->launches.fetch_add(1);
+    st = cuda_status(cudaGetLastError());
+    if (st != SRHPM_OK || a.n_chunks == 1) return st;
+    return launch_combine(ctx, a, stream);
+}
+
+template <int RP>
+int launch_fa_f16(srhpm_ctx * ctx, const FaArgs & a, const CUtensorMap & mk, const CUtensorMap & mv,
+                  cudaStream_t stream) {
+    static std::atomic<unsigned> done{ 0 };
+    int st = set_smem(ctx, fa_f16_kernel<RP>, SmemF<RP>::alloc, done);
+    if (st != SRHPM_OK) return st;
+    fa_f16_kernel<RP><<<dim3(a.n_chunks, a.Hkv * a.nrg), kFaThreads, SmemF<RP>::alloc, stream>>>(mk, mv, a);
+    ctx->launches.fetch_add(1);
+    st = cuda_status(cudaGetLastError());
+    if (st != SRHPM_OK || a.n_chunks == 1) return st;
+    return launch_combine(ctx, a, stream);
 }
 
 }  // namespace
@@ -882,6 +1311,27 @@ int fa_run(srhpm_ctx * ctx, const FaView & v, float scale, float max_bias, float
 
     EncodeTiled enc = fa_encode_fn();
     if (!enc) return SRHPM_ERR_CUDA;
+    if (v.kv_type == SRHPM_TYPE_F16) {
+        a.qscale = softcap != 0.0f ? scale / softcap : scale * kLog2e;  // applied to the f32 scores
+        CUtensorMap      mk, mv;
+        const cuuint64_t dims[3] = { kD, (cuuint64_t) v.L, (cuuint64_t) v.Hkv };
+        const cuuint64_t kst[2]  = { (cuuint64_t) v.knb1, (cuuint64_t) v.knb2 };
+        const cuuint64_t vst[2]  = { (cuuint64_t) v.vnb1, (cuuint64_t) v.vnb2 };
+        const cuuint32_t box[3]  = { 64, kT, 1 }, es[3] = { 1, 1, 1 };
+        if (enc(&mk, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint8_t *>(v.k), dims, kst, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+            enc(&mv, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint8_t *>(v.v), dims, vst, box, es,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS) {
+            return SRHPM_ERR_INVALID;
+        }
+        switch (p.rp) {
+            case 16: return launch_fa_f16<16>(ctx, a, mk, mv, stream);
+            case 32: return launch_fa_f16<32>(ctx, a, mk, mv, stream);
+            default: return launch_fa_f16<48>(ctx, a, mk, mv, stream);
+        }
+    }
     CUtensorMap      mk128, mk32, mv;
     const cuuint64_t kdims[3] = { kRowB / 4, (cuuint64_t) v.L, (cuuint64_t) v.Hkv };
     const cuuint64_t kstr[2]  = { (cuuint64_t) v.knb1, (cuuint64_t) v.knb2 };

@@ -50,7 +50,7 @@ size_t static_work_bytes();
 int    gemm_run_static(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                        const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, cudaStream_t stream);
 
-// fa_decode.cu: multi-query attention over a q8_0 KV cache, DK = DV = 256 (byte strides)
+// fa_decode.cu: multi-query attention over a q8_0 or f16 KV cache, DK = DV = 256 (byte strides)
 struct FaView {
     const float *   q;
     int64_t         qnb1, qnb2;  // token, head
@@ -59,7 +59,7 @@ struct FaView {
     int64_t         knb1, knb2;  // token, KV head
     const uint8_t * v;
     int64_t         vnb1, vnb2;
-    int             L, Hkv;
+    int             L, Hkv, kv_type;  // SRHPM_TYPE_Q8_0 or SRHPM_TYPE_F16
     const uint8_t * mask;  // f16 [L..][N..][mne2] or null
     int64_t         mnb1, mnb2;
     int             mne2;

@@ -189,11 +189,85 @@ def test_fa_status_codes(ctx):
     with pytest.raises(L.SrhpmError) as e:          # head count not a multiple of the KV heads
         ctx.flash_attn_ext(tq[:5], tk, tv, S.Q8_0)
     assert e.value.status == L.ERR_INVALID
-    with pytest.raises(L.SrhpmError) as e:          # f16 cache: not this kernel
+    with pytest.raises(L.SrhpmError) as e:          # K and V of different types
         kf = torch.zeros((2, 256, 512), dtype=torch.uint8, device="cuda")
-        ctx.flash_attn_ext(tq, kf, kf, S.F16)
-    assert e.value.status == L.UNSUPPORTED
+        ctx.flash_attn_ext(tq, kf, tv, S.F16)
+    assert e.value.status in (L.UNSUPPORTED, L.ERR_INVALID)
+    with pytest.raises(L.SrhpmError) as e:          # head size 128: not this kernel
+        k128 = torch.zeros((2, 256, 136), dtype=torch.uint8, device="cuda")
+        ctx.flash_attn_ext(tq[:, :, :128].contiguous(), k128, k128, S.Q8_0)
+    assert e.value.status in (L.UNSUPPORTED, L.ERR_ALIGN)
     with pytest.raises(L.SrhpmError) as e:          # token stride not a multiple of 16 bytes
         kk = torch.zeros((2, 256, 280), dtype=torch.uint8, device="cuda")[:, :, :272]
         ctx.flash_attn_ext(tq, kk, kk, S.Q8_0)
     assert e.value.status == L.ERR_ALIGN
+
+
+# ---- f16 KV cache ---------------------------------------------------------------------------------------------------
+
+def f16_inputs(rng, H, Hkv, N, L, qscale=1 / 16, kscale=1.0):
+    q = (rng.standard_normal((H, N, D)) * qscale).astype(np.float32)
+    k = (rng.standard_normal((Hkv, L, D)) * kscale).astype(np.float16).view(np.uint8)
+    v = rng.standard_normal((Hkv, L, D)).astype(np.float16).view(np.uint8)
+    return q, k, v
+
+
+def run16(ctx, q, k, v, mask=None, sinks=None, **kw):
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    out = ctx.flash_attn_ext(t(q), t(k), t(v), S.F16, mask=t(mask) if mask is not None else None,
+                             sinks=t(sinks) if sinks is not None else None, **kw)
+    torch.cuda.synchronize()
+    ctx.check()
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("H,Hkv,N,L", [(24, 4, 9, 2057), (24, 4, 8, 1000), (6, 2, 5, 192), (8, 8, 1, 77),
+                                       (12, 2, 16, 300), (4, 1, 3, 5000)])
+def test_fa_f16_vs_oracle_and_reference(ctx, ref, H, Hkv, N, L):
+    rng = np.random.default_rng(H * 1000 + L + 1)
+    q, k, v = f16_inputs(rng, H, Hkv, N, L)
+    mask = causal_mask(N, L)
+    got = run16(ctx, q, k, v, mask=mask)
+    exp = O.attention(q, O.F16, k, v, D, L, Hkv, mask=mask.view(np.uint16))
+    assert rel_l2(got, exp) < TOL
+    if ref is not None and 2 <= N <= 8:
+        r = O.ref_fa_gqa(q, O.F16, k, v, D, L, Hkv, mask=mask.view(np.uint16), nth=4, lib=ref)
+        assert rel_l2(got, r) < TOL
+
+
+@pytest.mark.parametrize("extras", ["sinks", "softcap", "alibi", "nomask", "peaky"])
+def test_fa_f16_options(ctx, ref, extras):
+    rng = np.random.default_rng(21)
+    H, Hkv, N, L = 24, 4, 8, 700
+    q, k, v = f16_inputs(rng, H, Hkv, N, L, qscale=1.0 if extras == "peaky" else 1 / 16)
+    mask, sinks, kw = causal_mask(N, L), None, dict(scale=1.0, max_bias=0.0, softcap=0.0)
+    if extras == "sinks":
+        sinks = rng.standard_normal(H).astype(np.float32)
+    elif extras == "softcap":
+        kw.update(scale=4.0, softcap=20.0)
+    elif extras == "alibi":
+        kw.update(max_bias=8.0)
+    elif extras == "peaky":
+        kw.update(scale=0.5)
+    else:
+        mask = None
+    got = run16(ctx, q, k, v, mask=mask, sinks=sinks, **kw)
+    m16 = mask.view(np.uint16) if mask is not None else None
+    exp = O.attention(q, O.F16, k, v, D, L, Hkv, mask=m16, sinks=sinks, **kw)
+    assert rel_l2(got, exp) < TOL
+    if ref is not None:
+        r = O.ref_fa_gqa(q, O.F16, k, v, D, L, Hkv, mask=m16, sinks=sinks, nth=4, lib=ref, **kw)
+        assert rel_l2(got, r) < TOL
+
+
+def test_fa_f16_llama_cache_layout(ctx):
+    rng = np.random.default_rng(22)
+    H, Hkv, N, L = 24, 4, 9, 2057
+    q, k, v = f16_inputs(rng, H, Hkv, N, L)
+    mask = causal_mask(N, L)
+    kl = torch.from_numpy(np.ascontiguousarray(k.transpose(1, 0, 2))).cuda().permute(1, 0, 2)
+    vl = torch.from_numpy(np.ascontiguousarray(v.transpose(1, 0, 2))).cuda().permute(1, 0, 2)
+    out = ctx.flash_attn_ext(torch.from_numpy(q).cuda(), kl, vl, S.F16, mask=torch.from_numpy(mask).cuda())
+    torch.cuda.synchronize()
+    exp = O.attention(q, O.F16, k, v, D, L, Hkv, mask=mask.view(np.uint16))
+    assert rel_l2(out.cpu().numpy(), exp) < TOL
