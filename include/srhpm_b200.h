@@ -169,6 +169,24 @@ int srhpm_accept_merge(srhpm_ctx * ctx, const srhpm_argmax_record * recs, int n_
                        const int32_t * draft, int n_draft, float relax, int32_t * out_ids, int32_t * out_n,
                        void * stream);
 
+/* ---- the element-wise operators of a dense decoder verify step (ggml semantics) ------------------------------------
+ * Device pointers, rows of d contiguous values, n <= 16 rows. These surround the verify GEMMs in a full model step
+ * (the 27B-class benchmark); the reference runs them as stock ggml operators.
+ *   srhpm_get_rows: out[i] = table row ids[i] (f16 or f32 table [d, n_rows] with row stride nb[1]) as f32
+ *   srhpm_add_rms_norm: x += delta (delta may be NULL), then y = x / sqrt(mean(x^2) + eps) * w     (x, y [n][d])
+ *   srhpm_rope_kv: qkv rows [n][ld] = n_head query heads | n_head_kv key heads | n_head_kv value heads of head_dim;
+ *       NeoX rotary embedding (pairs (j, j + head_dim/2), theta_j = pos * theta_base^(-2j/head_dim)) of the query and
+ *       key heads in place, then the keys and values are stored into the caches at token pos[t] (views as for
+ *       srhpm_flash_attn_ext: [head_dim, capacity, n_head_kv], f16 or q8_0 with the context's q8_0 mode)
+ *   srhpm_swiglu: out = silu(gate) * up, n values */
+int srhpm_get_rows(srhpm_ctx * ctx, const srhpm_tensor * table, const int32_t * ids, int n, float * out, void * stream);
+int srhpm_add_rms_norm(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y, int n,
+                       int64_t d, void * stream);
+int srhpm_rope_kv(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int n_head, int n_head_kv, int head_dim,
+                  const int32_t * pos, float theta_base, const srhpm_tensor * k_cache, const srhpm_tensor * v_cache,
+                  void * stream);
+int srhpm_swiglu(srhpm_ctx * ctx, const float * gate, const float * up, float * out, int64_t n, void * stream);
+
 /* ---- host-side weight quantizer (CPU) -------------------------------------------------------------------------
  * f32 rows -> GGUF blocks of `type` (Q4_K, Q5_K, Q6_K, Q3_K, IQ4_XS, Q8_0, F16). Host pointers. Returns the bytes
  * written. ggml_quantize_chunk's contract (upstream); imatrix is accepted and ignored (uniform importance). */

@@ -254,3 +254,98 @@ def random_blocks(qtype, nblocks, rng, d_lo=0.005, d_hi=0.02):
         d = rng.uniform(d_lo, d_hi, size=nblocks).astype(np.float16)
         blocks[:, off:off + 2] = d.view(np.uint8).reshape(nblocks, 2)
     return blocks
+
+
+# ---- a dense decoder verify step, restated -------------------------------------------------------------------------
+# The element-wise ggml operators around the verify GEMMs (upstream ggml, not in the reference: rms_norm + mul,
+# rope_ext NEOX, swiglu, get_rows, cpy into the KV cache) in numpy, and a whole step composed of them with the exact
+# matmul (mul_mat), attention (attention) and acceptance (accept) above.
+
+def rms_norm(x, w, eps):
+    """ggml_rms_norm (sum of squares in double, scale 1/sqrtf(mean + eps)) then ggml_mul by w: f32 [n, d]."""
+    x = np.asarray(x, np.float32)
+    mean = ((x.astype(np.float64) ** 2).sum(axis=-1, keepdims=True) / x.shape[-1]).astype(np.float32)
+    scale = (np.float32(1.0) / np.sqrt(mean + np.float32(eps))).astype(np.float32)
+    return (x * scale * np.asarray(w, np.float32)).astype(np.float32)
+
+
+def rope_neox(x, pos, base):
+    """ggml_rope_ext, mode NEOX over the whole head: x f32 [n, heads, hd]; pairs (j, j + hd/2) turned by
+    pos * base^(-2j/hd). f64 math, f32 result."""
+    x = np.asarray(x, np.float32)
+    hd = x.shape[-1]
+    half = hd // 2
+    theta = np.asarray(pos, np.float64)[:, None] * np.power(float(base), -2.0 * np.arange(half) / hd)[None, :]
+    c, s = np.cos(theta)[:, None, :], np.sin(theta)[:, None, :]
+    x0, x1 = x[..., :half].astype(np.float64), x[..., half:].astype(np.float64)
+    return np.concatenate([x0 * c - x1 * s, x0 * s + x1 * c], axis=-1).astype(np.float32)
+
+
+def swiglu(g, u):
+    """ggml_swiglu: silu(g) * u, f32."""
+    g64 = np.asarray(g, np.float64)
+    return (g64 / (1.0 + np.exp(-g64)) * np.asarray(u, np.float64)).astype(np.float32)
+
+
+def cache_rows(kv_type, x, q8_mode=Q8_0_SIMD):
+    """f32 head rows [..., hd] -> cache bytes [..., row] (ggml_cpy into an f16 or q8_0 cache)."""
+    x = np.asarray(x, np.float32)
+    if kv_type == F16:
+        return x.astype(np.float16).view(np.uint8)
+    flat = x.reshape(-1, x.shape[-1])
+    return np.stack([quantize_row_q8_0(r, q8_mode) for r in flat]).reshape(*x.shape[:-1], -1)
+
+
+def attn_window(layer, full_every, window, n_past, n):
+    """Keys [start, n_past + n) a layer's new rows attend to and the mask f16 [n, L] (causal; sliding layers also hide
+    keys at or beyond `window` positions back): full layers are those with layer % full_every == full_every - 1."""
+    L_all = n_past + n
+    full = window <= 0 or layer % full_every == full_every - 1
+    start = 0 if full else max(0, n_past - window + 1)
+    L = L_all - start
+    m = np.zeros((n, L), np.float16)
+    for t in range(n):
+        p = n_past + t
+        for j in range(L):
+            a = start + j
+            if a > p or (not full and a <= p - window):
+                m[t, j] = -np.inf
+    return start, m
+
+
+def decoder_step(cfg, w, kcache, vcache, ids, n_past, draft, q8_mode=Q8_0_SIMD, relax=0.0):
+    """One verify step of a dense decoder (RMSNorm, fused QKV, NEOX RoPE, GQA attention over the cache, SwiGLU FFN,
+    output head, greedy acceptance). cfg: dict n_layer, d, n_ff, H, Hkv, hd, n_vocab, base, eps, window, full_every,
+    kv_type, types {'qkv', 'o', 'gate', 'up', 'down', 'head'}. w: dict of host GGUF blocks per layer ('qkv'[l], ...),
+    f32 norms ('attn_norm'[l], 'ffn_norm'[l], 'out_norm'), 'head', 'emb' f16 [n_vocab, d]. kcache / vcache: per layer
+    uint8 [capacity, Hkv, row] (updated). Returns (logits f32 [n, n_vocab], accepted ids)."""
+    c = cfg
+    n = len(ids)
+    H, Hkv, hd, d = c["H"], c["Hkv"], c["hd"], c["d"]
+    ty = c["types"]
+    pos = np.arange(n_past, n_past + n)
+    x = w["emb"][np.asarray(ids)].astype(np.float32)
+    for l in range(c["n_layer"]):
+        y = rms_norm(x, w["attn_norm"][l], c["eps"])
+        qkv = mul_mat(ty["qkv"], w["qkv"][l], (H + 2 * Hkv) * hd, d, y, q8_mode).astype(np.float32)
+        q = rope_neox(qkv[:, :H * hd].reshape(n, H, hd), pos, c["base"])
+        k = rope_neox(qkv[:, H * hd:(H + Hkv) * hd].reshape(n, Hkv, hd), pos, c["base"])
+        v = qkv[:, (H + Hkv) * hd:].reshape(n, Hkv, hd)
+        kcache[l][n_past:n_past + n] = cache_rows(c["kv_type"], k, q8_mode)
+        vcache[l][n_past:n_past + n] = cache_rows(c["kv_type"], v, q8_mode)
+        start, mask = attn_window(l, c["full_every"], c["window"], n_past, n)
+        kk = np.ascontiguousarray(kcache[l][start:n_past + n].transpose(1, 0, 2))
+        vv = np.ascontiguousarray(vcache[l][start:n_past + n].transpose(1, 0, 2))
+        att = attention(np.ascontiguousarray(q.transpose(1, 0, 2)), c["kv_type"], kk, vv, hd, n_past + n - start, Hkv,
+                        mask=mask.view(np.uint16), scale=1.0 / np.sqrt(hd), q8_mode=q8_mode)
+        o = mul_mat(ty["o"], w["o"][l], d, H * hd, att.astype(np.float32).reshape(n, H * hd), q8_mode)
+        x = (x + o.astype(np.float32)).astype(np.float32)
+        y = rms_norm(x, w["ffn_norm"][l], c["eps"])
+        g = mul_mat(ty["gate"], w["gate"][l], c["n_ff"], d, y, q8_mode).astype(np.float32)
+        u = mul_mat(ty["up"], w["up"][l], c["n_ff"], d, y, q8_mode).astype(np.float32)
+        h = swiglu(g, u)
+        dn = mul_mat(ty["down"], w["down"][l], d, c["n_ff"], h, q8_mode)
+        x = (x + dn.astype(np.float32)).astype(np.float32)
+    y = rms_norm(x, w["out_norm"], c["eps"])
+    logits = mul_mat(ty["head"], w["head"], c["n_vocab"], d, y, q8_mode).astype(np.float32)
+    return logits, accept(logits, draft, relax)

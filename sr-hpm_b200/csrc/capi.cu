@@ -385,4 +385,42 @@ int srhpm_accept_merge(srhpm_ctx * ctx, const srhpm_argmax_record * recs, int n_
     return accept_merge_run(ctx, recs, n_shards, n_rows, draft, n_draft, relax, out_ids, out_n, (cudaStream_t) stream);
 }
 
+int srhpm_get_rows(srhpm_ctx * ctx, const srhpm_tensor * table, const int32_t * ids, int n, float * out, void * stream) {
+    if (!ctx || !table || !table->data || !ids || !out || n < 1 || n > 16) return SRHPM_ERR_INVALID;
+    if (table->type != SRHPM_TYPE_F16 && table->type != SRHPM_TYPE_F32) return SRHPM_UNSUPPORTED;
+    if (table->nb[0] != srhpm_type_size(table->type) || table->ne[0] < 1) return SRHPM_ERR_INVALID;
+    return get_rows_run(ctx, (const uint8_t *) table->data, (int64_t) table->nb[1], table->type == SRHPM_TYPE_F16, ids,
+                        n, table->ne[0], out, (cudaStream_t) stream);
+}
+
+int srhpm_add_rms_norm(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y, int n,
+                       int64_t d, void * stream) {
+    if (!ctx || !x || !w || !y || n < 1 || n > 16 || d < 1) return SRHPM_ERR_INVALID;
+    return add_rms_norm_run(ctx, x, delta, w, eps, y, n, d, (cudaStream_t) stream);
+}
+
+int srhpm_rope_kv(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int n_head, int n_head_kv, int head_dim,
+                  const int32_t * pos, float theta_base, const srhpm_tensor * k_cache, const srhpm_tensor * v_cache,
+                  void * stream) {
+    if (!ctx || !qkv || !pos || !k_cache || !v_cache || n < 1 || n > 16 || n_head < 1 || n_head_kv < 1) {
+        return SRHPM_ERR_INVALID;
+    }
+    if (head_dim != 256 || ld < (int64_t) (n_head + 2 * n_head_kv) * head_dim) return SRHPM_ERR_INVALID;
+    if (k_cache->type != v_cache->type || (k_cache->type != SRHPM_TYPE_F16 && k_cache->type != SRHPM_TYPE_Q8_0)) {
+        return SRHPM_UNSUPPORTED;
+    }
+    if (k_cache->ne[0] != head_dim || v_cache->ne[0] != head_dim || k_cache->ne[2] != n_head_kv ||
+        v_cache->ne[2] != n_head_kv || !k_cache->data || !v_cache->data) {
+        return SRHPM_ERR_INVALID;
+    }
+    return rope_kv_run(ctx, qkv, ld, n, n_head, n_head_kv, head_dim, pos, theta_base, (uint8_t *) k_cache->data,
+                       (int64_t) k_cache->nb[1], (int64_t) k_cache->nb[2], (uint8_t *) v_cache->data,
+                       (int64_t) v_cache->nb[1], (int64_t) v_cache->nb[2], k_cache->type, (cudaStream_t) stream);
+}
+
+int srhpm_swiglu(srhpm_ctx * ctx, const float * gate, const float * up, float * out, int64_t n, void * stream) {
+    if (!ctx || !gate || !up || !out || n < 1) return SRHPM_ERR_INVALID;
+    return swiglu_run(ctx, gate, up, out, n, (cudaStream_t) stream);
+}
+
 }  // extern "C"

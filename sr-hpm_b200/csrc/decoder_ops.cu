@@ -1,0 +1,188 @@
+// The element-wise operators around the verify GEMMs of a dense decoder step (ggml semantics):
+//   get_rows   token embeddings: rows of an f16 / f32 table -> f32 (ggml_get_rows)
+//   add_rms_norm  residual stream x += delta (ggml_add), then y = x / sqrt(mean(x^2) + eps) * w
+//                 (ggml_rms_norm followed by ggml_mul with the norm weight)
+//   rope_kv    NeoX rotary embedding of the query and key heads of a fused QKV row (ggml_rope_ext, mode NEOX,
+//              theta_i = pos * base^(-2i/d)); the rotated keys and the values are written into the KV cache at their
+//              positions as f16 or q8_0 (ggml_cpy of f32 rows into the cache view; q8_0 with the context's q8_0 mode)
+//   swiglu     silu(gate) * up (ggml_swiglu)
+// All rows are short (N <= 16 tokens): one CTA per (row, chunk) and grid-stride loops; these ops move a few hundred KB
+// per step against the ~12 GB of weights.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+
+#include "internal.h"
+
+namespace srhpm {
+namespace {
+
+__global__ void get_rows_kernel(const uint8_t * table, int64_t row_bytes, int is_f16, const int32_t * ids, int64_t d,
+                                float * out) {
+    const int64_t   i   = blockIdx.y;
+    const uint8_t * src = table + (int64_t) ids[i] * row_bytes;
+    for (int64_t j = blockIdx.x * blockDim.x + threadIdx.x; j < d; j += (int64_t) gridDim.x * blockDim.x) {
+        out[i * d + j] = is_f16 ? __half2float(reinterpret_cast<const __half *>(src)[j])
+                                : reinterpret_cast<const float *>(src)[j];
+    }
+}
+
+// one CTA per row
+__global__ void __launch_bounds__(512) add_rms_norm_kernel(float * x, const float * delta, const float * w, float eps,
+                                                           float * y, int64_t d) {
+    const int64_t i  = blockIdx.x;
+    float *       xr = x + i * d;
+    float         ss = 0.0f;
+    for (int64_t j = threadIdx.x; j < d; j += blockDim.x) {
+        float v = xr[j];
+        if (delta) {
+            v += delta[i * d + j];
+            xr[j] = v;
+        }
+        ss = fmaf(v, v, ss);
+    }
+    __shared__ float part[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        ss = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.0f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (threadIdx.x == 0) part[0] = ss;
+    }
+    __syncthreads();
+    const float scale = 1.0f / sqrtf(part[0] / (float) d + eps);
+    for (int64_t j = threadIdx.x; j < d; j += blockDim.x) y[i * d + j] = xr[j] * scale * w[j];
+}
+
+struct RopeArgs {
+    float *         qkv;         // [n][ld]: q heads (H x hd) | k heads (Hkv x hd) | v heads (Hkv x hd)
+    int64_t         ld;
+    int             n, H, Hkv, hd;
+    const int32_t * pos;         // [n]
+    float           theta_scale; // base^(-2/hd)
+    uint8_t *       kc;          // cache rows: token p, head g at kc + p * knb1 + g * knb2
+    uint8_t *       vc;
+    int64_t         knb1, knb2, vnb1, vnb2;
+    int             cache_type;  // SRHPM_TYPE_F16 or SRHPM_TYPE_Q8_0
+    int             q8mode;
+};
+
+// rotate the pair (j, j + hd/2) of one head row in place
+__device__ __forceinline__ void rope_pair(float * h, int j, int half, float p, float theta_scale) {
+    const float theta = p * powf(theta_scale, (float) j);
+    float       s, c;
+    sincosf(theta, &s, &c);
+    const float x0 = h[j], x1 = h[j + half];
+    h[j]        = x0 * c - x1 * s;
+    h[j + half] = x0 * s + x1 * c;
+}
+
+// q8_0 of 32 values (one warp lane per value; lanes of a block = a full warp), bytes to dst (34 bytes)
+__device__ __forceinline__ void q80_store_warp(float v, uint8_t * dst, int mode) {
+    const int lane = threadIdx.x & 31;
+    float     amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float  dd = __fdiv_rn(amax, 127.0f);
+    const __half dh = __float2half_rn(dd);
+    int          qv;
+    if (mode == SRHPM_Q8_0_ACT_SIMD) {
+        const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+        qv             = __float2int_rn(__fmul_rn(v, id));
+    } else {
+        const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+        qv             = (int) roundf(__fmul_rn(v, id));
+    }
+    if (lane == 0) *reinterpret_cast<__half *>(dst) = dh;
+    dst[2 + lane] = (uint8_t) (int8_t) qv;
+}
+
+// grid: (token, head of q + k + v); one CTA of hd/2 threads (f16 cache) or hd threads (q8_0: a warp per block)
+__global__ void rope_kv_kernel(const RopeArgs a) {
+    const int t = blockIdx.x, hh = blockIdx.y, half = a.hd / 2;
+    float *   row = a.qkv + (int64_t) t * a.ld;
+    const float p = (float) a.pos[t];
+    if (hh < a.H) {  // query head: rotate in place
+        float * h = row + (int64_t) hh * a.hd;
+        for (int j = threadIdx.x; j < half; j += blockDim.x) rope_pair(h, j, half, p, a.theta_scale);
+        return;
+    }
+    const bool isk = hh < a.H + a.Hkv;
+    const int  g   = isk ? hh - a.H : hh - a.H - a.Hkv;
+    float *    h   = row + (int64_t) (a.H + (isk ? 0 : a.Hkv) + g) * a.hd;
+    if (isk) {
+        for (int j = threadIdx.x; j < half; j += blockDim.x) rope_pair(h, j, half, p, a.theta_scale);
+        __syncthreads();
+    }
+    uint8_t * dst = (isk ? a.kc + (int64_t) a.pos[t] * a.knb1 + (int64_t) g * a.knb2
+                         : a.vc + (int64_t) a.pos[t] * a.vnb1 + (int64_t) g * a.vnb2);
+    if (a.cache_type == SRHPM_TYPE_F16) {
+        for (int j = threadIdx.x; j < a.hd; j += blockDim.x) reinterpret_cast<__half *>(dst)[j] = __float2half_rn(h[j]);
+    } else {
+        for (int j = threadIdx.x; j < a.hd; j += blockDim.x) {  // blockDim = hd: one warp per 32-value block
+            q80_store_warp(h[j], dst + (j >> 5) * 34, a.q8mode);
+        }
+    }
+}
+
+__global__ void swiglu_kernel(const float * gate, const float * up, float * out, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < n; i += (int64_t) gridDim.x * blockDim.x) {
+        const float g = gate[i];
+        out[i]        = g / (1.0f + expf(-g)) * up[i];
+    }
+}
+
+}  // namespace
+
+int get_rows_run(srhpm_ctx * ctx, const uint8_t * table, int64_t row_bytes, int is_f16, const int32_t * ids, int n,
+                 int64_t d, float * out, cudaStream_t stream) {
+    get_rows_kernel<<<dim3((unsigned) std::min<int64_t>(8, (d + 255) / 256), n), 256, 0, stream>>>(table, row_bytes,
+                                                                                                    is_f16, ids, d, out);
+    ctx->launches.fetch_add(1);
+    return cuda_status(cudaGetLastError());
+}
+
+int add_rms_norm_run(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y, int n,
+                     int64_t d, cudaStream_t stream) {
+    add_rms_norm_kernel<<<n, 512, 0, stream>>>(x, delta, w, eps, y, d);
+    ctx->launches.fetch_add(1);
+    return cuda_status(cudaGetLastError());
+}
+
+int rope_kv_run(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int H, int Hkv, int hd, const int32_t * pos,
+                float theta_base, uint8_t * kc, int64_t knb1, int64_t knb2, uint8_t * vc, int64_t vnb1, int64_t vnb2,
+                int cache_type, cudaStream_t stream) {
+    RopeArgs a;
+    a.qkv         = qkv;
+    a.ld          = ld;
+    a.n           = n;
+    a.H           = H;
+    a.Hkv         = Hkv;
+    a.hd          = hd;
+    a.pos         = pos;
+    a.theta_scale = powf(theta_base, -2.0f / (float) hd);
+    a.kc          = kc;
+    a.vc          = vc;
+    a.knb1        = knb1;
+    a.knb2        = knb2;
+    a.vnb1        = vnb1;
+    a.vnb2        = vnb2;
+    a.cache_type  = cache_type;
+    a.q8mode      = ctx->q8_0_act_mode;
+    rope_kv_kernel<<<dim3(n, H + 2 * Hkv), cache_type == SRHPM_TYPE_F16 ? hd / 2 : hd, 0, stream>>>(a);
+    ctx->launches.fetch_add(1);
+    return cuda_status(cudaGetLastError());
+}
+
+int swiglu_run(srhpm_ctx * ctx, const float * gate, const float * up, float * out, int64_t n, cudaStream_t stream) {
+    const int blocks = (int) std::min<int64_t>(4 * ctx->num_sms, (n + 255) / 256);
+    swiglu_kernel<<<blocks, 256, 0, stream>>>(gate, up, out, n);
+    ctx->launches.fetch_add(1);
+    return cuda_status(cudaGetLastError());
+}
+
+}  // namespace srhpm

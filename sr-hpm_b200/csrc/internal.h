@@ -81,4 +81,14 @@ int    accept_merge_run(srhpm_ctx * ctx, const srhpm_argmax_record * recs, int n
                         const int32_t * draft, int n_draft, float relax, int32_t * out_ids, int32_t * out_n,
                         cudaStream_t stream);
 
+// decoder_ops.cu
+int get_rows_run(srhpm_ctx * ctx, const uint8_t * table, int64_t row_bytes, int is_f16, const int32_t * ids, int n,
+                 int64_t d, float * out, cudaStream_t stream);
+int add_rms_norm_run(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y, int n,
+                     int64_t d, cudaStream_t stream);
+int rope_kv_run(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int H, int Hkv, int hd, const int32_t * pos,
+                float theta_base, uint8_t * kc, int64_t knb1, int64_t knb2, uint8_t * vc, int64_t vnb1, int64_t vnb2,
+                int cache_type, cudaStream_t stream);
+int swiglu_run(srhpm_ctx * ctx, const float * gate, const float * up, float * out, int64_t n, cudaStream_t stream);
+
 }  // namespace srhpm

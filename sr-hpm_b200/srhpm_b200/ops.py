@@ -57,6 +57,21 @@ def quantize_chunk(w, qtype):
     return out
 
 
+def row_size(qtype, K):
+    """Bytes of a row of K values of qtype (ggml_row_size)."""
+    return int(L.load().srhpm_row_size(qtype, K))
+
+
+def type_size(qtype):
+    """Bytes of one block of qtype (ggml_type_size)."""
+    return int(L.load().srhpm_type_size(qtype))
+
+
+def blck_size(qtype):
+    """Values per block of qtype (ggml_blck_size)."""
+    return int(L.load().srhpm_blck_size(qtype))
+
+
 class QuantTensor:
     """GGUF-packed weight rows in device memory: a ggml tensor of a quantized type with ne = [K, rows]."""
 
