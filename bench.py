@@ -38,8 +38,8 @@ JSON_OUT = sys.stdout  # replaced in main() by a private handle on the real stdo
 METRIC = "quantized verify-GEMM HBM GB/s (% peak) at k=2–8; 27B verify steps/sec"
 SHAPES = [(5120, 5120), (6144, 5120), (17408, 5120), (5120, 17408)]
 TYPE_NAMES = ["q4_K", "q5_K", "q6_K", "q8_0", "iq4_xs"]
-TYPE_IDS = {"q4_K": 12, "q5_K": 13, "q6_K": 14, "q8_0": 8, "iq4_xs": 23}
-BLOCK = {12: (256, 144), 13: (256, 176), 14: (256, 210), 8: (32, 34), 23: (256, 136)}
+TYPE_IDS = {"q4_K": 12, "q5_K": 13, "q6_K": 14, "q8_0": 8, "iq4_xs": 23, "q3_K": 11}  # q3_K: --only (the 27B FFN)
+BLOCK = {12: (256, 144), 13: (256, 176), 14: (256, 210), 8: (32, 34), 23: (256, 136), 11: (256, 110)}
 NS = [2, 4, 8]
 SEED = 1234
 
@@ -116,22 +116,23 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------------------------------
 # inputs
 
-def make_host_weights():
-    """{(type, rows, K): packed blocks (numpy uint8 [rows, row_bytes])}: one f32 matrix per shape, each type."""
+def make_host_weights(ops):
+    """{(type, rows, K): packed blocks (numpy uint8 [rows, row_bytes])}: one f32 N(0, 0.02) matrix per shape (the
+    same matrix for every type, in shape order), quantized to each type the products use."""
     import srhpm_b200 as S
     rng = np.random.default_rng(SEED)
     out = {}
-    for rows, K in SHAPES:
+    shapes = sorted({(rows, K) for _, _, rows, K in ops}, key=lambda sh: SHAPES.index(sh) if sh in SHAPES else 99)
+    for rows, K in shapes:
         w = rng.standard_normal((rows, K), dtype=np.float32) * np.float32(0.02)
-        for name in TYPE_NAMES:
-            t = TYPE_IDS[name]
+        for t in sorted({t for _, t, r, k in ops if (r, k) == (rows, K)}):
             out[(t, rows, K)] = S.quantize_chunk(w, t)
     return out
 
 
-def make_host_acts():
+def make_host_acts(ops):
     rng = np.random.default_rng(SEED + 1)
-    return {(N, K): rng.standard_normal((N, K), dtype=np.float32) for N in NS for K in sorted({k for _, k in SHAPES})}
+    return {(N, K): rng.standard_normal((N, K), dtype=np.float32) for N, K in sorted({(N, K) for N, _, _, K in ops})}
 
 
 def sweep_ops(only=None):
@@ -207,9 +208,9 @@ def run_reference(args):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     ref = O.load_ref()
-    host_w = make_host_weights()
-    host_x = make_host_acts()
     ops = sweep_ops(args.only)
+    host_w = make_host_weights(ops)
+    host_x = make_host_acts(ops)
     nth = os.cpu_count() or 1
     for _ in range(args.warmup):
         cpu_pass(host_w, host_x, ops, nth, O, ref)
@@ -254,9 +255,9 @@ def run_gpu(args):
     world, rank, local = dist_setup()
     dev = torch.device("cuda", local)
     ctx = S.Context(local)
-    host_w = make_host_weights()
-    host_x = make_host_acts()
     base_ops = sweep_ops(args.only)
+    host_w = make_host_weights(base_ops)
+    host_x = make_host_acts(base_ops)
     # with a single product, rotate over copies of its matrix so that consecutive calls never hit L2
     ncopy = 1
     if len(base_ops) == 1:
@@ -455,6 +456,11 @@ def run_gpu(args):
         if world == 1 and not args.no_attn:
             cfg["attention_q8_0"] = measure_attention(ctx, dev, peak)
             cfg["accept_k8_vocab151936"] = measure_accept(ctx, dev)
+        if world == 1 and not args.no_step:
+            from srhpm_b200 import _lib as L
+            cfg["verify_step_27b_f16kv_2048"] = measure_step_27b(ctx, dev, peak)
+            cfg["verify_step_27b_q8kv_131072"] = measure_step_27b(ctx, dev, peak, ks=(8,), kv_type=L.Q8_0,
+                                                                  n_past=131072, reps=5)
         cpu = None
         if world == 1 and not args.no_cpu:
             gbs, secs, passes, nth, kind, variant = cpu_sample(host_w, host_x, base_ops, args.cpu_seconds)
@@ -578,6 +584,85 @@ def measure_accept(ctx, dev, reps=50):
     return {"us": round(us, 2), "GBps": round(nbytes / (us * 1e-6) / 1e9, 1), "logits_bytes": nbytes, "draft": k}
 
 
+def step_bytes_27b(cfg, n_past, n):
+    """Algorithmic bytes of one verify step: every weight matrix once, the visible KV rows of every layer, the n
+    embedding rows and the n x vocab logits."""
+    from srhpm_b200 import _lib as L
+    row = 2 * 272 if cfg.kv_type == L.Q8_0 else 2 * 512  # K + V bytes per token and KV head
+    kv = 0
+    for layer in range(cfg.n_layer):
+        full = cfg.window <= 0 or layer % cfg.full_every == cfg.full_every - 1
+        vis = n_past + n if full else min(n_past + n, cfg.window + n - 1)
+        kv += vis * cfg.Hkv * row
+    return cfg.weight_bytes() + kv + n * cfg.d * 2 + n * cfg.n_vocab * 4
+
+
+def measure_step_27b(ctx, dev, peak, ks=(2, 4, 8), kv_type=None, n_past=2048, reps=10, seed=0):
+    """a whole verify step of the synthetic 27B-class decoder (64 layers, d 5120, FFN 17408,
+    24 / 4 heads of 256, full attention every 4th layer and a 4096-token window elsewhere, vocab 151936; Q4_K attention
+    and FFN-down, Q3_K gate / up, Q6_K head; random-init GGUF blocks) over a KV cache of n_past tokens, 1 accepted +
+    k drafted tokens, greedy acceptance. CUDA-graph replays; steps/s and bytes / time."""
+    import torch
+    from srhpm_b200 import _lib as L
+    from srhpm_b200 import verify_step as V
+    cfg = V.DecoderConfig(kv_type=kv_type if kv_type is not None else L.F16)
+    w = V.DeviceWeights.random(cfg, dev, seed)
+    cap = n_past + max(ks) + 1
+    rowb = 272 if cfg.kv_type == L.Q8_0 else 512
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed + 1)
+    caches = []
+    for layer in range(cfg.n_layer):
+        pair = []
+        for _ in range(2):
+            x = torch.randn((cap * cfg.Hkv, cfg.hd), device=dev, generator=g)
+            if cfg.kv_type == L.Q8_0:
+                pair.append(ctx.quantize_rows_q8_0(x).view(cap, cfg.Hkv, rowb))
+            else:
+                pair.append(x.half().view(torch.uint8).view(cap, cfg.Hkv, rowb))
+            del x
+        caches.append(pair)
+    kc = [p[0] for p in caches]
+    vc = [p[1] for p in caches]
+    out = {}
+    for k in ks:
+        n = k + 1
+        step = V.VerifyStep(ctx, cfg, w, kc, vc, n, n_past)
+        ids = torch.randint(0, cfg.n_vocab, (n,), generator=g, device=dev)
+        step.set_tokens(ids, ids[1:])
+        for _ in range(2):
+            step.run()
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        ctx.launch_count(reset=True)
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                step.run(s)
+        launches = ctx.launch_count(reset=True)
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ctx.check()
+        ms = e0.elapsed_time(e1) / reps
+        nbytes = step_bytes_27b(cfg, n_past, n)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[f"k{k}"] = {"ms": round(ms, 3), "steps_per_s": round(1e3 / ms, 1), "GBps": round(gbs, 1),
+                        "frac": round(gbs / peak, 4), "bytes": nbytes, "launches": launches,
+                        "accepted": int(step.out_n.item())}
+        del graph, step
+    del w, caches, kc, vc
+    torch.cuda.empty_cache()
+    return out
+
+
 def main():
     # stdout carries exactly one JSON line: keep a private handle on it and send everything else that libraries
     # write to file descriptor 1 (NCCL prints its version line there) to stderr
@@ -596,8 +681,19 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-attn", action="store_true", help="skip the attention and acceptance measurements")
     ap.add_argument("--attn", type=int, default=None, help="time only the attention at this KV length (profiling)")
+    ap.add_argument("--no-step", action="store_true", help="skip the 27B-class verify-step measurements")
+    ap.add_argument("--step27b", type=int, default=None, help="time only the 27B-class step with k drafted tokens")
     ap.add_argument("--traffic", type=float, default=None, help="ncu dram bytes per launch, when captured")
     args = ap.parse_args()
+    if args.step27b:
+        import torch
+        import srhpm_b200 as S
+        ctx = S.Context(0)
+        peak, kind = peaks()
+        print(json.dumps({"verify_step_27b_f16kv_2048": measure_step_27b(ctx, torch.device("cuda", 0), peak,
+                                                                          ks=(args.step27b,)), "peak_kind": kind}),
+              file=JSON_OUT, flush=True)
+        return 0
     if args.attn:
         import torch
         import srhpm_b200 as S
