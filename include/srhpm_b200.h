@@ -178,14 +178,16 @@ int srhpm_accept_merge(srhpm_ctx * ctx, const srhpm_argmax_record * recs, int n_
  *       NeoX rotary embedding (pairs (j, j + head_dim/2), theta_j = pos * theta_base^(-2j/head_dim)) of the query and
  *       key heads in place, then the keys and values are stored into the caches at token pos[t] (views as for
  *       srhpm_flash_attn_ext: [head_dim, capacity, n_head_kv], f16 or q8_0 with the context's q8_0 mode)
- *   srhpm_swiglu: out = silu(gate) * up, n values */
+ *   srhpm_swiglu: out[t][j] = silu(gate[t][j]) * up[t][j] for n rows of n_ff values (input row stride ld_in, output
+ *       ld_out, in floats; gate and up may be the two halves of one fused gate|up GEMM output) */
 int srhpm_get_rows(srhpm_ctx * ctx, const srhpm_tensor * table, const int32_t * ids, int n, float * out, void * stream);
 int srhpm_add_rms_norm(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y, int n,
                        int64_t d, void * stream);
 int srhpm_rope_kv(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int n_head, int n_head_kv, int head_dim,
                   const int32_t * pos, float theta_base, const srhpm_tensor * k_cache, const srhpm_tensor * v_cache,
                   void * stream);
-int srhpm_swiglu(srhpm_ctx * ctx, const float * gate, const float * up, float * out, int64_t n, void * stream);
+int srhpm_swiglu(srhpm_ctx * ctx, const float * gate, const float * up, int64_t ld_in, float * out, int64_t ld_out,
+                 int n, int64_t n_ff, void * stream);
 
 /* ---- host-side weight quantizer (CPU) -------------------------------------------------------------------------
  * f32 rows -> GGUF blocks of `type` (Q4_K, Q5_K, Q6_K, Q3_K, IQ4_XS, Q8_0, F16). Host pointers. Returns the bytes

@@ -418,9 +418,12 @@ int srhpm_rope_kv(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int n_head, i
                        (int64_t) v_cache->nb[1], (int64_t) v_cache->nb[2], k_cache->type, (cudaStream_t) stream);
 }
 
-int srhpm_swiglu(srhpm_ctx * ctx, const float * gate, const float * up, float * out, int64_t n, void * stream) {
-    if (!ctx || !gate || !up || !out || n < 1) return SRHPM_ERR_INVALID;
-    return swiglu_run(ctx, gate, up, out, n, (cudaStream_t) stream);
+int srhpm_swiglu(srhpm_ctx * ctx, const float * gate, const float * up, int64_t ld_in, float * out, int64_t ld_out,
+                 int n, int64_t n_ff, void * stream) {
+    if (!ctx || !gate || !up || !out || n < 1 || n > 16 || n_ff < 1 || ld_in < n_ff || ld_out < n_ff) {
+        return SRHPM_ERR_INVALID;
+    }
+    return swiglu_run(ctx, gate, up, ld_in, out, ld_out, n, n_ff, (cudaStream_t) stream);
 }
 
 }  // extern "C"

@@ -5,7 +5,7 @@
 //   rope_kv    NeoX rotary embedding of the query and key heads of a fused QKV row (ggml_rope_ext, mode NEOX,
 //              theta_i = pos * base^(-2i/d)); the rotated keys and the values are written into the KV cache at their
 //              positions as f16 or q8_0 (ggml_cpy of f32 rows into the cache view; q8_0 with the context's q8_0 mode)
-//   swiglu     silu(gate) * up (ggml_swiglu)
+//   swiglu     silu(gate) * up (ggml_swiglu); gate and up may be the two halves of one fused gate|up GEMM output
 // All rows are short (N <= 16 tokens): one CTA per (row, chunk) and grid-stride loops; these ops move a few hundred KB
 // per step against the ~12 GB of weights.
 #include <cuda_fp16.h>
@@ -28,19 +28,42 @@ __global__ void get_rows_kernel(const uint8_t * table, int64_t row_bytes, int is
     }
 }
 
-// one CTA per row
-__global__ void __launch_bounds__(512) add_rms_norm_kernel(float * x, const float * delta, const float * w, float eps,
-                                                           float * y, int64_t d) {
+// one CTA per row; the row (d <= 4 * 4 * blockDim) stays in registers between the sum and the scaling
+constexpr int kNormThreads = 1024;
+__global__ void __launch_bounds__(kNormThreads) add_rms_norm_kernel(float * x, const float * delta, const float * w,
+                                                                     float eps, float * y, int64_t d) {
     const int64_t i  = blockIdx.x;
     float *       xr = x + i * d;
+    const bool    vec = (d & 3) == 0 && (reinterpret_cast<uintptr_t>(xr) & 15) == 0 &&
+                     (delta == nullptr || (reinterpret_cast<uintptr_t>(delta + i * d) & 15) == 0) &&
+                     (reinterpret_cast<uintptr_t>(y + i * d) & 15) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0;
     float         ss = 0.0f;
-    for (int64_t j = threadIdx.x; j < d; j += blockDim.x) {
-        float v = xr[j];
-        if (delta) {
-            v += delta[i * d + j];
-            xr[j] = v;
+    float4        v[4];
+    const int64_t d4 = d >> 2;
+    if (vec) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int64_t j = threadIdx.x + (int64_t) k * kNormThreads;
+            if (j < d4) {
+                float4 a = reinterpret_cast<const float4 *>(xr)[j];
+                if (delta) {
+                    const float4 b = reinterpret_cast<const float4 *>(delta + i * d)[j];
+                    a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+                    reinterpret_cast<float4 *>(xr)[j] = a;
+                }
+                v[k] = a;
+                ss = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, ss))));
+            }
         }
-        ss = fmaf(v, v, ss);
+    } else {
+        for (int64_t j = threadIdx.x; j < d; j += kNormThreads) {
+            float a = xr[j];
+            if (delta) {
+                a += delta[i * d + j];
+                xr[j] = a;
+            }
+            ss = fmaf(a, a, ss);
+        }
     }
     __shared__ float part[32];
 #pragma unroll
@@ -48,14 +71,30 @@ __global__ void __launch_bounds__(512) add_rms_norm_kernel(float * x, const floa
     if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
     __syncthreads();
     if (threadIdx.x < 32) {
-        ss = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.0f;
+        ss = part[threadIdx.x];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         if (threadIdx.x == 0) part[0] = ss;
     }
     __syncthreads();
     const float scale = 1.0f / sqrtf(part[0] / (float) d + eps);
-    for (int64_t j = threadIdx.x; j < d; j += blockDim.x) y[i * d + j] = xr[j] * scale * w[j];
+    if (vec) {
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int64_t j = threadIdx.x + (int64_t) k * kNormThreads;
+            if (j < d4) {
+                const float4 ww = reinterpret_cast<const float4 *>(w)[j];
+                float4       o;
+                o.x = v[k].x * scale * ww.x;
+                o.y = v[k].y * scale * ww.y;
+                o.z = v[k].z * scale * ww.z;
+                o.w = v[k].w * scale * ww.w;
+                reinterpret_cast<float4 *>(y + i * d)[j] = o;
+            }
+        }
+    } else {
+        for (int64_t j = threadIdx.x; j < d; j += kNormThreads) y[i * d + j] = xr[j] * scale * w[j];
+    }
 }
 
 struct RopeArgs {
@@ -129,10 +168,12 @@ __global__ void rope_kv_kernel(const RopeArgs a) {
     }
 }
 
-__global__ void swiglu_kernel(const float * gate, const float * up, float * out, int64_t n) {
-    for (int64_t i = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; i < n; i += (int64_t) gridDim.x * blockDim.x) {
-        const float g = gate[i];
-        out[i]        = g / (1.0f + expf(-g)) * up[i];
+__global__ void swiglu_kernel(const float * gate, const float * up, int64_t ld_in, float * out, int64_t ld_out,
+                              int64_t cols) {
+    const int64_t r = blockIdx.y;
+    for (int64_t j = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; j < cols; j += (int64_t) gridDim.x * blockDim.x) {
+        const float g   = gate[r * ld_in + j];
+        out[r * ld_out + j] = g / (1.0f + expf(-g)) * up[r * ld_in + j];
     }
 }
 
@@ -148,7 +189,8 @@ int get_rows_run(srhpm_ctx * ctx, const uint8_t * table, int64_t row_bytes, int 
 
 int add_rms_norm_run(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y, int n,
                      int64_t d, cudaStream_t stream) {
-    add_rms_norm_kernel<<<n, 512, 0, stream>>>(x, delta, w, eps, y, d);
+    if (d > 4 * 4 * kNormThreads) return SRHPM_UNSUPPORTED;
+    add_rms_norm_kernel<<<n, kNormThreads, 0, stream>>>(x, delta, w, eps, y, d);
     ctx->launches.fetch_add(1);
     return cuda_status(cudaGetLastError());
 }
@@ -178,9 +220,10 @@ int rope_kv_run(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int H, int Hkv,
     return cuda_status(cudaGetLastError());
 }
 
-int swiglu_run(srhpm_ctx * ctx, const float * gate, const float * up, float * out, int64_t n, cudaStream_t stream) {
-    const int blocks = (int) std::min<int64_t>(4 * ctx->num_sms, (n + 255) / 256);
-    swiglu_kernel<<<blocks, 256, 0, stream>>>(gate, up, out, n);
+int swiglu_run(srhpm_ctx * ctx, const float * gate, const float * up, int64_t ld_in, float * out, int64_t ld_out,
+               int rows, int64_t cols, cudaStream_t stream) {
+    const int blocks = (int) std::min<int64_t>(std::max(1, 4 * ctx->num_sms / rows), (cols + 255) / 256);
+    swiglu_kernel<<<dim3(blocks, rows), 256, 0, stream>>>(gate, up, ld_in, out, ld_out, cols);
     ctx->launches.fetch_add(1);
     return cuda_status(cudaGetLastError());
 }

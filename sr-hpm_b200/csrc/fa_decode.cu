@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     const int g = blockIdx.y / a.nrg, rg = blockIdx.y % a.nrg;
     const int t0 = chunk * a.chunk_len, t1 = min(a.L, t0 + a.chunk_len);
     const int nt = (t1 - t0 + kT - 1) / kT;
-    const int row0 = rg * kRG;              // first row (of the KV head's R) of this group
+    const int row0 = rg * RP;               // first row (of the KV head's R) of this group
     const int rows = min(RP, a.R - row0);   // valid rows
     // compute threads: lane quarter q (KV token t = 32 q + lane of the tile), row quarter qr (rows rbase..rbase+RH-1)
     const int q = warp & 3, qr = (warp >> 2) & 3, t = 32 * q + lane, rbase = qr * RH;
@@ -777,7 +777,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     const int g = blockIdx.y / a.nrg, rg = blockIdx.y % a.nrg;
     const int t0 = chunk * a.chunk_len, t1 = min(a.L, t0 + a.chunk_len);
     const int nt = (t1 - t0 + kT - 1) / kT;
-    const int row0 = rg * kRG;
+    const int row0 = rg * RP;
     const int rows = min(RP, a.R - row0);
     const int q = warp & 3, qr = (warp >> 2) & 3, t = 32 * q + lane, rbase = qr * RH;
     bool      bad = false;
@@ -1131,20 +1131,37 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const FaArgs a) {
     pdl_wait();
     const int row = blockIdx.x, g = row / a.R, rr = row % a.R;
     const int h = g * a.G + rr / a.N, tq = rr % a.N;
+    __shared__ float w_s[256];  // per chunk: weight 2^(M_c - M) (0 for empty chunks)
+    __shared__ float s_s[256];
+    __shared__ float mf_s;
     const float2 * ms = a.part_ms + (int64_t) row * a.n_chunks;
-    float Mf = -INFINITY;
-    for (int c = 0; c < a.n_chunks; c++) {
-        const float2 m = ms[c];
-        if (m.y != 0.0f) Mf = fmaxf(Mf, m.x);
+    const int      nc = a.n_chunks;  // <= 256 (fa_plan: one chunk per CTA of a wave at most)
+    if (threadIdx.x < 32) {
+        float m = -INFINITY;
+        for (int c = threadIdx.x; c < nc; c += 32) {
+            const float2 v = ms[c];
+            if (v.y != 0.0f) m = fmaxf(m, v.x);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (threadIdx.x == 0) mf_s = m;
     }
-    const int dv = threadIdx.x;
-    float     acc = 0.0f, S = 0.0f;
-    for (int c = 0; c < a.n_chunks; c++) {
-        const float2 m = ms[c];
-        if (m.y == 0.0f) continue;
-        const float w = exp2f(m.x - Mf);
-        acc = fmaf(w, a.part_acc[((int64_t) row * a.n_chunks + c) * kD + dv], acc);
-        S   = fmaf(w, m.y, S);
+    __syncthreads();
+    const float Mf = mf_s;
+    for (int c = threadIdx.x; c < nc; c += blockDim.x) {
+        const float2 v = ms[c];
+        w_s[c]         = v.y != 0.0f ? exp2f(v.x - Mf) : 0.0f;
+        s_s[c]         = v.y;
+    }
+    __syncthreads();
+    const int      dv  = threadIdx.x;
+    const float *  src = a.part_acc + (int64_t) row * nc * kD + dv;
+    float          acc = 0.0f, S = 0.0f;
+#pragma unroll 8
+    for (int c = 0; c < nc; c++) {
+        const float w = w_s[c];
+        acc           = fmaf(w, w != 0.0f ? src[(int64_t) c * kD] : 0.0f, acc);
+        S             = fmaf(w, s_s[c], S);
     }
     if (a.sinks) {
         const float sk2 = a.sinks[h] * kLog2e;
@@ -1183,12 +1200,17 @@ struct Plan {
 };
 
 Plan fa_plan(int num_sms, int R, int L, int Hkv) {
-    Plan p;
-    p.nrg              = (R + kRG - 1) / kRG;
-    p.rp               = p.nrg > 1 ? kRG : (R + 15) / 16 * 16;
+    Plan      p;
+    const int max_ch = (L + kT - 1) / kT;
+    // long caches: 48-row groups (each KV byte read once per group); short caches (fewer 128-token tiles than SMs):
+    // 16-row groups for more CTAs (the extra K/V reads hit L2)
+    p.rp = Hkv * max_ch >= num_sms ? kRG : 16;
+    if (R <= 32 && p.rp == kRG) p.rp = (R + 15) / 16 * 16;
+    p.nrg              = (R + p.rp - 1) / p.rp;
     const int groups   = Hkv * p.nrg;
-    const int max_ch   = (L + kT - 1) / kT;
-    const int want     = std::max(1, std::min(max_ch, (num_sms + groups - 1) / groups));
+    int       want     = std::max(1, std::min(max_ch, (num_sms + groups - 1) / groups));
+    if (max_ch >= 2) want = std::min(want, max_ch / 2);  // two tiles per chunk at least
+    want               = std::max(1, want);
     const int per      = (L + want - 1) / want;
     p.chunk_len        = (per + kT - 1) / kT * kT;
     p.n_chunks         = (L + p.chunk_len - 1) / p.chunk_len;

@@ -89,6 +89,7 @@ int add_rms_norm_run(srhpm_ctx * ctx, float * x, const float * delta, const floa
 int rope_kv_run(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int H, int Hkv, int hd, const int32_t * pos,
                 float theta_base, uint8_t * kc, int64_t knb1, int64_t knb2, uint8_t * vc, int64_t vnb1, int64_t vnb2,
                 int cache_type, cudaStream_t stream);
-int swiglu_run(srhpm_ctx * ctx, const float * gate, const float * up, float * out, int64_t n, cudaStream_t stream);
+int swiglu_run(srhpm_ctx * ctx, const float * gate, const float * up, int64_t ld_in, float * out, int64_t ld_out,
+               int rows, int64_t cols, cudaStream_t stream);
 
 }  // namespace srhpm

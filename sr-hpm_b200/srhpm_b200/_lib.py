@@ -69,7 +69,8 @@ _SIGNATURES = {
     "srhpm_add_rms_norm": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_float, _P, ctypes.c_int, ctypes.c_int64, _P]),
     "srhpm_rope_kv": (ctypes.c_int, [_P, _P, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P,
                                      ctypes.c_float, _T, _T, _P]),
-    "srhpm_swiglu": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_int64, _P]),
+    "srhpm_swiglu": (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, _P, ctypes.c_int64, ctypes.c_int, ctypes.c_int64,
+                                    _P]),
     "srhpm_quantize_chunk": (ctypes.c_size_t, [ctypes.c_int, _P, _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                                 _P]),
 }

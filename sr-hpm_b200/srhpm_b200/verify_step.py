@@ -91,7 +91,12 @@ class DeviceWeights:
         for l in range(cfg.n_layer):
             lay = {}
             for name, t, rows, K in cfg.shapes():
-                lay[name] = QuantTensor.from_blocks(w[name][l], t, rows, K, device)
+                if name not in ("gate", "up"):
+                    lay[name] = QuantTensor.from_blocks(w[name][l], t, rows, K, device)
+            # gate and up as one matrix (gate rows, then up rows): one GEMM launch, SwiGLU reads the halves
+            gu = np.concatenate([np.asarray(w["gate"][l]).reshape(cfg.n_ff, -1),
+                                 np.asarray(w["up"][l]).reshape(cfg.n_ff, -1)])
+            lay["gate_up"] = QuantTensor.from_blocks(gu, cfg.types["gate"], 2 * cfg.n_ff, cfg.d, device)
             lay["attn_norm"] = torch.from_numpy(w["attn_norm"][l]).to(device)
             lay["ffn_norm"] = torch.from_numpy(w["ffn_norm"][l]).to(device)
             self.layers.append(lay)
@@ -106,7 +111,9 @@ class DeviceWeights:
         gen = torch.Generator(device=device)
         gen.manual_seed(seed)
         for _ in range(cfg.n_layer):
-            lay = {name: random_blocks_device(t, rows, K, gen, device) for name, t, rows, K in cfg.shapes()}
+            lay = {name: random_blocks_device(t, rows, K, gen, device) for name, t, rows, K in cfg.shapes()
+                   if name not in ("gate", "up")}
+            lay["gate_up"] = random_blocks_device(cfg.types["gate"], 2 * cfg.n_ff, cfg.d, gen, device)
             lay["attn_norm"] = 1.0 + 0.1 * torch.randn(cfg.d, device=device, generator=gen)
             lay["ffn_norm"] = 1.0 + 0.1 * torch.randn(cfg.d, device=device, generator=gen)
             self.layers.append(lay)
@@ -136,8 +143,7 @@ class VerifyStep:
         self.qkv = torch.zeros((n, (c.H + 2 * c.Hkv) * c.hd), **f32)
         self.att = torch.zeros((n, c.H * c.hd), **f32)
         self.o = torch.zeros((n, c.d), **f32)
-        self.g = torch.zeros((n, c.n_ff), **f32)
-        self.u = torch.zeros((n, c.n_ff), **f32)
+        self.gu = torch.zeros((n, 2 * c.n_ff), **f32)                      # gate | up
         self.h = torch.zeros((n, c.n_ff), **f32)
         self.logits = torch.zeros((n, c.n_vocab), **f32)
         self.out_ids = torch.zeros(n, dtype=torch.int32, device=dev)
@@ -218,10 +224,11 @@ class VerifyStep:
             calls.append(("add_rms_norm", lib.srhpm_add_rms_norm,
                           [h, self._ptr(self.x), self._ptr(self.o), self._ptr(lay["ffn_norm"]), ctypes.c_float(c.eps),
                            self._ptr(self.y), n, c.d], False))
-            calls.append(self._mm(lay["gate"], self.y, self.g))
-            calls.append(self._mm(lay["up"], self.y, self.u))
+            calls.append(self._mm(lay["gate_up"], self.y, self.gu))
+            up_ptr = ctypes.c_void_p(self.gu.data_ptr() + 4 * c.n_ff)
             calls.append(("swiglu", lib.srhpm_swiglu,
-                          [h, self._ptr(self.g), self._ptr(self.u), self._ptr(self.h), n * c.n_ff], False))
+                          [h, self._ptr(self.gu), up_ptr, self.gu.stride(0), self._ptr(self.h), self.h.stride(0), n,
+                           c.n_ff], False))
             calls.append(self._mm(lay["down"], self.h, self.o))  # o: the delta added by the next add_rms_norm
         calls.append(("add_rms_norm", lib.srhpm_add_rms_norm,
                       [h, self._ptr(self.x), self._ptr(self.o), self._ptr(self.w.out_norm), ctypes.c_float(c.eps),

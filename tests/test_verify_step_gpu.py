@@ -38,12 +38,13 @@ def test_add_rms_norm_and_swiglu(ctx):
     torch.cuda.synchronize()
     assert np.array_equal(tx.cpu().numpy(), x + dl)
     assert rel_l2(ty.cpu().numpy(), O.rms_norm(x + dl, w, 1e-6)) < 1e-6
-    g, u = rng.standard_normal((2, 9 * 17408)).astype(np.float32)
-    tg, tu = torch.from_numpy(g).cuda(), torch.from_numpy(u).cuda()
-    to = torch.empty_like(tg)
-    L.check(lib.srhpm_swiglu(ctx.handle, ptr(tg), ptr(tu), ptr(to), g.size, None), "swiglu")
+    gu = rng.standard_normal((9, 2 * 17408)).astype(np.float32)  # a fused gate | up output
+    tgu = torch.from_numpy(gu).cuda()
+    to = torch.empty((9, 17408), dtype=torch.float32, device="cuda")
+    L.check(lib.srhpm_swiglu(ctx.handle, ptr(tgu), ptr(tgu) + 4 * 17408, 2 * 17408, ptr(to), 17408, 9, 17408, None),
+            "swiglu")
     torch.cuda.synchronize()
-    assert rel_l2(to.cpu().numpy(), O.swiglu(g, u)) < 1e-6
+    assert rel_l2(to.cpu().numpy(), O.swiglu(gu[:, :17408], gu[:, 17408:])) < 1e-6
 
 
 def small_cfg(kv_type):
