@@ -188,6 +188,34 @@ __device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t * p) {
     return __funnelshift_r(q[0], q[1], 16);
 }
 
+// explicit shared-space loads at 32-bit shared addresses (generic pointers into shared memory can compile to generic
+// loads once their provenance is lost)
+__device__ __forceinline__ uint32_t sld32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 sld64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint4 sld128(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+// 8 bytes at a shared address that is 4-byte aligned (A4), or any (three aligned words and two funnel shifts)
+template <bool A4>
+__device__ __forceinline__ uint2 sld8_a2(uint32_t a) {
+    if constexpr (A4) {
+        return make_uint2(sld32(a), sld32(a + 4));
+    } else {
+        const uint32_t b = a & ~3u, sh = (a & 3u) * 8, w0 = sld32(b), w1 = sld32(b + 4), w2 = sld32(b + 8);
+        return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
+    }
+}
+
 __device__ __forceinline__ float half_bits_to_float(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
 __device__ __forceinline__ uint16_t lds_u16(const uint8_t * p) { return *reinterpret_cast<const uint16_t *>(p); }

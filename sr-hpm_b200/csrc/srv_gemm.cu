@@ -41,8 +41,9 @@ constexpr int     kMaxSplit  = 8;                 // K ranges per product at mos
 constexpr int     kBarBytes  = 128;               // room for the 2 * kMaxStages mbarriers
 
 __host__ __device__ constexpr int rec_nscales(bool q80, int NT) { return q80 ? 8 * NT : NT; }
+// [NT token rows of kTokStride bytes][f32 scales][K-quant records: NT int32 sums of each token's 256 codes]
 __host__ __device__ constexpr int rec_bytes(bool q80, int NT) {
-    return (NT * kTokStride + 4 * rec_nscales(q80, NT) + 15) / 16 * 16;
+    return (NT * kTokStride + 4 * rec_nscales(q80, NT) + (q80 ? 0 : 4 * NT) + 15) / 16 * 16;
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -76,7 +77,7 @@ __global__ void __launch_bounds__(256) quant_q8K_kernel(const float * __restrict
                                                          int NT, uint8_t * __restrict__ recs, int8_t * __restrict__ q,
                                                          float * __restrict__ d, int16_t * __restrict__ b32,
                                                          int16_t * __restrict__ b16, int32_t * __restrict__ cnt,
-                                                         int ncnt) {
+                                                         int ncnt, int perm) {
     // launched early behind the previous call's GEMM: let the next GEMM get resident, then wait for the previous
     // grid (it may still read the records and counters this kernel rewrites, or write the X it reads)
     pdl_launch_dependents();
@@ -139,10 +140,13 @@ __global__ void __launch_bounds__(256) quant_q8K_kernel(const float * __restrict
         if (b32 && (lane & 3) == 0) b32[(int64_t) t * (K / 32) + (int64_t) sb * 8 + lane / 4] = (int16_t) s32;
     } else {
         uint8_t * rec = recs + (size_t) sb * rec_bytes(false, NT);
-        *reinterpret_cast<uint2 *>(rec + t * kTokStride + 8 * lane) = pk;
+        // perm (Q3_K): each lane's 8 columns stored in the order 0 4 1 5 2 6 3 7, the k order of its decoder
+        const uint2 st = perm ? make_uint2(__byte_perm(pk.x, pk.y, 0x5140), __byte_perm(pk.x, pk.y, 0x7362)) : pk;
+        *reinterpret_cast<uint2 *>(rec + t * kTokStride + 8 * lane) = st;
         if (lane == 0) reinterpret_cast<float *>(rec + NT * kTokStride)[t] = dv;
         // per-32 sums of the quantized row, split into int8 halves s = 128 * hi + lo (lo in 0..127), in the token
-        // row's padding: hi at 256 + sub-block, lo at 264 + sub-block (the Q4_K / Q5_K minimum term)
+        // row's padding: hi at 256 + sub-block, lo at 264 + sub-block (the Q4_K / Q5_K minimum term); the sum over
+        // all 256 after the scales (the Q3_K offset term)
         int s32 = 0;
 #pragma unroll
         for (int j = 0; j < 8; j++) s32 += qv[j];
@@ -152,6 +156,10 @@ __global__ void __launch_bounds__(256) quant_q8K_kernel(const float * __restrict
             rec[t * kTokStride + 256 + lane / 4] = (uint8_t) (int8_t) (s32 >> 7);
             rec[t * kTokStride + 264 + lane / 4] = (uint8_t) (s32 & 127);
         }
+        int s256 = s32 + __shfl_xor_sync(0xffffffffu, s32, 4);
+        s256 += __shfl_xor_sync(0xffffffffu, s256, 8);
+        s256 += __shfl_xor_sync(0xffffffffu, s256, 16);
+        if (lane == 0) reinterpret_cast<int32_t *>(rec + NT * kTokStride + 4 * NT)[t] = s256;
     }
 }
 
@@ -491,70 +499,135 @@ struct DecQ6K {
 };
 
 // Q3_K (110 B: 32 bytes of high bits, 64 bytes of 2-bit codes, 12 bytes of 6-bit scales, d). Weight 128n + 32j + l:
-// bits 2j of qs[32n + l], high bit (4n + j) of hmask[l] (set = +0, clear = -4); scale index 8n + 2j + l/16, minus 32.
-// Scale record: int32 sc[16] | f32 d.
+// code c = bits 2j of qs[32n + l], high bit hb = bit (4n + j) of hmask[l] (set = +0, clear = -4), so q = i - 4 with
+// the 3-bit index i = c + 4 hb; scale s = 6 bits - 32 at index 8n + 2j + l/16.
+//
+// Every weight goes into the MMA already scaled, as the unsigned byte 128 - s q (s q in [-124, 128]): one prmt per 4
+// weights looks the indices up in the sub-block's 8-entry table, so a super-block is 8 k32 MMAs per row pair with the
+// sub-block scales inside, and the exact integer sum is recovered as sum s q x = 128 sum x - sum (128 - s q) x with
+// the token's code sum from the activation record.
+// Thread t takes l = 8t..8t+7 (one sub-block half h = t / 2) of every (n, j); two 32-bit words per 8 bytes of qs and
+// hmask are spread into nibble indices (nibble 2k: l = 8t + k, nibble 2k + 1: l = 8t + 4 + k), so its A registers
+// hold l = 8t + {0,4,1,5} and 8t + {2,6,3,7} -- the order in which the quantizer stores Q3_K activation records.
+// Scale record: 16 tables of 8 bytes, [h][n][j] | f32 d. Table of scale u = s + 32 (entry i = 128 - s (i - 4)):
+// bytes 0-3 = u * 0x01020304 + 0x60402000, bytes 4-7 = 0xE0C0A080 - u * 0x03020100 (no byte leaves 0..255).
 struct DecQ3K {
     static constexpr int  BS   = 110;
     static constexpr int  KC   = 2;
-    static constexpr int  RECB = 80;
+    static constexpr int  RECB = 144;
     static constexpr bool Q80  = false;
 
     __device__ __forceinline__ static void prep(const uint8_t * blk, uint8_t * rec) {
-        const uint32_t s0 = lds_u32_a2(blk + 96), s1 = lds_u32_a2(blk + 100), s2 = lds_u32_a2(blk + 104);
-        const uint32_t lo[4] = { s0 & 0x0F0F0F0Fu, s1 & 0x0F0F0F0Fu, (s0 >> 4) & 0x0F0F0F0Fu, (s1 >> 4) & 0x0F0F0F0Fu };
-        int4 *         ri    = reinterpret_cast<int4 *>(rec);
+        const uint32_t a  = smem_u32(blk + 96);
+        const uint32_t b  = a & ~3u, sh = (a & 3u) * 8;
+        const uint32_t w0 = sld32(b), w1 = sld32(b + 4), w2 = sld32(b + 8), w3 = sld32(b + 12);
+        const uint32_t s0 = __funnelshift_r(w0, w1, sh), s1 = __funnelshift_r(w1, w2, sh);
+        const uint32_t s2 = __funnelshift_r(w2, w3, sh);
+        uint32_t       w[4];  // byte k of w[i] = u of scale index 4i + k
+        w[0] = (s0 & 0x0F0F0F0Fu) | ((s2 << 4) & 0x30303030u);
+        w[1] = (s1 & 0x0F0F0F0Fu) | ((s2 << 2) & 0x30303030u);
+        w[2] = ((s0 >> 4) & 0x0F0F0F0Fu) | (s2 & 0x30303030u);
+        w[3] = ((s1 >> 4) & 0x0F0F0F0Fu) | ((s2 >> 2) & 0x30303030u);
+        uint4 * rt = reinterpret_cast<uint4 *>(rec);
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint32_t w = lo[i] | (((s2 >> (2 * i)) & 0x03030303u) << 4);
-            ri[i] = make_int4(ubyte(w, 0) - 32, ubyte(w, 1) - 32, ubyte(w, 2) - 32, ubyte(w, 3) - 32);
+        for (int h = 0; h < 2; h++) {
+#pragma unroll
+            for (int n = 0; n < 2; n++) {
+#pragma unroll
+                for (int jp = 0; jp < 2; jp++) {  // tables j = 2 jp, 2 jp + 1: scale indices 8n + 4jp + h, + 2
+                    const uint32_t u0 = __byte_perm(w[2 * n + jp], 0u, 0x4440u | (uint32_t) h);
+                    const uint32_t u1 = __byte_perm(w[2 * n + jp], 0u, 0x4440u | (uint32_t) (2 + h));
+                    rt[4 * h + 2 * n + jp] = make_uint4(u0 * 0x01020304u + 0x60402000u, 0xE0C0A080u - u0 * 0x03020100u,
+                                                        u1 * 0x01020304u + 0x60402000u, 0xE0C0A080u - u1 * 0x03020100u);
+                }
+            }
         }
-        *reinterpret_cast<float *>(rec + 64) = ldh(blk + 108);
+        *reinterpret_cast<float *>(rec + 128) = half_bits_to_float((uint16_t) __funnelshift_r(w3, w3, sh));
+    }
+
+    // the four selectors (j = 0..3) of one row and half n from its qs words q0 (l = 8t..8t+3), q1 (8t+4..8t+7) and
+    // hmask words h0, h1: nibble = c | hb << 2, bit 3 clear
+    __device__ __forceinline__ static void selectors(uint32_t q0, uint32_t q1, uint32_t h0, uint32_t h1, int n,
+                                                     uint32_t (&y)[4]) {
+        const uint32_t elo = (q0 & 0x0F0F0F0Fu) | ((q1 << 4) & 0xF0F0F0F0u);   // c0 c1 per nibble pair
+        const uint32_t ehi = ((q0 >> 4) & 0x0F0F0F0Fu) | (q1 & 0xF0F0F0F0u);   // c2 c3
+        const uint32_t f   = n == 0 ? (h0 & 0x0F0F0F0Fu) | ((h1 << 4) & 0xF0F0F0F0u)
+                                    : ((h0 >> 4) & 0x0F0F0F0Fu) | (h1 & 0xF0F0F0F0u);  // hb of j = 0..3 per nibble
+        const uint32_t f02 = f & 0x55555555u, f13 = (f >> 1) & 0x55555555u;
+        y[0] = (elo & 0x33333333u) | ((f02 << 2) & 0xCCCCCCCCu);
+        y[1] = ((elo >> 2) & 0x33333333u) | ((f13 << 2) & 0xCCCCCCCCu);
+        y[2] = (ehi & 0x33333333u) | (f02 & 0xCCCCCCCCu);
+        y[3] = ((ehi >> 2) & 0x33333333u) | (f13 & 0xCCCCCCCCu);
+    }
+
+    template <bool A4>
+    __device__ __forceinline__ static void load(uint32_t pa, uint32_t pb, uint2 & ha, uint2 & hb, uint2 (&qa)[2],
+                                                uint2 (&qb)[2]) {
+        ha    = sld8_a2<A4>(pa);
+        hb    = sld8_a2<A4>(pb);
+        qa[0] = sld8_a2<A4>(pa + 32);
+        qa[1] = sld8_a2<A4>(pa + 64);
+        qb[0] = sld8_a2<A4>(pb + 32);
+        qb[1] = sld8_a2<A4>(pb + 64);
     }
 
     template <int NG, bool DBG>
     __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * ra,
                                               const uint8_t * rb, const uint8_t * xr, int lane, float (&acc)[NG][4],
                                               const DbgOut & dbg, int64_t rg, int sbi) {
-        constexpr int NT = 8 * NG;
-        const int     t = lane & 3, g = lane >> 2;
-        int           im[NG][4], in[NG][4];
-        zero<NG>(im);
-        zero<NG>(in);
+        constexpr int  NT = 8 * NG;
+        const int      t = lane & 3, g = lane >> 2, h = t >> 1;
+        const uint32_t pa = smem_u32(wa) + 8 * t, pb = smem_u32(wb) + 8 * t;
+        uint2          ha, hb, qa[2], qb[2];
+        if (((pa | pb) & 3u) == 0) {
+            load<true>(pa, pb, ha, hb, qa, qb);
+        } else {
+            load<false>(pa, pb, ha, hb, qa, qb);
+        }
+        const uint32_t ta = smem_u32(ra) + 64 * h, tb = smem_u32(rb) + 64 * h;
+        const uint32_t xb = smem_u32(xr) + g * kTokStride + 8 * t;
+        int            im[2][NG][4];  // one accumulator chain per half n
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
-            const int      off = 16 * h + 4 * t;
-            const uint32_t hma = lds_u32_a2(wa + off), hmb = lds_u32_a2(wb + off);
+        for (int n = 0; n < 2; n++) {
+            zero<NG>(im[n]);
+            uint32_t ya[4], yb[4];
+            selectors(qa[n].x, qa[n].y, ha.x, ha.y, n, ya);
+            selectors(qb[n].x, qb[n].y, hb.x, hb.y, n, yb);
 #pragma unroll
-            for (int n = 0; n < 2; n++) {
-                const uint32_t qa = lds_u32_a2(wa + 32 + 32 * n + off), qb = lds_u32_a2(wb + 32 + 32 * n + off);
-                const int4     sA4[2] = { lds128i(ra + 32 * n), lds128i(ra + 32 * n + 16) };
-                const int4     sB4[2] = { lds128i(rb + 32 * n), lds128i(rb + 32 * n + 16) };
+            for (int jp = 0; jp < 2; jp++) {
+                const uint4 TA = sld128(ta + 32 * n + 16 * jp), TB = sld128(tb + 32 * n + 16 * jp);
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const int      hs = 4 * n + j;
-                    const uint32_t ua = vsub_small(((qa >> (2 * j)) & 0x03030303u) | (((hma >> hs) & 0x01010101u) << 2),
-                                                   0x04040404u);
-                    const uint32_t ub = vsub_small(((qb >> (2 * j)) & 0x03030303u) | (((hmb >> hs) & 0x01010101u) << 2),
-                                                   0x04040404u);
-                    const int is = 2 * j + h;
-                    const int sA = sel4(sA4[is >> 2], is & 3), sB = sel4(sB4[is >> 2], is & 3);
-                    const int b  = 4 * n + j;
+                for (int e = 0; e < 2; e++) {
+                    const int      j   = 2 * jp + e;
+                    const uint32_t alo = e ? TA.z : TA.x, ahi = e ? TA.w : TA.y;
+                    const uint32_t blo = e ? TB.z : TB.x, bhi = e ? TB.w : TB.y;
+                    const uint32_t a0 = prmt(alo, ahi, ya[j]), a2 = prmt(alo, ahi, ya[j] >> 16);
+                    const uint32_t a1 = prmt(blo, bhi, yb[j]), a3 = prmt(blo, bhi, yb[j] >> 16);
 #pragma unroll
                     for (int grp = 0; grp < NG; grp++) {
-                        const uint32_t x    = lds32(xr + (8 * grp + g) * kTokStride + 32 * b + off);
-                        int            c[4];
-                        mma_k16_z<false>(c, ua, ub, x);
-                        scale_acc<NG>(im, grp, sA, sB, c);
+                        const uint2 x = sld64(xb + 8 * grp * kTokStride + 32 * (4 * n + j));
+                        mma_k32<true>(im[n][grp], a0, a1, a2, a3, x.x, x.y);
                     }
                 }
             }
         }
+        const uint32_t xsum = smem_u32(xr) + NT * kTokStride + 4 * NT + 8 * t;  // code sums of tokens 2t, 2t + 1
+        int            is[NG][4];
+#pragma unroll
+        for (int grp = 0; grp < NG; grp++) {
+            const uint2 s2 = sld64(xsum + 32 * grp);
+            const int   x0 = 128 * (int) s2.x, x1 = 128 * (int) s2.y;
+            is[grp][0]     = x0 - (im[0][grp][0] + im[1][grp][0]);
+            is[grp][1]     = x1 - (im[0][grp][1] + im[1][grp][1]);
+            is[grp][2]     = x0 - (im[0][grp][2] + im[1][grp][2]);
+            is[grp][3]     = x1 - (im[0][grp][3] + im[1][grp][3]);
+        }
         if constexpr (DBG) {
-            dbg_store<NG>(dbg, im, false, rg, sbi, lane);
+            dbg_store<NG>(dbg, is, false, rg, sbi, lane);
         } else {
             const float * xs = reinterpret_cast<const float *>(xr + NT * kTokStride);
-            sb_update<NG, false>(acc, im, in, *reinterpret_cast<const float *>(ra + 64),
-                                 *reinterpret_cast<const float *>(rb + 64), 0.f, 0.f, xs, t);
+            sb_update<NG, false>(acc, is, is, *reinterpret_cast<const float *>(ra + 128),
+                                 *reinterpret_cast<const float *>(rb + 128), 0.f, 0.f, xs, t);
         }
     }
 };
@@ -1046,8 +1119,9 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     a.stage_bytes      = (a.rec_off + a.kc * RB + 127) / 128 * 128;
     const int scr      = kNCW * D::KC * 16 * D::RECB;
     // 4 stages while that keeps 2 CTAs per SM resident, else 3 (228 KB of shared memory per SM, 1 KB of it reserved
-    // per CTA). A measured alternative, 3 CTAs per SM with 3 stages, streamed slower.
-    a.S = kBarBytes + 4 * a.stage_bytes + scr <= 110 * 1024 ? 4 : 3;
+    // per CTA, a few bytes of static shared memory). A measured alternative, 3 CTAs per SM with 3 stages, streamed
+    // slower.
+    a.S = kBarBytes + 4 * a.stage_bytes + scr <= 115200 ? 4 : 3;
     a.scr_off         = kBarBytes + a.S * a.stage_bytes;
     const size_t smem = (size_t) a.scr_off + scr;
     if (smem > 200 * 1024 || a.Wbox > 1024) return SRHPM_ERR_INVALID;
@@ -1191,7 +1265,8 @@ int gemm_run_impl(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, i
                                    (uint8_t *) nullptr, cnt, nrb);
         } else {
             e = cudaLaunchKernelEx(&cfg, quant_q8K_kernel<false>, X, ldx, (int) N, nsb, NT, recs, (int8_t *) nullptr,
-                                   (float *) nullptr, (int16_t *) nullptr, (int16_t *) nullptr, cnt, nrb);
+                                   (float *) nullptr, (int16_t *) nullptr, (int16_t *) nullptr, cnt, nrb,
+                                   (int) (wtype == SRHPM_TYPE_Q3_K));
         }
         ctx->launches.fetch_add(1);
         const int st = cuda_status(e);
@@ -1247,7 +1322,7 @@ int quantize_q8K_dense(srhpm_ctx * ctx, const float * X, int64_t ldx, int64_t N,
     const int64_t warps  = (int64_t) nsb * N;
     const int     blocks = (int) ((warps + 7) / 8);
     quant_q8K_kernel<true><<<blocks, 256, 0, stream>>>(X, ldx, (int) N, nsb, 0, nullptr, q, d, b32, b16,
-                                                       nullptr, 0);
+                                                       nullptr, 0, 0);
     ctx->launches.fetch_add(1);
     return cuda_status(cudaGetLastError());
 }
