@@ -7,19 +7,24 @@
 //              positions as f16 or q8_0 (ggml_cpy of f32 rows into the cache view; q8_0 with the context's q8_0 mode)
 //   swiglu     silu(gate) * up (ggml_swiglu); gate and up may be the two halves of one fused gate|up GEMM output
 // All rows are short (N <= 16 tokens): one CTA per (row, chunk) and grid-stride loops; these ops move a few hundred KB
-// per step against the ~12 GB of weights.
+// per step against the ~12 GB of weights. Each is launched with programmatic dependent launch: it lets its successor
+// get resident at once and waits for its predecessor's writes before reading.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
 
 #include "internal.h"
+#include "launch.cuh"
+#include "ptx.cuh"
 
 namespace srhpm {
 namespace {
 
 __global__ void get_rows_kernel(const uint8_t * table, int64_t row_bytes, int is_f16, const int32_t * ids, int64_t d,
                                 float * out) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int64_t   i   = blockIdx.y;
     const uint8_t * src = table + (int64_t) ids[i] * row_bytes;
     for (int64_t j = blockIdx.x * blockDim.x + threadIdx.x; j < d; j += (int64_t) gridDim.x * blockDim.x) {
@@ -32,6 +37,8 @@ __global__ void get_rows_kernel(const uint8_t * table, int64_t row_bytes, int is
 constexpr int kNormThreads = 1024;
 __global__ void __launch_bounds__(kNormThreads) add_rms_norm_kernel(float * x, const float * delta, const float * w,
                                                                      float eps, float * y, int64_t d) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int64_t i  = blockIdx.x;
     float *       xr = x + i * d;
     const bool    vec = (d & 3) == 0 && (reinterpret_cast<uintptr_t>(xr) & 15) == 0 &&
@@ -142,6 +149,8 @@ __device__ __forceinline__ void q80_store_warp(float v, uint8_t * dst, int mode)
 
 // grid: (token, head of q + k + v); one CTA of hd/2 threads (f16 cache) or hd threads (q8_0: a warp per block)
 __global__ void rope_kv_kernel(const RopeArgs a) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int t = blockIdx.x, hh = blockIdx.y, half = a.hd / 2;
     float *   row = a.qkv + (int64_t) t * a.ld;
     const float p = (float) a.pos[t];
@@ -170,6 +179,8 @@ __global__ void rope_kv_kernel(const RopeArgs a) {
 
 __global__ void swiglu_kernel(const float * gate, const float * up, int64_t ld_in, float * out, int64_t ld_out,
                               int64_t cols) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int64_t r = blockIdx.y;
     for (int64_t j = blockIdx.x * (int64_t) blockDim.x + threadIdx.x; j < cols; j += (int64_t) gridDim.x * blockDim.x) {
         const float g   = gate[r * ld_in + j];
@@ -181,18 +192,19 @@ __global__ void swiglu_kernel(const float * gate, const float * up, int64_t ld_i
 
 int get_rows_run(srhpm_ctx * ctx, const uint8_t * table, int64_t row_bytes, int is_f16, const int32_t * ids, int n,
                  int64_t d, float * out, cudaStream_t stream) {
-    get_rows_kernel<<<dim3((unsigned) std::min<int64_t>(8, (d + 255) / 256), n), 256, 0, stream>>>(table, row_bytes,
-                                                                                                    is_f16, ids, d, out);
+    const cudaError_t e = launch_k_pdl(get_rows_kernel, dim3((unsigned) std::min<int64_t>(8, (d + 255) / 256), n),
+                                       dim3(256), 0, stream, table, row_bytes, is_f16, ids, d, out);
     ctx->launches.fetch_add(1);
-    return cuda_status(cudaGetLastError());
+    return cuda_status(e);
 }
 
 int add_rms_norm_run(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y, int n,
                      int64_t d, cudaStream_t stream) {
     if (d > 4 * 4 * kNormThreads) return SRHPM_UNSUPPORTED;
-    add_rms_norm_kernel<<<n, kNormThreads, 0, stream>>>(x, delta, w, eps, y, d);
+    const cudaError_t e = launch_k_pdl(add_rms_norm_kernel, dim3(n), dim3(kNormThreads), 0, stream, x, delta, w, eps,
+                                       y, d);
     ctx->launches.fetch_add(1);
-    return cuda_status(cudaGetLastError());
+    return cuda_status(e);
 }
 
 int rope_kv_run(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int H, int Hkv, int hd, const int32_t * pos,
@@ -215,17 +227,19 @@ int rope_kv_run(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int H, int Hkv,
     a.vnb2        = vnb2;
     a.cache_type  = cache_type;
     a.q8mode      = ctx->q8_0_act_mode;
-    rope_kv_kernel<<<dim3(n, H + 2 * Hkv), cache_type == SRHPM_TYPE_F16 ? hd / 2 : hd, 0, stream>>>(a);
+    const cudaError_t e = launch_k_pdl(rope_kv_kernel, dim3(n, H + 2 * Hkv),
+                                       dim3(cache_type == SRHPM_TYPE_F16 ? hd / 2 : hd), 0, stream, a);
     ctx->launches.fetch_add(1);
-    return cuda_status(cudaGetLastError());
+    return cuda_status(e);
 }
 
 int swiglu_run(srhpm_ctx * ctx, const float * gate, const float * up, int64_t ld_in, float * out, int64_t ld_out,
                int rows, int64_t cols, cudaStream_t stream) {
     const int blocks = (int) std::min<int64_t>(std::max(1, 4 * ctx->num_sms / rows), (cols + 255) / 256);
-    swiglu_kernel<<<dim3(blocks, rows), 256, 0, stream>>>(gate, up, ld_in, out, ld_out, cols);
+    const cudaError_t e = launch_k_pdl(swiglu_kernel, dim3(blocks, rows), dim3(256), 0, stream, gate, up, ld_in, out,
+                                       ld_out, cols);
     ctx->launches.fetch_add(1);
-    return cuda_status(cudaGetLastError());
+    return cuda_status(e);
 }
 
 }  // namespace srhpm

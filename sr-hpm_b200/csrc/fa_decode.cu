@@ -28,6 +28,7 @@
 #include <cmath>
 
 #include "internal.h"
+#include "launch.cuh"
 #include "ptx.cuh"
 #include "tc.cuh"
 
@@ -85,8 +86,9 @@ template <int RP> struct Smem {
     static constexpr int slope = fac + RP * 4;        // f32 [RP] ALiBi slope * log2e
     static constexpr int moff = slope + RP * 4;       // int64 [RP] mask row offsets
     static constexpr int mslot = moff + RP * 8;       // int32 [RP] staged mask row of each row (its query token)
-    static constexpr int mbuf = (mslot + RP * 4 + 15) / 16 * 16;  // f16 [2][8][kT] staged mask tiles
-    static constexpr int bar  = mbuf + 2 * 8 * kT * 2;
+    static constexpr int MBR  = RP == 48 ? 8 : 16;    // staged mask rows (query tokens); 48-row groups: no room for 16
+    static constexpr int mbuf = (mslot + RP * 4 + 15) / 16 * 16;  // f16 [2][MBR][kT] staged mask tiles
+    static constexpr int bar  = mbuf + 2 * MBR * kT * 2;
     static constexpr int nbar = 2 * kNSlot + 4;       // full[], empty[], s_full, s_free, pv_ready, pv_done
     static constexpr int misc = bar + nbar * 8;       // tmem base, flags[3]
     static constexpr int total = misc + 16;
@@ -229,7 +231,7 @@ template <int RH> __device__ __forceinline__ void store_p(uint8_t * pbase, int r
     }
 }
 
-// staged mask tile (mask_mode 1, N <= 8): row tq, tokens tok0..tok0+127 -> f16 [8][kT]; thread p < N * 16 moves 8 tokens
+// staged mask tile (mask_mode 1, N <= MBR): row tq, tokens tok0..tok0+127 -> f16 [MBR][kT]; thread p < N * 16 moves 8 tokens
 __device__ __forceinline__ uint4 mask_piece(const FaArgs & a, int p, int tok0) {
     const int  tq = p >> 4, e0 = tok0 + 8 * (p & 15);
     const uint8_t * src = a.mask + (int64_t) tq * a.mnb1 + 2 * (int64_t) e0;
@@ -322,6 +324,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         prefetch_tmap(&mk128);
         prefetch_tmap(&mk32);
         prefetch_tmap(&mv);
+    }
+    // launched behind the kernel that wrote the newest K/V rows and Q (programmatic dependent launch): everything
+    // above overlapped its tail; from here on its writes are visible
+    pdl_wait();
+    if (warp == kCW && lane == 0) {
         for (int n = 0; n < min(kNSlot, nload); n++) produce(n);
     }
     __syncwarp();
@@ -381,7 +388,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             mslot[r]  = tq;
             mu[r]     = -INFINITY;
         }
-        if (a.mask_mode == 1 && tid < a.N * 16) {  // N <= 8
+        if (a.mask_mode == 1 && tid < a.N * 16) {  // N <= MBR
             *reinterpret_cast<uint4 *>(mbuf + (tid >> 4) * kT + 8 * (tid & 15)) = mask_piece(a, tid, t0);
         }
         arm_scores<RP>(tS, q, rbase);
@@ -475,7 +482,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             // next tile's staged mask piece: loaded now, stored before this tile's first barrier (which orders it before
             // the next tile's reads)
             uint4      mnext = make_uint4(0, 0, 0, 0);
-            const bool stage = a.mask_mode == 1 && i + 1 < nt && tid < a.N * 16;  // N <= 8
+            const bool stage = a.mask_mode == 1 && i + 1 < nt && tid < a.N * 16;  // N <= MBR
             if (stage) mnext = mask_piece(a, tid, t0 + (i + 1) * kT);
             wait_or_flag(s_full, i & 1, a.status, bad);
             wait_or_flag(&full[kslot], (n / kNSlot) & 1, a.status, bad);  // (complete already) the d bytes
@@ -538,7 +545,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                 for (int r = 0; r < RH; r++) s[r] = a.softcap_l2 * tanhf(s[r]);
             }
             if (a.mask_mode == 1) {
-                const uint16_t * mb = mbuf + (i & 1) * 8 * kT + t;
+                const uint16_t * mb = mbuf + (i & 1) * S::MBR * kT + t;
 #pragma unroll
                 for (int r = 0; r < RH; r++) {
                     const float sl = a.max_bias > 0.0f ? slope2[rbase + r] : kLog2e;
@@ -576,7 +583,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             wait_or_flag(&full[vslot], ((n + 1) / kNSlot) & 1, a.status, bad);
             load_v_part(sm + S::ring + vslot * kSlot + t * kRowB, qr, vw);
             if (stage) {
-                *reinterpret_cast<uint4 *>(mbuf + ((i + 1) & 1) * 8 * kT + (tid >> 4) * kT + 8 * (tid & 15)) = mnext;
+                *reinterpret_cast<uint4 *>(mbuf + ((i + 1) & 1) * S::MBR * kT + (tid >> 4) * kT + 8 * (tid & 15)) = mnext;
             }
             named_bar_sync(1, kCW * 32);
             if (tid == 0) flags[(i + 2) % 3] = 0;
@@ -650,6 +657,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         }
 
         // ---------------- epilogue ----------------
+        // every CTA of the grid is resident by now: the chunk merge may launch (it waits for this grid to finish)
+        pdl_launch_dependents();
         wait_or_flag(pv_done, (nt - 1) & 1, a.status, bad);
         tc::fence_after();
 #pragma unroll
@@ -737,8 +746,9 @@ template <int RP> struct SmemF {
     static constexpr int slope = fac + RP * 4;
     static constexpr int moff  = slope + RP * 4;      // int64 [RP]
     static constexpr int mslot = moff + RP * 8;       // int32 [RP]
-    static constexpr int mbuf  = (mslot + RP * 4 + 15) / 16 * 16;  // f16 [2][8][kT]
-    static constexpr int bar   = mbuf + 2 * 8 * kT * 2;
+    static constexpr int MBR   = 16;                  // staged mask rows (query tokens)
+    static constexpr int mbuf  = (mslot + RP * 4 + 15) / 16 * 16;  // f16 [2][MBR][kT]
+    static constexpr int bar   = mbuf + 2 * MBR * kT * 2;
     static constexpr int misc  = bar + 12 * 8;        // tmem base, flags[3]
     static constexpr int total = misc + 16;
     static constexpr int alloc = total + 1024;
@@ -815,6 +825,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     if (warp == kCW && lane == 0) {
         prefetch_tmap(&mk);
         prefetch_tmap(&mv);
+    }
+    pdl_wait();  // programmatic dependent launch: the writer of Q and of the newest K/V rows has finished
+    if (warp == kCW && lane == 0) {
         for (int sl = 0; sl < 4; sl++) produce(0, sl);
     }
     __syncwarp();
@@ -854,7 +867,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             mslot[r]  = tq;
             mu[r]     = -INFINITY;
         }
-        if (a.mask_mode == 1 && tid < a.N * 16) {  // N <= 8
+        if (a.mask_mode == 1 && tid < a.N * 16) {  // N <= MBR
             *reinterpret_cast<uint4 *>(mbuf + (tid >> 4) * kT + 8 * (tid & 15)) = mask_piece(a, tid, t0);
         }
     }
@@ -965,7 +978,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             const int  tok   = t0 + i * kT + t;
             const bool valid = tok < t1;
             if (a.mask_mode == 1) {
-                const uint16_t * mb = mbuf + (i & 1) * 8 * kT + t;
+                const uint16_t * mb = mbuf + (i & 1) * S::MBR * kT + t;
 #pragma unroll
                 for (int r = 0; r < RH; r++) {
                     const float sl   = a.max_bias > 0.0f ? slope2[rbase + r] : kLog2e;
@@ -996,7 +1009,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             }
             if (lane == 0 && up) flags[i % 3] = 1;
             if (stage) {
-                *reinterpret_cast<uint4 *>(mbuf + ((i + 1) & 1) * 8 * kT + (tid >> 4) * kT + 8 * (tid & 15)) = mnext;
+                *reinterpret_cast<uint4 *>(mbuf + ((i + 1) & 1) * S::MBR * kT + (tid >> 4) * kT + 8 * (tid & 15)) = mnext;
             }
             named_bar_sync(1, kCW * 32);
             if (tid == 0) flags[(i + 2) % 3] = 0;
@@ -1059,6 +1072,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         }
 
         // ---------------- epilogue ----------------
+        // every CTA of the grid is resident by now: the chunk merge may launch (it waits for this grid to finish)
+        pdl_launch_dependents();
         wait_or_flag(pv_done, (nt - 1) & 1, a.status, bad);
         tc::fence_after();
 #pragma unroll
@@ -1202,18 +1217,36 @@ struct Plan {
 Plan fa_plan(int num_sms, int R, int L, int Hkv) {
     Plan      p;
     const int max_ch = (L + kT - 1) / kT;
-    // long caches: 48-row groups (each KV byte read once per group); short caches (fewer 128-token tiles than SMs):
-    // 16-row groups for more CTAs (the extra K/V reads hit L2)
-    p.rp = Hkv * max_ch >= num_sms ? kRG : 16;
-    if (R <= 32 && p.rp == kRG) p.rp = (R + 15) / 16 * 16;
-    p.nrg              = (R + p.rp - 1) / p.rp;
-    const int groups   = Hkv * p.nrg;
-    int       want     = std::max(1, std::min(max_ch, (num_sms + groups - 1) / groups));
-    if (max_ch >= 2) want = std::min(want, max_ch / 2);  // two tiles per chunk at least
-    want               = std::max(1, want);
-    const int per      = (L + want - 1) / want;
-    p.chunk_len        = (per + kT - 1) / kT * kT;
-    p.n_chunks         = (L + p.chunk_len - 1) / p.chunk_len;
+    if (Hkv * max_ch >= num_sms) {
+        // long caches: 48-row groups (each KV byte read once per group), chunks of two tiles at least
+        p.rp = R <= 32 ? (R + 15) / 16 * 16 : kRG;
+        p.nrg            = (R + p.rp - 1) / p.rp;
+        const int groups = Hkv * p.nrg;
+        int       want   = std::max(1, std::min(max_ch, (num_sms + groups - 1) / groups));
+        if (max_ch >= 2) want = std::min(want, max_ch / 2);
+        want             = std::max(1, want);
+        const int per    = (L + want - 1) / want;
+        p.chunk_len      = (per + kT - 1) / kT * kT;
+    } else {
+        // short caches (fewer 128-token tiles than SMs): one wave of CTAs with the fewest tiles each; among row-group
+        // sizes with equal tiles per CTA the one with the fewest padded rows, then the fewest groups (K/V reads)
+        int best_tpc = 1 << 30, best_pad = 0;
+        for (const int rp : { 16, 32, kRG }) {
+            const int nrg    = (R + rp - 1) / rp;
+            const int groups = Hkv * nrg;
+            const int want   = std::max(1, std::min(max_ch, num_sms / groups));
+            const int tpc    = (max_ch + want - 1) / want;
+            if (tpc < best_tpc || (tpc == best_tpc && nrg * rp < best_pad) ||
+                (tpc == best_tpc && nrg * rp == best_pad && nrg < p.nrg)) {
+                best_tpc = tpc;
+                best_pad = nrg * rp;
+                p.rp     = rp;
+                p.nrg    = nrg;
+            }
+        }
+        p.chunk_len = best_tpc * kT;
+    }
+    p.n_chunks = (L + p.chunk_len - 1) / p.chunk_len;
     return p;
 }
 
@@ -1248,9 +1281,9 @@ int launch_fa(srhpm_ctx * ctx, const FaArgs & a, const CUtensorMap & mk128, cons
     static std::atomic<unsigned> done{ 0 };
     int st = set_smem(ctx, fa_q80_kernel<RP>, Smem<RP>::alloc, done);
     if (st != SRHPM_OK) return st;
-    fa_q80_kernel<RP><<<dim3(a.n_chunks, a.Hkv * a.nrg), kFaThreads, Smem<RP>::alloc, stream>>>(mk128, mk32, mv, a);
+    st = cuda_status(launch_k_pdl(fa_q80_kernel<RP>, dim3(a.n_chunks, a.Hkv * a.nrg), dim3(kFaThreads),
+                                Smem<RP>::alloc, stream, mk128, mk32, mv, a));
     ctx->launches.fetch_add(1);
-    st = cuda_status(cudaGetLastError());
     if (st != SRHPM_OK || a.n_chunks == 1) return st;
     return launch_combine(ctx, a, stream);
 }
@@ -1261,9 +1294,9 @@ int launch_fa_f16(srhpm_ctx * ctx, const FaArgs & a, const CUtensorMap & mk, con
     static std::atomic<unsigned> done{ 0 };
     int st = set_smem(ctx, fa_f16_kernel<RP>, SmemF<RP>::alloc, done);
     if (st != SRHPM_OK) return st;
-    fa_f16_kernel<RP><<<dim3(a.n_chunks, a.Hkv * a.nrg), kFaThreads, SmemF<RP>::alloc, stream>>>(mk, mv, a);
+    st = cuda_status(launch_k_pdl(fa_f16_kernel<RP>, dim3(a.n_chunks, a.Hkv * a.nrg), dim3(kFaThreads),
+                                SmemF<RP>::alloc, stream, mk, mv, a));
     ctx->launches.fetch_add(1);
-    st = cuda_status(cudaGetLastError());
     if (st != SRHPM_OK || a.n_chunks == 1) return st;
     return launch_combine(ctx, a, stream);
 }
@@ -1305,7 +1338,9 @@ int fa_run(srhpm_ctx * ctx, const FaView & v, float scale, float max_bias, float
     a.mne0     = v.mne0;
     a.mask_mode = 0;
     if (v.mask) {
-        const bool staged = v.mne2 == 1 && v.N <= 8 && reinterpret_cast<uintptr_t>(v.mask) % 16 == 0 && v.mnb1 % 16 == 0;
+        const int  mbr    = v.kv_type == SRHPM_TYPE_F16 ? SmemF<16>::MBR : (p.rp == 48 ? Smem<48>::MBR : Smem<16>::MBR);
+        const bool staged = v.mne2 == 1 && v.N <= mbr && reinterpret_cast<uintptr_t>(v.mask) % 16 == 0 &&
+                            v.mnb1 % 16 == 0;
         a.mask_mode = staged ? 1 : 2;
     }
     if (softcap != 0.0f) {

@@ -1155,11 +1155,24 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
     const int     slots  = std::max(1, per_sm) * ctx->num_sms;
     const int64_t nrb    = (a.rows + kTileRows - 1) / kTileRows;
-    // split K so that the units fill the resident CTA slots (about one round), K ranges of >= 2 super-blocks
+    // split K so that the units fill the resident CTA slots: in units of one full-K row block, a product takes about
+    // rounds / ranges (rounds = units over the slots, rounded up) plus a fixed cost per unit (the split-K epilogue:
+    // fence, arrival counter, reduction) of ~15 %; take the cheapest split (the fewest ranges among equals), K ranges
+    // of >= 2 super-blocks. Products with a row block for every slot are not split.
     a.ksplit = 1;
-    if (!DBG && a.part) {
-        const int want = (int) ((slots + nrb / 2) / nrb);
-        a.ksplit       = std::max(1, std::min({ want, kMaxSplit, a.nsb / 2 }));
+    if (!DBG && a.part && nrb < slots) {
+        const int most = std::max(1, std::min(kMaxSplit, a.nsb / 2));
+        double    best = 1e30;
+        for (int ks = 1; ks <= most; ks++) {
+            const int     sbs    = (a.nsb + ks - 1) / ks;
+            const int     eff    = (a.nsb + sbs - 1) / sbs;  // non-empty ranges
+            const int64_t rounds = (nrb * eff + slots - 1) / slots;
+            const double  cost   = (double) rounds / eff + 0.15 * (double) rounds;
+            if (cost < best * 0.999) {
+                best     = cost;
+                a.ksplit = eff;
+            }
+        }
     }
     a.kr_sbs = (a.nsb + a.ksplit - 1) / a.ksplit;
     a.units  = (int) (nrb * a.ksplit);

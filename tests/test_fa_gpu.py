@@ -61,7 +61,7 @@ def oracle(q, k, v, Hkv, mask=None, sinks=None, **kw):
 
 
 @pytest.mark.parametrize("H,Hkv,N,L", [(24, 4, 8, 1000), (6, 2, 5, 192), (6, 1, 2, 129), (8, 8, 1, 77),
-                                       (12, 2, 16, 300), (4, 1, 3, 5000)])
+                                       (12, 2, 16, 300), (4, 1, 3, 5000), (4, 2, 12, 700)])
 def test_fa_q8_0_vs_oracle_and_reference(ctx, ref, H, Hkv, N, L):
     rng = np.random.default_rng(H * 1000 + L)
     q, k, v = inputs(rng, H, Hkv, N, L)
