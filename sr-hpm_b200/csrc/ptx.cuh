@@ -205,6 +205,16 @@ __device__ __forceinline__ uint4 sld128(uint32_t a) {
     asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
     return v;
 }
+// 4 bytes at a shared address that is 4-byte aligned (A4), or any even one (two aligned words and a funnel shift)
+template <bool A4>
+__device__ __forceinline__ uint32_t sld4_a2(uint32_t a) {
+    if constexpr (A4) {
+        return sld32(a);
+    } else {
+        const uint32_t b = a & ~3u;
+        return __funnelshift_r(sld32(b), sld32(b + 4), (a & 3u) * 8);
+    }
+}
 // 8 bytes at a shared address that is 4-byte aligned (A4), or any (three aligned words and two funnel shifts)
 template <bool A4>
 __device__ __forceinline__ uint2 sld8_a2(uint32_t a) {

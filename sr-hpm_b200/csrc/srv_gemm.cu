@@ -439,19 +439,23 @@ struct DecQ6K {
     static constexpr bool Q80  = false;
 
     __device__ __forceinline__ static void prep(const uint8_t * blk, uint8_t * rec) {
-        int4 * ri = reinterpret_cast<int4 *>(rec);
+        int4 *         ri = reinterpret_cast<int4 *>(rec);
+        const uint32_t a = smem_u32(blk + 192), b = a & ~3u, sh = (a & 3u) * 8;
+        uint32_t       wd[5];
+#pragma unroll
+        for (int i = 0; i < 5; i++) wd[i] = sld32(b + 4 * i);
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            const uint32_t w = lds_u32_a2(blk + 192 + 4 * i);
+            const uint32_t w = __funnelshift_r(wd[i], wd[i + 1], sh);
             ri[i]            = make_int4(sbyte(w, 0), sbyte(w, 1), sbyte(w, 2), sbyte(w, 3));
         }
         *reinterpret_cast<float *>(rec + 64) = ldh(blk + 208);
     }
 
-    template <int NG, bool DBG>
-    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * ra,
-                                              const uint8_t * rb, const uint8_t * xr, int lane, float (&acc)[NG][4],
-                                              const DbgOut & dbg, int64_t rg, int sbi) {
+    template <int NG, bool DBG, bool A4>
+    __device__ __forceinline__ static void sb_impl(uint32_t pa, uint32_t pb, const uint8_t * ra, const uint8_t * rb,
+                                                   const uint8_t * xr, int lane, float (&acc)[NG][4],
+                                                   const DbgOut & dbg, int64_t rg, int sbi) {
         constexpr int NT = 8 * NG;
         const int     t = lane & 3, g = lane >> 2;
         int           im[NG][4], in[NG][4];
@@ -464,9 +468,9 @@ struct DecQ6K {
 #pragma unroll
             for (int h = 0; h < 2; h++) {
                 const int      off = 16 * h + 4 * t;
-                const uint32_t l0a = lds_u32_a2(wa + 64 * n + off), l1a = lds_u32_a2(wa + 64 * n + 32 + off);
-                const uint32_t l0b = lds_u32_a2(wb + 64 * n + off), l1b = lds_u32_a2(wb + 64 * n + 32 + off);
-                const uint32_t qha = lds_u32_a2(wa + 128 + 32 * n + off), qhb = lds_u32_a2(wb + 128 + 32 * n + off);
+                const uint32_t l0a = sld4_a2<A4>(pa + 64 * n + off), l1a = sld4_a2<A4>(pa + 64 * n + 32 + off);
+                const uint32_t l0b = sld4_a2<A4>(pb + 64 * n + off), l1b = sld4_a2<A4>(pb + 64 * n + 32 + off);
+                const uint32_t qha = sld4_a2<A4>(pa + 128 + 32 * n + off), qhb = sld4_a2<A4>(pb + 128 + 32 * n + off);
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     const uint32_t la = (j & 1) ? l1a : l0a, lb = (j & 1) ? l1b : l0b;
@@ -494,6 +498,19 @@ struct DecQ6K {
             const float * xs = reinterpret_cast<const float *>(xr + NT * kTokStride);
             sb_update<NG, false>(acc, im, in, *reinterpret_cast<const float *>(ra + 64),
                                  *reinterpret_cast<const float *>(rb + 64), 0.f, 0.f, xs, t);
+        }
+    }
+
+    template <int NG, bool DBG>
+    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * ra,
+                                              const uint8_t * rb, const uint8_t * xr, int lane, float (&acc)[NG][4],
+                                              const DbgOut & dbg, int64_t rg, int sbi) {
+        // the choice must be warp-uniform: sb_impl issues mma.sync (rows of one warp can differ in alignment)
+        const uint32_t pa = smem_u32(wa), pb = smem_u32(wb);
+        if (__all_sync(0xffffffffu, ((pa | pb) & 3u) == 0)) {
+            sb_impl<NG, DBG, true>(pa, pb, ra, rb, xr, lane, acc, dbg, rg, sbi);
+        } else {
+            sb_impl<NG, DBG, false>(pa, pb, ra, rb, xr, lane, acc, dbg, rg, sbi);
         }
     }
 };
@@ -579,7 +596,7 @@ struct DecQ3K {
         const int      t = lane & 3, g = lane >> 2, h = t >> 1;
         const uint32_t pa = smem_u32(wa) + 8 * t, pb = smem_u32(wb) + 8 * t;
         uint2          ha, hb, qa[2], qb[2];
-        if (((pa | pb) & 3u) == 0) {
+        if (__all_sync(0xffffffffu, ((pa | pb) & 3u) == 0)) {  // warp-uniform: no divergence around the loads
             load<true>(pa, pb, ha, hb, qa, qb);
         } else {
             load<false>(pa, pb, ha, hb, qa, qb);
@@ -713,10 +730,23 @@ struct DecQ80 {
         rf[1]       = make_float4(ldh(blk + 136), ldh(blk + 170), ldh(blk + 204), ldh(blk + 238));
     }
 
-    template <int NG, bool DBG>
-    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * ra,
-                                              const uint8_t * rb, const uint8_t * xr, int lane, float (&acc)[NG][4],
-                                              const DbgOut & dbg, int64_t rg, int sbi) {
+    // 4 quant bytes at byte offset o of block i; rows are 16-byte aligned in practice (Q8_0 rows are multiples of
+    // 272 bytes), so block i's quants (at 34 i + 2) are 4-byte aligned for odd i and 2 mod 4 for even i
+    template <bool A4>
+    __device__ __forceinline__ static uint32_t q4(uint32_t base, int i, int o) {
+        const uint32_t a = base + 34 * i + o;
+        if constexpr (A4) {
+            if (i & 1) return sld32(a);
+            return __funnelshift_r(sld32(a - 2), sld32(a + 2), 16);
+        } else {
+            return sld4_a2<false>(a);
+        }
+    }
+
+    template <int NG, bool DBG, bool A4>
+    __device__ __forceinline__ static void sb_impl(uint32_t pa, uint32_t pb, const uint8_t * ra, const uint8_t * rb,
+                                                   const uint8_t * xr, int lane, float (&acc)[NG][4],
+                                                   const DbgOut & dbg, int64_t rg, int sbi) {
         constexpr int NT = 8 * NG;
         const int     t = lane & 3, g = lane >> 2;
         const float * xsb = reinterpret_cast<const float *>(xr + NT * kTokStride);
@@ -724,11 +754,9 @@ struct DecQ80 {
         const float4  dB4[2] = { *reinterpret_cast<const float4 *>(rb), *reinterpret_cast<const float4 *>(rb + 16) };
 #pragma unroll
         for (int i = 0; i < 8; i++) {
-            const uint8_t * ba = wa + 34 * i;
-            const uint8_t * bb = wb + 34 * i;
-            const uint32_t  a0 = lds_u32_a2(ba + 2 + 4 * t), a2 = lds_u32_a2(ba + 18 + 4 * t);
-            const uint32_t  a1 = lds_u32_a2(bb + 2 + 4 * t), a3 = lds_u32_a2(bb + 18 + 4 * t);
-            int             c[NG][4];
+            const uint32_t a0 = q4<A4>(pa, i, 2 + 4 * t), a2 = q4<A4>(pa, i, 18 + 4 * t);
+            const uint32_t a1 = q4<A4>(pb, i, 2 + 4 * t), a3 = q4<A4>(pb, i, 18 + 4 * t);
+            int            c[NG][4];
 #pragma unroll
             for (int grp = 0; grp < NG; grp++) {
                 const uint8_t * xp = xr + (8 * grp + g) * kTokStride + 32 * i + 4 * t;
@@ -751,6 +779,19 @@ struct DecQ80 {
                     acc[grp][3] += (dB * x.y) * (float) c[grp][3];
                 }
             }
+        }
+    }
+
+    template <int NG, bool DBG>
+    __device__ __forceinline__ static void sb(const uint8_t * wa, const uint8_t * wb, const uint8_t * ra,
+                                              const uint8_t * rb, const uint8_t * xr, int lane, float (&acc)[NG][4],
+                                              const DbgOut & dbg, int64_t rg, int sbi) {
+        // the choice must be warp-uniform: sb_impl issues mma.sync (rows of one warp can differ in alignment)
+        const uint32_t pa = smem_u32(wa), pb = smem_u32(wb);
+        if (__all_sync(0xffffffffu, ((pa | pb) & 3u) == 0)) {
+            sb_impl<NG, DBG, true>(pa, pb, ra, rb, xr, lane, acc, dbg, rg, sbi);
+        } else {
+            sb_impl<NG, DBG, false>(pa, pb, ra, rb, xr, lane, acc, dbg, rg, sbi);
         }
     }
 };
@@ -1006,9 +1047,15 @@ __global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_cons
             }
             __syncwarp();
             const uint8_t * xr = st + a.rec_off;
+            if (kcc == D::KC) {  // a full stage: straight-line code, so the super-blocks' loads and math can overlap
 #pragma unroll
-            for (int kb = 0; kb < D::KC; kb++) {
-                if (kb < kcc) {
+                for (int kb = 0; kb < D::KC; kb++) {
+                    D::template sb<NG, DBG>(wa + kb * D::BS, wb + kb * D::BS, scr + (kb * 16 + g) * D::RECB,
+                                            scr + (kb * 16 + g + 8) * D::RECB, xr + kb * RB, lane, acc, dbg, rg,
+                                            sb0 + kb);
+                }
+            } else {
+                for (int kb = 0; kb < kcc; kb++) {
                     D::template sb<NG, DBG>(wa + kb * D::BS, wb + kb * D::BS, scr + (kb * 16 + g) * D::RECB,
                                             scr + (kb * 16 + g + 8) * D::RECB, xr + kb * RB, lane, acc, dbg, rg,
                                             sb0 + kb);
