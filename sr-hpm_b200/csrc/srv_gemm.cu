@@ -345,6 +345,7 @@ struct DecK45 {
     static constexpr int  KC   = 2;
     static constexpr int  RECB = 48;
     static constexpr bool Q80  = false;
+    static constexpr int  MINB = 2;  // resident CTAs per SM the kernel is compiled for
     static constexpr int  QS   = Q5 ? 48 : 16;
 
     __device__ __forceinline__ static void prep(const uint8_t * blk, uint8_t * rec) {
@@ -437,6 +438,7 @@ struct DecQ6K {
     static constexpr int  KC   = 1;
     static constexpr int  RECB = 80;
     static constexpr bool Q80  = false;
+    static constexpr int  MINB = 4;  // resident CTAs per SM the kernel is compiled for (measured: 4 beats 2 here)
 
     __device__ __forceinline__ static void prep(const uint8_t * blk, uint8_t * rec) {
         int4 *         ri = reinterpret_cast<int4 *>(rec);
@@ -533,6 +535,7 @@ struct DecQ3K {
     static constexpr int  KC   = 2;
     static constexpr int  RECB = 144;
     static constexpr bool Q80  = false;
+    static constexpr int  MINB = 2;  // resident CTAs per SM the kernel is compiled for
 
     __device__ __forceinline__ static void prep(const uint8_t * blk, uint8_t * rec) {
         const uint32_t a  = smem_u32(blk + 96);
@@ -657,6 +660,7 @@ struct DecIQ4XS {
     static constexpr int  KC   = 2;
     static constexpr int  RECB = 48;
     static constexpr bool Q80  = false;
+    static constexpr int  MINB = 2;  // resident CTAs per SM the kernel is compiled for
 
     // the 16-entry code book as four words of int8 lanes (GGUF constant kvalues_iq4nl)
     static constexpr uint32_t T0 = 0xBFAD9881u, T1 = 0xF6EADDCFu, T2 = 0x26190D01u, T3 = 0x71594535u;
@@ -723,6 +727,7 @@ struct DecQ80 {
     static constexpr int  KC   = 1;
     static constexpr int  RECB = 32;
     static constexpr bool Q80  = true;
+    static constexpr int  MINB = 2;  // resident CTAs per SM the kernel is compiled for
 
     __device__ __forceinline__ static void prep(const uint8_t * blk, uint8_t * rec) {
         float4 * rf = reinterpret_cast<float4 *>(rec);
@@ -963,7 +968,7 @@ __device__ __forceinline__ const uint8_t * row_ptr(const GemmArgs & a, const uin
 }
 
 template <class D, int NG, bool DBG>
-__global__ void __launch_bounds__(kThreads, 2) srv_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
+__global__ void __launch_bounds__(kThreads, D::MINB) srv_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
                                                             const GemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     uint64_t * full   = reinterpret_cast<uint64_t *>(smem);
@@ -1165,10 +1170,20 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     a.rec_off          = (a.left_off + (a.G > 1 ? (a.G - 1) * a.LSR : 0) + 127) / 128 * 128;
     a.stage_bytes      = (a.rec_off + a.kc * RB + 127) / 128 * 128;
     const int scr      = kNCW * D::KC * 16 * D::RECB;
-    // 4 stages while that keeps 2 CTAs per SM resident, else 3 (228 KB of shared memory per SM, 1 KB of it reserved
-    // per CTA, a few bytes of static shared memory). A measured alternative, 3 CTAs per SM with 3 stages, streamed
-    // slower.
-    a.S = kBarBytes + 4 * a.stage_bytes + scr <= 115200 ? 4 : 3;
+    // the most resident CTAs per SM the decoder is compiled for (D::MINB: 2, or 4 for Q6_K; 228 KB of shared memory per
+    // SM, 1 KB of it reserved per CTA, a few bytes of static shared memory), then the most stages (4..2) that still
+    // fit them. Measured: 4 CTAs with 2-3 stages streamed slower than 2 CTAs with 3-4 stages for every type but Q6_K.
+    a.S = 0;
+    for (int c = D::MINB; c >= 2 && a.S == 0; c--) {
+        const int lim = 233472 / c - 1024 - 256;
+        for (int st = 4; st >= 2; st--) {
+            if (kBarBytes + st * a.stage_bytes + scr <= lim) {
+                a.S = st;
+                break;
+            }
+        }
+    }
+    if (a.S == 0) a.S = 2;
     a.scr_off         = kBarBytes + a.S * a.stage_bytes;
     const size_t smem = (size_t) a.scr_off + scr;
     if (smem > 200 * 1024 || a.Wbox > 1024) return SRHPM_ERR_INVALID;
