@@ -442,9 +442,14 @@ def run_gpu(args):
     e2e_value = step_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
     ctx.check()
 
+    step_tp = None
+    if world > 1 and not args.no_step:  # every rank takes part (NCCL all-reduces inside the step)
+        step_tp = measure_step_27b_tp(ctx, dev, rank, world)
     if rank == 0:
         cfg = workload_config(base_ops, world)
         cfg["timed"] = "CUDA graph of one step, replayed" if graph is not None else "eager calls"
+        if step_tp is not None:
+            cfg["verify_step_27b_f16kv_2048_tp"] = step_tp
         if ncopy > 1:
             cfg["copies_rotated"] = ncopy
         cfg["per_type_gbs"] = group(lambda op: [k for k, v in TYPE_IDS.items() if v == op[1]][0])
@@ -490,6 +495,62 @@ def run_gpu(args):
         dist.destroy_process_group()
     ctx.close()
     return 0
+
+
+def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0):
+    """BASELINE config 4 on `world` GPUs: the same 27B-class verify step in Megatron tensor parallelism (column-
+    parallel QKV / gate|up / head, row-parallel O / down with an NCCL all-reduce after each, KV heads split or
+    replicated per rank, vocabulary-sharded acceptance). Every rank holds 1/world of the weights (random blocks) and
+    its KV heads' cache; the step (kernels + 129 collectives) is one CUDA graph; time = max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from srhpm_b200 import _lib as L
+    from srhpm_b200 import verify_step as V
+    cfg = V.DecoderConfig(kv_type=L.F16)
+    w = V.DeviceWeights.random(cfg, dev, seed, rank=rank, world=world)
+    nkv = w.tp["g1"] - w.tp["g0"]
+    n = k + 1
+    cap = n_past + n
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed + 7 + rank)
+    kc = [torch.randn((cap * nkv, cfg.hd), device=dev, generator=g).half().view(torch.uint8).view(cap, nkv, 512)
+          for _ in range(cfg.n_layer)]
+    vc = [torch.randn((cap * nkv, cfg.hd), device=dev, generator=g).half().view(torch.uint8).view(cap, nkv, 512)
+          for _ in range(cfg.n_layer)]
+    step = V.VerifyStep(ctx, cfg, w, kc, vc, n, n_past, tp=V.TensorParallel(rank, world))
+    ids = torch.arange(n, dtype=torch.int32, device=dev) * 977 % cfg.n_vocab  # the same tokens on every rank
+    step.set_tokens(ids, ids[1:])
+    for _ in range(2):
+        step.run()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    ctx.launch_count(reset=True)
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            step.run(s)
+    launches = ctx.launch_count(reset=True)
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ctx.check()
+    tt = torch.tensor([e0.elapsed_time(e1) / reps], device=dev)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    ms = float(tt.item())
+    acc = int(step.out_n.item())
+    del graph  # holds NCCL calls: released before the process group
+    nbytes = step_bytes_27b(cfg, n_past, n)
+    return {f"k{k}": {"ms": round(ms, 3), "steps_per_s": round(1e3 / ms, 1), "gpus": world,
+                      "GBps_per_gpu": round(nbytes / world / (ms * 1e-3) / 1e9, 1), "bytes": nbytes,
+                      "kernel_launches_per_rank": launches, "accepted": acc}}
 
 
 def measure_attention(ctx, dev, peak, reps=20, lengths=(8192, 32768, 131072)):

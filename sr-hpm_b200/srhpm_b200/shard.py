@@ -38,6 +38,40 @@ def kv_heads(n_kv, world, rank):
     return per * rank, per * (rank + 1)
 
 
+def k_columns(blocks, blk, bpb, k0, k1):
+    """Columns [k0, k1) of packed weight rows (numpy uint8 [rows, row bytes], blk values per bpb-byte block; k0, k1 on
+    block boundaries) as a contiguous [rows, (k1 - k0) / blk * bpb] array."""
+    if k0 % blk or k1 % blk:
+        raise ValueError("a column range must start and end on block boundaries")
+    import numpy as np
+    return np.ascontiguousarray(blocks[:, k0 // blk * bpb:k1 // blk * bpb])
+
+
+def tp_layout(H, Hkv, n_ff, n_vocab, world, rank):
+    """Megatron tensor-parallel slices of rank `rank` of `world` for a GQA decoder (the split of the 27B step):
+    query heads [h0, h1); KV heads [g0, g1) (when world > Hkv each KV head is replicated on world / Hkv ranks, the
+    ones holding its query heads); FFN rows [f0, f1) on super-block boundaries (the K range of the row-parallel down
+    matrix); vocabulary rows [v0, v1) of the head. Column-parallel: QKV, gate, up, head. Row-parallel: O (K = the
+    rank's heads), down (K = its FFN rows)."""
+    if H % world:
+        raise ValueError(f"{H} query heads do not split over {world} ranks")
+    hq = H // world
+    h0, h1 = rank * hq, (rank + 1) * hq
+    if Hkv % world == 0:
+        g0, g1 = rank * (Hkv // world), (rank + 1) * (Hkv // world)
+    elif world % Hkv == 0:
+        g0 = rank // (world // Hkv)
+        g1 = g0 + 1
+    else:
+        raise ValueError(f"{Hkv} KV heads do not map onto {world} ranks")
+    G = H // Hkv
+    if not (g0 * G <= h0 and h1 <= g1 * G):
+        raise ValueError("a rank's query heads must share its KV heads")
+    f0, f1 = k_range(n_ff, world, rank)
+    v0, v1 = vocab_range(n_vocab, world, rank)
+    return dict(h0=h0, h1=h1, g0=g0, g1=g1, f0=f0, f1=f1, v0=v0, v1=v1)
+
+
 class PackedSlices:
     """Layout of the row slices of several products in one buffer per rank, for one all-gather per step.
 

@@ -78,60 +78,129 @@ def random_blocks_device(t, rows, K, gen, device, d_lo=1e-4, d_hi=2e-4):
 
 
 class DeviceWeights:
-    """The decoder's weights in device memory."""
+    """The decoder's weights in device memory; `tp` holds the tensor-parallel slice they are (shard.tp_layout: query
+    heads, KV heads, FFN rows, vocabulary rows, rank, world; the whole model when world = 1)."""
 
     def __init__(self, cfg, device):
         self.cfg, self.device = cfg, device
         self.layers = []
         self.out_norm = self.head = self.emb = None
+        self.tp = None
+
+    def _set_tp(self, rank, world):
+        from .shard import tp_layout
+        self.tp = dict(tp_layout(self.cfg.H, self.cfg.Hkv, self.cfg.n_ff, self.cfg.n_vocab, world, rank), rank=rank,
+                       world=world)
+        return self.tp
 
     @classmethod
-    def from_host(cls, cfg, w, device="cuda"):
+    def from_host(cls, cfg, w, device="cuda", rank=0, world=1):
+        """From host_weights (packed blocks of the whole model); rank / world cut one tensor-parallel rank's slices:
+        QKV rows of its query and KV heads, O columns of its heads, gate / up rows and down columns of its FFN rows,
+        head rows of its vocabulary range."""
+        from .shard import k_columns
         self = cls(cfg, device)
+        tp = self._set_tp(rank, world)
+        hd, H, Hkv = cfg.hd, cfg.H, cfg.Hkv
+        h0, h1, g0, g1, f0, f1 = tp["h0"], tp["h1"], tp["g0"], tp["g1"], tp["f0"], tp["f1"]
+        t = cfg.types
+
+        def kcols(blocks, qt, k0, k1):
+            return k_columns(np.asarray(blocks), blck_size(qt), type_size(qt), k0, k1)
+
         for l in range(cfg.n_layer):
             lay = {}
-            for name, t, rows, K in cfg.shapes():
-                if name not in ("gate", "up"):
-                    lay[name] = QuantTensor.from_blocks(w[name][l], t, rows, K, device)
+            qkv = np.asarray(w["qkv"][l]).reshape((H + 2 * Hkv) * hd, -1)
+            part = np.concatenate([qkv[h0 * hd:h1 * hd], qkv[(H + g0) * hd:(H + g1) * hd],
+                                   qkv[(H + Hkv + g0) * hd:(H + Hkv + g1) * hd]])
+            lay["qkv"] = QuantTensor.from_blocks(part, t["qkv"], (h1 - h0 + 2 * (g1 - g0)) * hd, cfg.d, device)
+            o = np.asarray(w["o"][l]).reshape(cfg.d, -1)
+            lay["o"] = QuantTensor.from_blocks(kcols(o, t["o"], h0 * hd, h1 * hd), t["o"], cfg.d, (h1 - h0) * hd, device)
             # gate and up as one matrix (gate rows, then up rows): one GEMM launch, SwiGLU reads the halves
-            gu = np.concatenate([np.asarray(w["gate"][l]).reshape(cfg.n_ff, -1),
-                                 np.asarray(w["up"][l]).reshape(cfg.n_ff, -1)])
-            lay["gate_up"] = QuantTensor.from_blocks(gu, cfg.types["gate"], 2 * cfg.n_ff, cfg.d, device)
+            gu = np.concatenate([np.asarray(w["gate"][l]).reshape(cfg.n_ff, -1)[f0:f1],
+                                 np.asarray(w["up"][l]).reshape(cfg.n_ff, -1)[f0:f1]])
+            lay["gate_up"] = QuantTensor.from_blocks(gu, t["gate"], 2 * (f1 - f0), cfg.d, device)
+            dn = np.asarray(w["down"][l]).reshape(cfg.d, -1)
+            lay["down"] = QuantTensor.from_blocks(kcols(dn, t["down"], f0, f1), t["down"], cfg.d, f1 - f0, device)
             lay["attn_norm"] = torch.from_numpy(w["attn_norm"][l]).to(device)
             lay["ffn_norm"] = torch.from_numpy(w["ffn_norm"][l]).to(device)
             self.layers.append(lay)
         self.out_norm = torch.from_numpy(w["out_norm"]).to(device)
-        self.head = QuantTensor.from_blocks(w["head"], cfg.types["head"], cfg.n_vocab, cfg.d, device)
+        head = np.asarray(w["head"]).reshape(cfg.n_vocab, -1)[tp["v0"]:tp["v1"]]
+        self.head = QuantTensor.from_blocks(head, t["head"], tp["v1"] - tp["v0"], cfg.d, device)
         self.emb = torch.from_numpy(w["emb"]).to(device)
         return self
 
     @classmethod
-    def random(cls, cfg, device="cuda", seed=0):
+    def random(cls, cfg, device="cuda", seed=0, rank=0, world=1):
+        """Random GGUF blocks of one tensor-parallel rank's slice shapes (the whole model when world = 1)."""
         self = cls(cfg, device)
+        tp = self._set_tp(rank, world)
         gen = torch.Generator(device=device)
-        gen.manual_seed(seed)
+        gen.manual_seed(seed + 1000 * rank)
+        hd, t = cfg.hd, cfg.types
+        nh, ng, nf = tp["h1"] - tp["h0"], tp["g1"] - tp["g0"], tp["f1"] - tp["f0"]
         for _ in range(cfg.n_layer):
-            lay = {name: random_blocks_device(t, rows, K, gen, device) for name, t, rows, K in cfg.shapes()
-                   if name not in ("gate", "up")}
-            lay["gate_up"] = random_blocks_device(cfg.types["gate"], 2 * cfg.n_ff, cfg.d, gen, device)
+            lay = {"qkv": random_blocks_device(t["qkv"], (nh + 2 * ng) * hd, cfg.d, gen, device),
+                   "o": random_blocks_device(t["o"], cfg.d, nh * hd, gen, device),
+                   "gate_up": random_blocks_device(t["gate"], 2 * nf, cfg.d, gen, device),
+                   "down": random_blocks_device(t["down"], cfg.d, nf, gen, device)}
             lay["attn_norm"] = 1.0 + 0.1 * torch.randn(cfg.d, device=device, generator=gen)
             lay["ffn_norm"] = 1.0 + 0.1 * torch.randn(cfg.d, device=device, generator=gen)
             self.layers.append(lay)
         self.out_norm = 1.0 + 0.1 * torch.randn(cfg.d, device=device, generator=gen)
-        self.head = random_blocks_device(cfg.types["head"], cfg.n_vocab, cfg.d, gen, device)
+        self.head = random_blocks_device(t["head"], tp["v1"] - tp["v0"], cfg.d, gen, device)
         self.emb = torch.randn((cfg.n_vocab, cfg.d), device=device, generator=gen).half()
         return self
+
+
+class TensorParallel:
+    """The collectives of a Megatron tensor-parallel step over torch.distributed (NCCL): one all-reduce after the
+    row-parallel O and down GEMMs of every layer (the SURVEY's 128 per step) and an all-gather of the vocabulary
+    shards' argmax records before the acceptance. Captured in the step's CUDA graph like the kernels."""
+
+    def __init__(self, rank, world, group=None):
+        self.rank, self.world, self.group = rank, world, group
+
+    def all_reduce(self, t):
+        import torch.distributed as dist
+        dist.all_reduce(t, group=self.group)
+
+    def all_gather(self, out, t):
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(out, t, group=self.group)
+
+
+def _py_call(f):
+    """A host callable in the step's call list (signature of the C-ABI calls: arguments then the stream, status
+    return). It issues on torch's current stream, which `run` makes the step's stream."""
+    def call(*args):
+        f()
+        return L.OK
+    return call
 
 
 class VerifyStep:
     """One verify step of n tokens (1 accepted + k drafted) at cache position n_past, with prebuilt C-ABI calls.
 
-    kcache / vcache: per layer uint8 [capacity, Hkv, row bytes] (f16 or q8_0 rows), the llama.cpp cache layout."""
+    kcache / vcache: per layer uint8 [capacity, Hkv, row bytes] (f16 or q8_0 rows), the llama.cpp cache layout.
+    With tensor parallelism (`tp`, and weights cut by gguf.load_decoder / DeviceWeights.shard) every dimension below
+    is this rank's: its query heads, its KV heads (caches hold only those), its FFN rows and its vocabulary rows; the
+    residual stream, norms and embeddings are replicated."""
 
-    def __init__(self, ctx, cfg, weights, kcache, vcache, n_tokens, n_past, relax=0.0):
+    def __init__(self, ctx, cfg, weights, kcache, vcache, n_tokens, n_past, relax=0.0, tp=None):
         self.ctx, self.cfg, self.w = ctx, cfg, weights
         self.kcache, self.vcache = kcache, vcache
         self.n, self.n_past, self.relax = n_tokens, n_past, relax
+        self.tp = tp if tp is not None and tp.world > 1 else None
+        lay = getattr(weights, "tp", None)
+        if self.tp is not None and lay is None:
+            raise ValueError("tensor parallelism needs the rank's weight slices")
+        self.H = lay["h1"] - lay["h0"] if lay else cfg.H
+        self.Hkv = lay["g1"] - lay["g0"] if lay else cfg.Hkv
+        self.n_ff = lay["f1"] - lay["f0"] if lay else cfg.n_ff
+        self.vocab_offset = lay["v0"] if lay else 0
+        self.V = weights.head.rows
         dev = weights.device
         c, n = cfg, n_tokens
         f32 = dict(dtype=torch.float32, device=dev)
@@ -140,14 +209,17 @@ class VerifyStep:
         self.pos = torch.arange(n_past, n_past + n, dtype=torch.int32, device=dev)
         self.x = torch.zeros((n, c.d), **f32)                              # residual stream
         self.y = torch.zeros((n, c.d), **f32)                              # normed input of a block
-        self.qkv = torch.zeros((n, (c.H + 2 * c.Hkv) * c.hd), **f32)
-        self.att = torch.zeros((n, c.H * c.hd), **f32)
+        self.qkv = torch.zeros((n, (self.H + 2 * self.Hkv) * c.hd), **f32)
+        self.att = torch.zeros((n, self.H * c.hd), **f32)
         self.o = torch.zeros((n, c.d), **f32)
-        self.gu = torch.zeros((n, 2 * c.n_ff), **f32)                      # gate | up
-        self.h = torch.zeros((n, c.n_ff), **f32)
-        self.logits = torch.zeros((n, c.n_vocab), **f32)
+        self.gu = torch.zeros((n, 2 * self.n_ff), **f32)                   # gate | up
+        self.h = torch.zeros((n, self.n_ff), **f32)
+        self.logits = torch.zeros((n, self.V), **f32)
         self.out_ids = torch.zeros(n, dtype=torch.int32, device=dev)
         self.out_n = torch.zeros(1, dtype=torch.int32, device=dev)
+        if self.tp is not None:
+            self.rec = torch.zeros((n, 16), dtype=torch.uint8, device=dev)            # srhpm_argmax_record rows
+            self.rec_all = torch.zeros((self.tp.world, n, 16), dtype=torch.uint8, device=dev)
         self.lib = L.load()
         self._keep = []
         self._calls = []
@@ -166,20 +238,26 @@ class VerifyStep:
         fn = self.lib.srhpm_mul_mat
         return ("mul_mat", fn, [self.ctx.handle, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv)], True)
 
+    def _all_reduce(self, t):
+        return ("all_reduce", _py_call(lambda: self.tp.all_reduce(t)), [], False)
+
     def _cache_view(self, cache, start, length):
         c = self.cfg
         t = cache[start:start + length]
         tsz = 34 if c.kv_type == L.Q8_0 else 2
-        blk = 32 if c.kv_type == L.Q8_0 else 1
         # cache [cap, Hkv, row] -> ggml view [hd, length, Hkv] (token stride = stride(0), head stride = stride(1))
-        return _tensor_view(t, c.kv_type, [c.hd, length, c.Hkv], [tsz, t.stride(0), t.stride(1)]), t
+        return _tensor_view(t, c.kv_type, [c.hd, length, self.Hkv], [tsz, t.stride(0), t.stride(1)]), t
 
     def _build(self):
         c, n, lib, h = self.cfg, self.n, self.lib, self.ctx.handle
+        H, Hkv, hd = self.H, self.Hkv, c.hd
         self._ws = 0
         calls = []
-        # embeddings
-        emb_v = _tensor_view(self.w.emb, L.F16, [c.d, c.n_vocab], [2, self.w.emb.stride(0) * 2])
+        # embeddings (the whole table on every rank)
+        n_emb = self.w.emb.shape[0]
+        emb_t = L.F16 if self.w.emb.dtype == torch.float16 else L.F32
+        esz = self.w.emb.element_size()
+        emb_v = _tensor_view(self.w.emb, emb_t, [c.d, n_emb], [esz, self.w.emb.stride(0) * esz])
         self._keep.append(emb_v)
         calls.append(("get_rows", lib.srhpm_get_rows,
                       [h, ctypes.byref(emb_v), self._ptr(self.ids), n, self._ptr(self.x)], False))
@@ -190,12 +268,17 @@ class VerifyStep:
             calls.append(("add_rms_norm", lib.srhpm_add_rms_norm,
                           [h, self._ptr(self.x), None if first else self._ptr(self.o), self._ptr(lay["attn_norm"]),
                            ctypes.c_float(c.eps), self._ptr(self.y), n, c.d], False))
-            calls.append(self._mm(lay["qkv"], self.y, self.qkv))
+            if "qkv" in lay:
+                calls.append(self._mm(lay["qkv"], self.y, self.qkv))
+            else:  # Q, K, V of different types: three GEMMs into the column ranges of the qkv rows
+                calls.append(self._mm(lay["q"], self.y, self.qkv[:, :H * hd]))
+                calls.append(self._mm(lay["k"], self.y, self.qkv[:, H * hd:(H + Hkv) * hd]))
+                calls.append(self._mm(lay["v"], self.y, self.qkv[:, (H + Hkv) * hd:]))
             kv_full, kt = self._cache_view(self.kcache[li], 0, self.kcache[li].shape[0])
             vv_full, vt = self._cache_view(self.vcache[li], 0, self.vcache[li].shape[0])
             self._keep += [kv_full, vv_full, kt, vt]
             calls.append(("rope_kv", lib.srhpm_rope_kv,
-                          [h, self._ptr(self.qkv), self.qkv.stride(0), n, c.H, c.Hkv, c.hd, self._ptr(self.pos),
+                          [h, self._ptr(self.qkv), self.qkv.stride(0), n, H, Hkv, hd, self._ptr(self.pos),
                            ctypes.c_float(c.base), ctypes.byref(kv_full), ctypes.byref(vv_full)], False))
             # attention over the visible keys (sliding-window layers: the last `window` positions)
             full = c.window <= 0 or li % c.full_every == c.full_every - 1
@@ -207,9 +290,9 @@ class VerifyStep:
             kv, kt2 = self._cache_view(self.kcache[li], start, L_all - start)
             vv, vt2 = self._cache_view(self.vcache[li], start, L_all - start)
             # q: the rotated query heads inside the qkv rows: ne [hd, n, H], token stride = row, head stride = hd
-            qv = _tensor_view(self.qkv, L.F32, [c.hd, n, c.H], [4, self.qkv.stride(0) * 4, c.hd * 4])
+            qv = _tensor_view(self.qkv, L.F32, [hd, n, H], [4, self.qkv.stride(0) * 4, hd * 4])
             # dst [hd, H, n]: head stride hd, token stride H * hd -> att rows [n][H * hd]
-            ov = _tensor_view(self.att, L.F32, [c.hd, c.H, n], [4, c.hd * 4, self.att.stride(0) * 4])
+            ov = _tensor_view(self.att, L.F32, [hd, H, n], [4, hd * 4, self.att.stride(0) * 4])
             mv = _tensor_view(mask, L.F16, [mask.shape[1], mask.shape[0], 1], [2, mask.stride(0) * 2])
             self._keep += [kv, vv, kt2, vt2, qv, ov, mv]
             sz = ctypes.c_size_t()
@@ -218,18 +301,26 @@ class VerifyStep:
             self._ws = max(self._ws, sz.value)
             calls.append(("flash_attn_ext", lib.srhpm_flash_attn_ext,
                           [h, ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(mv), None,
-                           ctypes.c_float(1.0 / math.sqrt(c.hd)), ctypes.c_float(0.0), ctypes.c_float(0.0),
+                           ctypes.c_float(1.0 / math.sqrt(hd)), ctypes.c_float(0.0), ctypes.c_float(0.0),
                            ctypes.byref(ov)], True))
             calls.append(self._mm(lay["o"], self.att, self.o))
+            if self.tp is not None:
+                calls.append(self._all_reduce(self.o))  # row-parallel O: partial sums over the rank's heads
             calls.append(("add_rms_norm", lib.srhpm_add_rms_norm,
                           [h, self._ptr(self.x), self._ptr(self.o), self._ptr(lay["ffn_norm"]), ctypes.c_float(c.eps),
                            self._ptr(self.y), n, c.d], False))
-            calls.append(self._mm(lay["gate_up"], self.y, self.gu))
-            up_ptr = ctypes.c_void_p(self.gu.data_ptr() + 4 * c.n_ff)
+            if "gate_up" in lay:
+                calls.append(self._mm(lay["gate_up"], self.y, self.gu))
+            else:
+                calls.append(self._mm(lay["gate"], self.y, self.gu[:, :self.n_ff]))
+                calls.append(self._mm(lay["up"], self.y, self.gu[:, self.n_ff:]))
+            up_ptr = ctypes.c_void_p(self.gu.data_ptr() + 4 * self.n_ff)
             calls.append(("swiglu", lib.srhpm_swiglu,
                           [h, self._ptr(self.gu), up_ptr, self.gu.stride(0), self._ptr(self.h), self.h.stride(0), n,
-                           c.n_ff], False))
+                           self.n_ff], False))
             calls.append(self._mm(lay["down"], self.h, self.o))  # o: the delta added by the next add_rms_norm
+            if self.tp is not None:
+                calls.append(self._all_reduce(self.o))  # row-parallel down
         calls.append(("add_rms_norm", lib.srhpm_add_rms_norm,
                       [h, self._ptr(self.x), self._ptr(self.o), self._ptr(self.w.out_norm), ctypes.c_float(c.eps),
                        self._ptr(self.y), n, c.d], False))
@@ -240,9 +331,18 @@ class VerifyStep:
         L.check(lib.srhpm_verify_accept_work_size(h, ctypes.byref(lv), ctypes.byref(sz)),
                 "srhpm_verify_accept_work_size")
         self._ws = max(self._ws, sz.value)
-        calls.append(("verify_accept", lib.srhpm_verify_accept,
-                      [h, ctypes.byref(lv), self._ptr(self.draft), n - 1, ctypes.c_float(self.relax),
-                       self._ptr(self.out_ids), self._ptr(self.out_n)], True))
+        if self.tp is None:
+            calls.append(("verify_accept", lib.srhpm_verify_accept,
+                          [h, ctypes.byref(lv), self._ptr(self.draft), n - 1, ctypes.c_float(self.relax),
+                           self._ptr(self.out_ids), self._ptr(self.out_n)], True))
+        else:  # vocabulary-sharded head: per-row (max, first index, draft logit) records, gathered, merged on every rank
+            calls.append(("argmax_shard", lib.srhpm_argmax_shard,
+                          [h, ctypes.byref(lv), ctypes.c_int64(self.vocab_offset), self._ptr(self.draft), n - 1,
+                           self._ptr(self.rec)], True))
+            calls.append(("all_gather", _py_call(lambda: self.tp.all_gather(self.rec_all, self.rec)), [], False))
+            calls.append(("accept_merge", lib.srhpm_accept_merge,
+                          [h, self._ptr(self.rec_all), self.tp.world, n, self._ptr(self.draft), n - 1,
+                           ctypes.c_float(self.relax), self._ptr(self.out_ids), self._ptr(self.out_n)], False))
         self.work = torch.empty(max(self._ws, 1 << 16), dtype=torch.uint8, device=self.w.device)
         wargs = [ctypes.c_void_p(self.work.data_ptr()), ctypes.c_size_t(self.work.numel())]
         self._calls = [(name, fn, args + wargs if with_work else args) for name, fn, args, with_work in calls]
@@ -266,11 +366,13 @@ class VerifyStep:
 
     def run(self, stream=None):
         """Issue the whole step on `stream` (the current stream by default)."""
-        s = ctypes.c_void_p((stream or torch.cuda.current_stream()).cuda_stream)
-        for name, fn, args in self._calls:
-            st = fn(*args, s)
-            if st != L.OK:
-                raise L.SrhpmError(st, "srhpm_" + name, self.lib)
+        st_obj = stream or torch.cuda.current_stream()
+        s = ctypes.c_void_p(st_obj.cuda_stream)
+        with torch.cuda.stream(st_obj):  # the collectives issue on torch's current stream
+            for name, fn, args in self._calls:
+                st = fn(*args, s)
+                if st != L.OK:
+                    raise L.SrhpmError(st, "srhpm_" + name, self.lib)
 
     def set_tokens(self, ids, draft):
         """Inputs of the step: ids int [n] (accepted token + drafted tokens), draft int [n - 1]."""
