@@ -183,6 +183,21 @@ int srhpm_accept_merge(srhpm_ctx * ctx, const srhpm_argmax_record * recs, int n_
 int srhpm_get_rows(srhpm_ctx * ctx, const srhpm_tensor * table, const int32_t * ids, int n, float * out, void * stream);
 int srhpm_add_rms_norm(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y, int n,
                        int64_t d, void * stream);
+/* Tensor-parallel residual add + RMSNorm with the all-reduce inside (row-parallel GEMM -> next norm):
+ * every rank's row-parallel GEMM (attention output, FFN down) writes its partial sum [n][d] f32 into slot `slot`
+ * (0 or 1) of its own symmetric buffer of srhpm_allreduce_buffer_size(d) bytes, zeroed once before first use and
+ * mapped on every rank (peer_buffers: a DEVICE array of `world` addresses, this rank's own at [rank]; IPC / symmetric
+ * memory set up by the caller). srhpm_add_rms_norm_allreduce then, per row: publishes a per-(slot, row) epoch to every
+ * peer, waits (bounded: 2 s, then SRHPM_ERR_DEVICE through srhpm_ctx_check) until every peer has published the same
+ * epoch, sums the rank's rows over ranks in rank order (identical on every rank), adds the sum to x and writes
+ * y = x / sqrt(mean(x^2) + eps) * w. epochs: this rank's uint32 [2][16] counters, zeroed once. n <= 16, world <= 8,
+ * d a multiple of 4 and <= 16384; x, w, y 16-byte aligned. The two slots alternate (O, down): a slot is rewritten only
+ * after the other slot's barrier has passed on every rank. Every rank must make the same sequence of calls. No
+ * counterpart in the reference (it runs on one device); the SURVEY's config 4 all-reduce after O and down. */
+size_t srhpm_allreduce_buffer_size(int64_t d);
+int srhpm_add_rms_norm_allreduce(srhpm_ctx * ctx, float * x, const uint64_t * peer_buffers, int world, int rank,
+                                 int slot, uint32_t * epochs, const float * w, float eps, float * y, int n, int64_t d,
+                                 void * stream);
 int srhpm_rope_kv(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int n_head, int n_head_kv, int head_dim,
                   const int32_t * pos, float theta_base, const srhpm_tensor * k_cache, const srhpm_tensor * v_cache,
                   void * stream);

@@ -399,6 +399,19 @@ int srhpm_add_rms_norm(srhpm_ctx * ctx, float * x, const float * delta, const fl
     return add_rms_norm_run(ctx, x, delta, w, eps, y, n, d, (cudaStream_t) stream);
 }
 
+size_t srhpm_allreduce_buffer_size(int64_t d) { return d > 0 ? allreduce_buffer_bytes(d) : 0; }
+
+int srhpm_add_rms_norm_allreduce(srhpm_ctx * ctx, float * x, const uint64_t * peer_buffers, int world, int rank,
+                                 int slot, uint32_t * epochs, const float * w, float eps, float * y, int n, int64_t d,
+                                 void * stream) {
+    if (!ctx || !x || !peer_buffers || !epochs || !w || !y || d < 1) return SRHPM_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) & 15) {
+        return SRHPM_ERR_ALIGN;
+    }
+    return add_rms_norm_ar_run(ctx, x, peer_buffers, world, rank, slot, epochs, w, eps, y, n, d,
+                               (cudaStream_t) stream);
+}
+
 int srhpm_rope_kv(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int n_head, int n_head_kv, int head_dim,
                   const int32_t * pos, float theta_base, const srhpm_tensor * k_cache, const srhpm_tensor * v_cache,
                   void * stream) {

@@ -104,6 +104,113 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_kernel(float * x, c
     }
 }
 
+// ---- residual add of a tensor-parallel partial sum + RMSNorm, the all-reduce done in the same kernel ------------
+// Every rank's row-parallel GEMM (attention output, FFN down) wrote its partial sum into slot `slot` of its own
+// symmetric buffer (mapped on every peer): [2 slots][16 rows][d] f32, then flags [2][16][kArMaxRanks] u32. CTA i
+// (row i): one thread bumps this rank's epoch of (slot, row), publishes it into every peer's flag (slot, i, rank),
+// waits until every peer's flag in its own buffer has reached it (bounded: 2 s, then an error status), and the row
+// is summed over ranks in rank order (every rank adds the same values in the same order: identical results). Each
+// slot is rewritten only after a later barrier of the same rows, so two suffice.
+// Ordering: the partial rows were written by the previous kernel of each rank (complete before this grid passes
+// griddepcontrol.wait) and sit in that GPU's L2, which serves peer reads over NVLink; the flags are strong relaxed
+// system-scope accesses and the peer rows are read uncached (ld.global.cv). A system-scope fence or release per
+// signal (a full memory barrier each) measured ~19 us per call on B200; without them the barrier is a round trip.
+constexpr int kArMaxRanks = 8;
+constexpr int kArRows     = 16;
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void st_relaxed_sys(uint32_t * p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t * p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__global__ void __launch_bounds__(kNormThreads) add_rms_norm_ar_kernel(float * x, const uint64_t * peers, int world,
+                                                                        int rank, int slot, uint32_t * epochs,
+                                                                        const float * w, float eps, float * y,
+                                                                        int64_t d, int32_t * status) {
+    pdl_launch_dependents();
+    pdl_wait();  // this rank's GEMM has written its partial rows
+    const int64_t i = blockIdx.x;
+    const size_t  part_bytes = (size_t) kArRows * d * sizeof(float);
+    const size_t  flag_off   = 2 * part_bytes;
+    __shared__ int ok_s;
+    if (threadIdx.x == 0) {
+        const uint32_t e = ++epochs[slot * kArRows + i];
+        const size_t fo = flag_off + ((size_t) (slot * kArRows + i) * kArMaxRanks + rank) * sizeof(uint32_t);
+        for (int j = 0; j < world; j++) st_relaxed_sys(reinterpret_cast<uint32_t *>(peers[j] + fo), e);
+        const uint32_t * mine = reinterpret_cast<const uint32_t *>(peers[rank] + flag_off) +
+                                (size_t) (slot * kArRows + i) * kArMaxRanks;
+        const uint64_t   t0 = global_timer_ns();
+        int              ok = 1;
+        for (int j = 0; j < world && ok; j++) {
+            while ((int32_t) (ld_relaxed_sys(mine + j) - e) < 0) {
+                if (global_timer_ns() - t0 > 2000000000ull) {
+                    ok = 0;
+                    atomicExch(status, kErrPeerWait);
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        ok_s = ok;
+    }
+    __syncthreads();
+    float * xr = x + i * d;
+    float   ss = 0.0f;
+    float4  v[4];
+    const int64_t d4 = d >> 2;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int64_t j = threadIdx.x + (int64_t) k * kNormThreads;
+        if (j < d4) {
+            float4 a = reinterpret_cast<const float4 *>(xr)[j];
+            if (ok_s) {
+                for (int r = 0; r < world; r++) {
+                    const float4 b = __ldcv(reinterpret_cast<const float4 *>(peers[r] + slot * part_bytes) + i * d4 + j);
+                    a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+                }
+            }
+            reinterpret_cast<float4 *>(xr)[j] = a;
+            v[k] = a;
+            ss = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, ss))));
+        }
+    }
+    __shared__ float part[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        ss = part[threadIdx.x];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (threadIdx.x == 0) part[0] = ss;
+    }
+    __syncthreads();
+    const float scale = 1.0f / sqrtf(part[0] / (float) d + eps);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int64_t j = threadIdx.x + (int64_t) k * kNormThreads;
+        if (j < d4) {
+            const float4 ww = reinterpret_cast<const float4 *>(w)[j];
+            float4       o;
+            o.x = v[k].x * scale * ww.x;
+            o.y = v[k].y * scale * ww.y;
+            o.z = v[k].z * scale * ww.z;
+            o.w = v[k].w * scale * ww.w;
+            reinterpret_cast<float4 *>(y + i * d)[j] = o;
+        }
+    }
+}
+
 struct RopeArgs {
     float *         qkv;         // [n][ld]: q heads (H x hd) | k heads (Hkv x hd) | v heads (Hkv x hd)
     int64_t         ld;
@@ -205,6 +312,24 @@ int add_rms_norm_run(srhpm_ctx * ctx, float * x, const float * delta, const floa
                                        y, d);
     ctx->launches.fetch_add(1);
     return cuda_status(e);
+}
+
+int add_rms_norm_ar_run(srhpm_ctx * ctx, float * x, const uint64_t * peers, int world, int rank, int slot,
+                        uint32_t * epochs, const float * w, float eps, float * y, int n, int64_t d,
+                        cudaStream_t stream) {
+    if (d > 4 * 4 * kNormThreads || (d & 3) != 0) return SRHPM_UNSUPPORTED;
+    if (n < 1 || n > kArRows || world < 1 || world > kArMaxRanks || rank < 0 || rank >= world || slot < 0 ||
+        slot > 1) {
+        return SRHPM_ERR_INVALID;
+    }
+    const cudaError_t e = launch_k_pdl(add_rms_norm_ar_kernel, dim3(n), dim3(kNormThreads), 0, stream, x, peers,
+                                       world, rank, slot, epochs, w, eps, y, d, ctx->d_status);
+    ctx->launches.fetch_add(1);
+    return cuda_status(e);
+}
+
+size_t allreduce_buffer_bytes(int64_t d) {
+    return 2 * (size_t) kArRows * d * sizeof(float) + 2 * kArRows * kArMaxRanks * sizeof(uint32_t);
 }
 
 int rope_kv_run(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int H, int Hkv, int hd, const int32_t * pos,

@@ -86,6 +86,10 @@ int get_rows_run(srhpm_ctx * ctx, const uint8_t * table, int64_t row_bytes, int 
                  int64_t d, float * out, cudaStream_t stream);
 int add_rms_norm_run(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y, int n,
                      int64_t d, cudaStream_t stream);
+int add_rms_norm_ar_run(srhpm_ctx * ctx, float * x, const uint64_t * peers, int world, int rank, int slot,
+                        uint32_t * epochs, const float * w, float eps, float * y, int n, int64_t d,
+                        cudaStream_t stream);
+size_t allreduce_buffer_bytes(int64_t d);
 int rope_kv_run(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int H, int Hkv, int hd, const int32_t * pos,
                 float theta_base, uint8_t * kc, int64_t knb1, int64_t knb2, uint8_t * vc, int64_t vnb1, int64_t vnb2,
                 int cache_type, cudaStream_t stream);

@@ -12,7 +12,7 @@ namespace srhpm {
 constexpr uint32_t kWaitLimit = 1u << 22;
 
 // error words written to the context's device status slot
-enum : int32_t { kErrNone = 0, kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3 };
+enum : int32_t { kErrNone = 0, kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3, kErrPeerWait = 4 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void * p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

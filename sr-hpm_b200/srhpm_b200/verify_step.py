@@ -155,12 +155,37 @@ class DeviceWeights:
 
 
 class TensorParallel:
-    """The collectives of a Megatron tensor-parallel step over torch.distributed (NCCL): one all-reduce after the
-    row-parallel O and down GEMMs of every layer (the SURVEY's 128 per step) and an all-gather of the vocabulary
-    shards' argmax records before the acceptance. Captured in the step's CUDA graph like the kernels."""
+    """The collectives of a Megatron tensor-parallel step over torch.distributed.
 
-    def __init__(self, rank, world, group=None):
-        self.rank, self.world, self.group = rank, world, group
+    fused=True (default): the row-parallel O and down GEMMs write their partial sums into a symmetric buffer (torch
+    symmetric memory: every rank's buffer mapped on every rank), and the next RMSNorm sums the ranks' rows itself
+    over NVLink peer loads after a flag barrier (srhpm_add_rms_norm_allreduce): no separate collective launch.
+    fused=False: an NCCL all-reduce after each of those GEMMs (the SURVEY's 128 per step). The vocabulary shards'
+    argmax records are all-gathered with NCCL before the acceptance either way. All of it is captured in the step's
+    CUDA graph."""
+
+    def __init__(self, rank, world, group=None, fused=True):
+        self.rank, self.world, self.group, self.fused = rank, world, group, fused
+        self.part = self.peers = self.epochs = None
+
+    def setup(self, d, device):
+        """Symmetric buffer for the fused all-reduce of rows of d values (collective: every rank calls it)."""
+        if not self.fused or self.part is not None:
+            return
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        lib = L.load()
+        nbytes = int(lib.srhpm_allreduce_buffer_size(d))
+        buf = symm.empty(nbytes, dtype=torch.uint8, device=device)
+        buf.zero_()
+        hdl = symm.rendezvous(buf, self.group if self.group is not None else dist.group.WORLD)
+        self._buf, self._hdl = buf, hdl
+        self.peers = torch.tensor([int(p) for p in hdl.buffer_ptrs], dtype=torch.int64, device=device)
+        self.epochs = torch.zeros(32, dtype=torch.int32, device=device)
+        slot = 16 * d * 4
+        self.part = [buf[k * slot:(k + 1) * slot].view(torch.float32).view(16, d) for k in (0, 1)]
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)
 
     def all_reduce(self, t):
         import torch.distributed as dist
@@ -220,6 +245,7 @@ class VerifyStep:
         if self.tp is not None:
             self.rec = torch.zeros((n, 16), dtype=torch.uint8, device=dev)            # srhpm_argmax_record rows
             self.rec_all = torch.zeros((self.tp.world, n, 16), dtype=torch.uint8, device=dev)
+            self.tp.setup(c.d, dev)
         self.lib = L.load()
         self._keep = []
         self._calls = []
@@ -240,6 +266,25 @@ class VerifyStep:
 
     def _all_reduce(self, t):
         return ("all_reduce", _py_call(lambda: self.tp.all_reduce(t)), [], False)
+
+    def _fused(self):
+        return self.tp is not None and self.tp.fused
+
+    def _rowpar_out(self, slot):
+        """Output of a row-parallel GEMM: the rank's partial sums (fused: slot `slot` of the symmetric buffer)."""
+        return self.tp.part[slot][:self.n] if self._fused() else self.o
+
+    def _norm(self, delta_slot, wnorm):
+        """Residual add of the pending delta (none for the first block) + RMSNorm into y."""
+        c, n, lib, h = self.cfg, self.n, self.lib, self.ctx.handle
+        if delta_slot is not None and self._fused():
+            tp = self.tp
+            return ("add_rms_norm_allreduce", lib.srhpm_add_rms_norm_allreduce,
+                    [h, self._ptr(self.x), self._ptr(tp.peers), tp.world, tp.rank, delta_slot, self._ptr(tp.epochs),
+                     self._ptr(wnorm), ctypes.c_float(c.eps), self._ptr(self.y), n, c.d], False)
+        return ("add_rms_norm", lib.srhpm_add_rms_norm,
+                [h, self._ptr(self.x), None if delta_slot is None else self._ptr(self.o), self._ptr(wnorm),
+                 ctypes.c_float(c.eps), self._ptr(self.y), n, c.d], False)
 
     def _cache_view(self, cache, start, length):
         c = self.cfg
@@ -264,10 +309,7 @@ class VerifyStep:
         L_all = self.n_past + n
         masks = {}
         for li, lay in enumerate(self.w.layers):
-            first = li == 0
-            calls.append(("add_rms_norm", lib.srhpm_add_rms_norm,
-                          [h, self._ptr(self.x), None if first else self._ptr(self.o), self._ptr(lay["attn_norm"]),
-                           ctypes.c_float(c.eps), self._ptr(self.y), n, c.d], False))
+            calls.append(self._norm(None if li == 0 else 1, lay["attn_norm"]))
             if "qkv" in lay:
                 calls.append(self._mm(lay["qkv"], self.y, self.qkv))
             else:  # Q, K, V of different types: three GEMMs into the column ranges of the qkv rows
@@ -303,12 +345,10 @@ class VerifyStep:
                           [h, ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(mv), None,
                            ctypes.c_float(1.0 / math.sqrt(hd)), ctypes.c_float(0.0), ctypes.c_float(0.0),
                            ctypes.byref(ov)], True))
-            calls.append(self._mm(lay["o"], self.att, self.o))
-            if self.tp is not None:
+            calls.append(self._mm(lay["o"], self.att, self._rowpar_out(0)))
+            if self.tp is not None and not self._fused():
                 calls.append(self._all_reduce(self.o))  # row-parallel O: partial sums over the rank's heads
-            calls.append(("add_rms_norm", lib.srhpm_add_rms_norm,
-                          [h, self._ptr(self.x), self._ptr(self.o), self._ptr(lay["ffn_norm"]), ctypes.c_float(c.eps),
-                           self._ptr(self.y), n, c.d], False))
+            calls.append(self._norm(0, lay["ffn_norm"]))
             if "gate_up" in lay:
                 calls.append(self._mm(lay["gate_up"], self.y, self.gu))
             else:
@@ -318,12 +358,11 @@ class VerifyStep:
             calls.append(("swiglu", lib.srhpm_swiglu,
                           [h, self._ptr(self.gu), up_ptr, self.gu.stride(0), self._ptr(self.h), self.h.stride(0), n,
                            self.n_ff], False))
-            calls.append(self._mm(lay["down"], self.h, self.o))  # o: the delta added by the next add_rms_norm
-            if self.tp is not None:
-                calls.append(self._all_reduce(self.o))  # row-parallel down
-        calls.append(("add_rms_norm", lib.srhpm_add_rms_norm,
-                      [h, self._ptr(self.x), self._ptr(self.o), self._ptr(self.w.out_norm), ctypes.c_float(c.eps),
-                       self._ptr(self.y), n, c.d], False))
+            # the delta added by the next norm (row-parallel: partial sums over the rank's FFN rows)
+            calls.append(self._mm(lay["down"], self.h, self._rowpar_out(1)))
+            if self.tp is not None and not self._fused():
+                calls.append(self._all_reduce(self.o))
+        calls.append(self._norm(1, self.w.out_norm))
         calls.append(self._mm(self.w.head, self.y, self.logits))
         lv = f32_rows_view(self.logits)
         self._keep.append(lv)

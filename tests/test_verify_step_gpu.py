@@ -179,7 +179,7 @@ def test_step_from_gguf_file_and_unfused_weights(ctx, tmp_path):
     gf.close()
 
 
-def _tp_worker(rank, world, port, cfg_kw, seed, cap, n_past, ids, draft, q):
+def _tp_worker(rank, world, port, cfg_kw, seed, cap, n_past, ids, draft, q, fused=True):
     import os
     import torch.distributed as dist
     try:
@@ -194,7 +194,8 @@ def _tp_worker(rank, world, port, cfg_kw, seed, cap, n_past, ids, draft, q):
         kcr = [torch.from_numpy(np.ascontiguousarray(a[:, g0:g1])).cuda() for a in kc]
         vcr = [torch.from_numpy(np.ascontiguousarray(a[:, g0:g1])).cuda() for a in vc]
         ctx = S.Context(rank)
-        step = V.VerifyStep(ctx, cfg, dev_w, kcr, vcr, len(ids), n_past, tp=V.TensorParallel(rank, world))
+        step = V.VerifyStep(ctx, cfg, dev_w, kcr, vcr, len(ids), n_past,
+                            tp=V.TensorParallel(rank, world, fused=fused))
         step.set_tokens(ids, draft)
         step.run()
         torch.cuda.synchronize()
@@ -211,15 +212,18 @@ def _tp_worker(rank, world, port, cfg_kw, seed, cap, n_past, ids, draft, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tensor_parallel_step_matches_one_gpu(ctx):
-    """Megatron TP over 2 GPUs (column-parallel QKV / gate|up / head, row-parallel O / down with NCCL all-reduces,
-    vocabulary-sharded acceptance) against the same step on one GPU: logits within 2e-2 (the partial sums change
-    f32 rounding, re-quantization flips follow, as in the oracle comparison), accepted ids equal where the top-1
-    margin is clear."""
+@pytest.mark.parametrize("Hkv,fused", [(2, True), (2, False), (1, True)])
+def test_tensor_parallel_step_matches_one_gpu(ctx, Hkv, fused):
+    """Megatron TP over 2 GPUs (column-parallel QKV / gate|up / head, row-parallel O / down, vocabulary-sharded
+    acceptance) against the same step on one GPU. The all-reduces run either inside the next RMSNorm over peer memory
+    (fused) or as NCCL calls; Hkv = 1 replicates the KV head on both ranks. Logits within 2e-2 (the partial sums
+    change f32 rounding, re-quantization flips follow, as in the oracle comparison), accepted ids equal where the
+    top-1 margin is clear."""
     import socket
     import torch.multiprocessing as mp
-    cfg = V.DecoderConfig(n_layer=3, d=512, n_ff=768, H=4, Hkv=2, hd=256, n_vocab=1000, base=1e6, eps=1e-6,
-                          window=40, full_every=2, kv_type=L.F16)
+    cfg_kw = dict(n_layer=3, d=512, n_ff=768, H=4, Hkv=Hkv, hd=256, n_vocab=1000, base=1e6, eps=1e-6, window=40,
+                  full_every=2, kv_type=L.F16)
+    cfg = V.DecoderConfig(**cfg_kw)
     seed, cap, n_past, ids = 21, 128, 100, [3, 17, 250, 999, 42]
     w = V.host_weights(cfg, seed=seed)
     kc, vc = _caches(cfg, cap, n_past, 512, seed + 1)
@@ -236,9 +240,7 @@ def test_tensor_parallel_step_matches_one_gpu(ctx):
     s.close()
     mpc = mp.get_context("spawn")
     q = mpc.SimpleQueue()
-    cfg_kw = dict(n_layer=3, d=512, n_ff=768, H=4, Hkv=2, hd=256, n_vocab=1000, base=1e6, eps=1e-6, window=40,
-                  full_every=2, kv_type=L.F16)
-    procs = [mpc.Process(target=_tp_worker, args=(r, 2, port, cfg_kw, seed, cap, n_past, ids, draft, q))
+    procs = [mpc.Process(target=_tp_worker, args=(r, 2, port, cfg_kw, seed, cap, n_past, ids, draft, q, fused))
              for r in range(2)]
     for p in procs:
         p.start()
@@ -260,3 +262,34 @@ def test_tensor_parallel_step_matches_one_gpu(ctx):
     exp = one.accepted()
     k = len(ids) if (margin > 1e-2).all() else int(np.argmin(margin > 1e-2))
     assert got[2][:k] == exp[:k]
+
+
+def test_allreduce_norm_peer_wait_times_out(ctx):
+    """The fused all-reduce's flag wait is bounded: a second 'rank' whose flag nothing ever sets (a plain local
+    buffer standing in for the peer) ends the wait after ~2 s with an error status read on the host, and the context
+    stays usable. No GPU fault and no hang: the kernel gives up and finishes."""
+    import time
+    lib = L.load()
+    d, n = 512, 2
+    nbytes = int(lib.srhpm_allreduce_buffer_size(d))
+    mine = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    fake = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    peers = torch.tensor([mine.data_ptr(), fake.data_ptr()], dtype=torch.int64, device="cuda")
+    epochs = torch.zeros(32, dtype=torch.int32, device="cuda")
+    x = torch.randn((n, d), device="cuda")
+    w = torch.ones(d, device="cuda")
+    y = torch.empty_like(x)
+    ptr = lambda t: t.data_ptr()
+    t0 = time.time()
+    L.check(lib.srhpm_add_rms_norm_allreduce(ctx.handle, ptr(x), ptr(peers), 2, 0, 0, ptr(epochs), ptr(w), 1e-6,
+                                             ptr(y), n, d, None), "srhpm_add_rms_norm_allreduce")
+    torch.cuda.synchronize()
+    assert time.time() - t0 > 1.5
+    with pytest.raises(L.SrhpmError):
+        ctx.check()
+    ctx.check()  # cleared: the context keeps working
+    # this rank published its epoch into both buffers' flags (slot 0, rows 0..n-1, rank 0)
+    off = 2 * 16 * d * 4
+    for buf in (mine, fake):
+        flags = buf[off:].view(torch.int32).view(2, 16, 8)
+        assert flags[0, :n, 0].tolist() == [1] * n
