@@ -183,6 +183,18 @@ int srhpm_accept_merge(srhpm_ctx * ctx, const srhpm_argmax_record * recs, int n_
 int srhpm_get_rows(srhpm_ctx * ctx, const srhpm_tensor * table, const int32_t * ids, int n, float * out, void * stream);
 int srhpm_add_rms_norm(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y, int n,
                        int64_t d, void * stream);
+/* Residual add + RMSNorm fused with the activation quantization of the GEMM that consumes y (the SURVEY's fused
+ * prologue): x += delta (delta may be NULL), y = x / sqrt(mean(x^2) + eps) * w as srhpm_add_rms_norm, and the
+ * activation records of y for the product with W_next (its type, rows and K = d: ne = [d, rows]) are written into
+ * wdata (sized by srhpm_mul_mat_work_size(W_next, X[d, n])), bit-identical to what srhpm_mul_mat's own quantizer
+ * would write; srhpm_mul_mat_prequantized(W_next, X, Y, same wdata) then runs the product on them (X's data is not
+ * read, only its shape). K-quant and IQ4_XS weights (Q8_0: SRHPM_UNSUPPORTED, use srhpm_mul_mat). n <= 16,
+ * d <= 16384; x, delta, w, y 16-byte aligned. */
+int srhpm_add_rms_norm_quant(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y,
+                             int n, const srhpm_tensor * W_next, void * wdata, size_t wsize, void * stream);
+int srhpm_mul_mat_prequantized(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, srhpm_tensor * Y,
+                               void * wdata, size_t wsize, void * stream);
+
 /* Tensor-parallel residual add + RMSNorm with the all-reduce inside (row-parallel GEMM -> next norm):
  * every rank's row-parallel GEMM (attention output, FFN down) writes its partial sum [n][d] f32 into slot `slot`
  * (0 or 1) of its own symmetric buffer of srhpm_allreduce_buffer_size(d) bytes, zeroed once before first use and

@@ -275,6 +275,31 @@ int srhpm_mul_mat(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * 
                     nullptr, nullptr, (cudaStream_t) stream);
 }
 
+int srhpm_add_rms_norm_quant(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y,
+                             int n, const srhpm_tensor * W_next, void * wdata, size_t wsize, void * stream) {
+    if (!ctx || !x || !w || !y || !W_next || n < 1 || n > 16) return SRHPM_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y) |
+         reinterpret_cast<uintptr_t>(delta)) & 15) {
+        return SRHPM_ERR_ALIGN;
+    }
+    const int64_t K = W_next->ne[0];
+    if (W_next->type != SRHPM_TYPE_Q4_K && W_next->type != SRHPM_TYPE_Q5_K && W_next->type != SRHPM_TYPE_Q6_K &&
+        W_next->type != SRHPM_TYPE_Q3_K && W_next->type != SRHPM_TYPE_IQ4_XS) {
+        return SRHPM_UNSUPPORTED;
+    }
+    return norm_quant_run(ctx, W_next->type, W_next->ne[1], K, n, x, delta, w, eps, y, wdata, wsize,
+                          (cudaStream_t) stream);
+}
+
+int srhpm_mul_mat_prequantized(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, srhpm_tensor * Y,
+                               void * wdata, size_t wsize, void * stream) {
+    if (!ctx || !Y) return SRHPM_ERR_INVALID;
+    const int st = check_mul_mat(W, X, Y);
+    if (st != SRHPM_OK) return st;
+    return gemm_run_prequant(ctx, W->type, (const uint8_t *) W->data, W->ne[1], W->ne[0], W->nb[1], X->ne[1],
+                             (float *) Y->data, (int64_t) (Y->nb[1] / 4), wdata, wsize, (cudaStream_t) stream);
+}
+
 int srhpm_mul_mat_static(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, srhpm_tensor * Y,
                          void * stream) {
     if (!ctx || !Y) return SRHPM_ERR_INVALID;

@@ -37,6 +37,10 @@ int    gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int
                 const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
                 int32_t * isum, int32_t * imin, cudaStream_t stream);
 size_t gemm_work_size_unsplit(int wtype, int64_t rows, int64_t K, int64_t N);
+int    gemm_run_prequant(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
+                         int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize, cudaStream_t stream);
+int    norm_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_t N, float * x, const float * delta,
+                      const float * w, float eps, float * y, void * wdata, size_t wsize, cudaStream_t stream);
 int    gemm_run_unsplit(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                         const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
                         cudaStream_t stream);

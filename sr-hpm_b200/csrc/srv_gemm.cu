@@ -26,6 +26,7 @@
 #include <cstring>
 
 #include "internal.h"
+#include "launch.cuh"
 #include "ptx.cuh"
 
 namespace srhpm {
@@ -72,6 +73,63 @@ __device__ __forceinline__ uint2 pack8(const int (&q)[8]) {
 
 // srv_quantize_row: amax = max |x| over 256; the first element of that magnitude (with its sign) gives
 // iscale = -127 / max; q = min(round_half_even(iscale * x), 127); d = 1 / iscale. IEEE division, no contraction.
+// One warp per (super-block, token); lane l holds columns 8l..8l+7 in v.
+__device__ __forceinline__ void q8K_quantize_warp(const float (&v)[8], int lane, int (&qv)[8], float & dv) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) amax = fmaxf(amax, fabsf(v[j]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    dv = 0.0f;
+    if (amax == 0.0f) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) qv[j] = 0;
+    } else {
+        int first = QK, jf = 0;
+#pragma unroll
+        for (int j = 7; j >= 0; j--) {
+            if (fabsf(v[j]) == amax) {
+                first = 8 * lane + j;
+                jf    = j;
+            }
+        }
+        float mine = v[0];
+#pragma unroll
+        for (int j = 1; j < 8; j++) mine = (j == jf) ? v[j] : mine;
+        const int   fmin   = __reduce_min_sync(0xffffffffu, first);
+        const float mx     = __shfl_sync(0xffffffffu, mine, fmin >> 3);
+        const float iscale = __fdiv_rn(-127.0f, mx);
+#pragma unroll
+        for (int j = 0; j < 8; j++) qv[j] = min(__float2int_rn(__fmul_rn(iscale, v[j])), 127);
+        dv = __fdiv_rn(1.0f, iscale);
+    }
+}
+
+// the token row t of one super-block's activation record: the lane's 8 codes (perm, Q3_K: stored in the order
+// 0 4 1 5 2 6 3 7, the k order of its decoder), the scale, the per-32 sums split into int8 halves s = 128 hi + lo
+// (lo in 0..127) in the row's padding (hi at 256 + sub-block, lo at 264 + sub-block: the Q4_K / Q5_K minimum term),
+// and the sum over all 256 after the scales (the Q3_K offset term)
+__device__ __forceinline__ void q8K_store_record(const int (&qv)[8], float dv, uint8_t * rec, int t, int NT, int lane,
+                                                 int perm) {
+    const uint2 pk = pack8(qv);
+    const uint2 st = perm ? make_uint2(__byte_perm(pk.x, pk.y, 0x5140), __byte_perm(pk.x, pk.y, 0x7362)) : pk;
+    *reinterpret_cast<uint2 *>(rec + t * kTokStride + 8 * lane) = st;
+    if (lane == 0) reinterpret_cast<float *>(rec + NT * kTokStride)[t] = dv;
+    int s32 = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) s32 += qv[j];
+    s32 += __shfl_xor_sync(0xffffffffu, s32, 1);
+    s32 += __shfl_xor_sync(0xffffffffu, s32, 2);
+    if ((lane & 3) == 0) {
+        rec[t * kTokStride + 256 + lane / 4] = (uint8_t) (int8_t) (s32 >> 7);
+        rec[t * kTokStride + 264 + lane / 4] = (uint8_t) (s32 & 127);
+    }
+    int s256 = s32 + __shfl_xor_sync(0xffffffffu, s32, 4);
+    s256 += __shfl_xor_sync(0xffffffffu, s256, 8);
+    s256 += __shfl_xor_sync(0xffffffffu, s256, 16);
+    if (lane == 0) reinterpret_cast<int32_t *>(rec + NT * kTokStride + 4 * NT)[t] = s256;
+}
+
 template <bool DENSE>
 __global__ void __launch_bounds__(256) quant_q8K_kernel(const float * __restrict__ X, int64_t ldx, int N, int nsb,
                                                          int NT, uint8_t * __restrict__ recs, int8_t * __restrict__ q,
@@ -97,38 +155,12 @@ __global__ void __launch_bounds__(256) quant_q8K_kernel(const float * __restrict
 #pragma unroll
         for (int j = 0; j < 8; j++) v[j] = 0.0f;
     }
-    float amax = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) amax = fmaxf(amax, fabsf(v[j]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     int   qv[8];
-    float dv = 0.0f;
-    if (amax == 0.0f) {
-#pragma unroll
-        for (int j = 0; j < 8; j++) qv[j] = 0;
-    } else {
-        int first = QK, jf = 0;
-#pragma unroll
-        for (int j = 7; j >= 0; j--) {
-            if (fabsf(v[j]) == amax) {
-                first = 8 * lane + j;
-                jf    = j;
-            }
-        }
-        float mine = v[0];
-#pragma unroll
-        for (int j = 1; j < 8; j++) mine = (j == jf) ? v[j] : mine;
-        const int   fmin   = __reduce_min_sync(0xffffffffu, first);
-        const float mx     = __shfl_sync(0xffffffffu, mine, fmin >> 3);
-        const float iscale = __fdiv_rn(-127.0f, mx);
-#pragma unroll
-        for (int j = 0; j < 8; j++) qv[j] = min(__float2int_rn(__fmul_rn(iscale, v[j])), 127);
-        dv = __fdiv_rn(1.0f, iscale);
-    }
-    const uint2 pk = pack8(qv);
+    float dv;
+    q8K_quantize_warp(v, lane, qv, dv);
     if constexpr (DENSE) {
-        const int64_t K = (int64_t) nsb * QK;
+        const uint2   pk = pack8(qv);
+        const int64_t K  = (int64_t) nsb * QK;
         *reinterpret_cast<uint2 *>(q + (int64_t) t * K + (int64_t) sb * QK + 8 * lane) = pk;
         if (lane == 0) d[(int64_t) t * nsb + sb] = dv;
         int s = 0;
@@ -139,27 +171,87 @@ __global__ void __launch_bounds__(256) quant_q8K_kernel(const float * __restrict
         if (b16 && (lane & 1) == 0) b16[(int64_t) t * (K / 16) + (int64_t) sb * 16 + lane / 2] = (int16_t) s16;
         if (b32 && (lane & 3) == 0) b32[(int64_t) t * (K / 32) + (int64_t) sb * 8 + lane / 4] = (int16_t) s32;
     } else {
-        uint8_t * rec = recs + (size_t) sb * rec_bytes(false, NT);
-        // perm (Q3_K): each lane's 8 columns stored in the order 0 4 1 5 2 6 3 7, the k order of its decoder
-        const uint2 st = perm ? make_uint2(__byte_perm(pk.x, pk.y, 0x5140), __byte_perm(pk.x, pk.y, 0x7362)) : pk;
-        *reinterpret_cast<uint2 *>(rec + t * kTokStride + 8 * lane) = st;
-        if (lane == 0) reinterpret_cast<float *>(rec + NT * kTokStride)[t] = dv;
-        // per-32 sums of the quantized row, split into int8 halves s = 128 * hi + lo (lo in 0..127), in the token
-        // row's padding: hi at 256 + sub-block, lo at 264 + sub-block (the Q4_K / Q5_K minimum term); the sum over
-        // all 256 after the scales (the Q3_K offset term)
-        int s32 = 0;
+        q8K_store_record(qv, dv, recs + (size_t) sb * rec_bytes(false, NT), t, NT, lane, perm);
+    }
+}
+
+// residual add + RMSNorm fused with the activation quantizer of the GEMM that consumes y (the SURVEY's fused
+// prologue): CTA t < N: x += delta; y = x / sqrt(mean(x^2) + eps) * w (as add_rms_norm); the row of y is staged in
+// shared memory and each warp quantizes super-blocks of it into the GEMM's activation records exactly as
+// quant_q8K_kernel does (same functions); CTAs N..NT-1 write the zero padding rows; CTA 0 zeroes the split-K counters.
+constexpr int kNormQThreads = 1024;
+__global__ void __launch_bounds__(kNormQThreads) add_rms_norm_q8K_kernel(float * x, const float * delta,
+                                                                          const float * w, float eps, float * y,
+                                                                          int N, int64_t d, int NT, uint8_t * recs,
+                                                                          int perm, int32_t * cnt, int ncnt) {
+    pdl_launch_dependents();
+    pdl_wait();
+    extern __shared__ float ys[];
+    const int     t  = blockIdx.x;
+    const int64_t d4 = d >> 2;
+    if (blockIdx.x == 0) {
+        for (int i = threadIdx.x; i < ncnt; i += blockDim.x) cnt[i] = 0;
+    }
+    if (t < N) {
+        float *  xr = x + (int64_t) t * d;
+        float    ss = 0.0f;
+        float4   v[4];
 #pragma unroll
-        for (int j = 0; j < 8; j++) s32 += qv[j];
-        s32 += __shfl_xor_sync(0xffffffffu, s32, 1);
-        s32 += __shfl_xor_sync(0xffffffffu, s32, 2);
-        if ((lane & 3) == 0) {
-            rec[t * kTokStride + 256 + lane / 4] = (uint8_t) (int8_t) (s32 >> 7);
-            rec[t * kTokStride + 264 + lane / 4] = (uint8_t) (s32 & 127);
+        for (int k = 0; k < 4; k++) {
+            const int64_t j = threadIdx.x + (int64_t) k * kNormQThreads;
+            if (j < d4) {
+                float4 a = reinterpret_cast<const float4 *>(xr)[j];
+                if (delta) {
+                    const float4 b = reinterpret_cast<const float4 *>(delta + (int64_t) t * d)[j];
+                    a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
+                    reinterpret_cast<float4 *>(xr)[j] = a;
+                }
+                v[k] = a;
+                ss = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, ss))));
+            }
         }
-        int s256 = s32 + __shfl_xor_sync(0xffffffffu, s32, 4);
-        s256 += __shfl_xor_sync(0xffffffffu, s256, 8);
-        s256 += __shfl_xor_sync(0xffffffffu, s256, 16);
-        if (lane == 0) reinterpret_cast<int32_t *>(rec + NT * kTokStride + 4 * NT)[t] = s256;
+        __shared__ float part[32];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            ss = part[threadIdx.x];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+            if (threadIdx.x == 0) part[0] = ss;
+        }
+        __syncthreads();
+        const float scale = 1.0f / sqrtf(part[0] / (float) d + eps);
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int64_t j = threadIdx.x + (int64_t) k * kNormQThreads;
+            if (j < d4) {
+                const float4 ww = reinterpret_cast<const float4 *>(w)[j];
+                float4       o;
+                o.x = v[k].x * scale * ww.x;
+                o.y = v[k].y * scale * ww.y;
+                o.z = v[k].z * scale * ww.z;
+                o.w = v[k].w * scale * ww.w;
+                reinterpret_cast<float4 *>(y + (int64_t) t * d)[j] = o;
+                reinterpret_cast<float4 *>(ys)[j] = o;
+            }
+        }
+    } else {
+        for (int64_t j = threadIdx.x; j < d4; j += kNormQThreads) reinterpret_cast<float4 *>(ys)[j] = make_float4(0, 0, 0, 0);
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nsb  = (int) (d / QK);
+    for (int sb = warp; sb < nsb; sb += kNormQThreads / 32) {
+        float v8[8];
+        const float4 a = reinterpret_cast<const float4 *>(ys + (int64_t) sb * QK + 8 * lane)[0];
+        const float4 b = reinterpret_cast<const float4 *>(ys + (int64_t) sb * QK + 8 * lane)[1];
+        v8[0] = a.x; v8[1] = a.y; v8[2] = a.z; v8[3] = a.w; v8[4] = b.x; v8[5] = b.y; v8[6] = b.z; v8[7] = b.w;
+        int   qv[8];
+        float dv;
+        q8K_quantize_warp(v8, lane, qv, dv);
+        q8K_store_record(qv, dv, recs + (size_t) sb * rec_bytes(false, NT), t, NT, lane, perm);
     }
 }
 
@@ -1311,7 +1403,7 @@ namespace {
 
 int gemm_run_impl(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                   const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
-                  int32_t * isum, int32_t * imin, bool split, cudaStream_t stream) {
+                  int32_t * isum, int32_t * imin, bool split, cudaStream_t stream, bool prequant = false) {
     const WorkLayout wl = split ? work_layout(wtype, rows, K, N) : work_layout_unsplit(wtype, rows, K, N);
     if (wsize < wl.total || !wdata) return SRHPM_ERR_WORKSPACE;
     const int  nsb  = (int) (K / QK);
@@ -1321,8 +1413,8 @@ int gemm_run_impl(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, i
     uint8_t *  recs = base + wl.recs;
     int32_t *  cnt  = reinterpret_cast<int32_t *>(base + wl.cnt);
     const int  nrb  = (int) ((rows + kTileRows - 1) / kTileRows);
-    // 1. activation records (and zeroed split-K counters)
-    {
+    // 1. activation records (and zeroed split-K counters); prequant: written by the preceding fused norm
+    if (!prequant) {
         const int64_t warps  = (int64_t) nsb * NT;
         const int     blocks = (int) ((warps + 7) / 8);
         cudaLaunchConfig_t cfg = {};
@@ -1377,6 +1469,39 @@ int gemm_run_impl(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, i
 }
 
 }  // namespace
+
+int gemm_run_prequant(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
+                      int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize, cudaStream_t stream) {
+    if (wtype == SRHPM_TYPE_Q8_0) return SRHPM_UNSUPPORTED;
+    return gemm_run_impl(ctx, wtype, W, rows, K, row_bytes, nullptr, K, N, Y, ldy, wdata, wsize, nullptr, nullptr,
+                         true, stream, true);
+}
+
+int norm_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_t N, float * x, const float * delta,
+                   const float * w, float eps, float * y, void * wdata, size_t wsize, cudaStream_t stream) {
+    if (wtype == SRHPM_TYPE_Q8_0) return SRHPM_UNSUPPORTED;
+    if (K % QK != 0 || K > 4 * 4 * kNormQThreads || N < 1 || N > 16) return SRHPM_ERR_INVALID;
+    const WorkLayout wl = work_layout(wtype, rows, K, N);
+    if (wsize < wl.total || !wdata) return SRHPM_ERR_WORKSPACE;
+    uint8_t * base = align256(wdata);
+    const int NT   = N <= 8 ? 8 : 16;
+    const int nrb  = (int) ((rows + kTileRows - 1) / kTileRows);
+    static std::atomic<unsigned> attr_done{ 0 };
+    int                          dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_done.load() & (1u << (dev & 31)))) {
+        const int st = cuda_status(cudaFuncSetAttribute(add_rms_norm_q8K_kernel,
+                                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024));
+        if (st != SRHPM_OK) return st;
+        attr_done.fetch_or(1u << (dev & 31));
+    }
+    const cudaError_t e = launch_k_pdl(add_rms_norm_q8K_kernel, dim3(NT), dim3(kNormQThreads), (size_t) K * 4, stream,
+                                       x, delta, w, eps, y, (int) N, K, NT, base + wl.recs,
+                                       (int) (wtype == SRHPM_TYPE_Q3_K), reinterpret_cast<int32_t *>(base + wl.cnt),
+                                       nrb);
+    ctx->launches.fetch_add(1);
+    return cuda_status(e);
+}
 
 int gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
              const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,

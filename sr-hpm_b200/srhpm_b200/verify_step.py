@@ -213,8 +213,9 @@ class VerifyStep:
     is this rank's: its query heads, its KV heads (caches hold only those), its FFN rows and its vocabulary rows; the
     residual stream, norms and embeddings are replicated."""
 
-    def __init__(self, ctx, cfg, weights, kcache, vcache, n_tokens, n_past, relax=0.0, tp=None):
+    def __init__(self, ctx, cfg, weights, kcache, vcache, n_tokens, n_past, relax=0.0, tp=None, fuse_prologue=True):
         self.ctx, self.cfg, self.w = ctx, cfg, weights
+        self.fuse_prologue = fuse_prologue  # RMSNorm writes the next GEMM's activation records itself
         self.kcache, self.vcache = kcache, vcache
         self.n, self.n_past, self.relax = n_tokens, n_past, relax
         self.tp = tp if tp is not None and tp.world > 1 else None
@@ -274,6 +275,25 @@ class VerifyStep:
         """Output of a row-parallel GEMM: the rank's partial sums (fused: slot `slot` of the symmetric buffer)."""
         return self.tp.part[slot][:self.n] if self._fused() else self.o
 
+    def _norm_mm(self, delta_slot, wnorm, W, Y):
+        """Residual add + RMSNorm of the pending delta, then the GEMM of W on the normed rows into Y: one fused
+        norm + activation-quantization launch and the GEMM on its records (srhpm_add_rms_norm_quant +
+        srhpm_mul_mat_prequantized), or the separate norm and srhpm_mul_mat (its own quantizer) where that does not
+        apply (tensor-parallel fused all-reduce norms, Q8_0 weights)."""
+        if not self.fuse_prologue or W.qtype == L.Q8_0 or (delta_slot is not None and self._fused()):
+            return [self._norm(delta_slot, wnorm), self._mm(W, self.y, Y)]
+        c, n, lib, h = self.cfg, self.n, self.lib, self.ctx.handle
+        st, ws = self.ctx.mul_mat_work_size(W, self.y)
+        L.check(st, "srhpm_mul_mat_work_size")
+        self._ws = max(self._ws, ws)
+        wv, xv, yv = W.view(), f32_rows_view(self.y), f32_rows_view(Y)
+        self._keep += [wv, xv, yv]
+        return [("add_rms_norm_quant", lib.srhpm_add_rms_norm_quant,
+                 [h, self._ptr(self.x), None if delta_slot is None else self._ptr(self.o), self._ptr(wnorm),
+                  ctypes.c_float(c.eps), self._ptr(self.y), n, ctypes.byref(wv)], True),
+                ("mul_mat_prequantized", lib.srhpm_mul_mat_prequantized,
+                 [h, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv)], True)]
+
     def _norm(self, delta_slot, wnorm):
         """Residual add of the pending delta (none for the first block) + RMSNorm into y."""
         c, n, lib, h = self.cfg, self.n, self.lib, self.ctx.handle
@@ -309,10 +329,10 @@ class VerifyStep:
         L_all = self.n_past + n
         masks = {}
         for li, lay in enumerate(self.w.layers):
-            calls.append(self._norm(None if li == 0 else 1, lay["attn_norm"]))
             if "qkv" in lay:
-                calls.append(self._mm(lay["qkv"], self.y, self.qkv))
+                calls += self._norm_mm(None if li == 0 else 1, lay["attn_norm"], lay["qkv"], self.qkv)
             else:  # Q, K, V of different types: three GEMMs into the column ranges of the qkv rows
+                calls.append(self._norm(None if li == 0 else 1, lay["attn_norm"]))
                 calls.append(self._mm(lay["q"], self.y, self.qkv[:, :H * hd]))
                 calls.append(self._mm(lay["k"], self.y, self.qkv[:, H * hd:(H + Hkv) * hd]))
                 calls.append(self._mm(lay["v"], self.y, self.qkv[:, (H + Hkv) * hd:]))
@@ -348,10 +368,10 @@ class VerifyStep:
             calls.append(self._mm(lay["o"], self.att, self._rowpar_out(0)))
             if self.tp is not None and not self._fused():
                 calls.append(self._all_reduce(self.o))  # row-parallel O: partial sums over the rank's heads
-            calls.append(self._norm(0, lay["ffn_norm"]))
             if "gate_up" in lay:
-                calls.append(self._mm(lay["gate_up"], self.y, self.gu))
+                calls += self._norm_mm(0, lay["ffn_norm"], lay["gate_up"], self.gu)
             else:
+                calls.append(self._norm(0, lay["ffn_norm"]))
                 calls.append(self._mm(lay["gate"], self.y, self.gu[:, :self.n_ff]))
                 calls.append(self._mm(lay["up"], self.y, self.gu[:, self.n_ff:]))
             up_ptr = ctypes.c_void_p(self.gu.data_ptr() + 4 * self.n_ff)
@@ -362,8 +382,7 @@ class VerifyStep:
             calls.append(self._mm(lay["down"], self.h, self._rowpar_out(1)))
             if self.tp is not None and not self._fused():
                 calls.append(self._all_reduce(self.o))
-        calls.append(self._norm(1, self.w.out_norm))
-        calls.append(self._mm(self.w.head, self.y, self.logits))
+        calls += self._norm_mm(1, self.w.out_norm, self.w.head, self.logits)
         lv = f32_rows_view(self.logits)
         self._keep.append(lv)
         sz = ctypes.c_size_t()

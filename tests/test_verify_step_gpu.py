@@ -293,3 +293,30 @@ def test_allreduce_norm_peer_wait_times_out(ctx):
     for buf in (mine, fake):
         flags = buf[off:].view(torch.int32).view(2, 16, 8)
         assert flags[0, :n, 0].tolist() == [1] * n
+
+
+def test_fused_norm_quant_prologue_is_exact(ctx):
+    """RMSNorm fused with the next GEMM's activation quantization writes the same records as the GEMM's own
+    quantizer: the whole step's logits, caches and accepted ids are identical with and without the fusion."""
+    cfg = small_cfg(L.F16)
+    w = V.host_weights(cfg, seed=31)
+    cap, n_past, ids, draft = 128, 70, [4, 8, 15, 16, 23, 42], [8, 15, 16, 23, 42]
+    kc, vc = _caches(cfg, cap, n_past, 512, 32)
+    dev_w = V.DeviceWeights.from_host(cfg, w)
+    outs = []
+    for fuse in (False, True):
+        kcd = [torch.from_numpy(a).cuda() for a in kc]
+        vcd = [torch.from_numpy(a).cuda() for a in vc]
+        step = V.VerifyStep(ctx, cfg, dev_w, kcd, vcd, len(ids), n_past, fuse_prologue=fuse)
+        step.set_tokens(ids, draft)
+        ctx.launch_count(reset=True)
+        step.run()
+        torch.cuda.synchronize()
+        launches = ctx.launch_count(reset=True)
+        ctx.check()
+        outs.append((step.logits.clone(), [a.clone() for a in kcd], step.accepted(), launches))
+    assert torch.equal(outs[0][0], outs[1][0])
+    assert all(torch.equal(a, b) for a, b in zip(outs[0][1], outs[1][1]))
+    assert outs[0][2] == outs[1][2]
+    # kernel launches: the quantizers of the QKV, gate|up and head GEMMs are gone (2 per layer + 1)
+    assert outs[0][3] - outs[1][3] == 2 * cfg.n_layer + 1
