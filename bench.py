@@ -443,8 +443,11 @@ def run_gpu(args):
     ctx.check()
 
     step_tp = None
-    if world > 1 and not args.no_step:  # every rank takes part (NCCL all-reduces inside the step)
-        step_tp = measure_step_27b_tp(ctx, dev, rank, world)
+    if world > 1 and not args.no_step:  # every rank takes part (collectives inside the step)
+        try:
+            step_tp = measure_step_27b_tp(ctx, dev, rank, world)
+        except Exception as e:  # recorded beside the sweep rather than losing its line
+            step_tp = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
     if rank == 0:
         cfg = workload_config(base_ops, world)
         cfg["timed"] = "CUDA graph of one step, replayed" if graph is not None else "eager calls"
