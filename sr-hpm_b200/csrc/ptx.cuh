@@ -12,7 +12,7 @@ namespace srhpm {
 constexpr uint32_t kWaitLimit = 1u << 22;
 
 // error words written to the context's device status slot
-enum : int32_t { kErrNone = 0, kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3, kErrPeerWait = 4 };
+enum : int32_t { kErrNone = 0, kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3, kErrPeerWait = 4, kErrClusterWait = 5 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void * p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -76,6 +76,40 @@ __device__ __forceinline__ void tma_load_2d(void * dst, const void * tmap, int x
 
 __device__ __forceinline__ void prefetch_tmap(const void * tmap) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// ---- thread-block clusters: distributed shared memory and remote mbarrier arrivals
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t cluster_addr) {
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+    return v;
+}
+// bounded wait on a local mbarrier whose arrivals come from other CTAs of the cluster (acquire at cluster scope)
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t * bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kWaitLimit; i++) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(smem_u32(bar)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
 }
 
 // barrier among `count` threads (a multiple of 32) on hardware barrier `id` (id 0 is __syncthreads)

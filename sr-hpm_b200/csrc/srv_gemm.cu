@@ -21,6 +21,9 @@
 // (one 8-byte load per row and nibble plane), the others the natural fragment order.
 #include <algorithm>
 #include <atomic>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include <cuda.h>
 #include <cstring>
@@ -39,7 +42,7 @@ constexpr int     kTileRows  = 16 * kNCW;         // weight rows per CTA tile
 constexpr int     kTokStride = 288;               // bytes per token row inside an activation record
 constexpr int     kMaxStages = 6;
 constexpr int     kMaxSplit  = 8;                 // K ranges per product at most
-constexpr int     kBarBytes  = 128;               // room for the 2 * kMaxStages mbarriers
+constexpr int     kBarBytes  = 128;               // room for the 2 * kMaxStages + 2 mbarriers
 
 __host__ __device__ constexpr int rec_nscales(bool q80, int NT) { return q80 ? 8 * NT : NT; }
 // [NT token rows of kTokStride bytes][f32 scales][K-quant records: NT int32 sums of each token's 256 codes]
@@ -923,6 +926,8 @@ struct GemmArgs {
     int             LSR;         // leftover slot stride
     int             rec_off;     // activation records inside a stage
     int             scr_off;     // per-warp scale-record scratch (after the stages)
+    int             red_off;     // cluster split K: this CTA's partial sums [NT][64] f32 (after the scratch)
+    int             cluster;     // the K ranges of a row block form a thread-block cluster (split-K in DSMEM)
     const uint8_t * recs;
     float *         part;        // split-K partial sums [ksplit][N][rows]
     int32_t *       cnt;         // split-K arrival counters, one per row block (zeroed by the quantizer kernel)
@@ -1063,20 +1068,28 @@ template <class D, int NG, bool DBG>
 __global__ void __launch_bounds__(kThreads, D::MINB) srv_gemm_kernel(const __grid_constant__ CUtensorMap wmap,
                                                             const GemmArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    uint64_t * full   = reinterpret_cast<uint64_t *>(smem);
-    uint64_t * empty  = full + kMaxStages;
-    uint8_t *  stage0 = smem + kBarBytes;
+    uint64_t * full       = reinterpret_cast<uint64_t *>(smem);
+    uint64_t * empty      = full + kMaxStages;
+    uint64_t * part_ready = full + 2 * kMaxStages;  // cluster split K, K range 0: the other ranges' partials are in
+    uint64_t * part_free  = part_ready + 1;         // cluster split K, K range > 0: range 0 has read this CTA's partials
+    uint8_t *  stage0     = smem + kBarBytes;
     const int  warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.S; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kNCW * 32);
         }
+        if (a.cluster) {
+            mbar_init(part_ready, a.ksplit - 1);
+            mbar_init(part_free, 1);
+        }
         fence_mbar_init();
     }
     __syncthreads();
+    if (a.cluster) cluster_sync_all();  // every CTA's barriers exist before any remote arrival
     if (warp == kNCW) {
         producer<D, NG>(a, &wmap, full, empty, stage0, lane);
+        if (a.cluster) cluster_sync_all();  // no CTA exits while a peer may still use its shared memory
         return;
     }
     pdl_launch_dependents();  // the next call's quantizer may start; it waits for this grid before touching data
@@ -1091,6 +1104,7 @@ __global__ void __launch_bounds__(kThreads, D::MINB) srv_gemm_kernel(const __gri
     uint8_t *      scr = smem + a.scr_off + warp * (D::KC * 16 * D::RECB);  // this warp's scale records
     __shared__ int last_flag;
     int            s = 0, ph = 0;
+    uint32_t       uidx = 0;  // units done (phase parity of the cluster split-K barriers)
     bool           bad = false;  // a wait ran out: skip further waits and work, keep meeting the barriers
     // a row's place in a stage: fixed offset + 16-byte phase (j * row_bytes + sb0 * BS) mod 16, j = row mod G
     const int      bsm = D::BS & 15;
@@ -1172,6 +1186,53 @@ __global__ void __launch_bounds__(kThreads, D::MINB) srv_gemm_kernel(const __gri
                         if (tok < a.N && row < a.rows) a.Y[(int64_t) tok * a.ldy + row] = acc[grp][e];
                     }
                 }
+            } else if (a.cluster) {
+                // split K inside a cluster: every K range keeps its partial sums in its own shared memory; K range 0
+                // (cluster rank 0) waits for the others' arrivals, adds their partials over DSMEM in K order and
+                // writes Y, then releases them
+                float * red = reinterpret_cast<float *>(smem + a.red_off);  // [8 NG tokens][64 rows]
+#pragma unroll
+                for (int grp = 0; grp < NG; grp++) {
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        red[(8 * grp + 2 * t + (e & 1)) * kTileRows + (e < 2 ? rl : rl + 8)] = acc[grp][e];
+                    }
+                }
+                named_bar_sync(1, kNCW * 32);
+                const uint32_t par = uidx & 1;
+                if (kr != 0) {
+                    if (threadIdx.x == 0) {
+                        fence_acq_rel_cluster();
+                        mbar_arrive_cluster(mapa_shared(smem_u32(part_ready), 0));
+                        if (!mbar_wait_cluster(part_free, par)) atomicExch(a.status, kErrClusterWait);
+                    }
+                    named_bar_sync(1, kNCW * 32);  // the partial buffer is free again
+                } else {
+                    if (threadIdx.x == 0 && !mbar_wait_cluster(part_ready, par)) atomicExch(a.status, kErrClusterWait);
+                    named_bar_sync(1, kNCW * 32);
+                    if (!bad) {
+#pragma unroll
+                        for (int grp = 0; grp < NG; grp++) {
+#pragma unroll
+                            for (int e = 0; e < 4; e++) {
+                                const int     tok = 8 * grp + 2 * t + (e & 1);
+                                const int     rlo = e < 2 ? rl : rl + 8;
+                                const int64_t row = row0 + rlo;
+                                if (tok < a.N && row < a.rows) {
+                                    const uint32_t ad = smem_u32(&red[tok * kTileRows + rlo]);
+                                    float          sum = acc[grp][e];
+                                    for (int k = 1; k < a.ksplit; k++) sum += ld_dsmem_f32(mapa_shared(ad, k));
+                                    a.Y[(int64_t) tok * a.ldy + row] = sum;
+                                }
+                            }
+                        }
+                    }
+                    named_bar_sync(1, kNCW * 32);  // every remote read is done
+                    if (threadIdx.x == 0) {
+                        for (int k = 1; k < a.ksplit; k++) mbar_arrive_cluster(mapa_shared(smem_u32(part_free), k));
+                    }
+                }
+                uidx++;
             } else {
                 // split K: partial sums out, then the last K range of this row block reduces them in K order
                 if (!bad) {
@@ -1213,6 +1274,7 @@ __global__ void __launch_bounds__(kThreads, D::MINB) srv_gemm_kernel(const __gri
             }
         }
     }
+    if (a.cluster) cluster_sync_all();
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -1262,6 +1324,7 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     a.rec_off          = (a.left_off + (a.G > 1 ? (a.G - 1) * a.LSR : 0) + 127) / 128 * 128;
     a.stage_bytes      = (a.rec_off + a.kc * RB + 127) / 128 * 128;
     const int scr      = kNCW * D::KC * 16 * D::RECB;
+    const int red      = kTileRows * 8 * NG * (int) sizeof(float);  // cluster split K: the CTA's partial sums
     // the most resident CTAs per SM the decoder is compiled for (D::MINB: 2, or 4 for Q6_K; 228 KB of shared memory per
     // SM, 1 KB of it reserved per CTA, a few bytes of static shared memory), then the most stages (4..2) that still
     // fit them. Measured: 4 CTAs with 2-3 stages streamed slower than 2 CTAs with 3-4 stages for every type but Q6_K.
@@ -1269,7 +1332,7 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     for (int c = D::MINB; c >= 2 && a.S == 0; c--) {
         const int lim = 233472 / c - 1024 - 256;
         for (int st = 4; st >= 2; st--) {
-            if (kBarBytes + st * a.stage_bytes + scr <= lim) {
+            if (kBarBytes + st * a.stage_bytes + scr + red <= lim) {
                 a.S = st;
                 break;
             }
@@ -1277,7 +1340,8 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     }
     if (a.S == 0) a.S = 2;
     a.scr_off         = kBarBytes + a.S * a.stage_bytes;
-    const size_t smem = (size_t) a.scr_off + scr;
+    a.red_off         = a.scr_off + scr;
+    const size_t smem = (size_t) a.red_off + red;
     if (smem > 200 * 1024 || a.Wbox > 1024) return SRHPM_ERR_INVALID;
 
     CUtensorMap wmap;
@@ -1309,42 +1373,82 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
     const int     slots  = std::max(1, per_sm) * ctx->num_sms;
     const int64_t nrb    = (a.rows + kTileRows - 1) / kTileRows;
-    // split K so that the units fill the resident CTA slots: in units of one full-K row block, a product takes about
-    // rounds / ranges (rounds = units over the slots, rounded up) plus a fixed cost per unit (the split-K epilogue:
-    // fence, arrival counter, reduction) of ~15 %; take the cheapest split (the fewest ranges among equals), K ranges
-    // of >= 2 super-blocks. Products with a row block for every slot are not split.
-    a.ksplit = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim           = dim3(kThreads);
+    cfg.dynamicSmemBytes   = smem;
+    cfg.stream             = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id                                         = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.y                           = 1;
+    attr[1].val.clusterDim.z                           = 1;
+    cfg.attrs                                          = attr;
+    // CTA slots usable by clusters of ks CTAs (placed whole inside a GPC, so maybe fewer than single CTAs); cached
+    // per (device, kernel, shared memory, ks)
+    auto cluster_slots = [&](int ks) -> int {
+        static std::mutex                            mu;
+        static std::map<std::tuple<int, size_t, int>, int> cache;
+        const auto                                   key = std::make_tuple(dev, smem, ks);
+        {
+            std::lock_guard<std::mutex> lk(mu);
+            const auto                  it = cache.find(key);
+            if (it != cache.end()) return it->second;
+        }
+        attr[1].val.clusterDim.x = (unsigned) ks;
+        cfg.gridDim              = dim3((unsigned) ks);
+        cfg.numAttrs             = 2;
+        int clusters             = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            clusters = 0;
+        }
+        const int v = std::min(slots, clusters * ks);
+        std::lock_guard<std::mutex> lk(mu);
+        cache[key] = v;
+        return v;
+    };
+    // split K so that the units fill the resident CTA slots in ONE round (measured: two rounds of half-size units
+    // cost far more than one round of full ones). In units of a full-K row block a one-round split of ks ranges takes
+    // about 1 / ks plus its epilogue: ~0.10 when the K ranges of a row block form a cluster and reduce in distributed
+    // shared memory (if cluster occupancy holds all units), ~0.18 through global memory (fence, arrival counter,
+    // reduction). Take the cheapest (the fewest ranges among equals), K ranges of >= 2 super-blocks. Products with a
+    // row block for every slot are not split.
+    a.ksplit  = 1;
+    a.cluster = 0;
+    int usable = slots;
     if (!DBG && a.part && nrb < slots) {
         const int most = std::max(1, std::min(kMaxSplit, a.nsb / 2));
-        double    best = 1e30;
-        for (int ks = 1; ks <= most; ks++) {
-            const int     sbs    = (a.nsb + ks - 1) / ks;
-            const int     eff    = (a.nsb + sbs - 1) / sbs;  // non-empty ranges
-            const int64_t rounds = (nrb * eff + slots - 1) / slots;
-            const double  cost   = (double) rounds / eff + 0.15 * (double) rounds;
+        double    best = 1.0;  // ks = 1: one round of full-K units
+        for (int ks = 2; ks <= most; ks++) {
+            const int     sbs   = (a.nsb + ks - 1) / ks;
+            const int     eff   = (a.nsb + sbs - 1) / sbs;  // non-empty ranges
+            const int64_t units = nrb * eff;
+            int           cl    = -1;
+            if (eff > 1 && units <= cluster_slots(eff)) {
+                cl = 1;
+            } else if (units <= slots) {
+                cl = 0;
+            }
+            if (cl < 0 || eff < 2) continue;
+            const double cost = 1.0 / eff + (cl ? 0.10 : 0.18);
             if (cost < best * 0.999) {
-                best     = cost;
-                a.ksplit = eff;
+                best      = cost;
+                a.ksplit  = eff;
+                a.cluster = cl;
+                usable    = cl ? cluster_slots(eff) : slots;
             }
         }
     }
     a.kr_sbs = (a.nsb + a.ksplit - 1) / a.ksplit;
     a.units  = (int) (nrb * a.ksplit);
+    attr[1].val.clusterDim.x = (unsigned) a.ksplit;
+    cfg.numAttrs             = a.cluster ? 2 : 1;
     // persistent grid: balanced rounds, a multiple of the K ranges
-    const int rounds = (a.units + slots - 1) / slots;
+    const int rounds = (a.units + usable - 1) / usable;
     int       grid   = (a.units + rounds - 1) / rounds;
     grid             = (grid + a.ksplit - 1) / a.ksplit * a.ksplit;
-
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim            = dim3((unsigned) grid);
-    cfg.blockDim           = dim3(kThreads);
-    cfg.dynamicSmemBytes   = smem;
-    cfg.stream             = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs                                          = attr;
-    cfg.numAttrs                                       = 1;
+    cfg.gridDim      = dim3((unsigned) grid);
     ctx->launches.fetch_add(1);
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, wmap, a));
 }
