@@ -10,6 +10,11 @@ namespace srhpm {
 // the phase is incomplete). A wait that runs out sets the kernel's error word and the kernel finishes without
 // hanging.
 constexpr uint32_t kWaitLimit = 1u << 22;
+// The stage waits of the GEMM pipeline pass a suspend-time hint instead: the waiting thread sleeps until the phase
+// completes or kSuspendNs elapse (no spinning that takes issue slots from the other warps); bound kSuspendLimit
+// probes, ~2 s at most.
+constexpr uint32_t kSuspendNs    = 20000;
+constexpr uint32_t kSuspendLimit = 100000;
 
 // error words written to the context's device status slot
 enum : int32_t { kErrNone = 0, kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3, kErrPeerWait = 4, kErrClusterWait = 5 };
@@ -45,6 +50,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t * bar, uint32_t parity) {
         : "r"(smem_u32(bar)), "r"(parity)
         : "memory");
     return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t * bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendNs)
+        : "memory");
+    return ok != 0;
+}
+
+// bounded wait with the suspend hint; false when the limit ran out
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t * bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kSuspendLimit; i++) {
+        if (mbar_try_wait_hint(bar, parity)) {
+            return true;
+        }
+    }
+    return false;
 }
 
 // bounded wait for the phase with the given parity to complete; false when the limit ran out
@@ -247,6 +274,24 @@ __device__ __forceinline__ uint32_t sld4_a2(uint32_t a) {
     } else {
         const uint32_t b = a & ~3u;
         return __funnelshift_r(sld32(b), sld32(b + 4), (a & 3u) * 8);
+    }
+}
+// 32-bit shared load at base + OFF (OFF folded into the instruction)
+template <int OFF>
+__device__ __forceinline__ uint32_t sld32o(uint32_t base) {
+    uint32_t v;
+    asm volatile("ld.shared.b32 %0, [%1+%2];" : "=r"(v) : "r"(base), "n"(OFF));
+    return v;
+}
+// 8 bytes at shared address base + OFF: base 4-byte aligned (A4), or any even address (three aligned words and two
+// funnel shifts by sh = 8 * (address mod 4))
+template <bool A4, int OFF>
+__device__ __forceinline__ uint2 sld8o(uint32_t base, uint32_t sh) {
+    if constexpr (A4) {
+        return make_uint2(sld32o<OFF>(base), sld32o<OFF + 4>(base));
+    } else {
+        const uint32_t w0 = sld32o<OFF>(base), w1 = sld32o<OFF + 4>(base), w2 = sld32o<OFF + 8>(base);
+        return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
     }
 }
 // 8 bytes at a shared address that is 4-byte aligned (A4), or any (three aligned words and two funnel shifts)

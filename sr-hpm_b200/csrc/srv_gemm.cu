@@ -675,15 +675,16 @@ struct DecQ3K {
         y[3] = ((ehi >> 2) & 0x33333333u) | (f13 & 0xCCCCCCCCu);
     }
 
+    // pa, pb: the rows' byte 8t rounded down to 4 bytes (A4: already aligned), sha, shb: 8 * the remainder
     template <bool A4>
-    __device__ __forceinline__ static void load(uint32_t pa, uint32_t pb, uint2 & ha, uint2 & hb, uint2 (&qa)[2],
-                                                uint2 (&qb)[2]) {
-        ha    = sld8_a2<A4>(pa);
-        hb    = sld8_a2<A4>(pb);
-        qa[0] = sld8_a2<A4>(pa + 32);
-        qa[1] = sld8_a2<A4>(pa + 64);
-        qb[0] = sld8_a2<A4>(pb + 32);
-        qb[1] = sld8_a2<A4>(pb + 64);
+    __device__ __forceinline__ static void load(uint32_t pa, uint32_t pb, uint32_t sha, uint32_t shb, uint2 & ha,
+                                                uint2 & hb, uint2 (&qa)[2], uint2 (&qb)[2]) {
+        ha    = sld8o<A4, 0>(pa, sha);
+        hb    = sld8o<A4, 0>(pb, shb);
+        qa[0] = sld8o<A4, 32>(pa, sha);
+        qa[1] = sld8o<A4, 64>(pa, sha);
+        qb[0] = sld8o<A4, 32>(pb, shb);
+        qb[1] = sld8o<A4, 64>(pb, shb);
     }
 
     template <int NG, bool DBG>
@@ -695,12 +696,13 @@ struct DecQ3K {
         const uint32_t pa = smem_u32(wa) + 8 * t, pb = smem_u32(wb) + 8 * t;
         uint2          ha, hb, qa[2], qb[2];
         if (__all_sync(0xffffffffu, ((pa | pb) & 3u) == 0)) {  // warp-uniform: no divergence around the loads
-            load<true>(pa, pb, ha, hb, qa, qb);
+            load<true>(pa, pb, 0, 0, ha, hb, qa, qb);
         } else {
-            load<false>(pa, pb, ha, hb, qa, qb);
+            load<false>(pa & ~3u, pb & ~3u, (pa & 3u) * 8, (pb & 3u) * 8, ha, hb, qa, qb);
         }
-        const uint32_t ta = smem_u32(ra) + 64 * h, tb = smem_u32(rb) + 64 * h;
-        const uint32_t xb = smem_u32(xr) + g * kTokStride + 8 * t;
+        const uint8_t * ta = ra + 64 * h;
+        const uint8_t * tb = rb + 64 * h;
+        const uint8_t * xt = xr + g * kTokStride + 8 * t;
         int            im[2][NG][4];  // one accumulator chain per half n
 #pragma unroll
         for (int n = 0; n < 2; n++) {
@@ -710,27 +712,27 @@ struct DecQ3K {
             selectors(qb[n].x, qb[n].y, hb.x, hb.y, n, yb);
 #pragma unroll
             for (int jp = 0; jp < 2; jp++) {
-                const uint4 TA = sld128(ta + 32 * n + 16 * jp), TB = sld128(tb + 32 * n + 16 * jp);
+                const int4 TA = lds128i(ta + 32 * n + 16 * jp), TB = lds128i(tb + 32 * n + 16 * jp);
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
                     const int      j   = 2 * jp + e;
-                    const uint32_t alo = e ? TA.z : TA.x, ahi = e ? TA.w : TA.y;
-                    const uint32_t blo = e ? TB.z : TB.x, bhi = e ? TB.w : TB.y;
+                    const uint32_t alo = (uint32_t) (e ? TA.z : TA.x), ahi = (uint32_t) (e ? TA.w : TA.y);
+                    const uint32_t blo = (uint32_t) (e ? TB.z : TB.x), bhi = (uint32_t) (e ? TB.w : TB.y);
                     const uint32_t a0 = prmt(alo, ahi, ya[j]), a2 = prmt(alo, ahi, ya[j] >> 16);
                     const uint32_t a1 = prmt(blo, bhi, yb[j]), a3 = prmt(blo, bhi, yb[j] >> 16);
 #pragma unroll
                     for (int grp = 0; grp < NG; grp++) {
-                        const uint2 x = sld64(xb + 8 * grp * kTokStride + 32 * (4 * n + j));
+                        const uint2 x = lds64(xt + 8 * grp * kTokStride + 32 * (4 * n + j));
                         mma_k32<true>(im[n][grp], a0, a1, a2, a3, x.x, x.y);
                     }
                 }
             }
         }
-        const uint32_t xsum = smem_u32(xr) + NT * kTokStride + 4 * NT + 8 * t;  // code sums of tokens 2t, 2t + 1
-        int            is[NG][4];
+        const uint8_t * xsum = xr + NT * kTokStride + 4 * NT + 8 * t;  // code sums of tokens 2t, 2t + 1
+        int             is[NG][4];
 #pragma unroll
         for (int grp = 0; grp < NG; grp++) {
-            const uint2 s2 = sld64(xsum + 32 * grp);
+            const uint2 s2 = lds64(xsum + 32 * grp);
             const int   x0 = 128 * (int) s2.x, x1 = 128 * (int) s2.y;
             is[grp][0]     = x0 - (im[0][grp][0] + im[1][grp][0]);
             is[grp][1]     = x1 - (im[0][grp][1] + im[1][grp][1]);
@@ -1011,7 +1013,7 @@ __device__ __forceinline__ void producer(const GemmArgs & a, const CUtensorMap *
     for (int u = blockIdx.x; u < a.units && ok; u += gridDim.x) {
         const int64_t row0 = (int64_t) (u / a.ksplit) * kTileRows;
         for (int c = 0; c < nck; c++) {
-            if (n >= a.S && !mbar_wait(&empty[s], ph)) {
+            if (n >= a.S && !mbar_wait_sleep(&empty[s], ph)) {
                 ok = false;
                 break;
             }
@@ -1127,7 +1129,7 @@ __global__ void __launch_bounds__(kThreads, D::MINB) srv_gemm_kernel(const __gri
                 s = 0;
                 ph ^= 1;
             }
-            if (!bad && !mbar_wait(&full[slot], par)) {
+            if (!bad && !mbar_wait_sleep(&full[slot], par)) {
                 if (lane == 0) atomicExch(a.status, kErrWaitFull);
                 bad = true;
             }
