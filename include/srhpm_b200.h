@@ -194,6 +194,11 @@ int srhpm_add_rms_norm_quant(srhpm_ctx * ctx, float * x, const float * delta, co
                              int n, const srhpm_tensor * W_next, void * wdata, size_t wsize, void * stream);
 int srhpm_mul_mat_prequantized(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, srhpm_tensor * Y,
                                void * wdata, size_t wsize, void * stream);
+/* SwiGLU fused the same way: out = silu(gate) * up as srhpm_swiglu (rows of ld_in / ld_out floats, n_ff = W_next's
+ * K columns), and the activation records of out for the product with W_next written into wdata for
+ * srhpm_mul_mat_prequantized. */
+int srhpm_swiglu_quant(srhpm_ctx * ctx, const float * gate, const float * up, int64_t ld_in, float * out,
+                       int64_t ld_out, int n, const srhpm_tensor * W_next, void * wdata, size_t wsize, void * stream);
 
 /* Tensor-parallel residual add + RMSNorm with the all-reduce inside (row-parallel GEMM -> next norm):
  * every rank's row-parallel GEMM (attention output, FFN down) writes its partial sum [n][d] f32 into slot `slot`

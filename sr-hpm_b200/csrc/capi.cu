@@ -291,6 +291,20 @@ int srhpm_add_rms_norm_quant(srhpm_ctx * ctx, float * x, const float * delta, co
                           (cudaStream_t) stream);
 }
 
+int srhpm_swiglu_quant(srhpm_ctx * ctx, const float * gate, const float * up, int64_t ld_in, float * out,
+                       int64_t ld_out, int n, const srhpm_tensor * W_next, void * wdata, size_t wsize, void * stream) {
+    if (!ctx || !gate || !up || !out || !W_next || n < 1 || n > 16 || ld_in < W_next->ne[0] ||
+        ld_out < W_next->ne[0]) {
+        return SRHPM_ERR_INVALID;
+    }
+    if (W_next->type != SRHPM_TYPE_Q4_K && W_next->type != SRHPM_TYPE_Q5_K && W_next->type != SRHPM_TYPE_Q6_K &&
+        W_next->type != SRHPM_TYPE_Q3_K && W_next->type != SRHPM_TYPE_IQ4_XS) {
+        return SRHPM_UNSUPPORTED;
+    }
+    return swiglu_quant_run(ctx, W_next->type, W_next->ne[1], W_next->ne[0], n, gate, up, ld_in, out, ld_out, wdata,
+                            wsize, (cudaStream_t) stream);
+}
+
 int srhpm_mul_mat_prequantized(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, srhpm_tensor * Y,
                                void * wdata, size_t wsize, void * stream) {
     if (!ctx || !Y) return SRHPM_ERR_INVALID;

@@ -41,6 +41,9 @@ int    gemm_run_prequant(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t 
                          int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize, cudaStream_t stream);
 int    norm_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_t N, float * x, const float * delta,
                       const float * w, float eps, float * y, void * wdata, size_t wsize, cudaStream_t stream);
+int    swiglu_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_t N, const float * gate,
+                        const float * up, int64_t ld_in, float * h, int64_t ld_out, void * wdata, size_t wsize,
+                        cudaStream_t stream);
 int    gemm_run_unsplit(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                         const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
                         cudaStream_t stream);

@@ -178,6 +178,49 @@ __global__ void __launch_bounds__(256) quant_q8K_kernel(const float * __restrict
     }
 }
 
+// SwiGLU fused with the activation quantizer of the GEMM that consumes h (the FFN down projection): one warp per
+// (super-block, token); h = silu(gate) * up for its 256 values (as swiglu_kernel: g / (1 + expf(-g)) * u), written to
+// h and quantized into the GEMM's records exactly as quant_q8K_kernel does; tokens N..NT-1 get zero rows; the first
+// CTA zeroes the split-K counters.
+__global__ void __launch_bounds__(256) swiglu_q8K_kernel(const float * __restrict__ gate, const float * __restrict__ up,
+                                                         int64_t ld_in, float * __restrict__ h, int64_t ld_out, int N,
+                                                         int nsb, int NT, uint8_t * __restrict__ recs, int perm,
+                                                         int32_t * __restrict__ cnt, int ncnt) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (blockIdx.x == 0) {
+        for (int i = threadIdx.x; i < ncnt; i += blockDim.x) cnt[i] = 0;
+    }
+    const int     lane = threadIdx.x & 31;
+    const int64_t wid  = (int64_t) blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (wid >= (int64_t) nsb * NT) return;
+    const int sb = (int) (wid / NT), t = (int) (wid % NT);
+    float     v[8];
+    if (t < N) {
+        const int64_t c0 = (int64_t) sb * QK + 8 * lane;
+        float         g8[8], u8[8];
+        load8(gate + (int64_t) t * ld_in + c0, g8);
+        load8(up + (int64_t) t * ld_in + c0, u8);
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = g8[j] / (1.0f + expf(-g8[j])) * u8[j];
+        float * hp = h + (int64_t) t * ld_out + c0;
+        if ((reinterpret_cast<uintptr_t>(hp) & 15) == 0) {
+            reinterpret_cast<float4 *>(hp)[0] = make_float4(v[0], v[1], v[2], v[3]);
+            reinterpret_cast<float4 *>(hp)[1] = make_float4(v[4], v[5], v[6], v[7]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) hp[j] = v[j];
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) v[j] = 0.0f;
+    }
+    int   qv[8];
+    float dv;
+    q8K_quantize_warp(v, lane, qv, dv);
+    q8K_store_record(qv, dv, recs + (size_t) sb * rec_bytes(false, NT), t, NT, lane, perm);
+}
+
 // residual add + RMSNorm fused with the activation quantizer of the GEMM that consumes y (the SURVEY's fused
 // prologue): CTA t < N: x += delta; y = x / sqrt(mean(x^2) + eps) * w (as add_rms_norm); the row of y is staged in
 // shared memory and each warp quantizes super-blocks of it into the GEMM's activation records exactly as
@@ -1605,6 +1648,26 @@ int norm_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_t 
                                        x, delta, w, eps, y, (int) N, K, NT, base + wl.recs,
                                        (int) (wtype == SRHPM_TYPE_Q3_K), reinterpret_cast<int32_t *>(base + wl.cnt),
                                        nrb);
+    ctx->launches.fetch_add(1);
+    return cuda_status(e);
+}
+
+int swiglu_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_t N, const float * gate,
+                     const float * up, int64_t ld_in, float * h, int64_t ld_out, void * wdata, size_t wsize,
+                     cudaStream_t stream) {
+    if (wtype == SRHPM_TYPE_Q8_0) return SRHPM_UNSUPPORTED;
+    if (K % QK != 0 || N < 1 || N > 16) return SRHPM_ERR_INVALID;
+    const WorkLayout wl = work_layout(wtype, rows, K, N);
+    if (wsize < wl.total || !wdata) return SRHPM_ERR_WORKSPACE;
+    uint8_t *     base   = align256(wdata);
+    const int     NT     = N <= 8 ? 8 : 16;
+    const int     nrb    = (int) ((rows + kTileRows - 1) / kTileRows);
+    const int     nsb    = (int) (K / QK);
+    const int64_t warps  = (int64_t) nsb * NT;
+    const int     blocks = (int) ((warps + 7) / 8);
+    const cudaError_t e = launch_k_pdl(swiglu_q8K_kernel, dim3(blocks), dim3(256), 0, stream, gate, up, ld_in, h,
+                                       ld_out, (int) N, nsb, NT, base + wl.recs, (int) (wtype == SRHPM_TYPE_Q3_K),
+                                       reinterpret_cast<int32_t *>(base + wl.cnt), nrb);
     ctx->launches.fetch_add(1);
     return cuda_status(e);
 }

@@ -70,6 +70,8 @@ _SIGNATURES = {
     "srhpm_add_rms_norm_quant": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_float, _P, ctypes.c_int, _T, _P,
                                                 ctypes.c_size_t, _P]),
     "srhpm_mul_mat_prequantized": (ctypes.c_int, [_P, _T, _T, _T, _P, ctypes.c_size_t, _P]),
+    "srhpm_swiglu_quant": (ctypes.c_int, [_P, _P, _P, ctypes.c_int64, _P, ctypes.c_int64, ctypes.c_int, _T, _P,
+                                          ctypes.c_size_t, _P]),
     "srhpm_add_rms_norm_allreduce": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P,
                                                     ctypes.c_float, _P, ctypes.c_int, ctypes.c_int64, _P]),
     "srhpm_add_rms_norm": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_float, _P, ctypes.c_int, ctypes.c_int64, _P]),

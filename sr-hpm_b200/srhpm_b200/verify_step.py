@@ -375,11 +375,24 @@ class VerifyStep:
                 calls.append(self._mm(lay["gate"], self.y, self.gu[:, :self.n_ff]))
                 calls.append(self._mm(lay["up"], self.y, self.gu[:, self.n_ff:]))
             up_ptr = ctypes.c_void_p(self.gu.data_ptr() + 4 * self.n_ff)
-            calls.append(("swiglu", lib.srhpm_swiglu,
-                          [h, self._ptr(self.gu), up_ptr, self.gu.stride(0), self._ptr(self.h), self.h.stride(0), n,
-                           self.n_ff], False))
-            # the delta added by the next norm (row-parallel: partial sums over the rank's FFN rows)
-            calls.append(self._mm(lay["down"], self.h, self._rowpar_out(1)))
+            # then the down GEMM: the delta added by the next norm (row-parallel: partial sums over the FFN rows)
+            if self.fuse_prologue and lay["down"].qtype != L.Q8_0:
+                Wd, Yd = lay["down"], self._rowpar_out(1)
+                st, ws = self.ctx.mul_mat_work_size(Wd, self.h)
+                L.check(st, "srhpm_mul_mat_work_size")
+                self._ws = max(self._ws, ws)
+                wv, xv, yv = Wd.view(), f32_rows_view(self.h), f32_rows_view(Yd)
+                self._keep += [wv, xv, yv]
+                calls.append(("swiglu_quant", lib.srhpm_swiglu_quant,
+                              [h, self._ptr(self.gu), up_ptr, self.gu.stride(0), self._ptr(self.h), self.h.stride(0),
+                               n, ctypes.byref(wv)], True))
+                calls.append(("mul_mat_prequantized", lib.srhpm_mul_mat_prequantized,
+                              [h, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv)], True))
+            else:
+                calls.append(("swiglu", lib.srhpm_swiglu,
+                              [h, self._ptr(self.gu), up_ptr, self.gu.stride(0), self._ptr(self.h), self.h.stride(0),
+                               n, self.n_ff], False))
+                calls.append(self._mm(lay["down"], self.h, self._rowpar_out(1)))
             if self.tp is not None and not self._fused():
                 calls.append(self._all_reduce(self.o))
         calls += self._norm_mm(1, self.w.out_norm, self.w.head, self.logits)

@@ -296,8 +296,8 @@ def test_allreduce_norm_peer_wait_times_out(ctx):
 
 
 def test_fused_norm_quant_prologue_is_exact(ctx):
-    """RMSNorm fused with the next GEMM's activation quantization writes the same records as the GEMM's own
-    quantizer: the whole step's logits, caches and accepted ids are identical with and without the fusion."""
+    """RMSNorm and SwiGLU fused with the next GEMM's activation quantization write the same records as the GEMM's
+    own quantizer: the whole step's logits, caches and accepted ids are identical with and without the fusion."""
     cfg = small_cfg(L.F16)
     w = V.host_weights(cfg, seed=31)
     cap, n_past, ids, draft = 128, 70, [4, 8, 15, 16, 23, 42], [8, 15, 16, 23, 42]
@@ -318,5 +318,5 @@ def test_fused_norm_quant_prologue_is_exact(ctx):
     assert torch.equal(outs[0][0], outs[1][0])
     assert all(torch.equal(a, b) for a, b in zip(outs[0][1], outs[1][1]))
     assert outs[0][2] == outs[1][2]
-    # kernel launches: the quantizers of the QKV, gate|up and head GEMMs are gone (2 per layer + 1)
-    assert outs[0][3] - outs[1][3] == 2 * cfg.n_layer + 1
+    # kernel launches: the quantizers of the QKV, gate|up, down and head GEMMs are gone (3 per layer + 1)
+    assert outs[0][3] - outs[1][3] == 3 * cfg.n_layer + 1
