@@ -149,26 +149,6 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// streaming global loads of read-once data: non-coherent path, no L1 allocation. volatile keeps them where the
-// code issues them (a prefetch must not sink to its first use)
-__device__ __forceinline__ uint4 ldg_stream128(const void * p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint2 ldg_stream64(const void * p) {
-    uint2 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-    return v;
-}
-__device__ __forceinline__ uint32_t ldg_stream32(const void * p) {
-    uint32_t v;
-    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
-    return v;
-}
-
 // programmatic dependent launch: wait for the preceding grid's writes / let the next grid start its prologue
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
@@ -225,45 +205,11 @@ __device__ __forceinline__ void mma_k16_z(int (&d)[4], uint32_t a0, uint32_t a1,
     }
 }
 
-// D = A(16x16, row) * B(16x8, col) + C, int8. a0 = A[g][4t..4t+3], a1 = A[g+8][4t..]; b0 = B[4t..4t+3][g].
-template <bool A_UNSIGNED>
-__device__ __forceinline__ void mma_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-    if constexpr (A_UNSIGNED) {
-        asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
-                     : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-                     : "r"(a0), "r"(a1), "r"(b0));
-    } else {
-        asm volatile("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
-                     : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-                     : "r"(a0), "r"(a1), "r"(b0));
-    }
-}
-
-// 4 bytes from a 2-byte-aligned shared-memory address (two aligned 32-bit loads and a funnel shift when needed)
-__device__ __forceinline__ uint32_t lds_u32_a2(const uint8_t * p) {
-    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
-    if ((a & 3) == 0) {
-        return *reinterpret_cast<const uint32_t *>(p);
-    }
-    const uint32_t * q = reinterpret_cast<const uint32_t *>(a & ~uintptr_t(3));
-    return __funnelshift_r(q[0], q[1], 16);
-}
-
 // explicit shared-space loads at 32-bit shared addresses (generic pointers into shared memory can compile to generic
 // loads once their provenance is lost)
 __device__ __forceinline__ uint32_t sld32(uint32_t a) {
     uint32_t v;
     asm volatile("ld.shared.b32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ uint2 sld64(uint32_t a) {
-    uint2 v;
-    asm volatile("ld.shared.v2.b32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
-    return v;
-}
-__device__ __forceinline__ uint4 sld128(uint32_t a) {
-    uint4 v;
-    asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
     return v;
 }
 // 4 bytes at a shared address that is 4-byte aligned (A4), or any even one (two aligned words and a funnel shift)
@@ -294,17 +240,6 @@ __device__ __forceinline__ uint2 sld8o(uint32_t base, uint32_t sh) {
         return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
     }
 }
-// 8 bytes at a shared address that is 4-byte aligned (A4), or any (three aligned words and two funnel shifts)
-template <bool A4>
-__device__ __forceinline__ uint2 sld8_a2(uint32_t a) {
-    if constexpr (A4) {
-        return make_uint2(sld32(a), sld32(a + 4));
-    } else {
-        const uint32_t b = a & ~3u, sh = (a & 3u) * 8, w0 = sld32(b), w1 = sld32(b + 4), w2 = sld32(b + 8);
-        return make_uint2(__funnelshift_r(w0, w1, sh), __funnelshift_r(w1, w2, sh));
-    }
-}
-
 __device__ __forceinline__ float half_bits_to_float(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
 __device__ __forceinline__ uint16_t lds_u16(const uint8_t * p) { return *reinterpret_cast<const uint16_t *>(p); }
