@@ -7,6 +7,8 @@ the step writes; the accepted ids identical wherever the oracle's top-1 margin e
 than the per-operator 1e-3 because every GEMM re-quantizes its input to int8: once an attention output differs by
 ~1e-4 (f16 P and V), ~2-3 % of the following activation codes land on the other side of a rounding boundary, and
 each such +-1 flip moves the GEMM output by ~0.4 % -- five chained GEMMs per layer, three layers (measured: 5.7e-3)."""
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -320,3 +322,55 @@ def test_fused_norm_quant_prologue_is_exact(ctx):
     assert outs[0][2] == outs[1][2]
     # kernel launches: the quantizers of the QKV, gate|up, down and head GEMMs are gone (3 per layer + 1)
     assert outs[0][3] - outs[1][3] == 3 * cfg.n_layer + 1
+
+
+def test_fused_entry_points_status_codes(ctx):
+    """The fused prologue / all-reduce entry points return status codes instead of failing: Q8_0 weights have no
+    fused prologue (UNSUPPORTED, srhpm_mul_mat quantizes itself), a short workspace, misaligned rows, bad ranks."""
+    lib = L.load()
+    ptr = lambda t: t.data_ptr()
+    d, n = 512, 3
+    x = torch.randn((n, d), device="cuda")
+    w = torch.ones(d, device="cuda")
+    y = torch.empty_like(x)
+    Wq8 = S.QuantTensor.quantize(np.random.default_rng(0).standard_normal((64, d)).astype(np.float32) * 0.02, S.Q8_0)
+    W4 = S.QuantTensor.quantize(np.random.default_rng(1).standard_normal((64, d)).astype(np.float32) * 0.02, S.Q4_K)
+    work = torch.zeros(1 << 20, dtype=torch.uint8, device="cuda")
+    v8, v4 = Wq8.view(), W4.view()
+    st = lib.srhpm_add_rms_norm_quant(ctx.handle, ptr(x), None, ptr(w), 1e-6, ptr(y), n, ctypes.byref(v8), ptr(work),
+                                      work.numel(), None)
+    assert st == L.UNSUPPORTED
+    st = lib.srhpm_add_rms_norm_quant(ctx.handle, ptr(x), None, ptr(w), 1e-6, ptr(y), n, ctypes.byref(v4), ptr(work),
+                                      16, None)
+    assert st == L.ERR_WORKSPACE
+    st = lib.srhpm_add_rms_norm_quant(ctx.handle, ptr(x) + 4, None, ptr(w), 1e-6, ptr(y), n, ctypes.byref(v4),
+                                      ptr(work), work.numel(), None)
+    assert st == L.ERR_ALIGN
+    st = lib.srhpm_swiglu_quant(ctx.handle, ptr(x), ptr(x), d, ptr(y), d, n, ctypes.byref(v8), ptr(work),
+                                work.numel(), None)
+    assert st == L.UNSUPPORTED
+    peers = torch.zeros(2, dtype=torch.int64, device="cuda")
+    epochs = torch.zeros(32, dtype=torch.int32, device="cuda")
+    for world, rank, slot in ((9, 0, 0), (2, 2, 0), (2, 0, 2), (0, 0, 0)):
+        st = lib.srhpm_add_rms_norm_allreduce(ctx.handle, ptr(x), ptr(peers), world, rank, slot, ptr(epochs),
+                                              ptr(w), 1e-6, ptr(y), n, d, None)
+        assert st == L.ERR_INVALID, (world, rank, slot)
+    torch.cuda.synchronize()
+    ctx.check()
+
+
+def test_verify_step_single_token(ctx):
+    """k = 0 (N = 1: only the accepted token, nothing drafted) through the fused prologues: matches the oracle and
+    emits exactly the greedy token."""
+    cfg = small_cfg(L.F16)
+    w = V.host_weights(cfg, seed=41)
+    cap, n_past, ids = 64, 30, [123]
+    kc, vc = _caches(cfg, cap, n_past, 512, 42)
+    okc, ovc = [a.copy() for a in kc], [a.copy() for a in vc]
+    logits_o, acc_o = O.decoder_step(cfg.as_dict(), w, okc, ovc, ids, n_past, [])
+    step = _run_step(ctx, cfg, V.DeviceWeights.from_host(cfg, w), [torch.from_numpy(a).cuda() for a in kc],
+                     [torch.from_numpy(a).cuda() for a in vc], ids, [], n_past)
+    assert rel_l2(step.logits.cpu().numpy(), logits_o) < 2e-2
+    srt = np.sort(logits_o[0])
+    if srt[-1] - srt[-2] > 1e-2:
+        assert step.accepted() == acc_o
