@@ -250,7 +250,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     using S           = Smem<RP>;
     constexpr int RH  = RP / 4;  // rows per compute thread
     extern __shared__ uint8_t smem_raw[];
-    uint8_t * sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned base, by pointer arithmetic on the shared array (an integer round trip would make every
+    // access through `sm` a generic load / store)
+    uint8_t * sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t * full    = reinterpret_cast<uint64_t *>(sm + S::bar);
     uint64_t * empty   = full + kNSlot;
     uint64_t * s_full  = empty + kNSlot;
@@ -764,7 +766,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     using S          = SmemF<RP>;
     constexpr int RH = RP / 4;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t * sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // 1024-byte aligned base, by pointer arithmetic on the shared array (an integer round trip would make every
+    // access through `sm` a generic load / store)
+    uint8_t * sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     uint64_t * full    = reinterpret_cast<uint64_t *>(sm + S::bar);
     uint64_t * empty   = full + 4;
     uint64_t * s_full  = empty + 4;
