@@ -1155,6 +1155,13 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const FaArgs a) {
     __shared__ float mf_s;
     const float2 * ms = a.part_ms + (int64_t) row * a.n_chunks;
     const int      nc = a.n_chunks;  // <= 256 (fa_plan: one chunk per CTA of a wave at most)
+    const int      dv  = threadIdx.x;
+    const float *  src = a.part_acc + (int64_t) row * nc * kD + dv;
+    // the first kPre chunks' partial outputs do not depend on the (max, sum) records: in flight with them
+    constexpr int kPre = 32;
+    float         pre[kPre];
+#pragma unroll
+    for (int c = 0; c < kPre; c++) pre[c] = c < nc ? __ldcg(src + (int64_t) c * kD) : 0.0f;
     if (threadIdx.x < 32) {
         float m = -INFINITY;
         for (int c = threadIdx.x; c < nc; c += 32) {
@@ -1173,11 +1180,17 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const FaArgs a) {
         s_s[c]         = v.y;
     }
     __syncthreads();
-    const int      dv  = threadIdx.x;
-    const float *  src = a.part_acc + (int64_t) row * nc * kD + dv;
-    float          acc = 0.0f, S = 0.0f;
+    float acc = 0.0f, S = 0.0f;
+#pragma unroll
+    for (int c = 0; c < kPre; c++) {
+        if (c < nc) {
+            const float w = w_s[c];
+            acc           = fmaf(w, w != 0.0f ? pre[c] : 0.0f, acc);
+            S             = fmaf(w, s_s[c], S);
+        }
+    }
 #pragma unroll 8
-    for (int c = 0; c < nc; c++) {
+    for (int c = kPre; c < nc; c++) {
         const float w = w_s[c];
         acc           = fmaf(w, w != 0.0f ? src[(int64_t) c * kD] : 0.0f, acc);
         S             = fmaf(w, s_s[c], S);
