@@ -11,6 +11,7 @@ Tensors are torch tensors in device memory; torch only provides allocation and s
 libsrhpm_b200.so through its C ABI; a missing library raises.
 """
 import ctypes
+import warnings
 
 import numpy as np
 import torch
@@ -86,7 +87,10 @@ class QuantTensor:
 
     @classmethod
     def from_blocks(cls, blocks, qtype, rows, K, device="cuda"):
-        t = torch.from_numpy(np.ascontiguousarray(blocks).reshape(-1)).to(device)
+        # a read-only map of a GGUF file is fine here: the host tensor is only read by the copy to the device
+        with warnings.catch_warnings():
+            warnings.filterwarnings("ignore", message="The given NumPy array is not writable")
+            t = torch.from_numpy(np.ascontiguousarray(blocks).reshape(-1)).to(device)
         return cls(t, qtype, rows, K)
 
     @classmethod
