@@ -448,11 +448,19 @@ def run_gpu(args):
             step_tp = measure_step_27b_tp(ctx, dev, rank, world)
         except Exception as e:  # recorded beside the sweep rather than losing its line
             step_tp = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+    attn_split = None
+    if world > 1 and not args.no_attn:  # every rank takes part (an all-gather per call)
+        try:
+            attn_split = measure_attention_split(ctx, dev, rank, world, peak)
+        except Exception as e:  # recorded beside the sweep rather than losing its line
+            attn_split = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
     if rank == 0:
         cfg = workload_config(base_ops, world)
         cfg["timed"] = "CUDA graph of one step, replayed" if graph is not None else "eager calls"
         if step_tp is not None:
             cfg["verify_step_27b_f16kv_2048_tp"] = step_tp
+        if attn_split is not None:
+            cfg["attention_q8_0_split_k"] = attn_split
         if ncopy > 1:
             cfg["copies_rotated"] = ncopy
         cfg["per_type_gbs"] = group(lambda op: [k for k, v in TYPE_IDS.items() if v == op[1]][0])
@@ -608,6 +616,74 @@ def measure_attention(ctx, dev, peak, reps=20, lengths=(8192, 32768, 131072)):
         gbs = nbytes / (us * 1e-6) / 1e9
         out[str(L)] = {"us": round(us, 2), "GBps": round(gbs, 1), "frac": round(gbs / peak, 4), "bytes": nbytes}
         del graph, kv
+        torch.cuda.empty_cache()
+    return out
+
+
+def measure_attention_split(ctx, dev, rank, world, peak, reps=20, lengths=(8192, 32768, 131072)):
+    """BASELINE config 3 on `world` GPUs, split over the KV range: rank j holds tokens shard.kv_range(L, world, j) of
+    the 4 KV heads' q8_0 cache; one call = the partial records of its range, an NCCL all-gather of the record sets
+    (24 * 8 * 1032 bytes per rank) and the merge, all in one CUDA graph over copies of the rank's range that together
+    exceed L2. Time = max over ranks; GB/s counts the whole cache once (plus Q and O), as on one GPU."""
+    import torch
+    import torch.distributed as dist
+    import srhpm_b200 as S
+    from srhpm_b200 import shard
+    from srhpm_b200.split_attn import SplitKAttention
+    H, Hkv, N, D = 24, 4, 8, 256
+    g = torch.Generator(device=dev)
+    g.manual_seed(3 + rank)
+    out = {}
+    for L in lengths:
+        t0, t1 = shard.kv_range(L, world, rank)
+        Lr = t1 - t0
+        nbytes = 2176 * L + 2 * H * N * D * 4
+        ncopy = max(2, -(-400_000_000 // max(1, 2176 * Lr)))
+        q = torch.randn((H, N, D), device=dev, generator=torch.Generator(device=dev).manual_seed(3)) / 16
+        kv = []
+        for _ in range(ncopy):
+            pair = []
+            for _ in range(2):
+                x = torch.randn((Hkv * Lr, D), device=dev, generator=g)
+                pair.append(ctx.quantize_rows_q8_0(x).view(Hkv, Lr, 272))
+                del x
+            kv.append(pair)
+        mask = torch.zeros((N, L), dtype=torch.float16, device=dev)
+        for t in range(N):
+            mask[t, L - N + t + 1:] = float("-inf")
+        mr = mask[:, t0:t1]
+        att = SplitKAttention(ctx, rank, world, H, N, dev)
+        st, ws = ctx.flash_attn_ext_work_size(q, kv[0][0], kv[0][1], S.Q8_0)
+        work = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+        for i in range(3):
+            att(q, *kv[i % ncopy], S.Q8_0, mask=mr, work=work)
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                for i in range(ncopy):
+                    att(q, *kv[i], S.Q8_0, mask=mr, work=work)
+        torch.cuda.synchronize()
+        graph.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        rounds = max(1, reps // ncopy)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(rounds):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ctx.check()
+        tt = torch.tensor([e0.elapsed_time(e1) * 1e3 / (rounds * ncopy)], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        us = float(tt.item())
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[str(L)] = {"us": round(us, 2), "GBps": round(gbs, 1), "GBps_per_gpu": round(gbs / world, 1),
+                       "frac_per_gpu": round(gbs / world / peak, 4), "bytes": nbytes, "gpus": world}
+        del graph, kv  # the graph holds NCCL calls: released before the process group
         torch.cuda.empty_cache()
     return out
 

@@ -139,6 +139,25 @@ int srhpm_flash_attn_ext(srhpm_ctx * ctx, const srhpm_tensor * q, const srhpm_te
                          const srhpm_tensor * mask, const srhpm_tensor * sinks, float scale, float max_bias,
                          float softcap, srhpm_tensor * dst, void * wdata, size_t wsize, void * stream);
 
+/* ---- attention split over the KV range across devices ----------------------------------------------------------
+ * Each device holds a range of the cache's tokens: k / v views (and the mask's columns) start at the range's first
+ * token and k->ne[1] = its token count (0 for an empty range; no work buffer then). srhpm_flash_attn_ext_partial
+ * takes the arguments of srhpm_flash_attn_ext except sinks and dst and writes the range's record set into `part`
+ * (srhpm_flash_attn_part_size(H, N) bytes, 16-byte aligned; wdata: srhpm_flash_attn_ext_work_size of the range's
+ * views): for row r = h * N + t, float {max, sum} pairs [H * N] (max of the scaled scores in base-2 units; sum = 0 for
+ * a range without a finite score), zero-padded to a multiple of 16 bytes, then float acc[H * N][256] (the row's output
+ * times its sum, not normalized).
+ * srhpm_flash_attn_merge combines n_parts (<= 256) such sets stored one after another (for example gathered from all
+ * devices in KV order), adds the sinks (f32 [H] or NULL) and writes dst f32 [256, H, N] as srhpm_flash_attn_ext would
+ * for the whole range. The reference splits the KV range into chunks over its CPU threads and merges their
+ * (max, sum, acc) records the same way (patch/srhpm.patch:555-579, 779-823); here the devices are the chunks. */
+size_t srhpm_flash_attn_part_size(int64_t n_head, int64_t n_tokens);
+int    srhpm_flash_attn_ext_partial(srhpm_ctx * ctx, const srhpm_tensor * q, const srhpm_tensor * k,
+                                    const srhpm_tensor * v, const srhpm_tensor * mask, float scale, float max_bias,
+                                    float softcap, void * part, void * wdata, size_t wsize, void * stream);
+int    srhpm_flash_attn_merge(srhpm_ctx * ctx, const void * parts, int n_parts, const srhpm_tensor * sinks,
+                              srhpm_tensor * dst, void * stream);
+
 /* ---- greedy acceptance -----------------------------------------------------------------------------------------
  * Target logits f32 [n_vocab, >= n_draft + 1] (row i scores the token after draft position i; row stride nb[1]) and
  * the drafted ids int32 [n_draft] (device): for i < n_draft, id_i = argmax of row i (the first maximum, as the

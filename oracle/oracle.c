@@ -509,6 +509,121 @@ int orc_attention(const float * q, int64_t DK, int64_t N, int64_t H, int kv_type
     return 0;
 }
 
+int orc_attention_partial(const float * q, int64_t DK, int64_t N, int64_t H, int kv_type, const void * k,
+                          const void * v, int64_t DV, int64_t L, int64_t Hkv, int64_t t0, int64_t t1,
+                          const uint16_t * mask, float scale, float max_bias, float softcap, int q8_mode,
+                          double * rec_m, double * rec_s, double * rec_acc) {
+    if (Hkv <= 0 || H % Hkv || (kv_type != ORC_F16 && kv_type != ORC_Q8_0) ||
+        (kv_type == ORC_Q8_0 && (DK % QK8 || DV % QK8)) || t0 < 0 || t1 < t0 || t1 > L) {
+        return -1;
+    }
+    const int64_t  G    = H / Hkv;
+    const size_t   krow = kv_type == ORC_Q8_0 ? (size_t) (DK / QK8) * 34 : (size_t) DK * 2;
+    const size_t   vrow = kv_type == ORC_Q8_0 ? (size_t) (DV / QK8) * 34 : (size_t) DV * 2;
+    const float    sc   = softcap != 0.0f ? scale / softcap : scale;
+    const uint32_t nhl2 = 1u << (uint32_t) floor(log2((double) H));
+    const double   m0   = pow(2.0, -(double) max_bias / nhl2);
+    const double   m1   = pow(2.0, -((double) max_bias / 2.0) / nhl2);
+    const int64_t  n    = t1 - t0;
+    double *       s    = (double *) malloc(sizeof(double) * (size_t) (n > 0 ? n : 1));
+    float *        vf   = (float *) malloc(sizeof(float) * (size_t) (DK > DV ? DK : DV));
+    uint8_t *      qq   = (uint8_t *) malloc((size_t) (DK / QK8 + 1) * 34);
+    for (int64_t h = 0; h < H; h++) {
+        const int64_t g     = h / G;
+        const double  slope = max_bias > 0.0f ? (h < (int64_t) nhl2 ? pow(m0, (double) (h + 1))
+                                                                      : pow(m1, (double) (2 * (h - nhl2) + 1)))
+                                              : 1.0;
+        for (int64_t t = 0; t < N; t++) {
+            const float * qr = q + (h * N + t) * DK;
+            if (kv_type == ORC_Q8_0) {
+                orc_quantize_row_q8_0(qr, qq, DK, q8_mode);
+            }
+            double mx = -INFINITY;
+            for (int64_t j = 0; j < n; j++) {
+                const uint8_t * kr  = (const uint8_t *) k + (size_t) (g * L + t0 + j) * krow;
+                double          dot = 0.0;
+                if (kv_type == ORC_Q8_0) {
+                    for (int64_t ib = 0; ib < DK / QK8; ib++) {
+                        int32_t isum = 0;
+                        for (int l = 0; l < QK8; l++) {
+                            isum += (int32_t) (int8_t) kr[ib * 34 + 2 + l] * (int8_t) qq[ib * 34 + 2 + l];
+                        }
+                        dot += (double) rd16(kr + ib * 34) * (double) rd16(qq + ib * 34) * (double) isum;
+                    }
+                } else {
+                    for (int64_t d = 0; d < DK; d++) dot += (double) qr[d] * (double) rd16(kr + 2 * d);
+                }
+                double sv = dot * sc;
+                if (softcap != 0.0f) {
+                    sv = softcap * tanh(sv);
+                }
+                if (mask) {
+                    sv += slope * (double) orc_fp16_to_fp32(mask[t * L + t0 + j]);
+                }
+                s[j] = sv;
+                mx   = sv > mx ? sv : mx;
+            }
+            const int64_t row = h * N + t;
+            double *      acc = rec_acc + row * DV;
+            for (int64_t d = 0; d < DV; d++) acc[d] = 0.0;
+            double sum = 0.0;
+            if (mx != -INFINITY) {
+                for (int64_t j = 0; j < n; j++) {
+                    if (s[j] == -INFINITY) continue;
+                    const double p = exp(s[j] - mx);
+                    sum += p;
+                    orc_dequantize(kv_type, (const uint8_t *) v + (size_t) (g * L + t0 + j) * vrow, vf, DV);
+                    for (int64_t d = 0; d < DV; d++) acc[d] += p * (double) vf[d];
+                }
+            }
+            rec_m[row] = mx;
+            rec_s[row] = sum;
+        }
+    }
+    free(s); free(vf); free(qq);
+    return 0;
+}
+
+int orc_attention_merge(int64_t n_parts, int64_t N, int64_t H, int64_t DV, const double * rec_m,
+                        const double * rec_s, const double * rec_acc, const float * sinks, double * dst) {
+    if (n_parts < 1 || N < 1 || H < 1 || DV < 1) {
+        return -1;
+    }
+    const int64_t rows = H * N;
+    for (int64_t h = 0; h < H; h++) {
+        for (int64_t t = 0; t < N; t++) {
+            const int64_t row = h * N + t;
+            double *      out = dst + (t * H + h) * DV;
+            double        Mf = -INFINITY, Sf = 0.0;
+            for (int64_t d = 0; d < DV; d++) out[d] = 0.0;
+            for (int64_t c = 0; c < n_parts; c++) {
+                const double sc = rec_s[c * rows + row];
+                if (sc == 0.0) continue;
+                const double   mc = rec_m[c * rows + row];
+                const double   Mn = Mf > mc ? Mf : mc;
+                const double   so = Mf == -INFINITY ? 0.0 : exp(Mf - Mn), sn = exp(mc - Mn);
+                const double * pa = rec_acc + (c * rows + row) * DV;
+                for (int64_t d = 0; d < DV; d++) out[d] = out[d] * so + pa[d] * sn;
+                Sf = Sf * so + sc * sn;
+                Mf = Mn;
+            }
+            if (sinks) {
+                const double sk = sinks[h];
+                if (Mf == -INFINITY || sk > Mf) {
+                    const double r = Mf == -INFINITY ? 0.0 : exp(Mf - sk);
+                    for (int64_t d = 0; d < DV; d++) out[d] *= r;
+                    Sf = Sf * r + 1.0;
+                } else {
+                    Sf += exp(sk - Mf);
+                }
+            }
+            const double inv = Sf == 0.0 ? 0.0 : 1.0 / Sf;
+            for (int64_t d = 0; d < DV; d++) out[d] *= inv;
+        }
+    }
+    return 0;
+}
+
 static int32_t argmax_row(const float * lg, int64_t n) {
     int64_t best = 0;
     for (int64_t i = 1; i < n; i++) {

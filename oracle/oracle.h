@@ -63,6 +63,21 @@ int orc_attention(const float * q, int64_t DK, int64_t N, int64_t H, int kv_type
                   int64_t DV, int64_t L, int64_t Hkv, const uint16_t * mask, const float * sinks, float scale,
                   float max_bias, float softcap, int q8_mode, double * dst);
 
+/* The record form of orc_attention for a split of the KV range (the reference's chunked path, whose per-chunk records
+ * are written at patch/srhpm.patch:779-784 and merged at :789-823; across devices the ranks are the chunks): over KV
+ * tokens [t0, t1) of the same buffers (L tokens per KV head), per row (h, t) the maximum score m (natural-log units,
+ * -inf when no score is finite), s = sum exp(score - m) and acc[d] = sum exp(score - m) v[d], unnormalized and
+ * without sinks. rec_m, rec_s [H][N], rec_acc [H][N][DV], all double. */
+int orc_attention_partial(const float * q, int64_t DK, int64_t N, int64_t H, int kv_type, const void * k,
+                          const void * v, int64_t DV, int64_t L, int64_t Hkv, int64_t t0, int64_t t1,
+                          const uint16_t * mask, float scale, float max_bias, float softcap, int q8_mode,
+                          double * rec_m, double * rec_s, double * rec_acc);
+
+/* Merge of n_parts record sets ([n_parts][H][N] for m and s, [n_parts][H][N][DV] for acc) in part order, then sinks
+ * and the division by the sum (patch/srhpm.patch:789-823): parts with s == 0 are skipped. dst f64 [N][H][DV]. */
+int orc_attention_merge(int64_t n_parts, int64_t N, int64_t H, int64_t DV, const double * rec_m,
+                        const double * rec_s, const double * rec_acc, const float * sinks, double * dst);
+
 /* Greedy longest-prefix acceptance (upstream common_sampler_sample_and_accept_n with greedy sampling, plus the
  * SR-HPM relax of patch/srhpm.patch:9-35). logits f32 [n_draft+1][n_vocab]; out_ids receives the accepted draft
  * tokens followed by one sampled token (at most n_draft+1 ids); returns that count. argmax ties -> lowest id. */

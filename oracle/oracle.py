@@ -60,6 +60,12 @@ def load_oracle():
         lib.orc_attention.argtypes = [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _P, _P,
                                       ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _P, _P, ctypes.c_float,
                                       ctypes.c_float, ctypes.c_float, ctypes.c_int, _P]
+        lib.orc_attention_partial.argtypes = [_P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int, _P,
+                                              _P, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                              ctypes.c_int64, _P, ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                              ctypes.c_int, _P, _P, _P]
+        lib.orc_attention_merge.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _P, _P,
+                                            _P, _P, _P]
         lib.orc_accept.argtypes = [_P, ctypes.c_int64, _P, ctypes.c_int, ctypes.c_float, _P]
         _orc = lib
     return _orc
@@ -181,6 +187,37 @@ def attention(q, kv_type, k, v, DV, L, Hkv, mask=None, sinks=None, scale=1.0, ma
     dst = np.empty((N, H, DV), np.float64)
     st = load_oracle().orc_attention(_ptr(q), DK, N, H, kv_type, _ptr(k), _ptr(v), DV, L, Hkv, _ptr(m), _ptr(s),
                                      scale, max_bias, softcap, q8_mode, _ptr(dst))
+    assert st == 0, st
+    return dst
+
+
+def attention_partial(q, kv_type, k, v, DV, L, Hkv, t0, t1, mask=None, scale=1.0, max_bias=0.0, softcap=0.0,
+                      q8_mode=Q8_0_SIMD):
+    """Records of KV tokens [t0, t1) (orc_attention_partial): (m [H, N], s [H, N], acc [H, N, DV]), all double;
+    m in natural-log units."""
+    q = np.ascontiguousarray(q, np.float32)
+    H, N, DK = q.shape
+    k = _u8(k)
+    v = _u8(v)
+    msk = np.ascontiguousarray(mask, np.uint16) if mask is not None else None
+    m = np.empty((H, N), np.float64)
+    s = np.empty((H, N), np.float64)
+    acc = np.empty((H, N, DV), np.float64)
+    st = load_oracle().orc_attention_partial(_ptr(q), DK, N, H, kv_type, _ptr(k), _ptr(v), DV, L, Hkv, t0, t1,
+                                             _ptr(msk), scale, max_bias, softcap, q8_mode, _ptr(m), _ptr(s), _ptr(acc))
+    assert st == 0, st
+    return m, s, acc
+
+
+def attention_merge(m, s, acc, sinks=None):
+    """Merge record sets stacked on a leading part axis (m, s [P, H, N], acc [P, H, N, DV]) -> double [N, H, DV]."""
+    m = np.ascontiguousarray(m, np.float64)
+    s = np.ascontiguousarray(s, np.float64)
+    acc = np.ascontiguousarray(acc, np.float64)
+    P, H, N, DV = acc.shape
+    sk = np.ascontiguousarray(sinks, np.float32) if sinks is not None else None
+    dst = np.empty((N, H, DV), np.float64)
+    st = load_oracle().orc_attention_merge(P, N, H, DV, _ptr(m), _ptr(s), _ptr(acc), _ptr(sk), _ptr(dst))
     assert st == 0, st
     return dst
 

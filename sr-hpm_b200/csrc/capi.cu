@@ -383,6 +383,61 @@ int srhpm_flash_attn_ext(srhpm_ctx * ctx, const srhpm_tensor * q, const srhpm_te
     return fa_run(ctx, fv, scale, max_bias, softcap, wdata, wsize, (cudaStream_t) stream);
 }
 
+size_t srhpm_flash_attn_part_size(int64_t n_head, int64_t n_tokens) {
+    if (n_head < 1 || n_tokens < 1) return 0;
+    return fa_part_bytes(n_head, n_tokens);
+}
+
+int srhpm_flash_attn_ext_partial(srhpm_ctx * ctx, const srhpm_tensor * q, const srhpm_tensor * k,
+                                 const srhpm_tensor * v, const srhpm_tensor * mask, float scale, float max_bias,
+                                 float softcap, void * part, void * wdata, size_t wsize, void * stream) {
+    if (!ctx || !q || !k || !v || !part) return SRHPM_ERR_INVALID;
+    if (!aligned(part, 16)) return SRHPM_ERR_ALIGN;
+    if (q->type != SRHPM_TYPE_F32 || q->ne[1] < 1 || q->ne[1] > 16 || q->ne[2] < 1 || q->ne[2] > 65536) {
+        return SRHPM_ERR_INVALID;
+    }
+    const size_t bytes = fa_part_bytes(q->ne[2], q->ne[1]);
+    if (k->ne[1] == 0 && v->ne[1] == 0) {  // an empty KV range: sums 0, skipped by the merge
+        return cuda_status(cudaMemsetAsync(part, 0, bytes, (cudaStream_t) stream));
+    }
+    srhpm_tensor d = {};  // dst is not written; its shape is checked like srhpm_flash_attn_ext's
+    d.type         = SRHPM_TYPE_F32;
+    d.ne[0]        = v->ne[0];
+    d.ne[1]        = q->ne[2];
+    d.ne[2]        = q->ne[1];
+    d.ne[3]        = 1;
+    d.nb[0]        = 4;
+    d.nb[1]        = 4 * (size_t) d.ne[0];
+    d.nb[2]        = d.nb[1] * (size_t) d.ne[1];
+    d.nb[3]        = d.nb[2] * (size_t) d.ne[2];
+    d.data         = part;
+    FaView    fv;
+    const int st = check_fa(q, k, v, mask, nullptr, &d, &fv);
+    if (st != SRHPM_OK) return st;
+    return fa_run(ctx, fv, scale, max_bias, softcap, wdata, wsize, (cudaStream_t) stream, part);
+}
+
+int srhpm_flash_attn_merge(srhpm_ctx * ctx, const void * parts, int n_parts, const srhpm_tensor * sinks,
+                           srhpm_tensor * dst, void * stream) {
+    if (!ctx || !parts || !dst || n_parts < 1 || n_parts > 256) return SRHPM_ERR_INVALID;
+    if (!aligned(parts, 16)) return SRHPM_ERR_ALIGN;
+    if (dst->type != SRHPM_TYPE_F32 || !dst->data || dst->ne[0] != 256 || dst->ne[1] < 1 || dst->ne[1] > 65536 ||
+        dst->ne[2] < 1 || dst->ne[2] > 16 || dst->ne[3] != 1) {
+        return SRHPM_ERR_INVALID;
+    }
+    if (dst->nb[0] != 4 || dst->nb[1] % 4 || dst->nb[2] % 4 || !aligned(dst->data, 4)) return SRHPM_ERR_INVALID;
+    const int H = (int) dst->ne[1], N = (int) dst->ne[2];
+    const float * sk = nullptr;
+    if (sinks) {
+        if (sinks->type != SRHPM_TYPE_F32 || sinks->ne[0] != H || sinks->nb[0] != 4 || !sinks->data) {
+            return SRHPM_ERR_INVALID;
+        }
+        sk = (const float *) sinks->data;
+    }
+    return fa_merge_run(ctx, parts, n_parts, N, H, sk, (float *) dst->data, (int64_t) dst->nb[1],
+                        (int64_t) dst->nb[2], (cudaStream_t) stream);
+}
+
 int srhpm_verify_accept_work_size(const srhpm_ctx * ctx, const srhpm_tensor * logits, size_t * size) {
     if (!ctx || !size) return SRHPM_ERR_INVALID;
     const int st = check_logits(logits, 1);

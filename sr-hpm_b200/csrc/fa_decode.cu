@@ -68,6 +68,12 @@ struct FaArgs {
     int64_t         dnb1, dnb2;  // bytes: head, token
     float *         part_acc;    // [Hkv * R][n_chunks][256]
     float2 *        part_ms;     // [Hkv * R][n_chunks] (max in log2 units, sum)
+    // what fa_combine reads: record (row, c) at part_ms[row * ms_row + c * ms_chunk] and
+    // part_acc[row * acc_row + c * acc_chunk + dv] (the layout above, or the record sets of several devices)
+    int64_t         ms_row, ms_chunk, acc_row, acc_chunk;
+    int             parts_out;   // 1: write this KV range's merged record (rec_ms, rec_acc), not dst; no sinks
+    float2 *        rec_ms;      // [Hkv * R]
+    float *         rec_acc;     // [Hkv * R][256]
     int32_t *       status;
     int             q8mode;
 };
@@ -671,7 +677,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             if (lane == 0) red[(nt & 1) * 4 * RP + q * RP + rbase + r] = v;
         }
         named_bar_sync(1, kCW * 32);
-        const bool single = a.n_chunks == 1;
+        const bool single = a.n_chunks == 1 && !a.parts_out;
         if (tid < rows) {
             const float * rs = red + (nt & 1) * 4 * RP;
             float Ssum = rs[tid];
@@ -1088,7 +1094,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             if (lane == 0) red[(nt & 1) * 4 * RP + q * RP + rbase + r] = v;
         }
         named_bar_sync(1, kCW * 32);
-        const bool single = a.n_chunks == 1;
+        const bool single = a.n_chunks == 1 && !a.parts_out;
         if (tid < rows) {
             const float * rs   = red + (nt & 1) * 4 * RP;
             float         Ssum = rs[tid];
@@ -1145,7 +1151,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     if (warp == 0) tc::tmem_free(tbase, 256);
 }
 
-// merge of the chunk records of one row (P:787-823), then sinks and normalization; one CTA per (KV head, row)
+// merge of the chunk records of one row (P:787-823), then sinks and normalization; one CTA per (KV head, row).
+// The same merge combines the record sets of several devices (each the merged record of its KV range) and, with
+// parts_out, leaves this device's merged record unnormalized for such a merge.
 __global__ void __launch_bounds__(256) fa_combine_kernel(const FaArgs a) {
     pdl_wait();
     const int row = blockIdx.x, g = row / a.R, rr = row % a.R;
@@ -1153,19 +1161,20 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const FaArgs a) {
     __shared__ float w_s[256];  // per chunk: weight 2^(M_c - M) (0 for empty chunks)
     __shared__ float s_s[256];
     __shared__ float mf_s;
-    const float2 * ms = a.part_ms + (int64_t) row * a.n_chunks;
-    const int      nc = a.n_chunks;  // <= 256 (fa_plan: one chunk per CTA of a wave at most)
+    const float2 * ms = a.part_ms + (int64_t) row * a.ms_row;
+    const int      nc = a.n_chunks;  // <= 256 (fa_plan: one chunk per CTA of a wave at most; merge: checked)
     const int      dv  = threadIdx.x;
-    const float *  src = a.part_acc + (int64_t) row * nc * kD + dv;
+    const float *  src = a.part_acc + (int64_t) row * a.acc_row + dv;
+    const int64_t  ac  = a.acc_chunk, mc = a.ms_chunk;
     // the first kPre chunks' partial outputs do not depend on the (max, sum) records: in flight with them
     constexpr int kPre = 32;
     float         pre[kPre];
 #pragma unroll
-    for (int c = 0; c < kPre; c++) pre[c] = c < nc ? __ldcg(src + (int64_t) c * kD) : 0.0f;
+    for (int c = 0; c < kPre; c++) pre[c] = c < nc ? __ldcg(src + c * ac) : 0.0f;
     if (threadIdx.x < 32) {
         float m = -INFINITY;
         for (int c = threadIdx.x; c < nc; c += 32) {
-            const float2 v = ms[c];
+            const float2 v = ms[c * mc];
             if (v.y != 0.0f) m = fmaxf(m, v.x);
         }
 #pragma unroll
@@ -1175,7 +1184,7 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const FaArgs a) {
     __syncthreads();
     const float Mf = mf_s;
     for (int c = threadIdx.x; c < nc; c += blockDim.x) {
-        const float2 v = ms[c];
+        const float2 v = ms[c * mc];
         w_s[c]         = v.y != 0.0f ? exp2f(v.x - Mf) : 0.0f;
         s_s[c]         = v.y;
     }
@@ -1192,8 +1201,13 @@ __global__ void __launch_bounds__(256) fa_combine_kernel(const FaArgs a) {
 #pragma unroll 8
     for (int c = kPre; c < nc; c++) {
         const float w = w_s[c];
-        acc           = fmaf(w, w != 0.0f ? src[(int64_t) c * kD] : 0.0f, acc);
+        acc           = fmaf(w, w != 0.0f ? src[c * ac] : 0.0f, acc);
         S             = fmaf(w, s_s[c], S);
+    }
+    if (a.parts_out) {  // an empty range leaves (-inf, 0) and zeros: skipped by the merge
+        if (dv == 0) a.rec_ms[row] = make_float2(Mf, S);
+        a.rec_acc[(int64_t) row * kD + dv] = acc;
+        return;
     }
     if (a.sinks) {
         const float sk2 = a.sinks[h] * kLog2e;
@@ -1328,7 +1342,7 @@ size_t fa_work_size(int num_sms, int R, int L, int Hkv) {
 }
 
 int fa_run(srhpm_ctx * ctx, const FaView & v, float scale, float max_bias, float softcap, void * wdata, size_t wsize,
-           cudaStream_t stream) {
+           cudaStream_t stream, void * rec) {
     const int  G   = v.H / v.Hkv;
     const int  R   = G * v.N;
     const Plan p   = fa_plan(ctx->num_sms, R, v.L, v.Hkv);
@@ -1380,6 +1394,22 @@ int fa_run(srhpm_ctx * ctx, const FaView & v, float scale, float max_bias, float
         a.part_acc        = reinterpret_cast<float *>(wdata);
         a.part_ms = reinterpret_cast<float2 *>(reinterpret_cast<uint8_t *>(wdata) + rows * kD * sizeof(float));
     }
+    a.ms_row    = p.n_chunks;
+    a.ms_chunk  = 1;
+    a.acc_row   = (int64_t) p.n_chunks * kD;
+    a.acc_chunk = kD;
+    if (rec) {
+        // record set of this KV range: {max, sum} per row, then the rows' unnormalized outputs; sinks belong to the
+        // merge of all ranges
+        a.parts_out = 1;
+        a.sinks     = nullptr;
+        a.rec_ms    = reinterpret_cast<float2 *>(rec);
+        a.rec_acc   = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(rec) + fa_part_ms_bytes(v.H, v.N));
+        if (p.n_chunks == 1) {  // the one chunk's record is the range's record
+            a.part_ms  = a.rec_ms;
+            a.part_acc = a.rec_acc;
+        }
+    }
     a.status = ctx->d_status;
     a.q8mode = ctx->q8_0_act_mode;
 
@@ -1428,6 +1458,36 @@ int fa_run(srhpm_ctx * ctx, const FaView & v, float scale, float max_bias, float
         case 32: return launch_fa<32>(ctx, a, mk128, mk32, mv, stream);
         default: return launch_fa<48>(ctx, a, mk128, mk32, mv, stream);
     }
+}
+
+// record set: {max, sum} pairs [H * N] padded to 16 bytes, then acc [H * N][256]
+size_t fa_part_ms_bytes(int64_t H, int64_t N) { return ((size_t) (H * N) * sizeof(float2) + 15) / 16 * 16; }
+size_t fa_part_bytes(int64_t H, int64_t N) { return fa_part_ms_bytes(H, N) + (size_t) (H * N) * kD * sizeof(float); }
+
+int fa_merge_run(srhpm_ctx * ctx, const void * parts, int n_parts, int N, int H, const float * sinks, float * dst,
+                 int64_t dnb1, int64_t dnb2, cudaStream_t stream) {
+    // one "KV head" holding every head: row = h * N + t, as in the record sets
+    const int64_t rows = (int64_t) H * N;
+    const size_t  set  = fa_part_bytes(H, N);
+    FaArgs        a    = {};
+    a.N         = N;
+    a.H         = H;
+    a.G         = H;
+    a.R         = H * N;
+    a.Hkv       = 1;
+    a.n_chunks  = n_parts;
+    a.part_ms   = reinterpret_cast<float2 *>(const_cast<void *>(parts));
+    a.part_acc  = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(const_cast<void *>(parts)) + fa_part_ms_bytes(H, N));
+    a.ms_row    = 1;
+    a.ms_chunk  = (int64_t) (set / sizeof(float2));
+    a.acc_row   = kD;
+    a.acc_chunk = (int64_t) (set / sizeof(float));
+    a.sinks     = sinks;
+    a.dst       = dst;
+    a.dnb1      = dnb1;
+    a.dnb2      = dnb2;
+    a.status    = ctx->d_status;
+    return launch_combine(ctx, a, stream);
 }
 
 }  // namespace srhpm

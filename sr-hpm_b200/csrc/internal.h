@@ -76,8 +76,15 @@ struct FaView {
     int64_t         dnb1, dnb2;
 };
 size_t fa_work_size(int num_sms, int R, int L, int Hkv);
+// rec != null: write this KV range's record set (fa_part_bytes(H, N): float2 {max, sum}[H * N] padded to
+// fa_part_ms_bytes(H, N), then f32 [H * N][256] unnormalized outputs; row h * N + t) instead of dst, without sinks
 int    fa_run(srhpm_ctx * ctx, const FaView & v, float scale, float max_bias, float softcap, void * wdata,
-              size_t wsize, cudaStream_t stream);
+              size_t wsize, cudaStream_t stream, void * rec = nullptr);
+size_t fa_part_ms_bytes(int64_t H, int64_t N);
+size_t fa_part_bytes(int64_t H, int64_t N);
+// merge of n_parts consecutive record sets (<= 256), then sinks and normalization into dst f32 [256][H][N]
+int    fa_merge_run(srhpm_ctx * ctx, const void * parts, int n_parts, int N, int H, const float * sinks, float * dst,
+                    int64_t dnb1, int64_t dnb2, cudaStream_t stream);
 
 // accept.cu: greedy acceptance (argmax of the target logits, longest accepted prefix)
 size_t argmax_work_size(int num_sms, int n_vocab, int n_rows);

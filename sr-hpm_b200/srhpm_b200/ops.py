@@ -267,6 +267,52 @@ class Context:
                                               _stream_ptr(stream)), "srhpm_flash_attn_ext")
         return out
 
+    # ---- attention split over the KV range across devices ------------------------------------------------------
+    def flash_attn_part_size(self, H, N):
+        """Bytes of one record set of srhpm_flash_attn_ext_partial for H heads and N query tokens."""
+        return int(self.lib.srhpm_flash_attn_part_size(H, N))
+
+    def flash_attn_ext_partial(self, q, k, v, kv_type, mask=None, scale=1.0, max_bias=0.0, softcap=0.0, out=None,
+                               stream=None, work=None):
+        """The record set of this KV range (k / v uint8 [Hkv, range tokens, row bytes], mask f16 [N', range tokens]
+        or [ne2, N', range tokens]; a range of 0 tokens is allowed): uint8 [flash_attn_part_size(H, N)] on the
+        device, for flash_attn_merge."""
+        H, N, D = q.shape
+        nbytes = self.flash_attn_part_size(H, N)
+        if out is None:
+            out = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+        assert out.dtype == torch.uint8 and out.numel() >= nbytes and out.data_ptr() % 16 == 0
+        qv, kvv, vv, mv, _, _ = self._fa_views(q, k, v, kv_type, mask, None, None)
+        ws = 0
+        if k.shape[1] > 0:
+            st, ws = self.flash_attn_ext_work_size(q, k, v, kv_type)
+            L.check(st, "srhpm_flash_attn_ext_work_size")
+        buf = work if work is not None else self.work(ws)
+        L.check(self.lib.srhpm_flash_attn_ext_partial(self.handle, ctypes.byref(qv), ctypes.byref(kvv),
+                                                      ctypes.byref(vv), ctypes.byref(mv) if mv is not None else None,
+                                                      scale, max_bias, softcap, ctypes.c_void_p(out.data_ptr()),
+                                                      ctypes.c_void_p(buf.data_ptr()), buf.numel(),
+                                                      _stream_ptr(stream)), "srhpm_flash_attn_ext_partial")
+        return out
+
+    def flash_attn_merge(self, parts, n_parts, H, N, sinks=None, out=None, stream=None):
+        """Merge n_parts record sets stored one after another in `parts` (uint8, e.g. gathered from all devices in
+        KV order), add the sinks and normalize: out f32 [N, H, 256], as flash_attn_ext over the whole range."""
+        assert parts.dtype == torch.uint8 and parts.is_contiguous()
+        assert parts.numel() >= n_parts * self.flash_attn_part_size(H, N)
+        if out is None:
+            out = torch.empty((N, H, 256), dtype=torch.float32, device=parts.device)
+        ov = _tensor_view(out, L.F32, [out.shape[2], out.shape[1], out.shape[0]],
+                          [4, out.stride(1) * 4, out.stride(0) * 4])
+        sv = None
+        if sinks is not None:
+            assert sinks.dtype == torch.float32 and sinks.dim() == 1 and sinks.stride(0) == 1
+            sv = _tensor_view(sinks, L.F32, [sinks.shape[0]], [4])
+        L.check(self.lib.srhpm_flash_attn_merge(self.handle, ctypes.c_void_p(parts.data_ptr()), n_parts,
+                                                ctypes.byref(sv) if sv is not None else None, ctypes.byref(ov),
+                                                _stream_ptr(stream)), "srhpm_flash_attn_merge")
+        return out
+
     # ---- greedy acceptance ------------------------------------------------------------------------------------------
     def sample_and_accept_n(self, logits, draft, relax=0.0, stream=None, work=None):
         """common_sampler_sample_and_accept_n (greedy): logits f32 [>= n_draft + 1, n_vocab] (rows = positions),

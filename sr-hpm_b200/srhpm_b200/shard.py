@@ -4,7 +4,9 @@ Output rows of a weight matrix are independent, so the verify GEMM shards by row
 matrix between its CPU and GPU (patch/srhpm.patch:6497-6529): rank j computes rows [rows*j/world, rows*(j+1)/world)
 and the slices are all-gathered. Row-parallel layers (attention output, FFN down) shard K on 256-column super-block
 boundaries and sum the partial products. The head shards the vocabulary; the acceptance merges per-shard argmax
-records (srhpm_argmax_shard / srhpm_accept_merge). Attention shards by KV head.
+records (srhpm_argmax_shard / srhpm_accept_merge). Attention shards by KV head, or by KV token range when there
+are more ranks than KV heads (each rank's (max, sum, acc) records are all-gathered and merged, as the reference
+merges the records of its KV chunks, patch/srhpm.patch:779-823).
 
 This module holds the index arithmetic and the gather layout; the collectives are torch.distributed calls made by the
 caller (NCCL on GPUs, gloo in the CPU tests).
@@ -36,6 +38,16 @@ def kv_heads(n_kv, world, rank):
         raise ValueError(f"{n_kv} KV heads do not split over {world} ranks")
     per = n_kv // world
     return per * rank, per * (rank + 1)
+
+
+KV_TILE = 128  # tokens per attention tile
+
+
+def kv_range(L, world, rank):
+    """KV tokens [t0, t1) of a split-K attention shard: whole 128-token tiles, balanced (tile counts differ by at
+    most one), the last range ending at L; a rank gets an empty range when there are fewer tiles than ranks."""
+    tiles = -(-L // KV_TILE)
+    return min(L, tiles * rank // world * KV_TILE), min(L, tiles * (rank + 1) // world * KV_TILE)
 
 
 def k_columns(blocks, blk, bpb, k0, k1):
