@@ -509,7 +509,7 @@ def run_gpu(args):
 
 
 def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0):
-    """BASELINE config 4 on `world` GPUs: the same 27B-class verify step in Megatron tensor parallelism (column-
+    """The 27B-class verify step (k = 8, f16 KV of 2048 tokens) on `world` GPUs in Megatron tensor parallelism (column-
     parallel QKV / gate|up / head, row-parallel O / down with an NCCL all-reduce after each, KV heads split or
     replicated per rank, vocabulary-sharded acceptance). Every rank holds 1/world of the weights (random blocks) and
     its KV heads' cache; the step (kernels + 129 collectives) is one CUDA graph; time = max over ranks."""
@@ -565,7 +565,7 @@ def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0
 
 
 def measure_attention(ctx, dev, peak, reps=20, lengths=(8192, 32768, 131072)):
-    """8 query rows, 24 query heads, 4 KV heads, head_dim 256, causal mask among the draft rows,
+    """Verify attention: 8 query rows, 24 query heads, 4 KV heads, head_dim 256, causal mask among the draft rows,
     q8_0 K/V (N(0,1) before quantization) of L past tokens, Q N(0,1) / 16. Timed as CUDA-graph replays over copies
     of the KV cache that together exceed L2."""
     import torch
@@ -621,10 +621,11 @@ def measure_attention(ctx, dev, peak, reps=20, lengths=(8192, 32768, 131072)):
 
 
 def measure_attention_split(ctx, dev, rank, world, peak, reps=20, lengths=(8192, 32768, 131072)):
-    """BASELINE config 3 on `world` GPUs, split over the KV range: rank j holds tokens shard.kv_range(L, world, j) of
-    the 4 KV heads' q8_0 cache; one call = the partial records of its range, an NCCL all-gather of the record sets
-    (24 * 8 * 1032 bytes per rank) and the merge, all in one CUDA graph over copies of the rank's range that together
-    exceed L2. Time = max over ranks; GB/s counts the whole cache once (plus Q and O), as on one GPU."""
+    """The verify attention of measure_attention on `world` GPUs, split over the KV range: rank j holds tokens
+    shard.kv_range(L, world, j) of the 4 KV heads' q8_0 cache; one call = the partial records of its range, an NCCL
+    all-gather of the record sets (24 * 8 * 1032 bytes per rank) and the merge, all in one CUDA graph over copies of
+    the rank's range that together exceed L2. Time = max over ranks; GB/s counts the whole cache once (plus Q and O),
+    as on one GPU."""
     import torch
     import torch.distributed as dist
     import srhpm_b200 as S
@@ -689,7 +690,7 @@ def measure_attention_split(ctx, dev, rank, world, peak, reps=20, lengths=(8192,
 
 
 def measure_accept(ctx, dev, reps=50):
-    """Greedy acceptance over the BASELINE 27B head: logits f32 [9, 151936] (k = 8), all drafted tokens accepted
+    """Greedy acceptance over the 27B-class head: logits f32 [9, 151936] (k = 8), all drafted tokens accepted
     (the longest scan)."""
     import torch
     V, k = 151936, 8
@@ -738,7 +739,7 @@ def step_bytes_27b(cfg, n_past, n):
 
 
 def measure_step_27b(ctx, dev, peak, ks=(2, 4, 8), kv_type=None, n_past=2048, reps=10, seed=0):
-    """a whole verify step of the synthetic 27B-class decoder (64 layers, d 5120, FFN 17408,
+    """A whole verify step of the synthetic 27B-class decoder (64 layers, d 5120, FFN 17408,
     24 / 4 heads of 256, full attention every 4th layer and a 4096-token window elsewhere, vocab 151936; Q4_K attention
     and FFN-down, Q3_K gate / up, Q6_K head; random-init GGUF blocks) over a KV cache of n_past tokens, 1 accepted +
     k drafted tokens, greedy acceptance. CUDA-graph replays; steps/s and bytes / time."""

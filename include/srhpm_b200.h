@@ -202,7 +202,7 @@ int srhpm_accept_merge(srhpm_ctx * ctx, const srhpm_argmax_record * recs, int n_
 int srhpm_get_rows(srhpm_ctx * ctx, const srhpm_tensor * table, const int32_t * ids, int n, float * out, void * stream);
 int srhpm_add_rms_norm(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y, int n,
                        int64_t d, void * stream);
-/* Residual add + RMSNorm fused with the activation quantization of the GEMM that consumes y (the SURVEY's fused
+/* Residual add + RMSNorm fused with the activation quantization of the GEMM that consumes y (a fused GEMM
  * prologue): x += delta (delta may be NULL), y = x / sqrt(mean(x^2) + eps) * w as srhpm_add_rms_norm, and the
  * activation records of y for the product with W_next (its type, rows and K = d: ne = [d, rows]) are written into
  * wdata (sized by srhpm_mul_mat_work_size(W_next, X[d, n])), bit-identical to what srhpm_mul_mat's own quantizer
@@ -229,7 +229,7 @@ int srhpm_swiglu_quant(srhpm_ctx * ctx, const float * gate, const float * up, in
  * y = x / sqrt(mean(x^2) + eps) * w. epochs: this rank's uint32 [2][16] counters, zeroed once. n <= 16, world <= 8,
  * d a multiple of 4 and <= 16384; x, w, y 16-byte aligned. The two slots alternate (O, down): a slot is rewritten only
  * after the other slot's barrier has passed on every rank. Every rank must make the same sequence of calls. No
- * counterpart in the reference (it runs on one device); the SURVEY's config 4 all-reduce after O and down. */
+ * counterpart in the reference (it runs on one device): the tensor-parallel decoder's all-reduce after O and down. */
 size_t srhpm_allreduce_buffer_size(int64_t d);
 int srhpm_add_rms_norm_allreduce(srhpm_ctx * ctx, float * x, const uint64_t * peer_buffers, int world, int rank,
                                  int slot, uint32_t * epochs, const float * w, float eps, float * y, int n, int64_t d,

@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(256) swiglu_q8K_kernel(const float * __restric
     q8K_store_record(qv, dv, recs + (size_t) sb * rec_bytes(false, NT), t, NT, lane, perm);
 }
 
-// residual add + RMSNorm fused with the activation quantizer of the GEMM that consumes y (the SURVEY's fused
+// residual add + RMSNorm fused with the activation quantizer of the GEMM that consumes y (a fused GEMM
 // prologue): CTA t < N: x += delta; y = x / sqrt(mean(x^2) + eps) * w (as add_rms_norm); the row of y is staged in
 // shared memory and each warp quantizes super-blocks of it into the GEMM's activation records exactly as
 // quant_q8K_kernel does (same functions); CTAs N..NT-1 write the zero padding rows; CTA 0 zeroes the split-K counters.

@@ -17,7 +17,7 @@ from .ops import QuantTensor, _tensor_view, blck_size, f32_rows_view, quantize_c
 
 
 class DecoderConfig:
-    """Architecture of the synthetic decoder (defaults: the BASELINE 27B-class model)."""
+    """Architecture of the synthetic decoder (defaults: the 27B-class model: 64 layers, d 5120, FFN 17408)."""
 
     def __init__(self, n_layer=64, d=5120, n_ff=17408, H=24, Hkv=4, hd=256, n_vocab=151936, base=1e6, eps=1e-6,
                  window=4096, full_every=4, kv_type=L.F16, types=None):
@@ -160,7 +160,7 @@ class TensorParallel:
     fused=True (default): the row-parallel O and down GEMMs write their partial sums into a symmetric buffer (torch
     symmetric memory: every rank's buffer mapped on every rank), and the next RMSNorm sums the ranks' rows itself
     over NVLink peer loads after a flag barrier (srhpm_add_rms_norm_allreduce): no separate collective launch.
-    fused=False: an NCCL all-reduce after each of those GEMMs (the SURVEY's 128 per step). The vocabulary shards'
+    fused=False: an NCCL all-reduce after each of those GEMMs (128 per step for 64 layers). The vocabulary shards'
     argmax records are all-gathered with NCCL before the acceptance either way. All of it is captured in the step's
     CUDA graph."""
 

@@ -11,7 +11,7 @@ from srhpm_b200 import _lib as L
 
 pytestmark = pytest.mark.gpu
 
-VOCAB = 151936  # the BASELINE 27B target's vocabulary
+VOCAB = 151936  # the 27B-class target's vocabulary
 
 
 def logits_with_winners(rng, rows, V, margin=0.5):

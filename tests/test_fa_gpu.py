@@ -159,8 +159,8 @@ def test_fa_q8_0_per_head_mask_and_masked_rows(ctx):
     assert rel_l2(got, exp) < TOL
 
 
-def test_fa_q8_0_config3_full_size(ctx):
-    """The BASELINE attention shape at L = 131072 (Q [256, 8, 24], q8_0 K/V [256, L, 4], causal mask among the 8
+def test_fa_q8_0_L131072_full_size(ctx):
+    """The verify attention shape at L = 131072 (Q [256, 8, 24], q8_0 K/V [256, L, 4], causal mask among the 8
     draft rows): the kernel runs the whole problem; the f64 oracle checks two of the four KV heads."""
     rng = np.random.default_rng(15)
     H, Hkv, N, L = 24, 4, 8, 131072
