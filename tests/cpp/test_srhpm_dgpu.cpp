@@ -91,11 +91,15 @@ void test_gpu(const Dgpu & d) {
     CHECK(tot > 0 && fr <= tot);
     std::mt19937 rng(3);
     const int64_t K = 1024, nrows = 300, xs = K + 8, ys = nrows + 5;  // strided x and dst
+    // the library keys its copies by the rows' address, as the reference does: every tensor stays alive (and at its
+    // address) until the end, so no two tensors share a key
+    std::vector<std::vector<uint8_t>> tensors(2);
     for (int kind : { 0, 1 }) {
         const int                type = kind == 0 ? SRHPM_TYPE_IQ4_XS : SRHPM_TYPE_Q3_K;
         const size_t             rowb = srhpm_row_size(type, K);
         const std::vector<float> wf   = randn(rng, (size_t) (nrows * K), 0.02f);
-        std::vector<uint8_t>     wq(rowb * nrows);
+        std::vector<uint8_t> &   wq   = tensors[kind];
+        wq.resize(rowb * nrows);
         CHECK(srhpm_quantize_chunk(type, wf.data(), wq.data(), 0, nrows, K, nullptr) == wq.size());
         const size_t held0 = d.pinned();
         for (int M = 1; M <= 8; M++) {
