@@ -445,6 +445,28 @@ class VerifyStep:
                 if st != L.OK:
                     raise L.SrhpmError(st, "srhpm_" + name, self.lib)
 
+    def set_past(self, n_past):
+        """Move the step to cache position n_past: new positions, masks and attention ranges, the same buffers. The
+        prebuilt calls are rebuilt on the host; a CUDA graph captured before must be captured again."""
+        cap = self.kcache[0].shape[0]
+        if n_past < 0 or n_past + self.n > cap:
+            raise ValueError(f"positions {n_past}..{n_past + self.n - 1} do not fit a cache of {cap} tokens")
+        torch.cuda.synchronize(self.w.device)  # the previous calls may still read the masks about to be replaced
+        self.n_past = n_past
+        self.pos.copy_(torch.arange(n_past, n_past + self.n, dtype=torch.int32))
+        self._keep = []
+        self._build()
+
+    def advance(self, n_emitted):
+        """The next step of a decode loop: n_emitted = len(accepted()) of this step (its accepted drafted tokens + 1).
+        The cache then holds valid rows up to n_past + n_emitted (this step's first token and the drafted tokens it
+        accepted); the rows after them, written for rejected drafted tokens, are hidden by the causal mask and
+        overwritten by the next step's KV store. That is the reference server's truncate-on-rollback
+        (n_rollback = k + 1 - accepted, patch/srhpm.patch:7202) without a separate pass."""
+        if not 1 <= n_emitted <= self.n:
+            raise ValueError(f"a step of {self.n} tokens emits 1..{self.n} ids, not {n_emitted}")
+        self.set_past(self.n_past + n_emitted)
+
     def set_tokens(self, ids, draft):
         """Inputs of the step: ids int [n] (accepted token + drafted tokens), draft int [n - 1]."""
         self.ids.copy_(torch.as_tensor(ids, dtype=torch.int32))

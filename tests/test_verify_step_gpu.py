@@ -374,3 +374,40 @@ def test_verify_step_single_token(ctx):
     srt = np.sort(logits_o[0])
     if srt[-1] - srt[-2] > 1e-2:
         assert step.accepted() == acc_o
+
+
+@pytest.mark.parametrize("kv_type", [L.F16, L.Q8_0])
+def test_verify_step_advance_matches_a_step_built_there(ctx, kv_type):
+    """Decode-loop bookkeeping: after a step, advance(len(accepted())) moves it to the next cache position (the rows
+    written for rejected drafted tokens are hidden, then overwritten: the reference server's truncate-on-rollback).
+    The moved step computes exactly what a step built at that position computes on the same cache contents: the same
+    logits, accepted ids and cache rows, bit for bit (the same kernels and plans on the same inputs). The sliding
+    window's first visible position moves with it (window 40 at position ~100)."""
+    cfg = small_cfg(kv_type)
+    w = V.host_weights(cfg, seed=51)
+    rowb = 272 if kv_type == L.Q8_0 else 512
+    cap, n_past, n = 160, 100, 5
+    kc, vc = _caches(cfg, cap, n_past, rowb, 52)
+    dev_w = V.DeviceWeights.from_host(cfg, w)
+    dkc = [torch.from_numpy(a).cuda() for a in kc]
+    dvc = [torch.from_numpy(a).cuda() for a in vc]
+    rng = np.random.default_rng(53)
+    ids = [int(i) for i in rng.integers(0, cfg.n_vocab, n)]
+    step = _run_step(ctx, cfg, dev_w, dkc, dvc, ids, ids[1:], n_past)
+    emitted = step.accepted()
+    kc2, vc2 = [a.clone() for a in dkc], [a.clone() for a in dvc]
+    step.advance(len(emitted))
+    assert step.n_past == n_past + len(emitted)
+    ids2 = [emitted[-1]] + [int(i) for i in rng.integers(0, cfg.n_vocab, n - 1)]
+    step.set_tokens(ids2, ids2[1:])
+    step.run()
+    torch.cuda.synchronize()
+    ctx.check()
+    fresh = _run_step(ctx, cfg, dev_w, kc2, vc2, ids2, ids2[1:], n_past + len(emitted))
+    assert torch.equal(step.logits, fresh.logits)
+    assert step.accepted() == fresh.accepted()
+    assert all(torch.equal(a, b) for a, b in zip(dkc + dvc, kc2 + vc2))
+    with pytest.raises(ValueError):
+        step.set_past(cap - n + 1)  # past the end of the cache
+    with pytest.raises(ValueError):
+        step.advance(0)  # a step emits at least one id
