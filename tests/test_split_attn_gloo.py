@@ -101,7 +101,8 @@ def test_kv_range_tiles_the_cache(L, world):
 
 class OracleCtx:
     """Stand-in for srhpm_b200.Context on CPU tensors: the record set of a KV range in the C ABI's byte layout
-    ({max, sum} f32 pairs [H * N] padded to 16 bytes, then f32 acc [H * N][D]) computed by the oracle, and the merge of such sets; the device kernels behind the same calls are tested on the GPU."""
+    ({max, sum} f32 pairs [H * N] padded to 16 bytes, then f32 acc [H * N][D]) computed by the oracle, and the
+    merge of such sets. The device kernels behind the same calls are tested on the GPU."""
 
     def __init__(self, D):
         self.D = D
