@@ -187,6 +187,40 @@ def test_oracle_attention_vs_reference_fa_gqa(ref, kv_type, extras):
     assert rel_l2(b, a) < 1e-5
 
 
+@pytest.mark.parametrize("kv_type", [O.F16, O.Q8_0])
+@pytest.mark.parametrize("extras", ["plain", "sinks", "softcap", "alibi"])
+def test_oracle_attention_records_and_merge(kv_type, extras):
+    """The record form (attention_partial over token ranges + attention_merge, the reference's chunk records and
+    merge, patch/srhpm.patch:779-823): one range merged is the pinned single pass bit for bit; any split of the range,
+    with empty ranges and a range the mask hides, agrees with it to f64 rounding."""
+    rng = np.random.default_rng(37)
+    q, k, v, mask = _fa_inputs(kv_type, rng)
+    H, N, D = q.shape
+    L = 160
+    mask = mask.copy()
+    mask[:, 40:80] = 0xFC00  # -inf: the range [40, 80) is hidden from every row
+    kw = dict(scale=1.0, max_bias=0.0, softcap=0.0)
+    sinks = None
+    if extras == "sinks":
+        sinks = rng.standard_normal(H).astype(np.float32)
+    elif extras == "softcap":
+        kw.update(scale=4.0, softcap=20.0)
+    elif extras == "alibi":
+        kw.update(max_bias=8.0)
+    whole = O.attention(q, kv_type, k, v, D, L, 2, mask=mask, sinks=sinks, **kw)
+    for cuts in ([0, L], [0, 40, 80, L], [0, 0, 33, 128, 128, L], [0, 1, L]):
+        recs = [O.attention_partial(q, kv_type, k, v, D, L, 2, a, b, mask=mask, **kw)
+                for a, b in zip(cuts[:-1], cuts[1:])]
+        got = O.attention_merge(*(np.stack([r[i] for r in recs]) for i in range(3)), sinks=sinks)
+        if len(cuts) == 2:
+            assert np.array_equal(got, whole)
+        else:
+            assert np.abs(got - whole).max() <= 1e-12 * np.abs(whole).max()
+    # a range with no finite score has sum 0
+    m, s_, acc = O.attention_partial(q, kv_type, k, v, D, L, 2, 40, 80, mask=mask, **kw)
+    assert np.all(s_ == 0) and np.all(acc == 0) and np.all(np.isneginf(m))
+
+
 def test_accept_semantics():
     V = 50
     lg = np.zeros((5, V), np.float32)
