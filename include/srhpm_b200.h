@@ -2,7 +2,7 @@
  *
  * The path verifies 1 + k drafted tokens against a quantized dense decoder in one pass:
  *   - small-batch quantized matmul (ggml_mul_mat with ne[1] = 1..16 on Q4_K / Q5_K / Q6_K / Q3_K / IQ4_XS / Q8_0)
- *   - multi-query attention over an f16 or q8_0 KV cache (ggml_flash_attn_ext with 2..8 query rows)
+ *   - multi-query attention over an f16 or q8_0 KV cache (ggml_flash_attn_ext with 1..16 query rows)
  *   - greedy longest-prefix acceptance over the target logits
  *
  * Conventions (all entry points):

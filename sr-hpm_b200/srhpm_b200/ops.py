@@ -2,7 +2,7 @@
 
     Context.mul_mat(W, X)          ggml_mul_mat(W, X) with ne[1] = N = 1..16 on a GGUF-quantized W
                                    (reference: tensor_traits_srv::compute_forward, patch/srhpm.patch:6400-6611)
-    Context.flash_attn_ext(...)    ggml_flash_attn_ext with 2..8 query rows over an f16 / q8_0 KV cache
+    Context.flash_attn_ext(...)    ggml_flash_attn_ext with 1..16 query rows over an f16 / q8_0 KV cache
                                    (reference: ggml_compute_forward_flash_attn_ext_gqa_small, patch/srhpm.patch:581-824)
     Context.sample_and_accept_n()  greedy longest-prefix acceptance (reference: common_sampler_sample_and_accept_n,
                                    patch/srhpm.patch:1-37)
