@@ -4,6 +4,10 @@
                                    (reference: tensor_traits_srv::compute_forward, patch/srhpm.patch:6400-6611)
     Context.flash_attn_ext(...)    ggml_flash_attn_ext with 1..16 query rows over an f16 / q8_0 KV cache
                                    (reference: ggml_compute_forward_flash_attn_ext_gqa_small, patch/srhpm.patch:581-824)
+    Context.flash_attn_ext_partial / flash_attn_merge
+                                   the same attention split over KV token ranges: one (max, sum, acc) record set per
+                                   range, merged after a gather (reference: its chunk records and their merge,
+                                   patch/srhpm.patch:779-823, with devices as the chunks)
     Context.sample_and_accept_n()  greedy longest-prefix acceptance (reference: common_sampler_sample_and_accept_n,
                                    patch/srhpm.patch:1-37)
 
