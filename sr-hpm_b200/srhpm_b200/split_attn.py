@@ -17,7 +17,8 @@ class SplitKAttention:
 
     __call__(q, k, v, kv_type, mask, ...) takes this rank's slices: k / v uint8 [Hkv, range tokens, row bytes] and
     the mask's columns of the range (f16 [N', range tokens]); q and sinks whole. Returns f32 [N, H, 256] on every
-    rank. Buffers are allocated once, so the call can be captured in a CUDA graph."""
+    rank, in the same buffer at every call (copy it to keep it past the next call). Buffers are allocated once, so
+    the call can be captured in a CUDA graph. Every rank of the group must make the same calls in the same order."""
 
     def __init__(self, ctx, rank, world, H, N, device, group=None):
         self.ctx, self.rank, self.world, self.H, self.N, self.group = ctx, rank, world, H, N, group
