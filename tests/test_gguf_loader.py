@@ -156,3 +156,33 @@ def test_split_types_detected(tmp_path):
     assert gf.tensors["blk.0.attn_v.weight"].type == S.Q6_K
     assert gf.tensors["blk.0.attn_q.weight"].type == cfg.types["qkv"]
     gf.close()
+
+
+def test_version_2_reads_like_3_and_others_are_refused(model, tmp_path):
+    """GGUF v2 has v3's layout (64-bit counts and string lengths; v3 only added big-endian files): the same file with
+    its version field set to 2 parses to the same metadata, tensor infos and bytes. Version 1 (32-bit counts) and
+    unknown versions are refused, and so is a file cut inside its header."""
+    import struct
+    cfg, w, path = model
+    raw = bytearray(open(path, "rb").read())
+    a = G.GGUFFile(path)
+    for ver, ok in ((2, True), (1, False), (4, False)):
+        raw[4:8] = struct.pack("<I", ver)
+        p = tmp_path / f"v{ver}.gguf"
+        p.write_bytes(bytes(raw))
+        if ok:
+            b = G.GGUFFile(p)
+            assert b.version == 2 and b.kv == a.kv and b.data_start == a.data_start
+            assert {n: (t.ne, t.type, t.offset) for n, t in b.tensors.items()} == \
+                   {n: (t.ne, t.type, t.offset) for n, t in a.tensors.items()}
+            assert np.array_equal(b.data("output.weight"), a.data("output.weight"))
+            b.close()
+        else:
+            with pytest.raises(ValueError):
+                G.GGUFFile(p)
+    raw[4:8] = struct.pack("<I", 3)
+    cut = tmp_path / "cut.gguf"
+    cut.write_bytes(bytes(raw[:200]))  # inside the key-value section
+    with pytest.raises(ValueError):
+        G.GGUFFile(cut)
+    a.close()
