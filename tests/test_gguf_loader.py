@@ -21,9 +21,12 @@ def small_cfg():
                            window=0, full_every=1)
 
 
-def write_decoder_gguf(path, cfg, w, arch="qwen2", qkv_split_types=False):
-    """A llama.cpp-style dense decoder file from host_weights `w` (fused QKV rows split back into attn_q / k / v)."""
+def write_decoder_gguf(path, cfg, w, arch="qwen2", qkv_split_types=False, extra_u32=None):
+    """A llama.cpp-style dense decoder file from host_weights `w` (fused QKV rows split back into attn_q / k / v);
+    extra_u32: more uint32 metadata {key: value}."""
     wr = gguf_py.GGUFWriter(str(path), arch)
+    for key, val in (extra_u32 or {}).items():
+        wr.add_uint32(key, val)
     wr.add_block_count(cfg.n_layer)
     wr.add_embedding_length(cfg.d)
     wr.add_feed_forward_length(cfg.n_ff)
@@ -186,3 +189,21 @@ def test_version_2_reads_like_3_and_others_are_refused(model, tmp_path):
     with pytest.raises(ValueError):
         G.GGUFFile(cut)
     a.close()
+
+
+def test_sliding_window_metadata(tmp_path):
+    """`<arch>.attention.sliding_window` sets the window of the sliding layers; full attention then comes every 4th
+    layer unless `full_every` says otherwise; explicit arguments override the file."""
+    cfg = small_cfg()
+    w = V.host_weights(cfg, seed=9)
+    path = tmp_path / "swa.gguf"
+    write_decoder_gguf(path, cfg, w, extra_u32={"qwen2.attention.sliding_window": 4096})
+    gf = G.GGUFFile(path)
+    assert gf.kv["qwen2.attention.sliding_window"] == 4096
+    c = G.decoder_config(gf)
+    assert c.window == 4096 and c.full_every == 4
+    c2 = G.decoder_config(gf, window=0)
+    assert c2.window == 0 and c2.full_every == 1
+    c3 = G.decoder_config(gf, full_every=2)
+    assert c3.window == 4096 and c3.full_every == 2
+    gf.close()
