@@ -19,7 +19,9 @@ roofline: achieved = algorithmic bytes of the step / timed step time (the quanti
          against the measured HBM copy bandwidth; per-product times for the breakdown come from a second graph with
          CUDA events between the products, replayed after the timed region.
 cpu_baseline: the reference's own SRV kernels (compiled from its patch into oracle/_ref; Q8_0 has no SRV kernel,
-         so its share runs the restated stock path) on all host cores, full passes of the same workload.
+         so its share runs the restated stock path) on all host cores, full passes of the same workload. Beside the
+         attention and acceptance figures, the same shapes on the host: the reference's own grouped attention
+         function (oracle/_ref, all threads) and the oracle's acceptance (one thread).
 
 --impl reference runs that CPU implementation alone as the reference arm (rank 0 only).
 """
@@ -513,6 +515,12 @@ def run_gpu(args):
         if world == 1 and not args.no_attn:
             cfg["attention_q8_0"] = measure_attention(ctx, dev, peak)
             cfg["accept_k8_vocab151936"] = measure_accept(ctx, dev)
+            if not args.no_cpu:  # the same shapes on the host cores, beside the device figures
+                try:
+                    cfg["attention_q8_0_cpu_reference"] = cpu_attention_reference()
+                    cfg["accept_k8_vocab151936_cpu_port"] = cpu_accept_port()
+                except Exception as e:  # recorded beside the line rather than losing it
+                    cfg["attention_q8_0_cpu_reference"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
         if world == 1 and not args.no_step:
             from srhpm_b200 import _lib as L
             cfg["verify_step_27b_f16kv_2048"] = measure_step_27b(ctx, dev, peak)
@@ -728,6 +736,60 @@ def measure_attention_split(ctx, dev, rank, world, peak, reps=20, lengths=(8192,
         del graph, kv  # the graph holds NCCL calls: released before the process group
         torch.cuda.empty_cache()
     return out
+
+
+def cpu_attention_reference(lengths=(8192, 32768, 131072), target_s=6.0):
+    """The verify attention of measure_attention on the host cores, through the reference's own grouped attention
+    function (ggml_compute_forward_flash_attn_ext_gqa_small, compiled from its patch into oracle/_ref): the same
+    shapes and q8_0 cache, all host threads, repeated calls for about target_s seconds in all."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    import srhpm_b200 as S
+    ref = O.load_ref()
+    if ref is None:
+        return {"unavailable": "the reference kernels (oracle/_ref) are not built"}
+    H, Hkv, N, D = 24, 4, 8, 256
+    rng = np.random.default_rng(3)
+    nth = os.cpu_count() or 1
+    out = {}
+    for L in lengths:
+        q = (rng.standard_normal((H, N, D), dtype=np.float32) / np.float32(16)).astype(np.float32)
+        kv = [S.quantize_chunk(rng.standard_normal((Hkv * L, D), dtype=np.float32), S.Q8_0).reshape(Hkv, L, 272)
+              for _ in range(2)]
+        mask = np.zeros((N, L), np.float16)
+        for t in range(N):
+            mask[t, L - N + t + 1:] = -np.inf
+        m16 = mask.view(np.uint16)
+
+        def call():
+            O.ref_fa_gqa(q, O.Q8_0, kv[0], kv[1], D, L, Hkv, mask=m16, scale=1.0 / 16, nth=nth, lib=ref)
+
+        call()  # warm-up
+        reps, t0 = 0, time.perf_counter()
+        while reps < 1 or (time.perf_counter() - t0 < target_s / len(lengths) and reps < 100):
+            call()
+            reps += 1
+        us = (time.perf_counter() - t0) / reps * 1e6
+        nbytes = 2176 * L + 2 * H * N * D * 4
+        out[str(L)] = {"us": round(us, 1), "GBps": round(nbytes / (us * 1e-6) / 1e9, 2), "calls": reps,
+                       "threads": nth}
+        del kv
+    return out
+
+
+def cpu_accept_port(reps=20):
+    """Greedy acceptance of 8 drafted tokens over the 151936-token head on one host core, through the oracle's C
+    restatement (the reference's acceptance is upstream llama.cpp code, absent here): all drafted tokens accepted."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    rng = np.random.default_rng(5)
+    logits = rng.standard_normal((9, 151936), dtype=np.float32)
+    draft = np.argmax(logits[:8], axis=1).astype(np.int32)
+    O.accept(logits, draft)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.accept(logits, draft)
+    return {"us": round((time.perf_counter() - t0) / reps * 1e6, 1), "threads": 1, "kind": "port"}
 
 
 def measure_accept(ctx, dev, reps=50):
