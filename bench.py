@@ -47,6 +47,7 @@ TYPE_IDS = {"q4_K": 12, "q5_K": 13, "q6_K": 14, "q8_0": 8, "iq4_xs": 23, "q3_K":
 BLOCK = {12: (256, 144), 13: (256, 176), 14: (256, 210), 8: (32, 34), 23: (256, 136), 11: (256, 110)}
 NS = [2, 4, 8]
 SEED = 1234
+DATA_DESC = "synthetic (seeded N(0,0.02) weights quantized on the host, N(0,1) activations)"
 
 
 def row_bytes(t, K):
@@ -121,18 +122,30 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------------------------------
 # inputs
 
-def make_host_weights(ops):
+def make_host_weights(ops, quantize):
     """{(type, rows, K): packed blocks (numpy uint8 [rows, row_bytes])}: one f32 N(0, 0.02) matrix per shape (the
-    same matrix for every type, in shape order), quantized to each type the products use."""
-    import srhpm_b200 as S
+    same matrix for every type, in shape order), quantized to each type the products use by quantize(w, type): the
+    library's quantizer on the device arm, the oracle's round-to-nearest one on the reference arm (which loads
+    nothing of the product)."""
     rng = np.random.default_rng(SEED)
     out = {}
     shapes = sorted({(rows, K) for _, _, rows, K in ops}, key=lambda sh: SHAPES.index(sh) if sh in SHAPES else 99)
     for rows, K in shapes:
         w = rng.standard_normal((rows, K), dtype=np.float32) * np.float32(0.02)
         for t in sorted({t for _, t, r, k in ops if (r, k) == (rows, K)}):
-            out[(t, rows, K)] = S.quantize_chunk(w, t)
+            out[(t, rows, K)] = quantize(w, t)
     return out
+
+
+def product_quantizer():
+    import srhpm_b200 as S
+    return S.quantize_chunk
+
+
+def oracle_quantizer():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    return lambda w, t: O.quantize_rtn(t, w)
 
 
 def make_host_acts(ops):
@@ -214,7 +227,7 @@ def run_reference(args):
     import oracle as O
     ref = O.load_ref()
     ops = sweep_ops(args.only)
-    host_w = make_host_weights(ops)
+    host_w = make_host_weights(ops, oracle_quantizer())
     host_x = make_host_acts(ops)
     nth = os.cpu_count() or 1
     for _ in range(args.warmup):
@@ -229,7 +242,7 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t / args.steps * 1e3, 3),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8 x quantized (int32 sums)",
-        "data": "synthetic", "config": workload_config(ops, world),
+        "data": DATA_DESC, "config": workload_config(ops, world),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": nth, "kind": kind,
                          "sample": f"{args.steps} full passes of the workload; reference srv kernels build "
                                    f"{O.ref_variant() or 'none'} (Q8_0: restated stock path)"},
@@ -261,7 +274,7 @@ def run_gpu(args):
     dev = torch.device("cuda", local)
     ctx = S.Context(local)
     base_ops = sweep_ops(args.only)
-    host_w = make_host_weights(base_ops)
+    host_w = make_host_weights(base_ops, product_quantizer())
     host_x = make_host_acts(base_ops)
     # with a single product, rotate over copies of its matrix so that consecutive calls never hit L2
     ncopy = 1
@@ -484,6 +497,17 @@ def run_gpu(args):
         e2e_ms = float(tt.item())
     e2e_value = step_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
     ctx.check()
+    meas = {}
+    # the sharded step's gathered outputs against the same products whole on one GPU (after the timed regions)
+    sweep_par = None
+    if world > 1:
+        try:
+            sweep_par = sweep_parity_multi(ctx, dev, rank, world, ops, host_w, xs, y_dev, packed)
+        except Exception as e:  # recorded beside the sweep rather than losing its line
+            sweep_par = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+    n1 = None
+    if world == 1 and not args.only:
+        n1 = measure_sweep_n1(ctx, dev, shards, peak)
 
     step_tp = None
     if world > 1 and not args.no_step:  # every rank takes part (collectives inside the step)
@@ -491,53 +515,72 @@ def run_gpu(args):
             step_tp = measure_step_27b_tp(ctx, dev, rank, world)
         except Exception as e:  # recorded beside the sweep rather than losing its line
             step_tp = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
-    attn_split = None
+    attn_split = attn_heads = None
     if world > 1 and not args.no_attn:  # every rank takes part (an all-gather per call)
         try:
             attn_split = measure_attention_split(ctx, dev, rank, world, peak)
         except Exception as e:  # recorded beside the sweep rather than losing its line
             attn_split = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+        if 4 % world == 0:  # the 4 KV heads of config 3 split whole over 2 or 4 ranks
+            try:
+                attn_heads = measure_attention_kv_heads(ctx, dev, rank, world, peak)
+            except Exception as e:  # recorded beside the sweep rather than losing its line
+                attn_heads = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
     if rank == 0:
         cfg = workload_config(base_ops, world)
-        cfg["timed"] = "CUDA graph of one step, replayed" if graph is not None else "eager calls"
+        meas["timed"] = "CUDA graph of one step, replayed" if graph is not None else "eager calls"
         if step_tp is not None:
-            cfg["verify_step_27b_f16kv_2048_tp"] = step_tp
+            meas["verify_step_27b_f16kv_2048_tp"] = step_tp
         if attn_split is not None:
-            cfg["attention_q8_0_split_k"] = attn_split
+            meas["attention_q8_0_split_k"] = attn_split
+        if attn_heads is not None:
+            meas["attention_q8_0_kv_heads"] = attn_heads
+        if sweep_par is not None:
+            meas["sweep_parity_vs_1gpu"] = sweep_par
         if ncopy > 1:
-            cfg["copies_rotated"] = ncopy
-        cfg["per_type_gbs"] = group(lambda op: [k for k, v in TYPE_IDS.items() if v == op[1]][0])
-        cfg["per_N_gbs"] = group(lambda op: op[0])
-        cfg["per_shape_gbs"] = group(lambda op: f"{op[2]}x{op[3]}")
+            meas["copies_rotated"] = ncopy
+        meas["per_type_gbs"] = group(lambda op: [k for k, v in TYPE_IDS.items() if v == op[1]][0])
+        meas["per_N_gbs"] = group(lambda op: op[0])
+        meas["per_shape_gbs"] = group(lambda op: f"{op[2]}x{op[3]}")
         c1 = [i for i, op in enumerate(ops) if op == (4, 12, 17408, 5120)]
         if op_ms and c1:
-            cfg["q4_K_17408x5120_N4_us"] = round(sum(op_ms[i] for i in c1) / len(c1) * 1e3, 2)
+            meas["q4_K_17408x5120_N4_us_in_sweep"] = round(sum(op_ms[i] for i in c1) / len(c1) * 1e3, 2)
+        if world == 1 and not args.only:
+            meas["config1_q4_K_17408x5120_N4"] = measure_one_product(ctx, dev, host_w, host_x, (4, 12, 17408, 5120),
+                                                                     peak)
+            meas["sweep_N1"] = n1
         if world == 1 and not args.no_attn:
-            cfg["attention_q8_0"] = measure_attention(ctx, dev, peak)
-            cfg["accept_k8_vocab151936"] = measure_accept(ctx, dev)
+            meas["attention_q8_0"] = measure_attention(ctx, dev, peak)
+            meas["accept_k8_vocab151936"] = measure_accept(ctx, dev)
             if not args.no_cpu:  # the same shapes on the host cores, beside the device figures
                 try:
-                    cfg["attention_q8_0_cpu_reference"] = cpu_attention_reference()
-                    cfg["accept_k8_vocab151936_cpu_port"] = cpu_accept_port()
+                    meas["attention_q8_0_cpu_reference"] = cpu_attention_reference()
+                    meas["accept_k8_vocab151936_cpu_port"] = cpu_accept_port()
                 except Exception as e:  # recorded beside the line rather than losing it
-                    cfg["attention_q8_0_cpu_reference"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+                    meas["attention_q8_0_cpu_reference"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
         if world == 1 and not args.no_step:
             from srhpm_b200 import _lib as L
-            cfg["verify_step_27b_f16kv_2048"] = measure_step_27b(ctx, dev, peak)
-            cfg["verify_step_27b_q8kv_131072"] = measure_step_27b(ctx, dev, peak, ks=(8,), kv_type=L.Q8_0,
-                                                                  n_past=131072, reps=5)
+            meas["verify_step_27b_f16kv_2048"] = measure_step_27b(ctx, dev, peak)
+            meas["verify_step_27b_q8kv_131072"] = measure_step_27b(ctx, dev, peak, ks=(8,), kv_type=L.Q8_0,
+                                                                   n_past=131072, reps=5)
         cpu = None
         if world == 1 and not args.no_cpu:
             gbs, secs, passes, nth, kind, variant = cpu_sample(host_w, host_x, base_ops, args.cpu_seconds)
             cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": nth, "kind": kind,
                    "sample": f"{passes} full passes of the workload ({secs:.1f} s of CPU time); reference srv "
                              f"kernels build {variant}; Q8_0 (no srv kernel) through the restated stock path"}
+            # the baseline's own outputs against the device's outputs of the timed step, every row of every product
+            try:
+                meas["sweep_parity_vs_reference_kernels"] = cpu_parity(host_w, host_x, ops, y_dev, yoff)
+            except Exception as e:  # recorded beside the line rather than losing it
+                meas["sweep_parity_vs_reference_kernels"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "int8 x quantized (int32 exact sums, f32 scales)",
-            "data": "synthetic (seeded N(0,0.02) weights quantized on the host, N(0,1) activations)",
+            "data": DATA_DESC,
             "config": cfg,
+            "measurements": meas,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "kernel": "srv_gemm_kernel (+ activation quantizer, PDL-overlapped)",
@@ -557,26 +600,195 @@ def run_gpu(args):
     return 0
 
 
+def rel_l2(a, b):
+    """Relative L2 distance of a from b (numpy or torch, any shape), as a float."""
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    nb = float(np.linalg.norm(b))
+    return float(np.linalg.norm(a - b) / nb) if nb > 0 else float(np.linalg.norm(a - b))
+
+
+def graph_us(fn, calls, reps=20):
+    """Device time of one call of fn (which issues `calls` calls) from CUDA-graph replays: warm-up, capture, then
+    reps replays between CUDA events; returns microseconds per call."""
+    import torch
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            fn()
+    torch.cuda.synchronize()
+    graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * calls)
+    del graph
+    return us
+
+
+def measure_one_product(ctx, dev, host_w, host_x, op, peak):
+    """One product alone (config 1 = Q4_K 17408x5120, N = 4): calls rotated over copies of its matrix that
+    together exceed 300 MB (no call finds its weights in L2), graph-replayed; us per call and GB/s of its bytes."""
+    import torch
+    import srhpm_b200 as S
+    N, t, rows, K = op
+    ncopy = max(2, -(-300_000_000 // (rows * row_bytes(t, K))))
+    Ws = [S.QuantTensor.from_blocks(host_w[(t, rows, K)], t, rows, K, dev) for _ in range(ncopy)]
+    x = torch.from_numpy(host_x[(N, K)]).to(dev)
+    y = torch.empty((N, rows), dtype=torch.float32, device=dev)
+    ws = ctx.mul_mat_work_size(Ws[0], x)[1]
+    work = torch.empty(ws, dtype=torch.uint8, device=dev)
+    runs = [ctx.prepare_mul_mat(W, x, y, work) for W in Ws]
+
+    def fn():
+        for r in runs:
+            r()
+
+    us = graph_us(fn, len(runs))
+    ctx.check()
+    nbytes = op_bytes(t, rows, K, N)
+    gbs = nbytes / (us * 1e-6) / 1e9
+    del Ws, runs
+    torch.cuda.empty_cache()
+    return {"us": round(us, 2), "GBps": round(gbs, 1), "frac": round(gbs / peak, 4), "bytes": nbytes,
+            "copies_rotated": ncopy, "timed": "CUDA graph of the calls over the copies, replayed"}
+
+
+def measure_sweep_n1(ctx, dev, shards, peak):
+    """The sweep's 20 matrices at N = 1 (one activation row: plain decode beside the verify widths), one graph of
+    the 20 products; GB/s of their bytes."""
+    import torch
+    rng = np.random.default_rng(SEED + 2)
+    ops1 = [(1, t, rows, K) for (t, rows, K, c) in shards if c == 0]
+    xs = {K: torch.from_numpy(rng.standard_normal((1, K), dtype=np.float32)).to(dev) for K in {op[3] for op in ops1}}
+    ys = [torch.empty((1, rows), dtype=torch.float32, device=dev) for (_, t, rows, K) in ops1]
+    ws = max(ctx.mul_mat_work_size(shards[(t, rows, K, 0)][0], xs[K])[1] for (_, t, rows, K) in ops1)
+    work = torch.empty(ws, dtype=torch.uint8, device=dev)
+    runs = [ctx.prepare_mul_mat(shards[(t, rows, K, 0)][0], xs[K], y, work) for (_, t, rows, K), y in zip(ops1, ys)]
+
+    def fn():
+        for r in runs:
+            r()
+
+    us = graph_us(fn, 1)
+    ctx.check()
+    nbytes = sum(op_bytes(t, rows, K, 1) for (_, t, rows, K) in ops1)
+    gbs = nbytes / (us * 1e-6) / 1e9
+    return {"products": len(ops1), "us_per_pass": round(us, 1), "GBps": round(gbs, 1), "frac": round(gbs / peak, 4),
+            "bytes": nbytes}
+
+
+def cpu_parity(host_w, host_x, ops, y_dev, yoff):
+    """Every product of the step through the reference's own kernels on the host cores (the CPU baseline's
+    computation) against the device's outputs of the step: relative L2 per product, the largest reported, bar 1e-3
+    (the reference's f32 accumulation against exact int32 sums)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    ref = O.load_ref()
+    nth = os.cpu_count() or 1
+    y = y_dev.cpu().numpy()
+    worst, worst_op, per_type = 0.0, None, {}
+    for i, (N, t, rows, K) in enumerate(ops):
+        W, X = host_w[(t, rows, K)], host_x[(N, K)]
+        want = O.mul_mat_q8_0_f32(W, rows, K, X, nth=nth) if t == TYPE_IDS["q8_0"] else \
+            O.ref_mul_mat(t, W, rows, K, X, nth=nth, off=1, paired=1, lib=ref)
+        got = y[yoff[i]:yoff[i] + N * rows].reshape(N, rows)
+        e = rel_l2(got, want)
+        name = [k for k, v in TYPE_IDS.items() if v == t][0]
+        per_type[name] = max(per_type.get(name, 0.0), e)
+        if e > worst or worst_op is None:
+            worst, worst_op = e, f"{name} {rows}x{K} N={N}"
+    return {"max_rel_l2": float(f"{worst:.3e}"), "worst": worst_op, "per_type_max": {k: float(f"{v:.3e}") for k, v in
+            per_type.items()}, "products": len(ops), "rows": "all", "bar": 1e-3,
+            "pass": bool(worst <= 1e-3), "checker": "the reference's srv kernels (oracle/_ref); Q8_0: restated stock path"}
+
+
+def sweep_parity_multi(ctx, dev, rank, world, ops, host_w, xs, y_dev, packed):
+    """Rank 0: every product of the sharded step (gathered from the ranks' row slices) against the same product
+    computed whole on rank 0's one GPU; relative L2, bar 1e-5 (the rows' arithmetic is the same, only the split-K
+    grouping of the sums may differ with the shard's size). The other ranks wait at a barrier."""
+    import torch
+    import torch.distributed as dist
+    import srhpm_b200 as S
+    out = None
+    if rank == 0:
+        try:
+            out = _sweep_parity_rank0(ctx, dev, world, ops, host_w, xs, y_dev, packed)
+        except Exception as e:  # reported; the other ranks must still leave the barrier below
+            out = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+    dist.barrier()
+    return out
+
+
+def _sweep_parity_rank0(ctx, dev, world, ops, host_w, xs, y_dev, packed):
+    import torch
+    import srhpm_b200 as S
+    worst, worst_op, done = 0.0, None, {}
+    for i, (N, t, rows, K) in enumerate(ops):
+        if (N, t, rows, K) in done:
+            continue
+        W = S.QuantTensor.from_blocks(host_w[(t, rows, K)], t, rows, K, dev)
+        want = ctx.mul_mat(W, xs[(N, K)]).float()
+        got = packed.unpack(y_dev, i)
+        torch.cuda.synchronize()
+        e = float(torch.linalg.vector_norm(got - want) / torch.linalg.vector_norm(want))
+        done[(N, t, rows, K)] = e
+        if e > worst or worst_op is None:
+            worst = e
+            worst_op = f"{[k for k, v in TYPE_IDS.items() if v == t][0]} {rows}x{K} N={N}"
+        del W
+    torch.cuda.empty_cache()
+    return {"max_rel_l2": float(f"{worst:.3e}"), "worst": worst_op, "products": len(done), "gpus": world,
+            "bar": 1e-5, "pass": bool(worst <= 1e-5), "against": "the same products whole on one GPU"}
+
+
+def _full_caches(cfg, dev, n_layer_cap, seed):
+    """f16 K / V caches of the whole model ([cap, Hkv, 512] bytes per layer), the same values on every rank (one
+    generator seed)."""
+    import torch
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    kc, vc = [], []
+    for _ in range(cfg.n_layer):
+        for lst in (kc, vc):
+            lst.append(torch.randn((n_layer_cap * cfg.Hkv, cfg.hd), device=dev, generator=g).half().view(
+                torch.uint8).view(n_layer_cap, cfg.Hkv, 512))
+    return kc, vc
+
+
 def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0):
-    """The 27B-class verify step (k = 8, f16 KV of 2048 tokens) on `world` GPUs in Megatron tensor parallelism (column-
-    parallel QKV / gate|up / head, row-parallel O / down with an NCCL all-reduce after each, KV heads split or
-    replicated per rank, vocabulary-sharded acceptance). Every rank holds 1/world of the weights (random blocks) and
-    its KV heads' cache; the step (kernels + 129 collectives) is one CUDA graph; time = max over ranks."""
+    """The 27B-class verify step (k = 8, f16 KV of 2048 tokens) on `world` GPUs in Megatron tensor parallelism
+    (column-parallel QKV / gate|up / head, row-parallel O / down with the all-reduce fused into the next RMSNorm, KV
+    heads split or replicated per rank, vocabulary-sharded acceptance). Every rank builds the same whole model
+    (random blocks, one seed) and cuts its slices on the device (DeviceWeights.slice_of), and the same whole cache
+    (its KV heads kept). The step (kernels + collectives) is one CUDA graph; time = max over ranks.
+
+    Parity, after the timed region: rank 0 runs the same model whole on its one GPU. The drafted tokens are the
+    one-GPU step's own greedy choices (built position by position, so all k are accepted there), and both runs
+    score the same tokens: the gathered tensor-parallel logits against the one-GPU logits (relative L2), and the
+    accepted ids against the one-GPU ones (rows whose top-1 margin exceeds the logits' difference must agree)."""
     import torch
     import torch.distributed as dist
     from srhpm_b200 import _lib as L
     from srhpm_b200 import verify_step as V
     cfg = V.DecoderConfig(kv_type=L.F16)
-    w = V.DeviceWeights.random(cfg, dev, seed, rank=rank, world=world)
-    nkv = w.tp["g1"] - w.tp["g0"]
+    full = V.DeviceWeights.random(cfg, dev, seed)
+    w = V.DeviceWeights.slice_of(full, rank, world)
+    g0, g1 = w.tp["g0"], w.tp["g1"]
     n = k + 1
     cap = n_past + n
-    g = torch.Generator(device=dev)
-    g.manual_seed(seed + 7 + rank)
-    kc = [torch.randn((cap * nkv, cfg.hd), device=dev, generator=g).half().view(torch.uint8).view(cap, nkv, 512)
-          for _ in range(cfg.n_layer)]
-    vc = [torch.randn((cap * nkv, cfg.hd), device=dev, generator=g).half().view(torch.uint8).view(cap, nkv, 512)
-          for _ in range(cfg.n_layer)]
+    kc_full, vc_full = _full_caches(cfg, dev, cap, seed + 7)
+    kc = [c[:, g0:g1].contiguous() for c in kc_full]
+    vc = [c[:, g0:g1].contiguous() for c in vc_full]
     step = V.VerifyStep(ctx, cfg, w, kc, vc, n, n_past, tp=V.TensorParallel(rank, world))
     ids = torch.arange(n, dtype=torch.int32, device=dev) * 977 % cfg.n_vocab  # the same tokens on every rank
     step.set_tokens(ids, ids[1:])
@@ -605,12 +817,66 @@ def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0
     tt = torch.tensor([e0.elapsed_time(e1) / reps], device=dev)
     dist.all_reduce(tt, op=dist.ReduceOp.MAX)
     ms = float(tt.item())
-    acc = int(step.out_n.item())
     del graph  # holds NCCL calls: released before the process group
+
+    # parity against the whole model on rank 0's GPU
+    par = None
+    ids1 = torch.zeros(n, dtype=torch.int32, device=dev)
+    one = None
+    if rank == 0:
+        try:
+            one = V.VerifyStep(ctx, cfg, full, kc_full, vc_full, n, n_past)
+            cur = ids.clone()
+            for i in range(k):  # the one-GPU step's own greedy continuation, position by position
+                one.set_tokens(cur, cur[1:])
+                one.run()
+                cur[i + 1] = one.logits[i].argmax().to(torch.int32)
+            ids1.copy_(cur)
+        except Exception as e:  # reported; the other ranks must still meet the collectives below
+            par = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+    dist.broadcast(ids1, 0)
+    step.set_tokens(ids1, ids1[1:])
+    step.run()
+    torch.cuda.synchronize()
+    # this rank's vocabulary slice of the logits, padded to one size, gathered in rank (= vocabulary) order
+    vmax = max(V_r1 - V_r0 for V_r0, V_r1 in (shard_vocab(cfg.n_vocab, world, j) for j in range(world)))
+    mine = torch.zeros((n, vmax), dtype=torch.float32, device=dev)
+    mine[:, :step.logits.shape[1]].copy_(step.logits)
+    allv = torch.empty((world, n, vmax), dtype=torch.float32, device=dev)
+    dist.all_gather_into_tensor(allv, mine)
+    if rank == 0 and par is None:
+        try:
+            one.set_tokens(ids1, ids1[1:])
+            one.run()
+            torch.cuda.synchronize()
+            tp_logits = torch.cat([allv[j, :, :shard_vocab(cfg.n_vocab, world, j)[1] - shard_vocab(cfg.n_vocab,
+                                   world, j)[0]] for j in range(world)], dim=1)
+            ref = one.logits
+            err = float(torch.linalg.vector_norm(tp_logits - ref) / torch.linalg.vector_norm(ref))
+            top2 = ref.topk(2, dim=1).values
+            margin = (top2[:, 0] - top2[:, 1]).cpu().tolist()
+            dmax = float((tp_logits - ref).abs().max())
+            acc_tp, acc_1 = step.accepted(), one.accepted()
+            clear = all(m > 2 * dmax for m in margin[:len(acc_1)])
+            par = {"logits_rel_l2": float(f"{err:.3e}"), "logits_max_abs_diff": float(f"{dmax:.3e}"),
+                   "bar": 2e-2, "accepted_tp": acc_tp, "accepted_1gpu": acc_1,
+                   "ids_equal": acc_tp == acc_1, "margins_clear": clear,
+                   "pass": bool(err <= 2e-2 and (acc_tp == acc_1 or not clear)),
+                   "against": "the same model and cache whole on one GPU, drafts = its own greedy choices"}
+        except Exception as e:
+            par = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+    acc = int(step.out_n.item())
+    del one
+    dist.barrier()
     nbytes = step_bytes_27b(cfg, n_past, n)
     return {f"k{k}": {"ms": round(ms, 3), "steps_per_s": round(1e3 / ms, 1), "gpus": world,
                       "GBps_per_gpu": round(nbytes / world / (ms * 1e-3) / 1e9, 1), "bytes": nbytes,
-                      "kernel_launches_per_rank": launches, "accepted": acc}}
+                      "kernel_launches_per_rank": launches, "accepted": acc, "parity": par}}
+
+
+def shard_vocab(n_vocab, world, j):
+    from srhpm_b200 import shard
+    return shard.vocab_range(n_vocab, world, j)
 
 
 def measure_attention(ctx, dev, peak, reps=20, lengths=(8192, 32768, 131072)):
@@ -669,12 +935,33 @@ def measure_attention(ctx, dev, peak, reps=20, lengths=(8192, 32768, 131072)):
     return out
 
 
+def _q80_cache(ctx, dev, Hkv, L, D, seed):
+    """A q8_0 K or V cache [Hkv, L, 272] of N(0, 1) values, quantized on the device; the same bytes on every rank
+    for one seed."""
+    import torch
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    x = torch.randn((Hkv * L, D), device=dev, generator=g)
+    out = ctx.quantize_rows_q8_0(x).view(Hkv, L, 272)
+    del x
+    return out
+
+
+def _causal_mask(N, L, dev):
+    import torch
+    mask = torch.zeros((N, L), dtype=torch.float16, device=dev)
+    for t in range(N):
+        mask[t, L - N + t + 1:] = float("-inf")
+    return mask
+
+
 def measure_attention_split(ctx, dev, rank, world, peak, reps=20, lengths=(8192, 32768, 131072)):
     """The verify attention of measure_attention on `world` GPUs, split over the KV range: rank j holds tokens
     shard.kv_range(L, world, j) of the 4 KV heads' q8_0 cache; one call = the partial records of its range, an NCCL
     all-gather of the record sets (24 * 8 * 1032 bytes per rank) and the merge, all in one CUDA graph over copies of
     the rank's range that together exceed L2. Time = max over ranks; GB/s counts the whole cache once (plus Q and O),
-    as on one GPU."""
+    as on one GPU. Parity: the first copy is the rank's range of one whole cache (same seed on every rank); its
+    merged output against the whole-range call on rank 0's one GPU (relative L2, bar 1e-3)."""
     import torch
     import torch.distributed as dist
     import srhpm_b200 as S
@@ -690,17 +977,16 @@ def measure_attention_split(ctx, dev, rank, world, peak, reps=20, lengths=(8192,
         nbytes = 2176 * L + 2 * H * N * D * 4
         ncopy = max(2, -(-400_000_000 // max(1, 2176 * Lr)))
         q = torch.randn((H, N, D), device=dev, generator=torch.Generator(device=dev).manual_seed(3)) / 16
-        kv = []
-        for _ in range(ncopy):
+        kfull, vfull = _q80_cache(ctx, dev, Hkv, L, D, 11), _q80_cache(ctx, dev, Hkv, L, D, 12)
+        kv = [(kfull[:, t0:t1].contiguous(), vfull[:, t0:t1].contiguous())]
+        for _ in range(ncopy - 1):
             pair = []
             for _ in range(2):
                 x = torch.randn((Hkv * Lr, D), device=dev, generator=g)
                 pair.append(ctx.quantize_rows_q8_0(x).view(Hkv, Lr, 272))
                 del x
             kv.append(pair)
-        mask = torch.zeros((N, L), dtype=torch.float16, device=dev)
-        for t in range(N):
-            mask[t, L - N + t + 1:] = float("-inf")
+        mask = _causal_mask(N, L, dev)
         mr = mask[:, t0:t1]
         att = SplitKAttention(ctx, rank, world, H, N, dev)
         st, ws = ctx.flash_attn_ext_work_size(q, kv[0][0], kv[0][1], S.Q8_0)
@@ -730,10 +1016,116 @@ def measure_attention_split(ctx, dev, rank, world, peak, reps=20, lengths=(8192,
         tt = torch.tensor([e0.elapsed_time(e1) * 1e3 / (rounds * ncopy)], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         us = float(tt.item())
+        del graph  # the graph holds NCCL calls: released before the process group
+        # parity: the first copy (this rank's range of the whole cache) merged, against the whole range on one GPU
+        got = att(q, *kv[0], S.Q8_0, mask=mr, work=work).clone()
+        torch.cuda.synchronize()
+        par = None
+        if rank == 0:
+            try:
+                want = ctx.flash_attn_ext(q, kfull, vfull, S.Q8_0, mask=mask)
+                torch.cuda.synchronize()
+                err = float(torch.linalg.vector_norm(got - want) / torch.linalg.vector_norm(want))
+                par = {"rel_l2": float(f"{err:.3e}"), "bar": 1e-3, "pass": bool(err <= 1e-3),
+                       "against": "the whole range on one GPU"}
+            except Exception as e:
+                par = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+        dist.barrier()
         gbs = nbytes / (us * 1e-6) / 1e9
         out[str(L)] = {"us": round(us, 2), "GBps": round(gbs, 1), "GBps_per_gpu": round(gbs / world, 1),
-                       "frac_per_gpu": round(gbs / world / peak, 4), "bytes": nbytes, "gpus": world}
-        del graph, kv  # the graph holds NCCL calls: released before the process group
+                       "frac_per_gpu": round(gbs / world / peak, 4), "bytes": nbytes, "gpus": world, "parity": par}
+        del kv, kfull, vfull
+        torch.cuda.empty_cache()
+    return out
+
+
+def measure_attention_kv_heads(ctx, dev, rank, world, peak, reps=20, lengths=(8192, 32768, 131072)):
+    """The verify attention of measure_attention sharded by KV head (config 3 over 2 or 4 GPUs): rank j holds KV
+    heads shard.kv_heads(4, world, j) of the q8_0 cache and computes their 6 query heads each over the whole range
+    (no reduction); one NCCL all-gather assembles the [N, 24, 256] output on every rank. One call = the attention
+    + the all-gather, in one CUDA graph over copies of the rank's heads that together exceed L2; time = max over
+    ranks. Parity: the first copy is the rank's heads of one whole cache (same seed on every rank); the assembled
+    output against the whole call on rank 0's one GPU (relative L2, bar 1e-3)."""
+    import torch
+    import torch.distributed as dist
+    import srhpm_b200 as S
+    from srhpm_b200 import shard
+    H, Hkv, N, D = 24, 4, 8, 256
+    G = H // Hkv
+    g0, g1 = shard.kv_heads(Hkv, world, rank)
+    hk = g1 - g0
+    g = torch.Generator(device=dev)
+    g.manual_seed(5 + rank)
+    out = {}
+    for L in lengths:
+        nbytes = 2176 * L + 2 * H * N * D * 4
+        ncopy = max(2, -(-400_000_000 // (544 * hk * L)))
+        q = torch.randn((H, N, D), device=dev, generator=torch.Generator(device=dev).manual_seed(3)) / 16
+        qr = q[g0 * G:g1 * G].contiguous()
+        kfull, vfull = _q80_cache(ctx, dev, Hkv, L, D, 11), _q80_cache(ctx, dev, Hkv, L, D, 12)
+        kv = [(kfull[g0:g1].contiguous(), vfull[g0:g1].contiguous())]
+        for _ in range(ncopy - 1):
+            pair = []
+            for _ in range(2):
+                x = torch.randn((hk * L, D), device=dev, generator=g)
+                pair.append(ctx.quantize_rows_q8_0(x).view(hk, L, 272))
+                del x
+            kv.append(pair)
+        mask = _causal_mask(N, L, dev)
+        o_r = torch.empty((N, hk * G, D), dtype=torch.float32, device=dev)
+        o_all = torch.empty((world, N, hk * G, D), dtype=torch.float32, device=dev)
+        st, ws = ctx.flash_attn_ext_work_size(qr, kv[0][0], kv[0][1], S.Q8_0)
+        work = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
+
+        def call(i):
+            ctx.flash_attn_ext(qr, *kv[i], S.Q8_0, mask=mask, out=o_r, work=work)
+            dist.all_gather_into_tensor(o_all, o_r)
+
+        for i in range(3):
+            call(i % ncopy)
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                for i in range(ncopy):
+                    call(i)
+        torch.cuda.synchronize()
+        graph.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        rounds = max(1, reps // ncopy)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(rounds):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ctx.check()
+        tt = torch.tensor([e0.elapsed_time(e1) * 1e3 / (rounds * ncopy)], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        us = float(tt.item())
+        del graph  # the graph holds NCCL calls: released before the process group
+        call(0)
+        got = o_all.permute(1, 0, 2, 3).reshape(N, H, D).clone()
+        torch.cuda.synchronize()
+        par = None
+        if rank == 0:
+            try:
+                want = ctx.flash_attn_ext(q, kfull, vfull, S.Q8_0, mask=mask)
+                torch.cuda.synchronize()
+                err = float(torch.linalg.vector_norm(got - want) / torch.linalg.vector_norm(want))
+                par = {"rel_l2": float(f"{err:.3e}"), "bar": 1e-3, "pass": bool(err <= 1e-3),
+                       "against": "all heads on one GPU"}
+            except Exception as e:
+                par = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+        dist.barrier()
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[str(L)] = {"us": round(us, 2), "GBps": round(gbs, 1), "GBps_per_gpu": round(gbs / world, 1),
+                       "frac_per_gpu": round(gbs / world / peak, 4), "bytes": nbytes, "gpus": world,
+                       "kv_heads_per_gpu": hk, "parity": par}
+        del kv, kfull, vfull
         torch.cuda.empty_cache()
     return out
 
@@ -744,7 +1136,6 @@ def cpu_attention_reference(lengths=(8192, 32768, 131072), target_s=6.0):
     shapes and q8_0 cache, all host threads, repeated calls for about target_s seconds in all."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
-    import srhpm_b200 as S
     ref = O.load_ref()
     if ref is None:
         return {"unavailable": "the reference kernels (oracle/_ref) are not built"}
@@ -754,7 +1145,7 @@ def cpu_attention_reference(lengths=(8192, 32768, 131072), target_s=6.0):
     out = {}
     for L in lengths:
         q = (rng.standard_normal((H, N, D), dtype=np.float32) / np.float32(16)).astype(np.float32)
-        kv = [S.quantize_chunk(rng.standard_normal((Hkv * L, D), dtype=np.float32), S.Q8_0).reshape(Hkv, L, 272)
+        kv = [O.quantize_rtn(O.Q8_0, rng.standard_normal((Hkv * L, D), dtype=np.float32)).reshape(Hkv, L, 272)
               for _ in range(2)]
         mask = np.zeros((N, L), np.float16)
         for t in range(N):

@@ -106,8 +106,9 @@ int srhpm_mul_mat_isums(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_ten
  * it, kept until the process exits; products are not split along K here. Limit: the activation records and row-block
  * counters of the product must fit 1 MiB (for K up to 32768 and N up to 16 that leaves room for 6 million weight
  * rows); beyond that the call returns SRHPM_ERR_TOO_LARGE and does nothing. The first call on a device looks up the array's device address
- * (make it before any stream capture). All calls share the array: calls whose work overlaps on the GPU race.
- * Allocates nothing. No counterpart in the reference. */
+ * (make it before any stream capture). All calls share the array: calls whose work overlaps on the GPU race. The
+ * context's device must be the calling thread's current device (else SRHPM_ERR_INVALID). Allocates nothing. No
+ * counterpart in the reference. */
 int srhpm_mul_mat_static(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, srhpm_tensor * Y,
                          void * stream);
 

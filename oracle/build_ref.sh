@@ -6,10 +6,14 @@
 #   oracle/_ref/libsrv_ref_vnni.so  same with AVX-VNNI (vpdpwssd path), built when the compiler accepts -mavxvnni
 # The reference's build system (cmake over the llama.cpp tree) is not used: the tree is not in the container.
 # Only the patch's own added lines are compiled, against the stand-ins in oracle/ref_shim.h and
-# oracle/ggml_restated.h. Usage: oracle/build_ref.sh [path-to-reference]
+# oracle/ggml_restated.h. Usage: oracle/build_ref.sh <path-to-reference> (or set SRHPM_REFERENCE)
 set -euo pipefail
 HERE="$(cd "$(dirname "$0")" && pwd)"
-REF="${1:-${SRHPM_REFERENCE:-/root/reference}}"
+REF="${1:-${SRHPM_REFERENCE:-}}"
+if [ -z "$REF" ]; then
+    echo "build_ref: give the reference checkout as the argument or in SRHPM_REFERENCE" >&2
+    exit 2
+fi
 PATCH="$REF/patch/srhpm.patch"
 OUT="$HERE/_ref"
 if [ ! -f "$PATCH" ]; then

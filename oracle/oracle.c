@@ -651,3 +651,173 @@ int orc_accept(const float * logits, int64_t n_vocab, const int32_t * draft, int
     out_ids[n++] = argmax_row(logits + (int64_t) i * n_vocab, n_vocab);
     return n;
 }
+
+/* ---- input generation: round-to-nearest weight quantizers -------------------------------------------------------
+ * The inverse of the block decoders above, with per-block scales from each block's range and no search. They only
+ * make valid GGUF blocks of a given f32 matrix for the CPU reference timings (the reference's own quantizers are
+ * upstream ggml code, absent here); nothing is pinned to them. */
+
+static uint16_t f16_of(float f, float * back) {
+    const uint16_t h = orc_fp32_to_fp16(f);
+    *back            = orc_fp16_to_fp32(h);
+    return h;
+}
+
+static int clampi(long v, int lo, int hi) { return v < lo ? lo : v > hi ? hi : (int) v; }
+
+static void put16(uint8_t * p, uint16_t h) { memcpy(p, &h, 2); }
+
+/* Q4_K / Q5_K: x = d sc q - dmin m per 32 weights, q in 0..nq */
+static void rtn_k45(const float * x, uint8_t * blk, int q5) {
+    const int nq = q5 ? 31 : 15;
+    float     scale[8], mn[8], smax = 0.0f, mmax = 0.0f;
+    for (int b = 0; b < 8; b++) {
+        float lo = x[32 * b], hi = x[32 * b];
+        for (int l = 1; l < 32; l++) {
+            lo = x[32 * b + l] < lo ? x[32 * b + l] : lo;
+            hi = x[32 * b + l] > hi ? x[32 * b + l] : hi;
+        }
+        mn[b]    = lo < 0.0f ? -lo : 0.0f;
+        scale[b] = (hi + mn[b]) / (float) nq;
+        smax     = scale[b] > smax ? scale[b] : smax;
+        mmax     = mn[b] > mmax ? mn[b] : mmax;
+    }
+    float d, dmin;
+    put16(blk, f16_of(smax / 63.0f, &d));
+    put16(blk + 2, f16_of(mmax / 63.0f, &dmin));
+    uint8_t * s = blk + 4;
+    memset(s, 0, 12);
+    uint8_t * qh = blk + 16;
+    uint8_t * qs = blk + (q5 ? 48 : 16);
+    if (q5) memset(qh, 0, 32);
+    memset(qs, 0, 128);
+    for (int b = 0; b < 8; b++) {
+        const int sc = d > 0.0f ? clampi(lrintf(scale[b] / d), 0, 63) : 0;
+        const int m  = dmin > 0.0f ? clampi(lrintf(mn[b] / dmin), 0, 63) : 0;
+        if (b < 4) {
+            s[b] |= (uint8_t) sc;
+            s[b + 4] |= (uint8_t) m;
+        } else {
+            s[b + 4] = (uint8_t) ((sc & 0xF) | ((m & 0xF) << 4));
+            s[b - 4] |= (uint8_t) ((sc >> 4) << 6);
+            s[b] |= (uint8_t) ((m >> 4) << 6);
+        }
+        const float step = d * (float) sc, off = dmin * (float) m;
+        for (int l = 0; l < 32; l++) {
+            const int i = 32 * b + l;
+            const int q = step > 0.0f ? clampi(lrintf((x[i] + off) / step), 0, nq) : 0;
+            qs[32 * (b / 2) + l] |= (uint8_t) ((q & 0xF) << (4 * (b & 1)));
+            if (q5) qh[l] |= (uint8_t) (((q >> 4) & 1) << b);
+        }
+    }
+}
+
+/* Q6_K: x = d sc q per 16 weights, q in -32..31, int8 sc */
+static void rtn_q6k(const float * x, uint8_t * blk) {
+    float scale[16], smax = 0.0f;
+    for (int g = 0; g < 16; g++) {
+        float a = 0.0f;
+        for (int l = 0; l < 16; l++) a = fabsf(x[16 * g + l]) > a ? fabsf(x[16 * g + l]) : a;
+        scale[g] = a / 31.0f;
+        smax     = scale[g] > smax ? scale[g] : smax;
+    }
+    float d;
+    put16(blk + 208, f16_of(smax / 127.0f, &d));
+    memset(blk, 0, 192);
+    for (int g = 0; g < 16; g++) {
+        const int sc = d > 0.0f ? clampi(lrintf(scale[g] / d), -128, 127) : 0;
+        blk[192 + g] = (uint8_t) (int8_t) sc;
+        const float step = d * (float) sc;
+        for (int l16 = 0; l16 < 16; l16++) {
+            const int i = 16 * g + l16, b = i / 32, l = i % 32, n = b / 4, j = b % 4;
+            const int q = (step != 0.0f ? clampi(lrintf(x[i] / step), -32, 31) : 0) + 32;
+            blk[64 * n + 32 * (j & 1) + l] |= (uint8_t) ((q & 0xF) << (4 * (j >> 1)));
+            blk[128 + 32 * n + l] |= (uint8_t) (((q >> 4) & 3) << (2 * j));
+        }
+    }
+}
+
+/* Q3_K: x = d sc q per 16 weights, q in -4..3, sc in -32..31 */
+static void rtn_q3k(const float * x, uint8_t * blk) {
+    float scale[16], smax = 0.0f;
+    for (int g = 0; g < 16; g++) {
+        float a = 0.0f;
+        for (int l = 0; l < 16; l++) a = fabsf(x[16 * g + l]) > a ? fabsf(x[16 * g + l]) : a;
+        scale[g] = a / 4.0f;
+        smax     = scale[g] > smax ? scale[g] : smax;
+    }
+    float d;
+    put16(blk + 108, f16_of(smax / 31.0f, &d));
+    memset(blk, 0, 108);
+    uint8_t * s = blk + 96;
+    for (int g = 0; g < 16; g++) {
+        const int sc = d > 0.0f ? clampi(lrintf(scale[g] / d), -32, 31) : 0;
+        const int u  = sc + 32;
+        if (g < 8) {
+            s[g] |= (uint8_t) (u & 0xF);
+        } else {
+            s[g - 8] |= (uint8_t) ((u & 0xF) << 4);
+        }
+        s[8 + (g & 3)] |= (uint8_t) (((u >> 4) & 3) << (2 * (g >> 2)));
+        const float step = d * (float) sc;
+        for (int l16 = 0; l16 < 16; l16++) {
+            const int i = 16 * g + l16, b = i / 32, l = i % 32, n = b / 4, j = b % 4;
+            const int q = step != 0.0f ? clampi(lrintf(x[i] / step), -4, 3) : 0;
+            const int hb = q >= 0, q2 = hb ? q : q + 4;
+            blk[32 + 32 * n + l] |= (uint8_t) (q2 << (2 * j));
+            blk[l] |= (uint8_t) (hb << (4 * n + j));
+        }
+    }
+}
+
+/* IQ4_XS: x = d ls kvalue per 32 weights, ls in -32..31, the nearest of the 16 non-linear values */
+static void rtn_iq4xs(const float * x, uint8_t * blk) {
+    float scale[8], smax = 0.0f;
+    for (int b = 0; b < 8; b++) {
+        float a = 0.0f;
+        for (int l = 0; l < 32; l++) a = fabsf(x[32 * b + l]) > a ? fabsf(x[32 * b + l]) : a;
+        scale[b] = a / 127.0f;
+        smax     = scale[b] > smax ? scale[b] : smax;
+    }
+    float d;
+    put16(blk, f16_of(smax / 31.0f, &d));
+    memset(blk + 2, 0, 134);
+    uint16_t sh = 0;
+    for (int b = 0; b < 8; b++) {
+        const int ls = d > 0.0f ? clampi(lrintf(scale[b] / d), -32, 31) : 0;
+        const int u  = ls + 32;
+        blk[4 + b / 2] |= (uint8_t) ((u & 0xF) << (4 * (b % 2)));
+        sh |= (uint16_t) (((u >> 4) & 3) << (2 * b));
+        const float step = d * (float) ls;
+        for (int l = 0; l < 32; l++) {
+            const float v = step != 0.0f ? x[32 * b + l] / step : 0.0f;
+            int         best = 0;
+            for (int k = 1; k < 16; k++) {
+                if (fabsf(v - (float) kv_iq4nl[k]) < fabsf(v - (float) kv_iq4nl[best])) best = k;
+            }
+            blk[8 + 16 * b + (l & 15)] |= (uint8_t) (best << (4 * (l >= 16)));
+        }
+    }
+    put16(blk + 2, sh);
+}
+
+int64_t orc_quantize_rtn(int type, const float * x, void * out, int64_t n) {
+    const int    qk = orc_block_elems(type);
+    const size_t bs = orc_block_bytes(type);
+    if (qk <= 1 || n % qk) return -1;
+    uint8_t * p = (uint8_t *) out;
+    for (int64_t ib = 0; ib < n / qk; ib++) {
+        const float * xb  = x + ib * qk;
+        uint8_t *     blk = p + ib * bs;
+        switch (type) {
+            case ORC_Q8_0: orc_quantize_row_q8_0(xb, blk, QK8, ORC_Q8_0_REF); break;
+            case ORC_Q4_K: rtn_k45(xb, blk, 0); break;
+            case ORC_Q5_K: rtn_k45(xb, blk, 1); break;
+            case ORC_Q6_K: rtn_q6k(xb, blk); break;
+            case ORC_Q3_K: rtn_q3k(xb, blk); break;
+            case ORC_IQ4_XS: rtn_iq4xs(xb, blk); break;
+            default: return -1;
+        }
+    }
+    return (int64_t) (n / qk * bs);
+}

@@ -84,6 +84,11 @@ int orc_attention_merge(int64_t n_parts, int64_t N, int64_t H, int64_t DV, const
 int orc_accept(const float * logits, int64_t n_vocab, const int32_t * draft, int n_draft, float relax,
                int32_t * out_ids);
 
+/* Input generation (not pinned): n f32 weights -> GGUF blocks of `type` by round-to-nearest with per-block scales
+ * from each block's range, the inverse of orc_dequantize. Returns the bytes written, -1 for an unsupported type or
+ * n not a multiple of the block size. For the CPU reference timings, whose inputs must not come from the product. */
+int64_t orc_quantize_rtn(int type, const float * x, void * out, int64_t n);
+
 #ifdef __cplusplus
 }
 #endif

@@ -67,6 +67,8 @@ def load_oracle():
         lib.orc_attention_merge.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _P, _P,
                                             _P, _P, _P]
         lib.orc_accept.argtypes = [_P, ctypes.c_int64, _P, ctypes.c_int, ctypes.c_float, _P]
+        lib.orc_quantize_rtn.restype = ctypes.c_int64
+        lib.orc_quantize_rtn.argtypes = [ctypes.c_int, _P, _P, ctypes.c_int64]
         _orc = lib
     return _orc
 
@@ -281,6 +283,31 @@ def ref_fa_gqa(q, kv_type, k, v, DV, L, Hkv, mask=None, sinks=None, scale=1.0, m
 
 
 # ---- inputs -----------------------------------------------------------------------------------------------------
+
+def quantize_rtn(qtype, w, nth=None):
+    """f32 [rows, K] -> GGUF blocks uint8 [rows, row_bytes] by the oracle's round-to-nearest quantizers (input
+    generation for the CPU reference timings; not pinned to ggml's quantizers). Rows are split over nth threads."""
+    from concurrent.futures import ThreadPoolExecutor
+    lib = load_oracle()
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, K = w.shape
+    qk = 32 if qtype == Q8_0 else 256
+    if K % qk:
+        raise ValueError(f"K = {K} is not a multiple of {qk}")
+    rb = K // qk * BLOCK_BYTES[qtype]
+    out = np.empty((rows, rb), np.uint8)
+    nth = nth or os.cpu_count() or 1
+    cut = [rows * i // nth for i in range(nth + 1)]
+
+    def part(i):
+        r0, r1 = cut[i], cut[i + 1]
+        if r1 > r0 and lib.orc_quantize_rtn(qtype, _ptr(w[r0:r1]), _ptr(out[r0:r1]), (r1 - r0) * K) < 0:
+            raise RuntimeError("orc_quantize_rtn failed")
+
+    with ThreadPoolExecutor(nth) as ex:
+        list(ex.map(part, range(nth)))
+    return out
+
 
 def random_blocks(qtype, nblocks, rng, d_lo=0.005, d_hi=0.02):
     """Random bytes in every field (all bit patterns of codes and scales) with sane f16 block scales, as the

@@ -111,10 +111,12 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_kernel(float * x, c
 // waits until every peer's flag in its own buffer has reached it (bounded: 2 s, then an error status), and the row
 // is summed over ranks in rank order (every rank adds the same values in the same order: identical results). Each
 // slot is rewritten only after a later barrier of the same rows, so two suffice.
-// Ordering: the partial rows were written by the previous kernel of each rank (complete before this grid passes
-// griddepcontrol.wait) and sit in that GPU's L2, which serves peer reads over NVLink; the flags are strong relaxed
-// system-scope accesses and the peer rows are read uncached (ld.global.cv). A system-scope fence or release per
-// signal (a full memory barrier each) measured ~19 us per call on B200; without them the barrier is a round trip.
+// Ordering (PTX memory model, system scope): the partial rows were written by the previous kernel of each rank,
+// complete and visible to this grid once it passes griddepcontrol.wait. Thread 0 then issues one fence.acq_rel.sys
+// before its relaxed flag stores (a release: the rows are ordered before the flags every peer polls) and one
+// fence.acq_rel.sys after its polls have seen every peer's flag (an acquire: the peers' rows are ordered before the
+// loads below); the CTA barrier carries that order to the other threads. One fence on each side per CTA, not one per
+// signal; the peer rows are read uncached (ld.global.cv).
 constexpr int kArMaxRanks = 8;
 constexpr int kArRows     = 16;
 
@@ -145,6 +147,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_ar_kernel(float * x
     if (threadIdx.x == 0) {
         const uint32_t e = ++epochs[slot * kArRows + i];
         const size_t fo = flag_off + ((size_t) (slot * kArRows + i) * kArMaxRanks + rank) * sizeof(uint32_t);
+        fence_acq_rel_sys();  // release: this rank's partial rows before its flags
         for (int j = 0; j < world; j++) st_relaxed_sys(reinterpret_cast<uint32_t *>(peers[j] + fo), e);
         const uint32_t * mine = reinterpret_cast<const uint32_t *>(peers[rank] + flag_off) +
                                 (size_t) (slot * kArRows + i) * kArMaxRanks;
@@ -160,6 +163,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_ar_kernel(float * x
                 __nanosleep(64);
             }
         }
+        fence_acq_rel_sys();  // acquire: every peer's partial rows after its flag
         ok_s = ok;
     }
     __syncthreads();

@@ -50,8 +50,14 @@ int gemm_run_static(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows,
                     const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, cudaStream_t stream) {
     const size_t need = gemm_work_size_unsplit(wtype, rows, K, N);
     if (need > kStaticWorkBytes) return SRHPM_ERR_TOO_LARGE;
-    void *    work = nullptr;
-    const int st   = static_work_ptr(ctx->device, &work);
+    // the kernels launch on the calling thread's current device: it must be the context's, or they would use the
+    // other device's copy of the array through a peer address
+    int cur = -1;
+    int st  = cuda_status(cudaGetDevice(&cur));
+    if (st != SRHPM_OK) return st;
+    if (cur != ctx->device) return SRHPM_ERR_INVALID;
+    void * work = nullptr;
+    st          = static_work_ptr(ctx->device, &work);
     if (st != SRHPM_OK) return st;
     return gemm_run_unsplit(ctx, wtype, W, rows, K, row_bytes, X, ldx, N, Y, ldy, work, kStaticWorkBytes, stream);
 }

@@ -153,6 +153,45 @@ class DeviceWeights:
         self.emb = torch.randn((cfg.n_vocab, cfg.d), device=device, generator=gen).half()
         return self
 
+    @classmethod
+    def slice_of(cls, full, rank, world):
+        """One tensor-parallel rank's slices cut on the device from the whole model `full` (world = 1 weights, fused
+        qkv and gate|up): the same cuts as from_host (QKV rows of the rank's query and KV heads, O columns of its
+        heads, gate / up rows and down columns of its FFN rows, head rows of its vocabulary range). Norms and
+        embeddings are shared with `full`."""
+        cfg = full.cfg
+        self = cls(cfg, full.device)
+        tp = self._set_tp(rank, world)
+        hd, H, Hkv = cfg.hd, cfg.H, cfg.Hkv
+        h0, h1, g0, g1, f0, f1 = tp["h0"], tp["h1"], tp["g0"], tp["g1"], tp["f0"], tp["f1"]
+
+        def rows2d(qt):
+            return qt.data[:qt.rows * qt.row_bytes].view(qt.rows, qt.row_bytes)
+
+        def kcols(qt, k0, k1):
+            b, bs = blck_size(qt.qtype), type_size(qt.qtype)
+            part = rows2d(qt)[:, k0 // b * bs:k1 // b * bs].contiguous()
+            return QuantTensor(part.view(-1), qt.qtype, qt.rows, k1 - k0)
+
+        for lay_f in full.layers:
+            lay = {}
+            q = rows2d(lay_f["qkv"])
+            part = torch.cat([q[h0 * hd:h1 * hd], q[(H + g0) * hd:(H + g1) * hd],
+                              q[(H + Hkv + g0) * hd:(H + Hkv + g1) * hd]])
+            lay["qkv"] = QuantTensor(part.reshape(-1), lay_f["qkv"].qtype, part.shape[0], cfg.d)
+            lay["o"] = kcols(lay_f["o"], h0 * hd, h1 * hd)
+            gu = rows2d(lay_f["gate_up"])
+            part = torch.cat([gu[f0:f1], gu[cfg.n_ff + f0:cfg.n_ff + f1]])
+            lay["gate_up"] = QuantTensor(part.reshape(-1), lay_f["gate_up"].qtype, part.shape[0], cfg.d)
+            lay["down"] = kcols(lay_f["down"], f0, f1)
+            lay["attn_norm"], lay["ffn_norm"] = lay_f["attn_norm"], lay_f["ffn_norm"]
+            self.layers.append(lay)
+        self.out_norm = full.out_norm
+        hr = rows2d(full.head)[tp["v0"]:tp["v1"]].contiguous()
+        self.head = QuantTensor(hr.view(-1), full.head.qtype, tp["v1"] - tp["v0"], cfg.d)
+        self.emb = full.emb
+        return self
+
 
 class TensorParallel:
     """The collectives of a Megatron tensor-parallel step over torch.distributed.

@@ -235,3 +235,18 @@ def test_accept_semantics():
     tie = np.zeros((1, V), np.float32)
     tie[0, [5, 2, 40]] = 2.0
     assert O.accept(tie, []) == [2]                                # ties -> lowest id
+
+
+@pytest.mark.parametrize("qtype", [O.Q4_K, O.Q5_K, O.Q6_K, O.Q3_K, O.IQ4_XS, O.Q8_0])
+def test_quantize_rtn_round_trip(qtype):
+    """The oracle's round-to-nearest quantizers (input generation for the CPU reference timings) make blocks that
+    the oracle's own decoders turn back into the input within the format's resolution."""
+    rng = np.random.default_rng(qtype)
+    w = (rng.standard_normal((37, 512)) * 0.02).astype(np.float32)
+    w[3] = 0.0
+    blocks = O.quantize_rtn(qtype, w, nth=3)
+    assert blocks.shape == (37, 512 // O.BLOCK_ELEMS[qtype] * O.BLOCK_BYTES[qtype])
+    back = O.dequantize(qtype, blocks.reshape(-1), w.size).reshape(w.shape)
+    bar = {O.Q3_K: 0.25, O.Q4_K: 0.12, O.IQ4_XS: 0.12, O.Q5_K: 0.06, O.Q6_K: 0.03, O.Q8_0: 0.01}[qtype]
+    assert np.linalg.norm(back - w) / np.linalg.norm(w) < bar
+    assert not back[3].any()

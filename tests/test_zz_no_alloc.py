@@ -3,7 +3,8 @@ owns every device buffer and offers no scratch per operation, or a decode loop w
 the device). Its scratch is a fixed array inside the library instead of a caller work buffer.
 
 Checked through the C ABI against srhpm_mul_mat (which uses a caller-provided work buffer) on two calls in a row,
-within the tolerance of the matmul parity tests. Collected last (file name) so that a failure here does not stop a
+within the tolerance of the matmul parity tests, and on three calls issued back to back without synchronisation
+against both srhpm_mul_mat and the exact oracle. Collected last (file name) so that a failure here does not stop a
 `-x` run before the other tests; it also passes alone in a fresh process, where its first call sets up the array."""
 import ctypes
 
@@ -46,6 +47,36 @@ def test_static_matches_work_buffer_path_twice():
         assert _static(lib, ctx, W, X, got) == L.OK
         torch.cuda.synchronize()
         assert rel_l2(got.cpu().numpy(), want.cpu().numpy()) < TOL
+    ctx.check()
+    ctx.close()
+
+
+def test_static_back_to_back_without_sync_matches_oracle():
+    """Three calls issued back to back on one stream with no synchronisation between them (the second reuses the
+    shared array while the first may still be finishing; the third repeats the first), each into its own output,
+    then one synchronisation: every output against srhpm_mul_mat and against the exact oracle."""
+    lib = L.load()
+    ctx = S.Context(0)
+    rng = np.random.default_rng(77)
+    cases = [(S.Q4_K, 6144, 5120, 8), (S.Q6_K, 5120, 5120, 3)]
+    prepared = []
+    for qtype, rows, K, N in cases:
+        w = (rng.standard_normal((rows, K)) * 0.02).astype(np.float32)
+        blocks = S.quantize_chunk(w, qtype)
+        Xh = rng.standard_normal((N, K)).astype(np.float32)
+        prepared.append((qtype, rows, K, blocks, S.QuantTensor.from_blocks(blocks, qtype, rows, K),
+                         torch.from_numpy(Xh).cuda(), Xh))
+    order = [0, 1, 0]
+    outs = [torch.full((prepared[i][5].shape[0], prepared[i][1]), float("nan"), device="cuda") for i in order]
+    torch.cuda.synchronize()
+    for i, y in zip(order, outs):
+        assert _static(lib, ctx, prepared[i][4], prepared[i][5], y) == L.OK
+    torch.cuda.synchronize()
+    for i, y in zip(order, outs):
+        qtype, rows, K, blocks, W, X, Xh = prepared[i]
+        got = y.cpu().numpy()
+        assert rel_l2(got, ctx.mul_mat(W, X).cpu().numpy()) < TOL
+        assert rel_l2(got, O.mul_mat(qtype, blocks, rows, K, Xh)) < TOL
     ctx.check()
     ctx.close()
 
