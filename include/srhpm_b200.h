@@ -235,6 +235,14 @@ size_t srhpm_allreduce_buffer_size(int64_t d);
 int srhpm_add_rms_norm_allreduce(srhpm_ctx * ctx, float * x, const uint64_t * peer_buffers, int world, int rank,
                                  int slot, uint32_t * epochs, const float * w, float eps, float * y, int n, int64_t d,
                                  void * stream);
+/* srhpm_add_rms_norm_allreduce fused with the activation quantization of the GEMM that consumes y, as
+ * srhpm_add_rms_norm_quant is for srhpm_add_rms_norm: the same flag barrier and rank-order sum of the peers' slot
+ * `slot` rows, the residual add and the norm, and W_next's activation records written into wdata for
+ * srhpm_mul_mat_prequantized. One launch instead of the norm plus srhpm_mul_mat's own quantizer. Same limits as both
+ * (K-quant and IQ4_XS W_next, n <= 16, d <= 16384, world <= 8). No counterpart in the reference (one device). */
+int srhpm_add_rms_norm_allreduce_quant(srhpm_ctx * ctx, float * x, const uint64_t * peer_buffers, int world,
+                                       int rank, int slot, uint32_t * epochs, const float * w, float eps, float * y,
+                                       int n, const srhpm_tensor * W_next, void * wdata, size_t wsize, void * stream);
 int srhpm_rope_kv(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int n_head, int n_head_kv, int head_dim,
                   const int32_t * pos, float theta_base, const srhpm_tensor * k_cache, const srhpm_tensor * v_cache,
                   void * stream);

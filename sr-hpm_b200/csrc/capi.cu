@@ -291,6 +291,21 @@ int srhpm_add_rms_norm_quant(srhpm_ctx * ctx, float * x, const float * delta, co
                           (cudaStream_t) stream);
 }
 
+int srhpm_add_rms_norm_allreduce_quant(srhpm_ctx * ctx, float * x, const uint64_t * peer_buffers, int world,
+                                       int rank, int slot, uint32_t * epochs, const float * w, float eps, float * y,
+                                       int n, const srhpm_tensor * W_next, void * wdata, size_t wsize, void * stream) {
+    if (!ctx || !x || !peer_buffers || !epochs || !w || !y || !W_next || n < 1 || n > 16) return SRHPM_ERR_INVALID;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) & 15) {
+        return SRHPM_ERR_ALIGN;
+    }
+    if (W_next->type != SRHPM_TYPE_Q4_K && W_next->type != SRHPM_TYPE_Q5_K && W_next->type != SRHPM_TYPE_Q6_K &&
+        W_next->type != SRHPM_TYPE_Q3_K && W_next->type != SRHPM_TYPE_IQ4_XS) {
+        return SRHPM_UNSUPPORTED;
+    }
+    return norm_quant_run(ctx, W_next->type, W_next->ne[1], W_next->ne[0], n, x, nullptr, w, eps, y, wdata, wsize,
+                          (cudaStream_t) stream, peer_buffers, world, rank, slot, epochs);
+}
+
 int srhpm_swiglu_quant(srhpm_ctx * ctx, const float * gate, const float * up, int64_t ld_in, float * out,
                        int64_t ld_out, int n, const srhpm_tensor * W_next, void * wdata, size_t wsize, void * stream) {
     if (!ctx || !gate || !up || !out || !W_next || n < 1 || n > 16 || ld_in < W_next->ne[0] ||

@@ -14,6 +14,7 @@
 
 #include <cmath>
 
+#include "allreduce.cuh"
 #include "internal.h"
 #include "launch.cuh"
 #include "ptx.cuh"
@@ -105,35 +106,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_kernel(float * x, c
 }
 
 // ---- residual add of a tensor-parallel partial sum + RMSNorm, the all-reduce done in the same kernel ------------
-// Every rank's row-parallel GEMM (attention output, FFN down) wrote its partial sum into slot `slot` of its own
-// symmetric buffer (mapped on every peer): [2 slots][16 rows][d] f32, then flags [2][16][kArMaxRanks] u32. CTA i
-// (row i): one thread bumps this rank's epoch of (slot, row), publishes it into every peer's flag (slot, i, rank),
-// waits until every peer's flag in its own buffer has reached it (bounded: 2 s, then an error status), and the row
-// is summed over ranks in rank order (every rank adds the same values in the same order: identical results). Each
-// slot is rewritten only after a later barrier of the same rows, so two suffice.
-// Ordering (PTX memory model, system scope): the partial rows were written by the previous kernel of each rank,
-// complete and visible to this grid once it passes griddepcontrol.wait. Thread 0 then issues one fence.acq_rel.sys
-// before its relaxed flag stores (a release: the rows are ordered before the flags every peer polls) and one
-// fence.acq_rel.sys after its polls have seen every peer's flag (an acquire: the peers' rows are ordered before the
-// loads below); the CTA barrier carries that order to the other threads. One fence on each side per CTA, not one per
-// signal; the peer rows are read uncached (ld.global.cv).
-constexpr int kArMaxRanks = 8;
-constexpr int kArRows     = 16;
-
-__device__ __forceinline__ uint64_t global_timer_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void st_relaxed_sys(uint32_t * p, uint32_t v) {
-    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t * p) {
-    uint32_t v;
-    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
+// CTA i (row i): the flag barrier of allreduce.cuh, then x += the ranks' partial rows (rank order) and the norm.
 __global__ void __launch_bounds__(kNormThreads) add_rms_norm_ar_kernel(float * x, const uint64_t * peers, int world,
                                                                         int rank, int slot, uint32_t * epochs,
                                                                         const float * w, float eps, float * y,
@@ -141,31 +114,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_ar_kernel(float * x
     pdl_launch_dependents();
     pdl_wait();  // this rank's GEMM has written its partial rows
     const int64_t i = blockIdx.x;
-    const size_t  part_bytes = (size_t) kArRows * d * sizeof(float);
-    const size_t  flag_off   = 2 * part_bytes;
     __shared__ int ok_s;
-    if (threadIdx.x == 0) {
-        const uint32_t e = ++epochs[slot * kArRows + i];
-        const size_t fo = flag_off + ((size_t) (slot * kArRows + i) * kArMaxRanks + rank) * sizeof(uint32_t);
-        fence_acq_rel_sys();  // release: this rank's partial rows before its flags
-        for (int j = 0; j < world; j++) st_relaxed_sys(reinterpret_cast<uint32_t *>(peers[j] + fo), e);
-        const uint32_t * mine = reinterpret_cast<const uint32_t *>(peers[rank] + flag_off) +
-                                (size_t) (slot * kArRows + i) * kArMaxRanks;
-        const uint64_t   t0 = global_timer_ns();
-        int              ok = 1;
-        for (int j = 0; j < world && ok; j++) {
-            while ((int32_t) (ld_relaxed_sys(mine + j) - e) < 0) {
-                if (global_timer_ns() - t0 > 2000000000ull) {
-                    ok = 0;
-                    atomicExch(status, kErrPeerWait);
-                    break;
-                }
-                __nanosleep(64);
-            }
-        }
-        fence_acq_rel_sys();  // acquire: every peer's partial rows after its flag
-        ok_s = ok;
-    }
+    if (threadIdx.x == 0) ok_s = ar_row_barrier(peers, world, rank, slot, epochs, (int) i, d, status);
     __syncthreads();
     float * xr = x + i * d;
     float   ss = 0.0f;
@@ -176,12 +126,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_ar_kernel(float * x
         const int64_t j = threadIdx.x + (int64_t) k * kNormThreads;
         if (j < d4) {
             float4 a = reinterpret_cast<const float4 *>(xr)[j];
-            if (ok_s) {
-                for (int r = 0; r < world; r++) {
-                    const float4 b = __ldcv(reinterpret_cast<const float4 *>(peers[r] + slot * part_bytes) + i * d4 + j);
-                    a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
-                }
-            }
+            if (ok_s) ar_add_row4(a, peers, world, slot, (int) i, d4, j);
             reinterpret_cast<float4 *>(xr)[j] = a;
             v[k] = a;
             ss = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, ss))));

@@ -39,8 +39,11 @@ int    gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int
 size_t gemm_work_size_unsplit(int wtype, int64_t rows, int64_t K, int64_t N);
 int    gemm_run_prequant(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                          int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize, cudaStream_t stream);
+// peers != null: the delta is the all-reduce of the ranks' partial rows (srhpm_add_rms_norm_allreduce_quant)
 int    norm_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_t N, float * x, const float * delta,
-                      const float * w, float eps, float * y, void * wdata, size_t wsize, cudaStream_t stream);
+                      const float * w, float eps, float * y, void * wdata, size_t wsize, cudaStream_t stream,
+                      const uint64_t * peers = nullptr, int world = 1, int rank = 0, int slot = 0,
+                      uint32_t * epochs = nullptr);
 int    swiglu_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_t N, const float * gate,
                         const float * up, int64_t ld_in, float * h, int64_t ld_out, void * wdata, size_t wsize,
                         cudaStream_t stream);

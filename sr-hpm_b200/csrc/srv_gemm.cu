@@ -28,6 +28,7 @@
 #include <cuda.h>
 #include <cstring>
 
+#include "allreduce.cuh"
 #include "internal.h"
 #include "launch.cuh"
 #include "ptx.cuh"
@@ -52,6 +53,16 @@ __host__ __device__ constexpr int rec_bytes(bool q80, int NT) {
 
 // ---------------------------------------------------------------------------------------------------------------
 // activation quantizers
+
+// Warm L2 with this warp's activation segment (256 floats: one 128-byte line per 4 lanes) while the previous grid is
+// still finishing. A hint only: the loads after griddepcontrol.wait still return what that grid wrote (L2 is the
+// point of coherence the writes reach), so X may be the previous kernel's output.
+__device__ __forceinline__ void prefetch_act_l2(const float * X, int64_t ldx, int N, int nsb, int TT, int lane) {
+    const int64_t wid = (int64_t) blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (wid >= (int64_t) nsb * TT || (lane & 3) != 0) return;
+    const int sb = (int) (wid / TT), t = (int) (wid % TT);
+    if (t < N) asm volatile("prefetch.global.L2 [%0];" ::"l"(X + (int64_t) t * ldx + (int64_t) sb * QK + 8 * lane));
+}
 
 // one warp per (super-block, token); lane l owns columns 8l..8l+7
 __device__ __forceinline__ void load8(const float * __restrict__ xp, float (&v)[8]) {
@@ -142,6 +153,7 @@ __global__ void __launch_bounds__(256) quant_q8K_kernel(const float * __restrict
     // launched early behind the previous call's GEMM: let the next GEMM get resident, then wait for the previous
     // grid (it may still read the records and counters this kernel rewrites, or write the X it reads)
     pdl_launch_dependents();
+    if (X) prefetch_act_l2(X, ldx, N, nsb, DENSE ? N : NT, threadIdx.x & 31);
     pdl_wait();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncnt; i += gridDim.x * blockDim.x) cnt[i] = 0;
     const int     lane = threadIdx.x & 31;
@@ -225,11 +237,22 @@ __global__ void __launch_bounds__(256) swiglu_q8K_kernel(const float * __restric
 // prologue): CTA t < N: x += delta; y = x / sqrt(mean(x^2) + eps) * w (as add_rms_norm); the row of y is staged in
 // shared memory and each warp quantizes super-blocks of it into the GEMM's activation records exactly as
 // quant_q8K_kernel does (same functions); CTAs N..NT-1 write the zero padding rows; CTA 0 zeroes the split-K counters.
+// With ar.peers set, the delta is the tensor-parallel all-reduce of the ranks' partial rows instead (the flag barrier
+// and the rank-order sum of allreduce.cuh, as add_rms_norm_ar_kernel does): all-reduce, residual add, norm and the
+// next GEMM's activation records in one kernel.
+struct NormAr {
+    const uint64_t * peers;  // null: no all-reduce
+    int              world, rank, slot;
+    uint32_t *       epochs;
+    int32_t *        status;
+};
+
 constexpr int kNormQThreads = 1024;
 __global__ void __launch_bounds__(kNormQThreads) add_rms_norm_q8K_kernel(float * x, const float * delta,
                                                                           const float * w, float eps, float * y,
                                                                           int N, int64_t d, int NT, uint8_t * recs,
-                                                                          int perm, int32_t * cnt, int ncnt) {
+                                                                          int perm, int32_t * cnt, int ncnt,
+                                                                          const NormAr ar) {
     pdl_launch_dependents();
     pdl_wait();
     extern __shared__ float ys[];
@@ -242,12 +265,22 @@ __global__ void __launch_bounds__(kNormQThreads) add_rms_norm_q8K_kernel(float *
         float *  xr = x + (int64_t) t * d;
         float    ss = 0.0f;
         float4   v[4];
+        __shared__ int ok_s;
+        if (ar.peers) {
+            if (threadIdx.x == 0) {
+                ok_s = ar_row_barrier(ar.peers, ar.world, ar.rank, ar.slot, ar.epochs, t, d, ar.status);
+            }
+            __syncthreads();
+        }
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             const int64_t j = threadIdx.x + (int64_t) k * kNormQThreads;
             if (j < d4) {
                 float4 a = reinterpret_cast<const float4 *>(xr)[j];
-                if (delta) {
+                if (ar.peers) {
+                    if (ok_s) ar_add_row4(a, ar.peers, ar.world, ar.slot, t, d4, j);
+                    reinterpret_cast<float4 *>(xr)[j] = a;
+                } else if (delta) {
                     const float4 b = reinterpret_cast<const float4 *>(delta + (int64_t) t * d)[j];
                     a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
                     reinterpret_cast<float4 *>(xr)[j] = a;
@@ -311,6 +344,7 @@ __global__ void __launch_bounds__(256) quant_q80_kernel(const float * __restrict
     // launched early behind the previous call's GEMM: let the next GEMM get resident, then wait for the previous
     // grid (it may still read the records and counters this kernel rewrites, or write the X it reads)
     pdl_launch_dependents();
+    prefetch_act_l2(X, ldx, N, nsb, DENSE ? N : NT, threadIdx.x & 31);
     pdl_wait();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncnt; i += gridDim.x * blockDim.x) cnt[i] = 0;
     const int     lane = threadIdx.x & 31;
@@ -1627,9 +1661,15 @@ int gemm_run_prequant(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t row
 }
 
 int norm_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_t N, float * x, const float * delta,
-                   const float * w, float eps, float * y, void * wdata, size_t wsize, cudaStream_t stream) {
+                   const float * w, float eps, float * y, void * wdata, size_t wsize, cudaStream_t stream,
+                   const uint64_t * peers, int world, int rank, int slot, uint32_t * epochs) {
     if (wtype == SRHPM_TYPE_Q8_0) return SRHPM_UNSUPPORTED;
     if (K % QK != 0 || K > 4 * 4 * kNormQThreads || N < 1 || N > 16) return SRHPM_ERR_INVALID;
+    if (peers && (N > kArRows || world < 1 || world > kArMaxRanks || rank < 0 || rank >= world || slot < 0 ||
+                  slot > 1 || !epochs)) {
+        return SRHPM_ERR_INVALID;
+    }
+    const NormAr ar = { peers, world, rank, slot, epochs, ctx->d_status };
     const WorkLayout wl = work_layout(wtype, rows, K, N);
     if (wsize < wl.total || !wdata) return SRHPM_ERR_WORKSPACE;
     uint8_t * base = align256(wdata);
@@ -1647,7 +1687,7 @@ int norm_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_t 
     const cudaError_t e = launch_k_pdl(add_rms_norm_q8K_kernel, dim3(NT), dim3(kNormQThreads), (size_t) K * 4, stream,
                                        x, delta, w, eps, y, (int) N, K, NT, base + wl.recs,
                                        (int) (wtype == SRHPM_TYPE_Q3_K), reinterpret_cast<int32_t *>(base + wl.cnt),
-                                       nrb);
+                                       nrb, ar);
     ctx->launches.fetch_add(1);
     return cuda_status(e);
 }

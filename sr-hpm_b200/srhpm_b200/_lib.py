@@ -78,6 +78,9 @@ _SIGNATURES = {
                                           ctypes.c_size_t, _P]),
     "srhpm_add_rms_norm_allreduce": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P,
                                                     ctypes.c_float, _P, ctypes.c_int, ctypes.c_int64, _P]),
+    "srhpm_add_rms_norm_allreduce_quant": (ctypes.c_int, [_P, _P, _P, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P,
+                                                          _P, ctypes.c_float, _P, ctypes.c_int, _T, _P, ctypes.c_size_t,
+                                                          _P]),
     "srhpm_add_rms_norm": (ctypes.c_int, [_P, _P, _P, _P, ctypes.c_float, _P, ctypes.c_int, ctypes.c_int64, _P]),
     "srhpm_rope_kv": (ctypes.c_int, [_P, _P, ctypes.c_int64, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, _P,
                                      ctypes.c_float, _T, _T, _P]),

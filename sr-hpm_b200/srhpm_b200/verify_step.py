@@ -203,8 +203,12 @@ class TensorParallel:
     argmax records are all-gathered with NCCL before the acceptance either way. All of it is captured in the step's
     CUDA graph."""
 
-    def __init__(self, rank, world, group=None, fused=True):
+    def __init__(self, rank, world, group=None, fused=True, fused_quant=False):
         self.rank, self.world, self.group, self.fused = rank, world, group, fused
+        # fused_quant: the all-reduce norm also writes the next GEMM's activation records
+        # (srhpm_add_rms_norm_allreduce_quant). Off by default: on two B200s the separate quantizer launch measured
+        # faster (7.34 vs 7.42 ms per 27B step at k = 8, same box).
+        self.fused_quant = fused_quant
         self.part = self.peers = self.epochs = None
 
     def setup(self, d, device):
@@ -316,10 +320,11 @@ class VerifyStep:
 
     def _norm_mm(self, delta_slot, wnorm, W, Y):
         """Residual add + RMSNorm of the pending delta, then the GEMM of W on the normed rows into Y: one fused
-        norm + activation-quantization launch and the GEMM on its records (srhpm_add_rms_norm_quant +
-        srhpm_mul_mat_prequantized), or the separate norm and srhpm_mul_mat (its own quantizer) where that does not
-        apply (tensor-parallel fused all-reduce norms, Q8_0 weights)."""
-        if not self.fuse_prologue or W.qtype == L.Q8_0 or (delta_slot is not None and self._fused()):
+        norm + activation-quantization launch and the GEMM on its records (srhpm_add_rms_norm_quant, or with the
+        tensor-parallel fused all-reduce and TensorParallel.fused_quant srhpm_add_rms_norm_allreduce_quant, +
+        srhpm_mul_mat_prequantized), or the separate norm and srhpm_mul_mat (its own quantizer) otherwise."""
+        ar = delta_slot is not None and self._fused()
+        if not self.fuse_prologue or W.qtype == L.Q8_0 or (ar and not self.tp.fused_quant):
             return [self._norm(delta_slot, wnorm), self._mm(W, self.y, Y)]
         c, n, lib, h = self.cfg, self.n, self.lib, self.ctx.handle
         st, ws = self.ctx.mul_mat_work_size(W, self.y)
@@ -327,11 +332,17 @@ class VerifyStep:
         self._ws = max(self._ws, ws)
         wv, xv, yv = W.view(), f32_rows_view(self.y), f32_rows_view(Y)
         self._keep += [wv, xv, yv]
-        return [("add_rms_norm_quant", lib.srhpm_add_rms_norm_quant,
-                 [h, self._ptr(self.x), None if delta_slot is None else self._ptr(self.o), self._ptr(wnorm),
-                  ctypes.c_float(c.eps), self._ptr(self.y), n, ctypes.byref(wv)], True),
-                ("mul_mat_prequantized", lib.srhpm_mul_mat_prequantized,
-                 [h, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv)], True)]
+        if ar:
+            tp = self.tp
+            norm = ("add_rms_norm_allreduce_quant", lib.srhpm_add_rms_norm_allreduce_quant,
+                    [h, self._ptr(self.x), self._ptr(tp.peers), tp.world, tp.rank, delta_slot, self._ptr(tp.epochs),
+                     self._ptr(wnorm), ctypes.c_float(c.eps), self._ptr(self.y), n, ctypes.byref(wv)], True)
+        else:
+            norm = ("add_rms_norm_quant", lib.srhpm_add_rms_norm_quant,
+                    [h, self._ptr(self.x), None if delta_slot is None else self._ptr(self.o), self._ptr(wnorm),
+                     ctypes.c_float(c.eps), self._ptr(self.y), n, ctypes.byref(wv)], True)
+        return [norm, ("mul_mat_prequantized", lib.srhpm_mul_mat_prequantized,
+                       [h, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv)], True)]
 
     def _norm(self, delta_slot, wnorm):
         """Residual add of the pending delta (none for the first block) + RMSNorm into y."""

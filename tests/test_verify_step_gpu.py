@@ -196,20 +196,28 @@ def _tp_worker(rank, world, port, cfg_kw, seed, cap, n_past, ids, draft, q, fuse
         kcr = [torch.from_numpy(np.ascontiguousarray(a[:, g0:g1])).cuda() for a in kc]
         vcr = [torch.from_numpy(np.ascontiguousarray(a[:, g0:g1])).cuda() for a in vc]
         ctx = S.Context(rank)
-        step = V.VerifyStep(ctx, cfg, dev_w, kcr, vcr, len(ids), n_past,
-                            tp=V.TensorParallel(rank, world, fused=fused))
+        tp = V.TensorParallel(rank, world, fused=fused, fused_quant=True)
+        step = V.VerifyStep(ctx, cfg, dev_w, kcr, vcr, len(ids), n_past, tp=tp)
         step.set_tokens(ids, draft)
         step.run()
         torch.cuda.synchronize()
         ctx.check()
+        # the same step without the fused prologues (separate all-reduce norm and GEMM quantizer): bit-identical
+        plain = V.VerifyStep(ctx, cfg, dev_w, [a.clone() for a in kcr], [a.clone() for a in vcr], len(ids), n_past,
+                             tp=tp, fuse_prologue=False)
+        plain.set_tokens(ids, draft)
+        plain.run()
+        torch.cuda.synchronize()
+        ctx.check()
+        same = bool(torch.equal(plain.logits, step.logits))
         parts = [torch.zeros_like(step.logits) for _ in range(world)]
         dist.all_gather(parts, step.logits.contiguous())
         if rank == 0:
-            q.put(("ok", torch.cat(parts, dim=1).cpu().numpy(), step.accepted()))
+            q.put(("ok", torch.cat(parts, dim=1).cpu().numpy(), step.accepted(), same))
         dist.barrier()
         dist.destroy_process_group()
     except BaseException as e:  # report instead of hanging the parent
-        q.put(("err", f"rank {rank}: {type(e).__name__}: {e}", None))
+        q.put(("err", f"rank {rank}: {type(e).__name__}: {e}", None, None))
         raise
 
 
@@ -220,7 +228,8 @@ def test_tensor_parallel_step_matches_one_gpu(ctx, Hkv, fused):
     acceptance) against the same step on one GPU. The all-reduces run either inside the next RMSNorm over peer memory
     (fused) or as NCCL calls; Hkv = 1 replicates the KV head on both ranks. Logits within 2e-2 (the partial sums
     change f32 rounding, re-quantization flips follow, as in the oracle comparison), accepted ids equal where the
-    top-1 margin is clear."""
+    top-1 margin is clear. On each rank the step with the fused prologues (the all-reduce norm writing the next
+    GEMM's activation records) gives the same logits bit for bit as the step without them."""
     import socket
     import torch.multiprocessing as mp
     cfg_kw = dict(n_layer=3, d=512, n_ff=768, H=4, Hkv=Hkv, hd=256, n_vocab=1000, base=1e6, eps=1e-6, window=40,
@@ -258,6 +267,7 @@ def test_tensor_parallel_step_matches_one_gpu(ctx, Hkv, fused):
     errs = [r[1] for r in res if r[0] == "err"]
     assert not errs, errs
     got = [r for r in res if r[0] == "ok"][0]
+    assert got[3], "fused and unfused prologues differ"
     assert rel_l2(got[1], logits1) < 2e-2, rel_l2(got[1], logits1)
     srt = np.sort(logits1, axis=1)
     margin = srt[:, -1] - srt[:, -2]
@@ -295,6 +305,36 @@ def test_allreduce_norm_peer_wait_times_out(ctx):
     for buf in (mine, fake):
         flags = buf[off:].view(torch.int32).view(2, 16, 8)
         assert flags[0, :n, 0].tolist() == [1] * n
+
+
+def test_allreduce_norm_quant_peer_wait_times_out(ctx):
+    """The fused all-reduce + norm + quantization prologue has the same bounded flag wait: against a stand-in peer
+    whose flag nothing sets it gives up after ~2 s with an error status, and the context stays usable."""
+    import time
+    lib = L.load()
+    d, n, rows = 512, 2, 64
+    nbytes = int(lib.srhpm_allreduce_buffer_size(d))
+    mine = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    fake = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    peers = torch.tensor([mine.data_ptr(), fake.data_ptr()], dtype=torch.int64, device="cuda")
+    epochs = torch.zeros(32, dtype=torch.int32, device="cuda")
+    x = torch.randn((n, d), device="cuda")
+    w = torch.ones(d, device="cuda")
+    y = torch.empty_like(x)
+    W = S.QuantTensor.from_blocks(O.random_blocks(S.Q4_K, rows * d // 256, np.random.default_rng(3)), S.Q4_K, rows, d)
+    wv = W.view()
+    st, ws = ctx.mul_mat_work_size(W, x)
+    work = torch.empty(ws, dtype=torch.uint8, device="cuda")
+    ptr = lambda t: t.data_ptr()
+    t0 = time.time()
+    L.check(lib.srhpm_add_rms_norm_allreduce_quant(ctx.handle, ptr(x), ptr(peers), 2, 0, 0, ptr(epochs), ptr(w),
+                                                   1e-6, ptr(y), n, ctypes.byref(wv), ptr(work), work.numel(), None),
+            "srhpm_add_rms_norm_allreduce_quant")
+    torch.cuda.synchronize()
+    assert time.time() - t0 > 1.5
+    with pytest.raises(L.SrhpmError):
+        ctx.check()
+    ctx.check()
 
 
 def test_fused_norm_quant_prologue_is_exact(ctx):
