@@ -48,6 +48,10 @@ BLOCK = {12: (256, 144), 13: (256, 176), 14: (256, 210), 8: (32, 34), 23: (256, 
 NS = [2, 4, 8]
 SEED = 1234
 DATA_DESC = "synthetic (seeded N(0,0.02) weights quantized on the host, N(0,1) activations)"
+# DRAM bytes (read + write) per srv_gemm_kernel launch over one step of the default sweep on one GPU, from one ncu
+# capture (profiles/srv_gemm_sweep_60products_launches.md): 2612.05 MB over the 60 launches; the algorithmic bytes
+# per launch are 43.53 MB as well
+SWEEP_TRAFFIC_PER_LAUNCH = 43.534e6
 
 
 def row_bytes(t, K):
@@ -480,6 +484,37 @@ def run_gpu(args):
         barrier()
         return e0.elapsed_time(e1)
 
+    # several ranks: the same chunks, each with its own packed buffers and all-gather; a chunk's gathered outputs go
+    # back on the copy stream while the next chunk's products and all-gather run
+    def chunked_multi():
+        out = []
+        for c in range(nchunk):
+            idx = list(range(cb[c], cb[c + 1]))
+            pk = shard.PackedSlices([(ops[i][0], ops[i][2]) for i in idx], world)
+            yl = torch.zeros(pk.size, dtype=torch.float32, device=dev)
+            yg = torch.zeros(world * pk.size, dtype=torch.float32, device=dev)
+            yh = torch.empty(world * pk.size, dtype=torch.float32).pin_memory()
+            rr = []
+            for j, i in enumerate(idx):
+                N, t, rows, K = ops[i]
+                W = shards[(t, rows, K, copy_of[i])][0]
+                rr.append(ctx.prepare_mul_mat(W, xs[(N, K)], pk.local_view(yl, j, rank), work))
+            out.append((rr, yl, yg, yh))
+        return out
+
+    def e2e_step_pipelined_multi():
+        x_dev.copy_(x_host, non_blocking=True)
+        for c, (rr, yl, yg, yh) in enumerate(chunks):
+            stream.wait_event(copied[c])
+            for run in rr:
+                run()
+            dist.all_gather_into_tensor(yg, yl)
+            ran[c].record(stream)
+            copy_s.wait_event(ran[c])
+            with torch.cuda.stream(copy_s):
+                yh.copy_(yg, non_blocking=True)
+            copied[c].record(copy_s)
+
     e2e_mode = "serial: H2D, the products, one D2H of all outputs"
     if world == 1:
         try:
@@ -489,8 +524,12 @@ def run_gpu(args):
             torch.cuda.synchronize()
             e2e_ms = time_e2e(e2e_step_serial)
             e2e_mode += f" (chunked form failed: {type(e).__name__})"
-    else:
-        e2e_ms = time_e2e(e2e_step_serial)
+    else:  # every rank takes the same path (collectives inside): no per-rank fallback
+        chunks = chunked_multi()
+        d2h = sum(ch[3].numel() * 4 for ch in chunks)
+        e2e_ms = time_e2e(e2e_step_pipelined_multi, copied[-1])
+        e2e_mode = (f"{nchunk} chunks, each its products, its all-gather and its D2H on a second stream while the "
+                    "next chunk runs")
     if world > 1:
         tt = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -509,12 +548,18 @@ def run_gpu(args):
     if world == 1 and not args.only:
         n1 = measure_sweep_n1(ctx, dev, shards, peak)
 
-    step_tp = None
+    step_tp = step_tp_q8 = None
     if world > 1 and not args.no_step:  # every rank takes part (collectives inside the step)
         try:
             step_tp = measure_step_27b_tp(ctx, dev, rank, world)
         except Exception as e:  # recorded beside the sweep rather than losing its line
             step_tp = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+        torch.cuda.empty_cache()
+        try:
+            step_tp_q8 = measure_step_27b_tp(ctx, dev, rank, world, n_past=131072, reps=5, kv_q8=True)
+        except Exception as e:  # recorded beside the sweep rather than losing its line
+            step_tp_q8 = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+        torch.cuda.empty_cache()
     attn_split = attn_heads = None
     if world > 1 and not args.no_attn:  # every rank takes part (an all-gather per call)
         try:
@@ -526,11 +571,16 @@ def run_gpu(args):
                 attn_heads = measure_attention_kv_heads(ctx, dev, rank, world, peak)
             except Exception as e:  # recorded beside the sweep rather than losing its line
                 attn_heads = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+    traffic, traffic_src = args.traffic, "--traffic" if args.traffic is not None else None
+    if traffic is None and world == 1 and not args.only:
+        traffic, traffic_src = SWEEP_TRAFFIC_PER_LAUNCH, "ncu capture of one sweep step on one B200 (profiles/)"
     if rank == 0:
         cfg = workload_config(base_ops, world)
         meas["timed"] = "CUDA graph of one step, replayed" if graph is not None else "eager calls"
         if step_tp is not None:
             meas["verify_step_27b_f16kv_2048_tp"] = step_tp
+        if step_tp_q8 is not None:
+            meas["verify_step_27b_q8kv_131072_tp"] = step_tp_q8
         if attn_split is not None:
             meas["attention_q8_0_split_k"] = attn_split
         if attn_heads is not None:
@@ -584,7 +634,10 @@ def run_gpu(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "kernel": "srv_gemm_kernel (+ activation quantizer, PDL-overlapped)",
-                         "traffic": args.traffic},
+                         "algorithmic_bytes_per_launch": round(sum(my_bytes) / len(my_bytes)),
+                         "launch_us": round(ms_step * 1e3 / len(ops), 3),
+                         "traffic": traffic,
+                         "traffic_source": traffic_src},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "copies": e2e_mode},
@@ -765,8 +818,9 @@ def _full_caches(cfg, dev, n_layer_cap, seed):
     return kc, vc
 
 
-def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0):
-    """The 27B-class verify step (k = 8, f16 KV of 2048 tokens) on `world` GPUs in Megatron tensor parallelism
+def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0, kv_q8=False):
+    """The 27B-class verify step (k = 8, f16 KV of 2048 tokens; kv_q8: q8_0 KV of n_past tokens, BASELINE config 5,
+    timed without the parity pass) on `world` GPUs in Megatron tensor parallelism
     (column-parallel QKV / gate|up / head, row-parallel O / down with the all-reduce fused into the next RMSNorm, KV
     heads split or replicated per rank, vocabulary-sharded acceptance). Every rank builds the same whole model
     (random blocks, one seed) and cuts its slices on the device (DeviceWeights.slice_of), and the same whole cache
@@ -780,15 +834,26 @@ def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0
     import torch.distributed as dist
     from srhpm_b200 import _lib as L
     from srhpm_b200 import verify_step as V
-    cfg = V.DecoderConfig(kv_type=L.F16)
+    cfg = V.DecoderConfig(kv_type=L.Q8_0 if kv_q8 else L.F16)
     full = V.DeviceWeights.random(cfg, dev, seed)
     w = V.DeviceWeights.slice_of(full, rank, world)
     g0, g1 = w.tp["g0"], w.tp["g1"]
     n = k + 1
     cap = n_past + n
-    kc_full, vc_full = _full_caches(cfg, dev, cap, seed + 7)
-    kc = [c[:, g0:g1].contiguous() for c in kc_full]
-    vc = [c[:, g0:g1].contiguous() for c in vc_full]
+    if kv_q8:  # this rank's KV heads only, N(0, 1) quantized on the device
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed + 7 + rank)
+        kc, vc = [], []
+        for _ in range(cfg.n_layer):
+            for lst in (kc, vc):
+                x = torch.randn((cap * (g1 - g0), cfg.hd), device=dev, generator=gen)
+                lst.append(ctx.quantize_rows_q8_0(x).view(cap, g1 - g0, 272))
+                del x
+        kc_full = vc_full = None
+    else:
+        kc_full, vc_full = _full_caches(cfg, dev, cap, seed + 7)
+        kc = [c[:, g0:g1].contiguous() for c in kc_full]
+        vc = [c[:, g0:g1].contiguous() for c in vc_full]
     step = V.VerifyStep(ctx, cfg, w, kc, vc, n, n_past, tp=V.TensorParallel(rank, world))
     ids = torch.arange(n, dtype=torch.int32, device=dev) * 977 % cfg.n_vocab  # the same tokens on every rank
     step.set_tokens(ids, ids[1:])
@@ -819,6 +884,15 @@ def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0
     ms = float(tt.item())
     del graph  # holds NCCL calls: released before the process group
 
+    if kv_q8:
+        acc = int(step.out_n.item())
+        del step, kc, vc, full, w
+        torch.cuda.empty_cache()
+        dist.barrier()
+        nbytes = step_bytes_27b(cfg, n_past, n)
+        return {f"k{k}": {"ms": round(ms, 3), "steps_per_s": round(1e3 / ms, 1), "gpus": world,
+                          "GBps_per_gpu": round(nbytes / world / (ms * 1e-3) / 1e9, 1), "bytes": nbytes,
+                          "kernel_launches_per_rank": launches, "accepted": acc, "kv": f"q8_0, {n_past} past tokens"}}
     # parity against the whole model on rank 0's GPU
     par = None
     ids1 = torch.zeros(n, dtype=torch.int32, device=dev)
@@ -960,8 +1034,10 @@ def measure_attention_split(ctx, dev, rank, world, peak, reps=20, lengths=(8192,
     shard.kv_range(L, world, j) of the 4 KV heads' q8_0 cache; one call = the partial records of its range, an NCCL
     all-gather of the record sets (24 * 8 * 1032 bytes per rank) and the merge, all in one CUDA graph over copies of
     the rank's range that together exceed L2. Time = max over ranks; GB/s counts the whole cache once (plus Q and O),
-    as on one GPU. Parity: the first copy is the rank's range of one whole cache (same seed on every rank); its
-    merged output against the whole-range call on rank 0's one GPU (relative L2, bar 1e-3)."""
+    as on one GPU. Two exchanges of the records: an NCCL all-gather, and every rank reading the others'
+    symmetric-memory buffers after a flag barrier (no collective). Parity: the first copy is the rank's range of one
+    whole cache (same seed on every rank); its merged output against the whole-range call on rank 0's one GPU
+    (relative L2, bar 1e-3)."""
     import torch
     import torch.distributed as dist
     import srhpm_b200 as S
@@ -988,52 +1064,56 @@ def measure_attention_split(ctx, dev, rank, world, peak, reps=20, lengths=(8192,
             kv.append(pair)
         mask = _causal_mask(N, L, dev)
         mr = mask[:, t0:t1]
-        att = SplitKAttention(ctx, rank, world, H, N, dev)
         st, ws = ctx.flash_attn_ext_work_size(q, kv[0][0], kv[0][1], S.Q8_0)
         work = torch.empty(max(ws, 16), dtype=torch.uint8, device=dev)
-        for i in range(3):
-            att(q, *kv[i % ncopy], S.Q8_0, mask=mr, work=work)
-        torch.cuda.synchronize()
-        s = torch.cuda.Stream(dev)
-        s.wait_stream(torch.cuda.current_stream())
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(s):
-            with torch.cuda.graph(graph, stream=s):
-                for i in range(ncopy):
-                    att(q, *kv[i], S.Q8_0, mask=mr, work=work)
-        torch.cuda.synchronize()
-        graph.replay()
-        torch.cuda.synchronize()
-        dist.barrier()
-        rounds = max(1, reps // ncopy)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(rounds):
+        res = {}
+        for exchange in ("nccl", "peers"):
+            att = SplitKAttention(ctx, rank, world, H, N, dev, exchange=exchange)
+            for i in range(3):
+                att(q, *kv[i % ncopy], S.Q8_0, mask=mr, work=work)
+            torch.cuda.synchronize()
+            s = torch.cuda.Stream(dev)
+            s.wait_stream(torch.cuda.current_stream())
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(graph, stream=s):
+                    for i in range(ncopy):
+                        att(q, *kv[i], S.Q8_0, mask=mr, work=work)
+            torch.cuda.synchronize()
             graph.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        ctx.check()
-        tt = torch.tensor([e0.elapsed_time(e1) * 1e3 / (rounds * ncopy)], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        us = float(tt.item())
-        del graph  # the graph holds NCCL calls: released before the process group
-        # parity: the first copy (this rank's range of the whole cache) merged, against the whole range on one GPU
-        got = att(q, *kv[0], S.Q8_0, mask=mr, work=work).clone()
-        torch.cuda.synchronize()
-        par = None
-        if rank == 0:
-            try:
-                want = ctx.flash_attn_ext(q, kfull, vfull, S.Q8_0, mask=mask)
-                torch.cuda.synchronize()
-                err = float(torch.linalg.vector_norm(got - want) / torch.linalg.vector_norm(want))
-                par = {"rel_l2": float(f"{err:.3e}"), "bar": 1e-3, "pass": bool(err <= 1e-3),
-                       "against": "the whole range on one GPU"}
-            except Exception as e:
-                par = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
-        dist.barrier()
-        gbs = nbytes / (us * 1e-6) / 1e9
-        out[str(L)] = {"us": round(us, 2), "GBps": round(gbs, 1), "GBps_per_gpu": round(gbs / world, 1),
-                       "frac_per_gpu": round(gbs / world / peak, 4), "bytes": nbytes, "gpus": world, "parity": par}
+            torch.cuda.synchronize()
+            dist.barrier()
+            rounds = max(1, reps // ncopy)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(rounds):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ctx.check()
+            tt = torch.tensor([e0.elapsed_time(e1) * 1e3 / (rounds * ncopy)], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            us = float(tt.item())
+            del graph  # the graph holds NCCL calls: released before the process group
+            # parity: the first copy (this rank's range of the whole cache) merged, against the whole range on one GPU
+            got = att(q, *kv[0], S.Q8_0, mask=mr, work=work).clone()
+            torch.cuda.synchronize()
+            par = None
+            if rank == 0:
+                try:
+                    want = ctx.flash_attn_ext(q, kfull, vfull, S.Q8_0, mask=mask)
+                    torch.cuda.synchronize()
+                    err = float(torch.linalg.vector_norm(got - want) / torch.linalg.vector_norm(want))
+                    par = {"rel_l2": float(f"{err:.3e}"), "bar": 1e-3, "pass": bool(err <= 1e-3),
+                           "against": "the whole range on one GPU"}
+                except Exception as e:
+                    par = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+            dist.barrier()
+            gbs = nbytes / (us * 1e-6) / 1e9
+            res[exchange] = {"us": round(us, 2), "GBps": round(gbs, 1), "GBps_per_gpu": round(gbs / world, 1),
+                             "frac_per_gpu": round(gbs / world / peak, 4), "parity": par}
+            del att
+        out[str(L)] = {"bytes": nbytes, "gpus": world, "exchange": res}
         del kv, kfull, vfull
         torch.cuda.empty_cache()
     return out

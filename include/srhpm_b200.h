@@ -158,6 +158,18 @@ int    srhpm_flash_attn_ext_partial(srhpm_ctx * ctx, const srhpm_tensor * q, con
                                     float softcap, void * part, void * wdata, size_t wsize, void * stream);
 int    srhpm_flash_attn_merge(srhpm_ctx * ctx, const void * parts, int n_parts, const srhpm_tensor * sinks,
                               srhpm_tensor * dst, void * stream);
+/* The same merge without a collective: every rank's record set sits at the start of its own buffer of
+ * srhpm_flash_attn_peer_buffer_size(H, N) bytes, mapped on every rank (peer_buffers[j] = rank j's buffer as this rank
+ * addresses it: symmetric memory), written there by srhpm_flash_attn_ext_partial. Per row, the call meets the other
+ * ranks' calls at a flag barrier in those buffers (bounded: 2 s, then an error status), reads every rank's record
+ * over NVLink in rank order, adds the sinks, writes dst as srhpm_flash_attn_merge does (the same arithmetic, so the
+ * same result), and meets them at a second barrier once it has read them, so that no rank's next partial call
+ * overwrites records a peer still reads. epochs: u32 [H * N] on this device, zero at the start, counted per call
+ * identically on every rank. Every rank must make the same calls in the same order; world <= 8. No counterpart in
+ * the reference (one device). */
+size_t srhpm_flash_attn_peer_buffer_size(int64_t n_head, int64_t n_tokens);
+int    srhpm_flash_attn_merge_peers(srhpm_ctx * ctx, const uint64_t * peer_buffers, int world, int rank,
+                                    uint32_t * epochs, const srhpm_tensor * sinks, srhpm_tensor * dst, void * stream);
 
 /* ---- greedy acceptance -----------------------------------------------------------------------------------------
  * Target logits f32 [n_vocab, >= n_draft + 1] (row i scores the token after draft position i; row stride nb[1]) and

@@ -1,5 +1,6 @@
-// The peer-memory all-reduce of the tensor-parallel decoder step, shared by the kernels that fuse it into their
-// prologue (add_rms_norm_ar_kernel in decoder_ops.cu, add_rms_norm_q8K_kernel in srv_gemm.cu).
+// The peer-memory flag barrier across the GPUs of one box, and the all-reduce of the tensor-parallel decoder step built
+// on it (add_rms_norm_ar_kernel in decoder_ops.cu, add_rms_norm_q8K_kernel in srv_gemm.cu); the attention's record
+// merge over peer memory (fa_merge_peers_kernel in fa_decode.cu) uses the same barrier.
 //
 // Every rank's row-parallel GEMM (attention output, FFN down) writes its partial sums into slot `slot` of its own
 // symmetric buffer (mapped on every peer): [2 slots][kArRows rows][d] f32, then flags [2][kArRows][kArMaxRanks] u32.
@@ -42,19 +43,18 @@ __device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t * p) {
 // bytes of one slot's partial rows
 __host__ __device__ inline size_t ar_part_bytes(int64_t d) { return (size_t) kArRows * d * sizeof(float); }
 
-// The flag barrier of row i (one thread calls it): returns false (and sets the status word) when a peer's flag did
-// not arrive within 2 s.
-__device__ inline bool ar_row_barrier(const uint64_t * peers, int world, int rank, int slot, uint32_t * epochs, int i,
-                                      int64_t d, int32_t * status) {
-    const size_t   flag_off = 2 * ar_part_bytes(d);
-    const uint32_t e        = ++epochs[slot * kArRows + i];
-    const size_t   fo = flag_off + ((size_t) (slot * kArRows + i) * kArMaxRanks + rank) * sizeof(uint32_t);
-    fence_acq_rel_sys();  // release: this rank's partial rows before its flags
+// One flag round of `row` (one thread calls it): publish epoch e into flag [row][rank] of every rank's buffer (flags
+// [rows][kArMaxRanks] u32 at byte offset flag_off), then wait until every rank's flag [row][j] in this rank's buffer
+// has reached e. Release before the stores, acquire after the polls (see above). Returns false (and sets the status
+// word) when a peer's flag did not arrive within 2 s.
+__device__ inline bool peer_row_barrier(const uint64_t * peers, int world, int rank, size_t flag_off, int row,
+                                        uint32_t e, int32_t * status) {
+    const size_t fo = flag_off + ((size_t) row * kArMaxRanks + rank) * sizeof(uint32_t);
+    fence_acq_rel_sys();  // release: this rank's data before its flags
     for (int j = 0; j < world; j++) st_relaxed_sys(reinterpret_cast<uint32_t *>(peers[j] + fo), e);
-    const uint32_t * mine = reinterpret_cast<const uint32_t *>(peers[rank] + flag_off) +
-                            (size_t) (slot * kArRows + i) * kArMaxRanks;
-    const uint64_t   t0 = global_timer_ns();
-    bool             ok = true;
+    const uint32_t * mine = reinterpret_cast<const uint32_t *>(peers[rank] + flag_off) + (size_t) row * kArMaxRanks;
+    const uint64_t   t0   = global_timer_ns();
+    bool             ok   = true;
     for (int j = 0; j < world && ok; j++) {
         while ((int32_t) (ld_relaxed_sys(mine + j) - e) < 0) {
             if (global_timer_ns() - t0 > 2000000000ull) {
@@ -65,8 +65,15 @@ __device__ inline bool ar_row_barrier(const uint64_t * peers, int world, int ran
             __nanosleep(64);
         }
     }
-    fence_acq_rel_sys();  // acquire: every peer's partial rows after its flag
+    fence_acq_rel_sys();  // acquire: every peer's data after its flag
     return ok;
+}
+
+// The flag barrier of row i of the all-reduce (one thread calls it).
+__device__ inline bool ar_row_barrier(const uint64_t * peers, int world, int rank, int slot, uint32_t * epochs, int i,
+                                      int64_t d, int32_t * status) {
+    const uint32_t e = ++epochs[slot * kArRows + i];
+    return peer_row_barrier(peers, world, rank, 2 * ar_part_bytes(d), slot * kArRows + i, e, status);
 }
 
 // x4 += the ranks' partial sums of float4 j of row i, in rank order

@@ -453,6 +453,31 @@ int srhpm_flash_attn_merge(srhpm_ctx * ctx, const void * parts, int n_parts, con
                         (int64_t) dst->nb[2], (cudaStream_t) stream);
 }
 
+size_t srhpm_flash_attn_peer_buffer_size(int64_t n_head, int64_t n_tokens) {
+    if (n_head < 1 || n_tokens < 1) return 0;
+    return fa_peer_buffer_bytes(n_head, n_tokens);
+}
+
+int srhpm_flash_attn_merge_peers(srhpm_ctx * ctx, const uint64_t * peer_buffers, int world, int rank,
+                                 uint32_t * epochs, const srhpm_tensor * sinks, srhpm_tensor * dst, void * stream) {
+    if (!ctx || !peer_buffers || !epochs || !dst) return SRHPM_ERR_INVALID;
+    if (dst->type != SRHPM_TYPE_F32 || !dst->data || dst->ne[0] != 256 || dst->ne[1] < 1 || dst->ne[1] > 65536 ||
+        dst->ne[2] < 1 || dst->ne[2] > 16 || dst->ne[3] != 1) {
+        return SRHPM_ERR_INVALID;
+    }
+    if (dst->nb[0] != 4 || dst->nb[1] % 4 || dst->nb[2] % 4 || !aligned(dst->data, 4)) return SRHPM_ERR_INVALID;
+    const int H = (int) dst->ne[1], N = (int) dst->ne[2];
+    const float * sk = nullptr;
+    if (sinks) {
+        if (sinks->type != SRHPM_TYPE_F32 || sinks->ne[0] != H || sinks->nb[0] != 4 || !sinks->data) {
+            return SRHPM_ERR_INVALID;
+        }
+        sk = (const float *) sinks->data;
+    }
+    return fa_merge_peers_run(ctx, peer_buffers, world, rank, epochs, N, H, sk, (float *) dst->data,
+                              (int64_t) dst->nb[1], (int64_t) dst->nb[2], (cudaStream_t) stream);
+}
+
 int srhpm_verify_accept_work_size(const srhpm_ctx * ctx, const srhpm_tensor * logits, size_t * size) {
     if (!ctx || !size) return SRHPM_ERR_INVALID;
     const int st = check_logits(logits, 1);

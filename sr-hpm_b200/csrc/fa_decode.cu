@@ -27,6 +27,7 @@
 #include <atomic>
 #include <cmath>
 
+#include "allreduce.cuh"
 #include "internal.h"
 #include "launch.cuh"
 #include "ptx.cuh"
@@ -1463,6 +1464,84 @@ int fa_run(srhpm_ctx * ctx, const FaView & v, float scale, float max_bias, float
 // record set: {max, sum} pairs [H * N] padded to 16 bytes, then acc [H * N][256]
 size_t fa_part_ms_bytes(int64_t H, int64_t N) { return ((size_t) (H * N) * sizeof(float2) + 15) / 16 * 16; }
 size_t fa_part_bytes(int64_t H, int64_t N) { return fa_part_ms_bytes(H, N) + (size_t) (H * N) * kD * sizeof(float); }
+
+// ---- the record merge over peer memory ---------------------------------------------------------------------------
+// Every rank's buffer (mapped on every rank) holds its record set (fa_part_bytes(H, N), written by
+// srhpm_flash_attn_ext_partial), then two flag arrays [H * N][kArMaxRanks] u32: "ready" and "done". CTA = row
+// r = h * N + t. A flag round on "ready" (allreduce.cuh) says every rank's merge kernel has passed griddepcontrol.wait,
+// so every rank's record set is complete; the row is merged over the ranks in rank order with fa_combine_kernel's
+// arithmetic (read from the peers' buffers with uncached loads), sinks added, normalized into dst; a flag round on
+// "done" says every rank has read this row, so no rank's next partial call can overwrite records a peer still reads.
+__global__ void __launch_bounds__(256) fa_merge_peers_kernel(const uint64_t * peers, int world, int rank,
+                                                             uint32_t * epochs, int N, int H, size_t ms_bytes,
+                                                             size_t set, const float * sinks, float * dst,
+                                                             int64_t dnb1, int64_t dnb2, int32_t * status) {
+    pdl_launch_dependents();
+    pdl_wait();  // this rank's partial records are complete
+    const int    row = blockIdx.x, h = row / N, tq = row % N, rows = H * N;
+    const size_t ready_off = set, done_off = set + (size_t) rows * kArMaxRanks * sizeof(uint32_t);
+    __shared__ int      ok_s;
+    __shared__ uint32_t e_s;
+    __shared__ float    w_s[kArMaxRanks], s_s[kArMaxRanks];
+    __shared__ float    mf_s;
+    if (threadIdx.x == 0) {
+        const uint32_t e = ++epochs[row];
+        e_s              = e;
+        ok_s             = peer_row_barrier(peers, world, rank, ready_off, row, e, status);
+        if (ok_s) {
+            float m = -INFINITY;
+            for (int r = 0; r < world; r++) {
+                const float2 v = __ldcv(reinterpret_cast<const float2 *>(peers[r]) + row);
+                w_s[r]         = v.x;
+                s_s[r]         = v.y;
+                if (v.y != 0.0f) m = fmaxf(m, v.x);
+            }
+            mf_s = m;
+            for (int r = 0; r < world; r++) w_s[r] = s_s[r] != 0.0f ? exp2f(w_s[r] - m) : 0.0f;
+        }
+    }
+    __syncthreads();
+    const int dv  = threadIdx.x;
+    float     acc = 0.0f, S = 0.0f;
+    if (ok_s) {
+        const float Mf = mf_s;
+        for (int r = 0; r < world; r++) {
+            const float w = w_s[r];
+            const float v = __ldcv(reinterpret_cast<const float *>(peers[r] + ms_bytes) + (int64_t) row * kD + dv);
+            acc           = fmaf(w, w != 0.0f ? v : 0.0f, acc);
+            S             = fmaf(w, s_s[r], S);
+        }
+        if (sinks) {
+            const float sk2 = sinks[h] * kLog2e;
+            if (sk2 > Mf) {
+                const float m2 = exp2f(Mf - sk2);
+                acc *= m2;
+                S = S * m2 + 1.0f;
+            } else {
+                S += exp2f(sk2 - Mf);
+            }
+        }
+    }
+    const float inv = S == 0.0f ? 0.0f : 1.0f / S;
+    float * out = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(dst) + h * dnb1 + tq * dnb2);
+    out[dv]     = acc * inv;
+    __syncthreads();  // every thread has read the peers' row
+    if (threadIdx.x == 0 && ok_s) peer_row_barrier(peers, world, rank, done_off, row, e_s, status);
+}
+
+size_t fa_peer_buffer_bytes(int64_t H, int64_t N) {
+    return fa_part_bytes(H, N) + 2 * (size_t) (H * N) * kArMaxRanks * sizeof(uint32_t);
+}
+
+int fa_merge_peers_run(srhpm_ctx * ctx, const uint64_t * peers, int world, int rank, uint32_t * epochs, int N, int H,
+                       const float * sinks, float * dst, int64_t dnb1, int64_t dnb2, cudaStream_t stream) {
+    if (world < 1 || world > kArMaxRanks || rank < 0 || rank >= world || N < 1 || H < 1) return SRHPM_ERR_INVALID;
+    const cudaError_t e = launch_k_pdl(fa_merge_peers_kernel, dim3((unsigned) (H * N)), dim3(kD), 0, stream, peers,
+                                       world, rank, epochs, N, H, fa_part_ms_bytes(H, N), fa_part_bytes(H, N), sinks,
+                                       dst, dnb1, dnb2, ctx->d_status);
+    ctx->launches.fetch_add(1);
+    return cuda_status(e);
+}
 
 int fa_merge_run(srhpm_ctx * ctx, const void * parts, int n_parts, int N, int H, const float * sinks, float * dst,
                  int64_t dnb1, int64_t dnb2, cudaStream_t stream) {

@@ -88,6 +88,11 @@ size_t fa_part_bytes(int64_t H, int64_t N);
 // merge of n_parts consecutive record sets (<= 256), then sinks and normalization into dst f32 [256][H][N]
 int    fa_merge_run(srhpm_ctx * ctx, const void * parts, int n_parts, int N, int H, const float * sinks, float * dst,
                     int64_t dnb1, int64_t dnb2, cudaStream_t stream);
+// the merge of every rank's record set read over peer memory (two flag rounds per row); buffer per rank: the record
+// set, then the ready and done flags
+size_t fa_peer_buffer_bytes(int64_t H, int64_t N);
+int    fa_merge_peers_run(srhpm_ctx * ctx, const uint64_t * peers, int world, int rank, uint32_t * epochs, int N, int H,
+                          const float * sinks, float * dst, int64_t dnb1, int64_t dnb2, cudaStream_t stream);
 
 // accept.cu: greedy acceptance (argmax of the target logits, longest accepted prefix)
 size_t argmax_work_size(int num_sms, int n_vocab, int n_rows);

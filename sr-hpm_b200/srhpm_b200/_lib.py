@@ -64,6 +64,8 @@ _SIGNATURES = {
     "srhpm_flash_attn_ext_partial": (ctypes.c_int, [_P, _T, _T, _T, _T, ctypes.c_float, ctypes.c_float, ctypes.c_float,
                                                     _P, _P, ctypes.c_size_t, _P]),
     "srhpm_flash_attn_merge": (ctypes.c_int, [_P, _P, ctypes.c_int, _T, _T, _P]),
+    "srhpm_flash_attn_peer_buffer_size": (ctypes.c_size_t, [ctypes.c_int64, ctypes.c_int64]),
+    "srhpm_flash_attn_merge_peers": (ctypes.c_int, [_P, _P, ctypes.c_int, ctypes.c_int, _P, _T, _T, _P]),
     "srhpm_verify_accept_work_size": (ctypes.c_int, [_P, _T, ctypes.POINTER(ctypes.c_size_t)]),
     "srhpm_verify_accept": (ctypes.c_int, [_P, _T, _P, ctypes.c_int, ctypes.c_float, _P, _P, _P, ctypes.c_size_t, _P]),
     "srhpm_argmax_shard": (ctypes.c_int, [_P, _T, ctypes.c_int64, _P, ctypes.c_int, _P, _P, ctypes.c_size_t, _P]),

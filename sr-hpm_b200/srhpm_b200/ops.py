@@ -317,6 +317,29 @@ class Context:
                                                 _stream_ptr(stream)), "srhpm_flash_attn_merge")
         return out
 
+    def flash_attn_peer_buffer_size(self, H, N):
+        """Bytes of one rank's buffer for flash_attn_merge_peers: the record set, then its two flag arrays."""
+        return int(self.lib.srhpm_flash_attn_peer_buffer_size(H, N))
+
+    def flash_attn_merge_peers(self, peers, world, rank, epochs, H, N, sinks=None, out=None, stream=None):
+        """srhpm_flash_attn_merge_peers: every rank's record set at the start of its own peer buffer (peers: int64
+        device tensor of the world buffers' addresses on this device), merged in rank order after a flag barrier;
+        epochs: int32 [H * N] device counters, zero at the start. Returns out f32 [N, H, 256]."""
+        if out is None:
+            out = torch.empty((N, H, 256), dtype=torch.float32, device=peers.device)
+        ov = _tensor_view(out, L.F32, [out.shape[2], out.shape[1], out.shape[0]],
+                          [4, out.stride(1) * 4, out.stride(0) * 4])
+        sv = None
+        if sinks is not None:
+            assert sinks.dtype == torch.float32 and sinks.dim() == 1 and sinks.stride(0) == 1
+            sv = _tensor_view(sinks, L.F32, [sinks.shape[0]], [4])
+        assert epochs.numel() >= H * N
+        L.check(self.lib.srhpm_flash_attn_merge_peers(self.handle, ctypes.c_void_p(peers.data_ptr()), world, rank,
+                                                      ctypes.c_void_p(epochs.data_ptr()),
+                                                      ctypes.byref(sv) if sv is not None else None, ctypes.byref(ov),
+                                                      _stream_ptr(stream)), "srhpm_flash_attn_merge_peers")
+        return out
+
     # ---- greedy acceptance ------------------------------------------------------------------------------------------
     def sample_and_accept_n(self, logits, draft, relax=0.0, stream=None, work=None):
         """common_sampler_sample_and_accept_n (greedy): logits f32 [>= n_draft + 1, n_vocab] (rows = positions),

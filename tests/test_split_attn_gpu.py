@@ -140,16 +140,18 @@ def _nccl_worker(rank, world, port, q, k, v, mask, sinks, outdir, resq):
         dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
         ctx = S.Context(rank)
         H, N, _ = q.shape
-        att = SplitKAttention(ctx, rank, world, H, N, torch.device("cuda", rank))
-        t0, t1 = att.range(k.shape[1])
         dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
-        out = att(dev(q), dev(k[:, t0:t1]), dev(v[:, t0:t1]), L.Q8_0, mask=dev(mask[:, t0:t1]), sinks=dev(sinks),
-                  scale=1 / 16)
-        torch.cuda.synchronize()
-        ctx.check()
-        # the output goes through a file: a queue message larger than the pipe's buffer would block until the
-        # parent reads it, and the parent reads after joining
-        np.save(os.path.join(outdir, f"rank{rank}.npy"), out.cpu().numpy())
+        for exchange in ("nccl", "peers"):
+            att = SplitKAttention(ctx, rank, world, H, N, torch.device("cuda", rank), exchange=exchange)
+            t0, t1 = att.range(k.shape[1])
+            for _ in range(3):  # repeated calls reuse the buffers (the peer flags count the calls)
+                out = att(dev(q), dev(k[:, t0:t1]), dev(v[:, t0:t1]), L.Q8_0, mask=dev(mask[:, t0:t1]),
+                          sinks=dev(sinks), scale=1 / 16)
+            torch.cuda.synchronize()
+            ctx.check()
+            # the output goes through a file: a queue message larger than the pipe's buffer would block until the
+            # parent reads it, and the parent reads after joining
+            np.save(os.path.join(outdir, f"rank{rank}_{exchange}.npy"), out.cpu().numpy())
         resq.put(("ok", rank, None))
         dist.barrier()
         dist.destroy_process_group()
@@ -161,7 +163,8 @@ def _nccl_worker(rank, world, port, q, k, v, mask, sinks, outdir, resq):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_split_over_two_gpus_nccl(ctx, tmp_path):
     """SplitKAttention over 2 GPUs: each rank holds half the cache's tokens; the record sets are all-gathered with
-    NCCL and merged on both ranks, which must agree bit for bit and match the oracle over the whole range."""
+    NCCL, or read from the peers' symmetric-memory buffers after a flag barrier, and merged on both ranks. Both ranks
+    and both exchanges must agree bit for bit and match the oracle over the whole range."""
     import socket
     import torch.multiprocessing as mp
     rng = np.random.default_rng(11)
@@ -191,6 +194,30 @@ def test_split_over_two_gpus_nccl(ctx, tmp_path):
     errs = [r[2] for r in res if r[0] == "err"]
     assert not errs, errs
     assert sorted(r[1] for r in res if r[0] == "ok") == [0, 1]
-    outs = {r: np.load(tmp_path / f"rank{r}.npy") for r in (0, 1)}
-    assert np.array_equal(outs[0], outs[1])
-    assert rel_l2(outs[0], exp) < TOL, rel_l2(outs[0], exp)
+    outs = {(r, x): np.load(tmp_path / f"rank{r}_{x}.npy") for r in (0, 1) for x in ("nccl", "peers")}
+    base = outs[(0, "nccl")]
+    for key, o in outs.items():
+        assert np.array_equal(o, base), key
+    assert rel_l2(base, exp) < TOL, rel_l2(base, exp)
+
+
+def test_merge_peers_single_rank_equals_merge(ctx):
+    """srhpm_flash_attn_merge_peers with one rank (its own buffer as the only peer) equals srhpm_flash_attn_merge of
+    that record set bit for bit, over repeated calls (the flag epochs advance each call)."""
+    rng = np.random.default_rng(13)
+    H, Hkv, N, L_ = 6, 2, 3, 640
+    q, k, v, mask = make(rng, L.Q8_0, H, Hkv, N, L_)
+    sinks = torch.from_numpy(rng.standard_normal(H).astype(np.float32)).cuda()
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    buf = torch.zeros(ctx.flash_attn_peer_buffer_size(H, N), dtype=torch.uint8, device="cuda")
+    peers = torch.tensor([buf.data_ptr()], dtype=torch.int64, device="cuda")
+    epochs = torch.zeros(H * N, dtype=torch.int32, device="cuda")
+    part = buf[:ctx.flash_attn_part_size(H, N)]
+    for _ in range(3):
+        ctx.flash_attn_ext_partial(dev(q), dev(k), dev(v), L.Q8_0, mask=dev(mask), scale=1 / 16, out=part)
+        got = ctx.flash_attn_merge_peers(peers, 1, 0, epochs, H, N, sinks=sinks).cpu().numpy()
+        want = ctx.flash_attn_merge(part.clone(), 1, H, N, sinks=sinks).cpu().numpy()
+        ctx.check()
+        assert np.array_equal(got, want)
+    assert epochs.cpu().tolist() == [3] * (H * N)
+    assert ctx.flash_attn_peer_buffer_size(H, N) == ctx.flash_attn_part_size(H, N) + 2 * H * N * 8 * 4
