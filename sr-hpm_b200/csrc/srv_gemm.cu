@@ -119,14 +119,34 @@ __device__ __forceinline__ void q8K_quantize_warp(const float (&v)[8], int lane,
     }
 }
 
-// the token row t of one super-block's activation record: the lane's 8 codes (perm, Q3_K: stored in the order
+// record byte orders (the k order inside an MMA is free as long as weights and activations agree): natural; Q3_K:
+// each lane's 8 columns in the order 0 4 1 5 2 6 3 7; IQ4_XS: in each 32-column sub-block, the pairs (l, l + 16)
+// interleaved so that bytes 4t..4t+3 hold columns 4t, 4t+16, 4t+1, 4t+17 and bytes 16+4t.. hold 4t+2, 4t+18, 4t+3,
+// 4t+19 (the order of the decoder's table lookups)
+enum : int { kPermNone = 0, kPermQ3K = 1, kPermIQ4XS = 2 };
+__host__ __device__ constexpr int record_perm(int wtype) {
+    return wtype == SRHPM_TYPE_Q3_K ? kPermQ3K : wtype == SRHPM_TYPE_IQ4_XS ? kPermIQ4XS : kPermNone;
+}
+
+// the token row t of one super-block's activation record: the lane's 8 codes (perm: stored in the order
 // 0 4 1 5 2 6 3 7, the k order of its decoder), the scale, the per-32 sums split into int8 halves s = 128 hi + lo
 // (lo in 0..127) in the row's padding (hi at 256 + sub-block, lo at 264 + sub-block: the Q4_K / Q5_K minimum term),
 // and the sum over all 256 after the scales (the Q3_K offset term)
 __device__ __forceinline__ void q8K_store_record(const int (&qv)[8], float dv, uint8_t * rec, int t, int NT, int lane,
                                                  int perm) {
     const uint2 pk = pack8(qv);
-    const uint2 st = perm ? make_uint2(__byte_perm(pk.x, pk.y, 0x5140), __byte_perm(pk.x, pk.y, 0x7362)) : pk;
+    uint2       st = pk;
+    if (perm == kPermQ3K) {
+        st = make_uint2(__byte_perm(pk.x, pk.y, 0x5140), __byte_perm(pk.x, pk.y, 0x7362));
+    } else if (perm == kPermIQ4XS) {
+        // lane 4b + k holds columns 8k..8k+7 of sub-block b; lanes k < 2 write bytes 8k.. from the low halves of
+        // their own and lane k + 2's words, lanes k >= 2 from the high halves of lane k - 2's and their own
+        const uint32_t ox = __shfl_xor_sync(0xffffffffu, pk.x, 2), oy = __shfl_xor_sync(0xffffffffu, pk.y, 2);
+        const bool     lo = (lane & 2) == 0;
+        const uint2    A = lo ? pk : make_uint2(ox, oy), B = lo ? make_uint2(ox, oy) : pk;
+        const uint32_t sel = lo ? 0x5140u : 0x7362u;
+        st = make_uint2(__byte_perm(A.x, B.x, sel), __byte_perm(A.y, B.y, sel));
+    }
     *reinterpret_cast<uint2 *>(rec + t * kTokStride + 8 * lane) = st;
     if (lane == 0) reinterpret_cast<float *>(rec + NT * kTokStride)[t] = dv;
     int s32 = 0;
@@ -839,14 +859,13 @@ struct DecIQ4XS {
     // the 16-entry code book as four words of int8 lanes (GGUF constant kvalues_iq4nl)
     static constexpr uint32_t T0 = 0xBFAD9881u, T1 = 0xF6EADDCFu, T2 = 0x26190D01u, T3 = 0x71594535u;
 
-    // v holds 8 indices (byte j: low nibble = weight j, high nibble = weight j + 16) -> lo / hi value words
-    __device__ __forceinline__ static void lookup(uint32_t v, uint32_t & lo, uint32_t & hi) {
+    // v holds 8 indices (byte j: low nibble = weight j, high nibble = weight j + 16) -> the values in nibble order:
+    // r0 = weights 0, 16, 1, 17 and r1 = 2, 18, 3, 19 (the activation records are stored in this order, kPermIQ4XS)
+    __device__ __forceinline__ static void lookup(uint32_t v, uint32_t & r0, uint32_t & r1) {
         const uint32_t v7  = v & 0x77777777u;
         const uint32_t sel = 0x32103210u | ((v & 0x88888888u) >> 1);  // bit 2 set: take the upper table's byte
-        const uint32_t r0  = prmt(prmt(T0, T1, v7), prmt(T2, T3, v7), sel);
-        const uint32_t r1  = prmt(prmt(T0, T1, v7 >> 16), prmt(T2, T3, v7 >> 16), sel >> 16);
-        lo                 = prmt(r0, r1, 0x6420u);
-        hi                 = prmt(r0, r1, 0x7531u);
+        r0                 = prmt(prmt(T0, T1, v7), prmt(T2, T3, v7), sel);
+        r1                 = prmt(prmt(T0, T1, v7 >> 16), prmt(T2, T3, v7 >> 16), sel >> 16);
     }
 
     __device__ __forceinline__ static void prep(const uint8_t * blk, uint8_t * rec) {
@@ -1616,7 +1635,7 @@ int gemm_run_impl(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, i
         } else {
             e = cudaLaunchKernelEx(&cfg, quant_q8K_kernel<false>, X, ldx, (int) N, nsb, NT, recs, (int8_t *) nullptr,
                                    (float *) nullptr, (int16_t *) nullptr, (int16_t *) nullptr, cnt, nrb,
-                                   (int) (wtype == SRHPM_TYPE_Q3_K));
+                                   record_perm(wtype));
         }
         ctx->launches.fetch_add(1);
         const int st = cuda_status(e);
@@ -1686,7 +1705,7 @@ int norm_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_t 
     }
     const cudaError_t e = launch_k_pdl(add_rms_norm_q8K_kernel, dim3(NT), dim3(kNormQThreads), (size_t) K * 4, stream,
                                        x, delta, w, eps, y, (int) N, K, NT, base + wl.recs,
-                                       (int) (wtype == SRHPM_TYPE_Q3_K), reinterpret_cast<int32_t *>(base + wl.cnt),
+                                       record_perm(wtype), reinterpret_cast<int32_t *>(base + wl.cnt),
                                        nrb, ar);
     ctx->launches.fetch_add(1);
     return cuda_status(e);
@@ -1706,7 +1725,7 @@ int swiglu_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_
     const int64_t warps  = (int64_t) nsb * NT;
     const int     blocks = (int) ((warps + 7) / 8);
     const cudaError_t e = launch_k_pdl(swiglu_q8K_kernel, dim3(blocks), dim3(256), 0, stream, gate, up, ld_in, h,
-                                       ld_out, (int) N, nsb, NT, base + wl.recs, (int) (wtype == SRHPM_TYPE_Q3_K),
+                                       ld_out, (int) N, nsb, NT, base + wl.recs, record_perm(wtype),
                                        reinterpret_cast<int32_t *>(base + wl.cnt), nrb);
     ctx->launches.fetch_add(1);
     return cuda_status(e);

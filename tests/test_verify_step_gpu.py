@@ -364,6 +364,48 @@ def test_fused_norm_quant_prologue_is_exact(ctx):
     assert outs[0][3] - outs[1][3] == 3 * cfg.n_layer + 1
 
 
+@pytest.mark.parametrize("qtype", [S.Q4_K, S.Q5_K, S.Q6_K, S.Q3_K, S.IQ4_XS])
+def test_fused_prologues_match_the_gemm_quantizer_every_type(ctx, qtype):
+    """srhpm_add_rms_norm_quant and srhpm_swiglu_quant write the activation records in each weight type's byte order
+    (natural, Q3_K's and IQ4_XS's permutations): the prequantized GEMM equals srhpm_mul_mat on the same rows bit for
+    bit."""
+    lib = L.load()
+    rng = np.random.default_rng(50 + qtype)
+    n, d, rows = 5, 1024, 192
+    W = S.QuantTensor.from_blocks(O.random_blocks(qtype, rows * d // 256, rng).reshape(rows, -1), qtype, rows, d)
+    wv = W.view()
+    x = torch.from_numpy(rng.standard_normal((n, d)).astype(np.float32)).cuda()
+    nw = torch.from_numpy((1 + 0.1 * rng.standard_normal(d)).astype(np.float32)).cuda()
+    y = torch.empty_like(x)
+    st, ws = ctx.mul_mat_work_size(W, x)
+    work = torch.empty(ws, dtype=torch.uint8, device="cuda")
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())
+    yq = torch.empty((n, rows), device="cuda")
+    xv, yqv = S.f32_rows_view(y), S.f32_rows_view(yq)
+    xc = x.clone()
+    L.check(lib.srhpm_add_rms_norm_quant(ctx.handle, ptr(xc), None, ptr(nw), ctypes.c_float(1e-6), ptr(y), n,
+                                         ctypes.byref(wv), ptr(work), work.numel(), None), "srhpm_add_rms_norm_quant")
+    L.check(lib.srhpm_mul_mat_prequantized(ctx.handle, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yqv),
+                                           ptr(work), work.numel(), None), "srhpm_mul_mat_prequantized")
+    want = ctx.mul_mat(W, y)
+    torch.cuda.synchronize()
+    ctx.check()
+    assert torch.equal(yq, want)
+    # SwiGLU prologue: gate | up halves of one row block
+    gu = torch.from_numpy(rng.standard_normal((n, 2 * d)).astype(np.float32)).cuda()
+    h = torch.empty((n, d), device="cuda")
+    L.check(lib.srhpm_swiglu_quant(ctx.handle, ptr(gu), ctypes.c_void_p(gu.data_ptr() + 4 * d), gu.stride(0), ptr(h),
+                                   h.stride(0), n, ctypes.byref(wv), ptr(work), work.numel(), None),
+            "srhpm_swiglu_quant")
+    hv = S.f32_rows_view(h)
+    L.check(lib.srhpm_mul_mat_prequantized(ctx.handle, ctypes.byref(wv), ctypes.byref(hv), ctypes.byref(yqv),
+                                           ptr(work), work.numel(), None), "srhpm_mul_mat_prequantized")
+    want = ctx.mul_mat(W, h)
+    torch.cuda.synchronize()
+    ctx.check()
+    assert torch.equal(yq, want)
+
+
 def test_fused_entry_points_status_codes(ctx):
     """The fused prologue / all-reduce entry points return status codes instead of failing: Q8_0 weights have no
     fused prologue (UNSUPPORTED, srhpm_mul_mat quantizes itself), a short workspace, misaligned rows, bad ranks."""
