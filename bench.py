@@ -10,11 +10,12 @@ value  = algorithmic bytes (weights + activations read + outputs written) / devi
          over ranks. With N GPUs every matrix is sharded by output rows (each rank computes rows/N rows, then
          an all-gather of Y over NCCL): strong scaling.
          The timed steps replay a CUDA graph of one step (1 GPU); --eager times the calls as issued.
-e2e    = the same products through the public API with host buffers, issued call by call: one H2D copy of the
-         step's activations from pinned host memory, the 60 products, and D2H copies of every output into pinned
-         host memory, all timed. On one GPU the outputs go back in 6 chunks on a second stream as their products
-         finish (the reads overlap the products still running; the timed region ends after the last read); with
-         several ranks they go back in one copy after the step's all-gather. config's e2e "copies" says which ran.
+e2e    = the same products through the public API with host buffers: one H2D copy of the step's activations from
+         pinned host memory, the 60 products, and D2H copies of every output into pinned host memory, all timed.
+         The outputs go back in 6 chunks on a second stream as their products finish (with several ranks, after
+         each chunk's all-gather); the step's calls and copies are captured once into a CUDA graph and replayed,
+         as a serving loop runs them. The same step issued call by call from the host is reported beside it
+         (measurements.e2e_calls_issued_eagerly_gbs). The line's e2e "copies" says which ran.
 roofline: achieved = algorithmic bytes of the step / timed step time (the quantizer kernels count against the GEMM),
          against the measured HBM copy bandwidth; per-product times for the breakdown come from a second graph with
          CUDA events between the products, replayed after the timed region.
@@ -455,18 +456,24 @@ def run_gpu(args):
     ran = [torch.cuda.Event() for _ in range(nchunk)]     # a chunk's products are done
     copied = [torch.cuda.Event() for _ in range(nchunk)]  # a chunk's outputs are on the host
 
-    def e2e_step_pipelined():
+    # captured=True: the form recorded into a CUDA graph, which replays step after step: no wait on the previous
+    # step's reads (the replays are serial), and the copy stream joins the step's stream at its end
+    def e2e_step_pipelined(captured=False):
+        cur = torch.cuda.current_stream()
         x_dev.copy_(x_host, non_blocking=True)
         for c in range(nchunk):
-            stream.wait_event(copied[c])
+            if not captured:
+                cur.wait_event(copied[c])
             for run in runs[cb[c]:cb[c + 1]]:
                 run()
-            ran[c].record(stream)
+            ran[c].record(cur)
             copy_s.wait_event(ran[c])
             lo, hi = ybound[cb[c]], ybound[cb[c + 1]]
             with torch.cuda.stream(copy_s):
                 y_host[lo:hi].copy_(y_dev[lo:hi], non_blocking=True)
             copied[c].record(copy_s)
+        if captured:
+            cur.wait_event(copied[nchunk - 1])
 
     def time_e2e(e2e_step, tail=None):
         for _ in range(max(1, args.warmup)):
@@ -482,6 +489,31 @@ def run_gpu(args):
         e1.record(stream)
         torch.cuda.synchronize()
         barrier()
+        return e0.elapsed_time(e1)
+
+    # the same step's API calls and copies captured once into a CUDA graph and replayed (what a serving loop does)
+    def time_e2e_graph(e2e_step):
+        for _ in range(max(1, args.warmup)):
+            e2e_step()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream(dev)
+        cs.wait_stream(stream)
+        with torch.cuda.stream(cs):
+            with torch.cuda.graph(g, stream=cs):
+                e2e_step(captured=True)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        del g  # may hold NCCL calls: released before the process group
         return e0.elapsed_time(e1)
 
     # several ranks: the same chunks, each with its own packed buffers and all-gather; a chunk's gathered outputs go
@@ -502,24 +534,32 @@ def run_gpu(args):
             out.append((rr, yl, yg, yh))
         return out
 
-    def e2e_step_pipelined_multi():
+    def e2e_step_pipelined_multi(captured=False):
+        cur = torch.cuda.current_stream()
         x_dev.copy_(x_host, non_blocking=True)
         for c, (rr, yl, yg, yh) in enumerate(chunks):
-            stream.wait_event(copied[c])
+            if not captured:
+                cur.wait_event(copied[c])
             for run in rr:
                 run()
             dist.all_gather_into_tensor(yg, yl)
-            ran[c].record(stream)
+            ran[c].record(cur)
             copy_s.wait_event(ran[c])
             with torch.cuda.stream(copy_s):
                 yh.copy_(yg, non_blocking=True)
             copied[c].record(copy_s)
+        if captured:
+            cur.wait_event(copied[nchunk - 1])
 
     e2e_mode = "serial: H2D, the products, one D2H of all outputs"
+    e2e_eager_ms = None
     if world == 1:
         try:
-            e2e_ms = time_e2e(e2e_step_pipelined, copied[-1])
-            e2e_mode = f"outputs read back in {nchunk} chunks on a second stream as their products finish"
+            e2e_eager_ms = time_e2e(e2e_step_pipelined, copied[-1])
+            e2e_ms = time_e2e_graph(e2e_step_pipelined)
+            e2e_mode = (f"the step's API calls and copies as one CUDA graph, replayed: H2D of the activations, the "
+                        f"products, the outputs read back in {nchunk} chunks on a second stream as their products "
+                        f"finish")
         except Exception as e:  # measured the serial way instead, and said so
             torch.cuda.synchronize()
             e2e_ms = time_e2e(e2e_step_serial)
@@ -527,9 +567,14 @@ def run_gpu(args):
     else:  # every rank takes the same path (collectives inside): no per-rank fallback
         chunks = chunked_multi()
         d2h = sum(ch[3].numel() * 4 for ch in chunks)
-        e2e_ms = time_e2e(e2e_step_pipelined_multi, copied[-1])
-        e2e_mode = (f"{nchunk} chunks, each its products, its all-gather and its D2H on a second stream while the "
-                    "next chunk runs")
+        e2e_eager_ms = time_e2e(e2e_step_pipelined_multi, copied[-1])
+        e2e_ms = time_e2e_graph(e2e_step_pipelined_multi)
+        e2e_mode = (f"the step's API calls, collectives and copies as one CUDA graph, replayed: {nchunk} chunks, "
+                    "each its products, its all-gather and its D2H on a second stream while the next chunk runs")
+    if e2e_eager_ms is not None and world > 1:
+        tt = torch.tensor([e2e_eager_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e2e_eager_ms = float(tt.item())
     if world > 1:
         tt = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
@@ -537,6 +582,8 @@ def run_gpu(args):
     e2e_value = step_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
     ctx.check()
     meas = {}
+    if e2e_eager_ms is not None:  # the same copies and calls issued one by one from the host, for comparison
+        meas["e2e_calls_issued_eagerly_gbs"] = round(step_bytes / (e2e_eager_ms / args.steps * 1e-3) / 1e9, 2)
     # the sharded step's gathered outputs against the same products whole on one GPU (after the timed regions)
     sweep_par = None
     if world > 1:
