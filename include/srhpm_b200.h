@@ -93,6 +93,20 @@ int srhpm_mul_mat_work_size(const srhpm_tensor * W, const srhpm_tensor * X, size
 int srhpm_mul_mat(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, srhpm_tensor * Y, void * wdata,
                   size_t wsize, void * stream);
 
+/* srhpm_mul_mat in ONE kernel launch: the matmul grid quantizes its own activations (every consumer warp of the grid
+ * takes a share of the (super-block, row) pairs) and meets at an arrival counter before any CTA loads the records;
+ * the same records, so the output is bit-identical to srhpm_mul_mat's. Same work buffer (srhpm_mul_mat_work_size).
+ * Faster after a small kernel that leaves the SMs free (attention output -> its projection: the grid is resident
+ * early and the activations sit in L2), slower right after another large matmul (the grid becomes resident piecewise
+ * as that one drains and the meet waits for its last CTA): measured on a B200, -0.13 ms per 27B-class verify step
+ * as the attention output projection, +1.5 us per product in a sweep of back-to-back products. The counter is kept by
+ * the context, one per work buffer: calls through one context on several streams need separate work buffers (as
+ * their activation records already do). Products whose grid would get more than two quantization jobs per warp
+ * fall back to the separate quantizer. No reference counterpart (the reference quantizes on its CPU threads before
+ * the barrier, patch/srhpm.patch:6455-6461). */
+int srhpm_mul_mat_fused_quant(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, srhpm_tensor * Y,
+                              void * wdata, size_t wsize, void * stream);
+
 /* The integer part of srhpm_mul_mat, for bit-exact checks: per (token t, row r, block j) the int32 sum of
  * (integer block scale) x (code . activation) over block j (super-block of 256, or the 32-block for Q8_0), written to
  * isum[(t * rows + r) * nblk + j], and for Q4_K / Q5_K the sum of (integer min) x (activation sum) to imin (same

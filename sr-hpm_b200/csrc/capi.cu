@@ -159,8 +159,11 @@ int srhpm_ctx_create(int device, srhpm_ctx ** out) {
     srhpm_ctx * c = new srhpm_ctx();
     c->device     = device;
     cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, device);
-    st = cuda_status(cudaMalloc(&c->d_status, 64));
-    if (st == SRHPM_OK) st = cuda_status(cudaMemset(c->d_status, 0, 64));
+    // the status word (64 bytes), then the GEMM grids' arrival counters
+    const size_t dev_bytes = 64 + (size_t) kSyncSlots * sizeof(uint32_t);
+    st = cuda_status(cudaMalloc(&c->d_status, dev_bytes));
+    if (st == SRHPM_OK) st = cuda_status(cudaMemset(c->d_status, 0, dev_bytes));
+    if (st == SRHPM_OK) c->d_sync = reinterpret_cast<uint32_t *>(reinterpret_cast<uint8_t *>(c->d_status) + 64);
     cudaSetDevice(prev);
     if (st != SRHPM_OK) {
         if (c->d_status) cudaFree(c->d_status);
@@ -273,6 +276,16 @@ int srhpm_mul_mat(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * 
     return gemm_run(ctx, W->type, (const uint8_t *) W->data, W->ne[1], W->ne[0], W->nb[1], (const float *) X->data,
                     (int64_t) (X->nb[1] / 4), X->ne[1], (float *) Y->data, (int64_t) (Y->nb[1] / 4), wdata, wsize,
                     nullptr, nullptr, (cudaStream_t) stream);
+}
+
+int srhpm_mul_mat_fused_quant(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * X, srhpm_tensor * Y,
+                              void * wdata, size_t wsize, void * stream) {
+    if (!ctx || !Y) return SRHPM_ERR_INVALID;
+    const int st = check_mul_mat(W, X, Y);
+    if (st != SRHPM_OK) return st;
+    return gemm_run(ctx, W->type, (const uint8_t *) W->data, W->ne[1], W->ne[0], W->nb[1], (const float *) X->data,
+                    (int64_t) (X->nb[1] / 4), X->ne[1], (float *) Y->data, (int64_t) (Y->nb[1] / 4), wdata, wsize,
+                    nullptr, nullptr, (cudaStream_t) stream, true);
 }
 
 int srhpm_add_rms_norm_quant(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y,

@@ -4,6 +4,8 @@
 
 #include <atomic>
 #include <cstdint>
+#include <mutex>
+#include <unordered_map>
 
 #include "srhpm_b200.h"
 
@@ -13,9 +15,17 @@ struct srhpm_ctx {
     int                  num_sms       = 148;
     int32_t *            d_status      = nullptr;  // device status word of the bounded waits
     std::atomic<int64_t> launches{ 0 };
+    // arrival counters of the GEMM grids that quantize their own activations (srhpm_mul_mat_fused_quant), one per work
+    // buffer in use: kSyncSlots words after the status word, zero at creation; a launch adds exactly 2^20 to its counter
+    uint32_t *                            d_sync      = nullptr;
+    std::mutex                            sync_mu;
+    std::unordered_map<uintptr_t, int>    sync_slots;  // work buffer (aligned base) -> counter index
+    int                                   sync_next = 0;
 };
 
 namespace srhpm {
+
+constexpr int kSyncSlots = 4096;
 
 void set_last_cuda_error(cudaError_t e);
 
@@ -33,9 +43,10 @@ int  weight_block_bytes(int type);
 
 // srv_gemm.cu
 size_t gemm_work_size(int wtype, int64_t rows, int64_t K, int64_t N);
+// fused_quant: the GEMM grid quantizes its own activations (srhpm_mul_mat_fused_quant)
 int    gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                 const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
-                int32_t * isum, int32_t * imin, cudaStream_t stream);
+                int32_t * isum, int32_t * imin, cudaStream_t stream, bool fused_quant = false);
 size_t gemm_work_size_unsplit(int wtype, int64_t rows, int64_t K, int64_t N);
 int    gemm_run_prequant(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                          int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize, cudaStream_t stream);

@@ -17,7 +17,15 @@ constexpr uint32_t kSuspendNs    = 20000;
 constexpr uint32_t kSuspendLimit = 100000;
 
 // error words written to the context's device status slot
-enum : int32_t { kErrNone = 0, kErrWaitFull = 1, kErrWaitEmpty = 2, kErrWaitDrain = 3, kErrPeerWait = 4, kErrClusterWait = 5 };
+enum : int32_t {
+    kErrNone        = 0,
+    kErrWaitFull    = 1,
+    kErrWaitEmpty   = 2,
+    kErrWaitDrain   = 3,
+    kErrPeerWait    = 4,
+    kErrClusterWait = 5,
+    kErrGridWait    = 6,
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void * p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -148,6 +156,28 @@ __device__ __forceinline__ void named_bar_sync(int id, int count) {
 // orders this thread's generic-proxy shared-memory writes before later async-proxy (bulk copy) accesses
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// orders generic-proxy global-memory accesses with async-proxy (bulk copy / TMA) accesses of the same locations
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// barrier arrival without waiting (the waiting side calls named_bar_sync with the same id and count)
+__device__ __forceinline__ void named_bar_arrive(int id, int count) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t * p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
 
 // programmatic dependent launch: wait for the preceding grid's writes / let the next grid start its prologue

@@ -6,7 +6,9 @@
 //   1. quant_q8K_kernel / quant_q80_kernel: each activation row is quantized per 256 columns to int8 with one f32
 //      scale (bit-identical to srv_quantize_row, patch/srhpm.patch:5518-5575) -- or per 32 columns to q8_0 for Q8_0
 //      weights -- into "activation records": for each super-block, NT = 8 or 16 token rows of 256 int8 values at a
-//      288-byte stride (so that consecutive tokens fall on different shared-memory banks), then the scales.
+//      288-byte stride (so that consecutive tokens fall on different shared-memory banks), then the scales. Only the
+//      N real token rows are written: the padding rows (N..NT-1) reach only MMA output columns that are never stored.
+//      srhpm_mul_mat_fused_quant does the same work in the GEMM kernel's own prologue (fq_quantize, fq_grid_meet).
 //   2. srv_gemm_kernel: persistent CTAs over (64-row block, K range) units. A producer warp streams each unit
 //      through a 3-4 stage shared-memory ring, one super-block column at a time: 2-D TMA boxes of the 64 row
 //      segments (rows grouped G at a time when the row stride is not a multiple of 16 bytes; the < G rows past
@@ -89,12 +91,11 @@ __device__ __forceinline__ uint2 pack8(const int (&q)[8]) {
 // iscale = -127 / max; q = min(round_half_even(iscale * x), 127); d = 1 / iscale. IEEE division, no contraction.
 // One warp per (super-block, token); lane l holds columns 8l..8l+7 in v.
 __device__ __forceinline__ void q8K_quantize_warp(const float (&v)[8], int lane, int (&qv)[8], float & dv) {
-    float amax = 0.0f;
-#pragma unroll
+    float amax = 0.0f;  // fmaxf from 0 drops NaNs, so the lane maxima are non-negative, NaN-free floats, which order
+#pragma unroll          // as their bit patterns: one integer warp reduction gives the maximum
     for (int j = 0; j < 8; j++) amax = fmaxf(amax, fabsf(v[j]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    dv = 0.0f;
+    amax = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(amax)));
+    dv   = 0.0f;
     if (amax == 0.0f) {
 #pragma unroll
         for (int j = 0; j < 8; j++) qv[j] = 0;
@@ -158,9 +159,8 @@ __device__ __forceinline__ void q8K_store_record(const int (&qv)[8], float dv, u
         rec[t * kTokStride + 256 + lane / 4] = (uint8_t) (int8_t) (s32 >> 7);
         rec[t * kTokStride + 264 + lane / 4] = (uint8_t) (s32 & 127);
     }
-    int s256 = s32 + __shfl_xor_sync(0xffffffffu, s32, 4);
-    s256 += __shfl_xor_sync(0xffffffffu, s256, 8);
-    s256 += __shfl_xor_sync(0xffffffffu, s256, 16);
+    // s32 is the sum of the lane's group of 4: the 8 groups' sums are the quarter of the lanes' total
+    const int s256 = __reduce_add_sync(0xffffffffu, s32) >> 2;
     if (lane == 0) reinterpret_cast<int32_t *>(rec + NT * kTokStride + 4 * NT)[t] = s256;
 }
 
@@ -173,11 +173,11 @@ __global__ void __launch_bounds__(256) quant_q8K_kernel(const float * __restrict
     // launched early behind the previous call's GEMM: let the next GEMM get resident, then wait for the previous
     // grid (it may still read the records and counters this kernel rewrites, or write the X it reads)
     pdl_launch_dependents();
-    if (X) prefetch_act_l2(X, ldx, N, nsb, DENSE ? N : NT, threadIdx.x & 31);
+    if (X) prefetch_act_l2(X, ldx, N, nsb, N, threadIdx.x & 31);
     pdl_wait();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncnt; i += gridDim.x * blockDim.x) cnt[i] = 0;
     const int     lane = threadIdx.x & 31;
-    const int     TT   = DENSE ? N : NT;
+    const int     TT   = N;  // records: the padding token rows are never read into a stored output
     const int64_t wid  = (int64_t) blockIdx.x * 8 + (threadIdx.x >> 5);
     if (wid >= (int64_t) nsb * TT) {
         return;
@@ -356,6 +356,35 @@ __global__ void __launch_bounds__(kNormQThreads) add_rms_norm_q8K_kernel(float *
 
 // q8_0 quantizer, per 32 columns (4 lanes per block): d = amax / 127 stored as f16. SIMD mode: id = 127 / amax,
 // q = round_half_even(x * id); REF mode: id = 1 / d (f32 d), q = roundf(x * id).
+// q8_0 quantization of one warp's 256 values (lane l holds columns 8l..8l+7: 32-block l / 4) with the context's
+// q8_0 mode; returns the codes packed and the block's f16 scale
+__device__ __forceinline__ uint2 q80_quantize_warp(const float (&v)[8], int mode, __half & dh) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) amax = fmaxf(amax, fabsf(v[j]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const float dd = __fdiv_rn(amax, 127.0f);
+    dh             = __float2half_rn(dd);
+    int qv[8];
+    if (mode == SRHPM_Q8_0_ACT_SIMD) {
+        const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) qv[j] = __float2int_rn(__fmul_rn(v[j], id));
+    } else {
+        const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) qv[j] = (int) roundf(__fmul_rn(v[j], id));
+    }
+    return pack8(qv);
+}
+
+// token row t of one super-block's q8_0 activation record: the codes, then the 8 block scales at [blk * NT + t]
+__device__ __forceinline__ void q80_store_record(uint2 pk, __half dh, uint8_t * rec, int t, int NT, int lane) {
+    *reinterpret_cast<uint2 *>(rec + t * kTokStride + 8 * lane) = pk;
+    if ((lane & 3) == 0) reinterpret_cast<float *>(rec + NT * kTokStride)[(lane >> 2) * NT + t] = __half2float(dh);
+}
+
 template <bool DENSE>
 __global__ void __launch_bounds__(256) quant_q80_kernel(const float * __restrict__ X, int64_t ldx, int N, int nsb,
                                                          int NT, int mode, uint8_t * __restrict__ recs,
@@ -364,11 +393,11 @@ __global__ void __launch_bounds__(256) quant_q80_kernel(const float * __restrict
     // launched early behind the previous call's GEMM: let the next GEMM get resident, then wait for the previous
     // grid (it may still read the records and counters this kernel rewrites, or write the X it reads)
     pdl_launch_dependents();
-    prefetch_act_l2(X, ldx, N, nsb, DENSE ? N : NT, threadIdx.x & 31);
+    prefetch_act_l2(X, ldx, N, nsb, N, threadIdx.x & 31);
     pdl_wait();
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ncnt; i += gridDim.x * blockDim.x) cnt[i] = 0;
     const int     lane = threadIdx.x & 31;
-    const int     TT   = DENSE ? N : NT;
+    const int     TT   = N;  // records: the padding token rows are never read into a stored output
     const int64_t wid  = (int64_t) blockIdx.x * 8 + (threadIdx.x >> 5);
     if (wid >= (int64_t) nsb * TT) {
         return;
@@ -381,24 +410,8 @@ __global__ void __launch_bounds__(256) quant_q80_kernel(const float * __restrict
 #pragma unroll
         for (int j = 0; j < 8; j++) v[j] = 0.0f;
     }
-    float amax = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) amax = fmaxf(amax, fabsf(v[j]));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-    const float  dd = __fdiv_rn(amax, 127.0f);
-    const __half dh = __float2half_rn(dd);
-    int          qv[8];
-    if (mode == SRHPM_Q8_0_ACT_SIMD) {
-        const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-#pragma unroll
-        for (int j = 0; j < 8; j++) qv[j] = __float2int_rn(__fmul_rn(v[j], id));
-    } else {
-        const float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
-#pragma unroll
-        for (int j = 0; j < 8; j++) qv[j] = (int) roundf(__fmul_rn(v[j], id));
-    }
-    const uint2 pk  = pack8(qv);
+    __half      dh;
+    const uint2 pk  = q80_quantize_warp(v, mode, dh);
     const int   blk = lane >> 2;  // 32-block inside the super-block
     if constexpr (DENSE) {
         const int64_t nb32 = (int64_t) nsb * 8;
@@ -410,9 +423,7 @@ __global__ void __launch_bounds__(256) quant_q80_kernel(const float * __restrict
         qs[2] = (uint16_t) (pk.y & 0xffff);
         qs[3] = (uint16_t) (pk.y >> 16);
     } else {
-        uint8_t * rec = recs + (size_t) sb * rec_bytes(true, NT);
-        *reinterpret_cast<uint2 *>(rec + t * kTokStride + 8 * lane) = pk;
-        if ((lane & 3) == 0) reinterpret_cast<float *>(rec + NT * kTokStride)[blk * NT + t] = __half2float(dh);
+        q80_store_record(pk, dh, recs + (size_t) sb * rec_bytes(true, NT), t, NT, lane);
     }
 }
 
@@ -1036,7 +1047,74 @@ struct GemmArgs {
     int32_t *       isum;        // integer outputs (srhpm_mul_mat_isums), else null
     int32_t *       imin;
     int             nblk;        // blocks per row in the integer outputs
+    // fused quantization: the consumer warps of the whole grid quantize X into the records themselves (one job per
+    // (super-block, token) and warp), zero the split-K counters, and the grid meets at *sync before any CTA loads a
+    // record; otherwise a separate quantizer kernel ran before this one
+    int             fq;
+    const float *   X;
+    int64_t         ldx;
+    int             perm;        // record byte order (record_perm)
+    int             q80mode;     // the context's q8_0 mode (Q8_0 weights)
+    int             ncnt;        // split-K counters to zero
+    uint32_t *      sync;        // this work buffer's arrival counter: every launch adds exactly 2^20 to it
 };
+
+// The consumer warps' share of the activation quantization (fused form): warp w of the grid quantizes the
+// (super-block, token) pairs w, w + warps, ... of the N real tokens (the records' padding tokens feed only output
+// columns that are never stored) and the grid zeroes the split-K counters. Same device functions and records as
+// quant_q8K_kernel / quant_q80_kernel.
+template <class D, int NG>
+__device__ __forceinline__ void fq_quantize(const GemmArgs & a, int warp, int lane) {
+    constexpr int NT = 8 * NG;
+    constexpr int RB = rec_bytes(D::Q80, NT);
+    const int     nw = (int) gridDim.x * kNCW;
+    const int     jobs = a.nsb * a.N;
+    for (int j = (int) blockIdx.x * kNCW + warp; j < jobs; j += nw) {
+        const int sb = j / a.N, t = j - sb * a.N;
+        float     v[8];
+        load8(a.X + (int64_t) t * a.ldx + (int64_t) sb * QK + 8 * lane, v);
+        uint8_t * rec = const_cast<uint8_t *>(a.recs) + (size_t) sb * RB;
+        if constexpr (D::Q80) {
+            __half      dh;
+            const uint2 pk = q80_quantize_warp(v, a.q80mode, dh);
+            q80_store_record(pk, dh, rec, t, NT, lane);
+        } else {
+            int   qv[8];
+            float dv;
+            q8K_quantize_warp(v, lane, qv, dv);
+            q8K_store_record(qv, dv, rec, t, NT, lane, a.perm);
+        }
+    }
+    for (int i = (int) blockIdx.x * (kNCW * 32) + (int) threadIdx.x; i < a.ncnt; i += (int) gridDim.x * (kNCW * 32)) {
+        a.cnt[i] = 0;
+    }
+    // the records are read by other CTAs' bulk copies (async proxy)
+    fence_proxy_async_global();
+}
+
+// Fused form, producer lane 0 of every CTA, after the CTA's consumers finished their quantization jobs: publish the
+// CTA's arrival (release) and wait (acquire, bounded: 2 s, then an error status) until every CTA of the grid has
+// arrived. Each launch adds exactly 2^20 to the counter (CTA 0 adds the remainder of the equal shares), so the counter
+// is a multiple of 2^20 between launches, the value a CTA reads before adding its own share lies in its launch's
+// epoch, and the launch is complete at the next multiple (modulo 2^32). All CTAs are resident together (the grid is
+// sized to the resident CTA slots), and the launch before this one on the stream never waits for this one.
+__device__ __forceinline__ void fq_grid_meet(const GemmArgs & a) {
+    __threadfence();
+    const uint32_t q   = (1u << 20) / gridDim.x;
+    const uint32_t inc = blockIdx.x == 0 ? (1u << 20) - (gridDim.x - 1) * q : q;
+    const uint32_t old = atomicAdd(a.sync, inc);
+    const uint32_t target = ((old >> 20) + 1u) << 20;
+    const uint64_t t0 = globaltimer_ns();
+    while ((int32_t) (ld_acquire_gpu(a.sync) - target) < 0) {
+        if (globaltimer_ns() - t0 > 2000000000ull) {
+            atomicExch(a.status, kErrGridWait);
+            break;
+        }
+        __nanosleep(32);
+    }
+    __threadfence();
+    fence_proxy_async_global();  // the bulk copies that follow read what other CTAs wrote
+}
 
 // 1-D copy of the row segment [start, end) of W into dst (16-byte aligned, holding the segment at its own 16-byte
 // phase): bulk bytes below the last 16-byte boundary of W, hand copy of the ragged end. Returns the bulk bytes.
@@ -1127,6 +1205,11 @@ __device__ __forceinline__ void producer(const GemmArgs & a, const CUtensorMap *
             if (pre && (n == a.S || (c + 1 == nck && u + (int) gridDim.x >= a.units))) {
                 pdl_wait();
                 waited = true;
+                if (a.fq) {
+                    named_bar_sync(2, kThreads);  // this CTA's consumers have written their records
+                    if (lane == 0) fq_grid_meet(a);
+                    __syncwarp();
+                }
                 if (lane == 0) {
                     for (int m = 0; m < n; m++) {  // the records of the stages issued so far (slot m, first use)
                         const int sbm = sbA + (m % nck) * a.kc, kcm = min(a.kc, sbB - sbm);
@@ -1137,7 +1220,14 @@ __device__ __forceinline__ void producer(const GemmArgs & a, const CUtensorMap *
             }
         }
     }
-    if (!waited) pdl_wait();
+    if (!waited) {
+        pdl_wait();
+        if (a.fq) {  // the grid's counter takes this CTA's share in every case
+            named_bar_sync(2, kThreads);
+            if (lane == 0) fq_grid_meet(a);
+            __syncwarp();
+        }
+    }
     // drain: every copy this warp issued has landed before the CTA may exit
     for (int m = max(0, n - a.S); m < n; m++) {
         if (!mbar_wait(&full[m % a.S], (m / a.S) & 1)) ok = false;
@@ -1191,7 +1281,18 @@ __global__ void __launch_bounds__(kThreads, D::MINB) srv_gemm_kernel(const __gri
         return;
     }
     pdl_launch_dependents();  // the next call's quantizer may start; it waits for this grid before touching data
+    if (a.fq) {  // warm L2 with the activation segment of this warp's first quantization job (a hint, as above)
+        const int j = (int) blockIdx.x * kNCW + warp;
+        if (j < a.nsb * a.N && (lane & 3) == 0) {
+            const int sb = j / a.N, t = j - sb * a.N;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(a.X + (int64_t) t * a.ldx + (int64_t) sb * QK + 8 * lane));
+        }
+    }
     pdl_wait();  // the split-K counters and partials are written below; the quantizer grid zeroes the counters
+    if (a.fq) {
+        fq_quantize<D, NG>(a, warp, lane);
+        named_bar_arrive(2, kThreads);  // the producer meets the grid for this CTA, then loads the records
+    }
     constexpr int  RB  = rec_bytes(D::Q80, 8 * NG);
     const int      g = lane >> 2, t = lane & 3;
     const int      rl  = warp * 16 + g;
@@ -1401,6 +1502,33 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
+// the separate activation quantizer (records and zeroed split-K counters), launched before the GEMM when the GEMM
+// does not quantize in its own prologue
+int launch_quantizer(srhpm_ctx * ctx, const GemmArgs & a, int NT, bool q80, cudaStream_t stream) {
+    const int64_t      warps  = (int64_t) a.nsb * a.N;  // one per (super-block, real token)
+    const int          blocks = (int) ((warps + 7) / 8);
+    cudaLaunchConfig_t cfg    = {};
+    cfg.gridDim               = dim3((unsigned) blocks);
+    cfg.blockDim              = dim3(256);
+    cfg.stream                = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs                                          = attr;
+    cfg.numAttrs                                       = 1;
+    uint8_t *   recs = const_cast<uint8_t *>(a.recs);
+    cudaError_t e;
+    if (q80) {
+        e = cudaLaunchKernelEx(&cfg, quant_q80_kernel<false>, a.X, a.ldx, a.N, a.nsb, NT, a.q80mode, recs,
+                               (uint8_t *) nullptr, a.cnt, a.ncnt);
+    } else {
+        e = cudaLaunchKernelEx(&cfg, quant_q8K_kernel<false>, a.X, a.ldx, a.N, a.nsb, NT, recs, (int8_t *) nullptr,
+                               (float *) nullptr, (int16_t *) nullptr, (int16_t *) nullptr, a.cnt, a.ncnt, a.perm);
+    }
+    ctx->launches.fetch_add(1);
+    return cuda_status(e);
+}
+
 template <class D, int NG, bool DBG>
 int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     constexpr int RB = rec_bytes(D::Q80, 8 * NG);
@@ -1547,6 +1675,14 @@ int launch_gemm(srhpm_ctx * ctx, GemmArgs a, cudaStream_t stream) {
     int       grid   = (a.units + rounds - 1) / rounds;
     grid             = (grid + a.ksplit - 1) / a.ksplit * a.ksplit;
     cfg.gridDim      = dim3((unsigned) grid);
+    // activations: quantized in the GEMM's own prologue (one launch per product) when the grid's consumer warps get
+    // at most two (super-block, token) jobs each; else by the separate quantizer kernel first (a.X null: the records
+    // were written by a fused norm / SwiGLU prologue)
+    if (a.fq && (int64_t) a.nsb * a.N > 2LL * grid * kNCW) a.fq = 0;
+    if (a.X && !a.fq) {
+        const int st = launch_quantizer(ctx, a, 8 * NG, D::Q80, stream);
+        if (st != SRHPM_OK) return st;
+    }
     ctx->launches.fetch_add(1);
     return cuda_status(cudaLaunchKernelEx(&cfg, kern, wmap, a));
 }
@@ -1603,46 +1739,47 @@ size_t gemm_work_size_unsplit(int wtype, int64_t rows, int64_t K, int64_t N) {
 
 namespace {
 
+// the arrival counter of the grids that use this work buffer (one per buffer, so that calls with different buffers
+// may run concurrently on other streams); null when the context's table is full
+uint32_t * sync_counter(srhpm_ctx * ctx, const void * work) {
+    if (!ctx->d_sync) return nullptr;
+    std::lock_guard<std::mutex> lk(ctx->sync_mu);
+    const uintptr_t             key = reinterpret_cast<uintptr_t>(work);
+    const auto                  it  = ctx->sync_slots.find(key);
+    if (it != ctx->sync_slots.end()) return ctx->d_sync + it->second;
+    if (ctx->sync_next >= kSyncSlots) return nullptr;
+    const int slot        = ctx->sync_next++;
+    ctx->sync_slots[key] = slot;
+    return ctx->d_sync + slot;
+}
+
 int gemm_run_impl(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                   const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
-                  int32_t * isum, int32_t * imin, bool split, cudaStream_t stream, bool prequant = false) {
+                  int32_t * isum, int32_t * imin, bool split, cudaStream_t stream, bool prequant = false,
+                  bool fused_ok = false) {
     const WorkLayout wl = split ? work_layout(wtype, rows, K, N) : work_layout_unsplit(wtype, rows, K, N);
     if (wsize < wl.total || !wdata) return SRHPM_ERR_WORKSPACE;
     const int  nsb  = (int) (K / QK);
-    const int  NT   = N <= 8 ? 8 : 16;
     const bool q80  = wtype == SRHPM_TYPE_Q8_0;
     uint8_t *  base = align256(wdata);
     uint8_t *  recs = base + wl.recs;
     int32_t *  cnt  = reinterpret_cast<int32_t *>(base + wl.cnt);
     const int  nrb  = (int) ((rows + kTileRows - 1) / kTileRows);
-    // 1. activation records (and zeroed split-K counters); prequant: written by the preceding fused norm
-    if (!prequant) {
-        const int64_t warps  = (int64_t) nsb * NT;
-        const int     blocks = (int) ((warps + 7) / 8);
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim            = dim3((unsigned) blocks);
-        cfg.blockDim           = dim3(256);
-        cfg.stream             = stream;
-        cudaLaunchAttribute attr[1];
-        attr[0].id                                         = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs                                          = attr;
-        cfg.numAttrs                                       = 1;
-        cudaError_t e;
-        if (q80) {
-            e = cudaLaunchKernelEx(&cfg, quant_q80_kernel<false>, X, ldx, (int) N, nsb, NT, ctx->q8_0_act_mode, recs,
-                                   (uint8_t *) nullptr, cnt, nrb);
-        } else {
-            e = cudaLaunchKernelEx(&cfg, quant_q8K_kernel<false>, X, ldx, (int) N, nsb, NT, recs, (int8_t *) nullptr,
-                                   (float *) nullptr, (int16_t *) nullptr, (int16_t *) nullptr, cnt, nrb,
-                                   record_perm(wtype));
-        }
-        ctx->launches.fetch_add(1);
-        const int st = cuda_status(e);
-        if (st != SRHPM_OK) return st;
-    }
-    // 2. the matmul
+    // the activation records (and zeroed split-K counters) come from the GEMM's own prologue or a quantizer kernel
+    // launched just before it (launch_gemm); prequant: written by the preceding fused norm / SwiGLU
     GemmArgs a  = {};
+    if (!prequant) {
+        a.X       = X;
+        a.ldx     = ldx;
+        a.perm    = record_perm(wtype);
+        a.q80mode = ctx->q8_0_act_mode;
+        a.ncnt    = nrb;
+        a.fq      = fused_ok ? 1 : 0;
+        if (a.fq) {
+            a.sync = sync_counter(ctx, recs);
+            if (!a.sync) a.fq = 0;
+        }
+    }
     a.W         = W;
     a.rows      = rows;
     a.row_bytes = (int64_t) row_bytes;
@@ -1733,8 +1870,9 @@ int swiglu_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_
 
 int gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
              const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
-             int32_t * isum, int32_t * imin, cudaStream_t stream) {
-    return gemm_run_impl(ctx, wtype, W, rows, K, row_bytes, X, ldx, N, Y, ldy, wdata, wsize, isum, imin, true, stream);
+             int32_t * isum, int32_t * imin, cudaStream_t stream, bool fused_quant) {
+    return gemm_run_impl(ctx, wtype, W, rows, K, row_bytes, X, ldx, N, Y, ldy, wdata, wsize, isum, imin, true, stream,
+                         false, fused_quant);
 }
 
 int gemm_run_unsplit(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,

@@ -163,8 +163,9 @@ class Context:
         st = self.lib.srhpm_mul_mat_work_size(ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(sz))
         return st, sz.value
 
-    def mul_mat(self, W, X, out=None, stream=None, work=None):
-        """Y[N, rows] = X[N, K] . W[rows, K]^T (ggml_mul_mat(W, X): dst ne = [rows, N])."""
+    def mul_mat(self, W, X, out=None, stream=None, work=None, fused_quant=False):
+        """Y[N, rows] = X[N, K] . W[rows, K]^T (ggml_mul_mat(W, X): dst ne = [rows, N]). fused_quant: one launch, the
+        matmul grid quantizes its own activations (srhpm_mul_mat_fused_quant; bit-identical output)."""
         X = X if X.stride(-1) == 1 else X.contiguous()
         N = X.shape[0]
         if out is None:
@@ -173,12 +174,12 @@ class Context:
         st, ws = self.mul_mat_work_size(W, X)
         L.check(st, "srhpm_mul_mat_work_size")
         buf = work if work is not None else self.work(ws)
-        L.check(self.lib.srhpm_mul_mat(self.handle, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv),
-                                       ctypes.c_void_p(buf.data_ptr()), buf.numel(), _stream_ptr(stream)),
-                "srhpm_mul_mat")
+        fn = self.lib.srhpm_mul_mat_fused_quant if fused_quant else self.lib.srhpm_mul_mat
+        L.check(fn(self.handle, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv), ctypes.c_void_p(buf.data_ptr()),
+                   buf.numel(), _stream_ptr(stream)), "srhpm_mul_mat")
         return out
 
-    def prepare_mul_mat(self, W, X, Y, work):
+    def prepare_mul_mat(self, W, X, Y, work, fused_quant=False):
         """A zero-argument callable that issues srhpm_mul_mat(W, X) -> Y on the current stream with prebuilt
         arguments (the per-call host cost is one ctypes call); usable under CUDA-graph capture, since the call
         allocates nothing."""
@@ -187,7 +188,7 @@ class Context:
         L.check(st, "srhpm_mul_mat_work_size")
         if work.numel() < ws:
             raise ValueError("work buffer too small")
-        fn, lib = self.lib.srhpm_mul_mat, self.lib
+        fn, lib = (self.lib.srhpm_mul_mat_fused_quant if fused_quant else self.lib.srhpm_mul_mat), self.lib
         args = [self.handle, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv), ctypes.c_void_p(work.data_ptr()),
                 work.numel()]
         keep = (wv, xv, yv, W, X, Y, work)

@@ -256,9 +256,13 @@ class VerifyStep:
     is this rank's: its query heads, its KV heads (caches hold only those), its FFN rows and its vocabulary rows; the
     residual stream, norms and embeddings are replicated."""
 
-    def __init__(self, ctx, cfg, weights, kcache, vcache, n_tokens, n_past, relax=0.0, tp=None, fuse_prologue=True):
+    def __init__(self, ctx, cfg, weights, kcache, vcache, n_tokens, n_past, relax=0.0, tp=None, fuse_prologue=True,
+                 fused_quant_o=True):
         self.ctx, self.cfg, self.w = ctx, cfg, weights
         self.fuse_prologue = fuse_prologue  # RMSNorm writes the next GEMM's activation records itself
+        # the attention output projection quantizes its activations in its own grid (srhpm_mul_mat_fused_quant: one
+        # launch; the attention before it leaves the SMs free, so the grid is resident early)
+        self.fused_quant_o = fused_quant_o
         self.kcache, self.vcache = kcache, vcache
         self.n, self.n_past, self.relax = n_tokens, n_past, relax
         self.tp = tp if tp is not None and tp.world > 1 else None
@@ -299,12 +303,15 @@ class VerifyStep:
     def _ptr(self, t):
         return ctypes.c_void_p(t.data_ptr())
 
-    def _mm(self, W, X, Y):
+    def _mm(self, W, X, Y, fused_quant=False):
         st, ws = self.ctx.mul_mat_work_size(W, X)
         L.check(st, "srhpm_mul_mat_work_size")
         self._ws = max(self._ws, ws)
         wv, xv, yv = W.view(), f32_rows_view(X), f32_rows_view(Y)
         self._keep += [wv, xv, yv]
+        if fused_quant:
+            return ("mul_mat_fused_quant", self.lib.srhpm_mul_mat_fused_quant,
+                    [self.ctx.handle, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv)], True)
         fn = self.lib.srhpm_mul_mat
         return ("mul_mat", fn, [self.ctx.handle, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv)], True)
 
@@ -415,7 +422,7 @@ class VerifyStep:
                           [h, ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(mv), None,
                            ctypes.c_float(1.0 / math.sqrt(hd)), ctypes.c_float(0.0), ctypes.c_float(0.0),
                            ctypes.byref(ov)], True))
-            calls.append(self._mm(lay["o"], self.att, self._rowpar_out(0)))
+            calls.append(self._mm(lay["o"], self.att, self._rowpar_out(0), self.fused_quant_o))
             if self.tp is not None and not self._fused():
                 calls.append(self._all_reduce(self.o))  # row-parallel O: partial sums over the rank's heads
             if "gate_up" in lay:

@@ -346,10 +346,11 @@ def test_fused_norm_quant_prologue_is_exact(ctx):
     kc, vc = _caches(cfg, cap, n_past, 512, 32)
     dev_w = V.DeviceWeights.from_host(cfg, w)
     outs = []
-    for fuse in (False, True):
+    for fuse, fq_o in ((False, False), (True, False), (True, True)):
+        # fq_o: the attention output projection quantizes its activations in its own grid (one launch instead of 2)
         kcd = [torch.from_numpy(a).cuda() for a in kc]
         vcd = [torch.from_numpy(a).cuda() for a in vc]
-        step = V.VerifyStep(ctx, cfg, dev_w, kcd, vcd, len(ids), n_past, fuse_prologue=fuse)
+        step = V.VerifyStep(ctx, cfg, dev_w, kcd, vcd, len(ids), n_past, fuse_prologue=fuse, fused_quant_o=fq_o)
         step.set_tokens(ids, draft)
         ctx.launch_count(reset=True)
         step.run()
@@ -357,11 +358,14 @@ def test_fused_norm_quant_prologue_is_exact(ctx):
         launches = ctx.launch_count(reset=True)
         ctx.check()
         outs.append((step.logits.clone(), [a.clone() for a in kcd], step.accepted(), launches))
-    assert torch.equal(outs[0][0], outs[1][0])
-    assert all(torch.equal(a, b) for a, b in zip(outs[0][1], outs[1][1]))
-    assert outs[0][2] == outs[1][2]
-    # kernel launches: the quantizers of the QKV, gate|up, down and head GEMMs are gone (3 per layer + 1)
+    for o in outs[1:]:
+        assert torch.equal(outs[0][0], o[0])
+        assert all(torch.equal(a, b) for a, b in zip(outs[0][1], o[1]))
+        assert outs[0][2] == o[2]
+    # kernel launches: the quantizers of the QKV, gate|up, down and head GEMMs are gone (3 per layer + 1), and with
+    # the fused output projection the O GEMM's (1 per layer) when its grid is large enough for the fused form
     assert outs[0][3] - outs[1][3] == 3 * cfg.n_layer + 1
+    assert outs[1][3] - outs[2][3] in (0, cfg.n_layer)
 
 
 @pytest.mark.parametrize("qtype", [S.Q4_K, S.Q5_K, S.Q6_K, S.Q3_K, S.IQ4_XS])
