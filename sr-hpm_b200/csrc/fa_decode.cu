@@ -137,31 +137,6 @@ template <int HI> __device__ __forceinline__ uint32_t magic_pair(uint32_t wx) {
     return prmt(wx, 0x64u, HI ? 0x4342u : 0x4140u);
 }
 
-// packed f32 pairs (sm_100 f32x2 instructions: one issue for two lanes of arithmetic)
-typedef unsigned long long f2;
-__device__ __forceinline__ f2 f2_pack(float a, float b) {
-    f2 r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-    return r;
-}
-__device__ __forceinline__ void f2_unpack(f2 r, float & a, float & b) {
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
-}
-__device__ __forceinline__ f2 f2_add(f2 a, f2 b) {
-    f2 r;
-    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ f2 f2_mul(f2 a, f2 b) {
-    f2 r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ f2 f2_fma(f2 a, f2 b, f2 c) {
-    f2 r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
 __device__ __forceinline__ float ex2(float x) {
     float r;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
@@ -1250,11 +1225,14 @@ Plan fa_plan(int num_sms, int R, int L, int Hkv) {
     Plan      p;
     const int max_ch = (L + kT - 1) / kT;
     if (Hkv * max_ch >= num_sms) {
-        // long caches: 48-row groups (each KV byte read once per group), chunks of two tiles at least
-        p.rp = R <= 32 ? (R + 15) / 16 * 16 : kRG;
-        p.nrg            = (R + p.rp - 1) / p.rp;
+        // long caches: the fewest row groups of <= 48 rows (each group reads every KV byte), rows split evenly
+        // between them (54 rows: 2 x 32, not 48 + 16: equal groups advance through the same tiles together, so the
+        // second read of a tile comes from L2, and neither carries a mostly empty tile); as many chunks of at least
+        // two tiles as fill the SMs in ONE wave (one CTA per SM: a CTA more than the SMs runs as a second wave)
+        p.nrg            = (R + kRG - 1) / kRG;
+        p.rp             = ((R + p.nrg - 1) / p.nrg + 15) / 16 * 16;
         const int groups = Hkv * p.nrg;
-        int       want   = std::max(1, std::min(max_ch, (num_sms + groups - 1) / groups));
+        int       want   = std::max(1, std::min(max_ch, num_sms / groups));
         if (max_ch >= 2) want = std::min(want, max_ch / 2);
         want             = std::max(1, want);
         const int per    = (L + want - 1) / want;

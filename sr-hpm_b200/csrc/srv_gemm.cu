@@ -39,6 +39,7 @@ namespace srhpm {
 namespace {
 
 constexpr int     QK         = 256;
+constexpr int     kMagic32   = 0x4B400000;        // the bits of 12582912.0f (1.5 * 2^23)
 constexpr int     kNCW       = 4;                 // consumer warps, one per 16-row slice
 constexpr int     kThreads   = (kNCW + 1) * 32;   // + 1 producer warp
 constexpr int     kTileRows  = 16 * kNCW;         // weight rows per CTA tile
@@ -485,23 +486,25 @@ __device__ __forceinline__ void zero(int (&v)[NG][4]) {
     for (int grp = 0; grp < NG; grp++) v[grp][0] = v[grp][1] = v[grp][2] = v[grp][3] = 0;
 }
 
-// f32 update of one super-block: acc += (d_row * x_tok) * isum  [- (dmin_row * x_tok) * imin]
+// f32 update of one super-block: acc += (d_row * x_tok) * isum  [- (dmin_row * x_tok) * imin], in f32 pairs (the
+// two tokens of a thread: one f32x2 multiply and one f32x2 fused multiply-add per row, each lane rounded as the
+// scalar pair would be)
 template <int NG, bool MIN>
 __device__ __forceinline__ void sb_update(float (&acc)[NG][4], const int (&im)[NG][4], const int (&in)[NG][4],
                                           float dA, float dB, float mA, float mB, const float * xs, int t) {
 #pragma unroll
     for (int grp = 0; grp < NG; grp++) {
         const float2 x  = *reinterpret_cast<const float2 *>(xs + 8 * grp + 2 * t);
-        acc[grp][0] += (dA * x.x) * (float) im[grp][0];
-        acc[grp][1] += (dA * x.y) * (float) im[grp][1];
-        acc[grp][2] += (dB * x.x) * (float) im[grp][2];
-        acc[grp][3] += (dB * x.y) * (float) im[grp][3];
+        const f2     xx = f2_pack(x.x, x.y);
+        f2           a01 = f2_pack(acc[grp][0], acc[grp][1]), a23 = f2_pack(acc[grp][2], acc[grp][3]);
+        a01 = f2_fma(f2_mul(f2_pack(dA, dA), xx), f2_pack((float) im[grp][0], (float) im[grp][1]), a01);
+        a23 = f2_fma(f2_mul(f2_pack(dB, dB), xx), f2_pack((float) im[grp][2], (float) im[grp][3]), a23);
         if constexpr (MIN) {
-            acc[grp][0] -= (mA * x.x) * (float) in[grp][0];
-            acc[grp][1] -= (mA * x.y) * (float) in[grp][1];
-            acc[grp][2] -= (mB * x.x) * (float) in[grp][2];
-            acc[grp][3] -= (mB * x.y) * (float) in[grp][3];
+            a01 = f2_fma(f2_mul(f2_pack(-mA, -mA), xx), f2_pack((float) in[grp][0], (float) in[grp][1]), a01);
+            a23 = f2_fma(f2_mul(f2_pack(-mB, -mB), xx), f2_pack((float) in[grp][2], (float) in[grp][3]), a23);
         }
+        f2_unpack(a01, acc[grp][0], acc[grp][1]);
+        f2_unpack(a23, acc[grp][2], acc[grp][3]);
     }
 }
 
@@ -969,7 +972,13 @@ struct DecQ80 {
 #pragma unroll
             for (int grp = 0; grp < NG; grp++) {
                 const uint8_t * xp = xr + (8 * grp + g) * kTokStride + 32 * i + 4 * t;
-                mma_k32_z<false>(c[grp], a0, a1, a2, a3, lds32(xp), lds32(xp + 16));
+                if constexpr (DBG) {
+                    mma_k32_z<false>(c[grp], a0, a1, a2, a3, lds32(xp), lds32(xp + 16));
+                } else {
+                    // the block sum i (|i| <= 32 * 128 * 127 < 2^22) on top of 0x4B400000 reads as the float
+                    // 12582912 + i exactly: one f32x2 subtraction per pair gives the sums as floats
+                    mma_k32_c<false>(c[grp], a0, a1, a2, a3, lds32(xp), lds32(xp + 16), kMagic32);
+                }
             }
             if constexpr (DBG) {
                 dbg_store<NG>(dbg, c, false, rg, 8 * sbi + i, lane);
@@ -979,13 +988,18 @@ struct DecQ80 {
                 const float    dA = (i & 3) == 0 ? qa.x : (i & 3) == 1 ? qa.y : (i & 3) == 2 ? qa.z : qa.w;
                 const float    dB = (i & 3) == 0 ? qb.x : (i & 3) == 1 ? qb.y : (i & 3) == 2 ? qb.z : qb.w;
                 const float *  xs = xsb + i * NT;
+                const f2       nm = f2_pack(-12582912.0f, -12582912.0f);
 #pragma unroll
                 for (int grp = 0; grp < NG; grp++) {
-                    const float2 x = *reinterpret_cast<const float2 *>(xs + 8 * grp + 2 * t);
-                    acc[grp][0] += (dA * x.x) * (float) c[grp][0];
-                    acc[grp][1] += (dA * x.y) * (float) c[grp][1];
-                    acc[grp][2] += (dB * x.x) * (float) c[grp][2];
-                    acc[grp][3] += (dB * x.y) * (float) c[grp][3];
+                    const float2 x  = *reinterpret_cast<const float2 *>(xs + 8 * grp + 2 * t);
+                    const f2     xx = f2_pack(x.x, x.y);
+                    const f2     c01 = f2_add(f2_pack(__int_as_float(c[grp][0]), __int_as_float(c[grp][1])), nm);
+                    const f2     c23 = f2_add(f2_pack(__int_as_float(c[grp][2]), __int_as_float(c[grp][3])), nm);
+                    f2           a01 = f2_pack(acc[grp][0], acc[grp][1]), a23 = f2_pack(acc[grp][2], acc[grp][3]);
+                    a01 = f2_fma(f2_mul(f2_pack(dA, dA), xx), c01, a01);
+                    a23 = f2_fma(f2_mul(f2_pack(dB, dB), xx), c23, a23);
+                    f2_unpack(a01, acc[grp][0], acc[grp][1]);
+                    f2_unpack(a23, acc[grp][2], acc[grp][3]);
                 }
             }
         }
