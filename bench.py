@@ -50,9 +50,9 @@ NS = [2, 4, 8]
 SEED = 1234
 DATA_DESC = "synthetic (seeded N(0,0.02) weights quantized on the host, N(0,1) activations)"
 # DRAM bytes (read + write) per srv_gemm_kernel launch over one step of the default sweep on one GPU, from one ncu
-# capture (profiles/srv_gemm_sweep_60products_launches.md): 2612.05 MB over the 60 launches; the algorithmic bytes
-# per launch are 43.53 MB as well
-SWEEP_TRAFFIC_PER_LAUNCH = 43.534e6
+# capture (profiles/srv_gemm_sweep_60products_launches.md): 2611.35 MB over the 60 launches; the algorithmic bytes
+# per launch are 43.53 MB
+SWEEP_TRAFFIC_PER_LAUNCH = 43.522e6
 
 
 def row_bytes(t, K):
@@ -1000,13 +1000,13 @@ def shard_vocab(n_vocab, world, j):
     return shard.vocab_range(n_vocab, world, j)
 
 
-def measure_attention(ctx, dev, peak, reps=20, lengths=(8192, 32768, 131072)):
-    """Verify attention: 8 query rows, 24 query heads, 4 KV heads, head_dim 256, causal mask among the draft rows,
-    q8_0 K/V (N(0,1) before quantization) of L past tokens, Q N(0,1) / 16. Timed as CUDA-graph replays over copies
-    of the KV cache that together exceed L2."""
+def measure_attention(ctx, dev, peak, reps=20, lengths=(8192, 32768, 131072), N=8):
+    """Verify attention: N query rows (8: BASELINE config 3; 9: the rows of the k = 8 verify step), 24 query heads,
+    4 KV heads, head_dim 256, causal mask among the draft rows, q8_0 K/V (N(0,1) before quantization) of L past
+    tokens, Q N(0,1) / 16. Timed as CUDA-graph replays over copies of the KV cache that together exceed L2."""
     import torch
     import srhpm_b200 as S
-    H, Hkv, N, D = 24, 4, 8, 256
+    H, Hkv, D = 24, 4, 256
     g = torch.Generator(device=dev)
     g.manual_seed(3)
     out = {}
@@ -1444,7 +1444,10 @@ def main():
     ap.add_argument("--no-attn", action="store_true", help="skip the attention and acceptance measurements")
     ap.add_argument("--attn", type=int, default=None, help="time only the attention at this KV length (profiling)")
     ap.add_argument("--no-step", action="store_true", help="skip the 27B-class verify-step measurements")
+    ap.add_argument("--attn-rows", type=int, default=8, help="query tokens of the --attn leg (9: the k = 8 step's)")
     ap.add_argument("--step27b", type=int, default=None, help="time only the 27B-class step with k drafted tokens")
+    ap.add_argument("--step27b-long", type=int, default=None,
+                    help="time only the long-context 27B-class step (q8_0 KV of 131072 tokens) with k drafted tokens")
     ap.add_argument("--traffic", type=float, default=None, help="ncu dram bytes per launch, when captured")
     args = ap.parse_args()
     if args.step27b:
@@ -1456,13 +1459,25 @@ def main():
                                                                           ks=(args.step27b,)), "peak_kind": kind}),
               file=JSON_OUT, flush=True)
         return 0
+    if args.step27b_long:
+        import torch
+        import srhpm_b200 as S
+        from srhpm_b200 import _lib as L
+        ctx = S.Context(0)
+        peak, kind = peaks()
+        print(json.dumps({"verify_step_27b_q8kv_131072": measure_step_27b(ctx, torch.device("cuda", 0), peak,
+                                                                           ks=(args.step27b_long,), kv_type=L.Q8_0,
+                                                                           n_past=131072, reps=5),
+                          "peak_kind": kind}), file=JSON_OUT, flush=True)
+        return 0
     if args.attn:
         import torch
         import srhpm_b200 as S
         ctx = S.Context(0)
         peak, kind = peaks()
-        print(json.dumps({"attention_q8_0": measure_attention(ctx, torch.device("cuda", 0), peak, lengths=(args.attn,)),
-                          "peak_kind": kind}), file=JSON_OUT, flush=True)
+        print(json.dumps({"attention_q8_0": measure_attention(ctx, torch.device("cuda", 0), peak, lengths=(args.attn,),
+                                                              N=args.attn_rows),
+                          "rows": args.attn_rows, "peak_kind": kind}), file=JSON_OUT, flush=True)
         return 0
     if args.warmup < 3 and args.impl == "srhpm":
         args.warmup = 3
