@@ -250,10 +250,10 @@ int srhpm_swiglu_quant(srhpm_ctx * ctx, const float * gate, const float * up, in
  * every rank's row-parallel GEMM (attention output, FFN down) writes its partial sum [n][d] f32 into slot `slot`
  * (0 or 1) of its own symmetric buffer of srhpm_allreduce_buffer_size(d) bytes, zeroed once before first use and
  * mapped on every rank (peer_buffers: a DEVICE array of `world` addresses, this rank's own at [rank]; IPC / symmetric
- * memory set up by the caller). srhpm_add_rms_norm_allreduce then, per row: publishes a per-(slot, row) epoch to every
- * peer, waits (bounded: 2 s, then SRHPM_ERR_DEVICE through srhpm_ctx_check) until every peer has published the same
- * epoch, sums the rank's rows over ranks in rank order (identical on every rank), adds the sum to x and writes
- * y = x / sqrt(mean(x^2) + eps) * w. epochs: this rank's uint32 [2][16] counters, zeroed once. n <= 16, world <= 8,
+ * memory set up by the caller). srhpm_add_rms_norm_allreduce then, per row: sends each of its partial values with a
+ * per-(slot, row) epoch, as one 8-byte word, into the receive area of every rank's buffer, waits (bounded: 2 s, then
+ * SRHPM_ERR_DEVICE through srhpm_ctx_check) until every word it receives carries the epoch, sums the ranks' values in
+ * rank order (identical on every rank), adds the sum to x and writes y = x / sqrt(mean(x^2) + eps) * w. epochs: this rank's uint32 [2][16] counters, zeroed once. n <= 16, world <= 8,
  * d a multiple of 4 and <= 16384; x, w, y 16-byte aligned. The two slots alternate (O, down): a slot is rewritten only
  * after the other slot's barrier has passed on every rank. Every rank must make the same sequence of calls. No
  * counterpart in the reference (it runs on one device): the tensor-parallel decoder's all-reduce after O and down. */
@@ -262,7 +262,7 @@ int srhpm_add_rms_norm_allreduce(srhpm_ctx * ctx, float * x, const uint64_t * pe
                                  int slot, uint32_t * epochs, const float * w, float eps, float * y, int n, int64_t d,
                                  void * stream);
 /* srhpm_add_rms_norm_allreduce fused with the activation quantization of the GEMM that consumes y, as
- * srhpm_add_rms_norm_quant is for srhpm_add_rms_norm: the same flag barrier and rank-order sum of the peers' slot
+ * srhpm_add_rms_norm_quant is for srhpm_add_rms_norm: the same exchange and rank-order sum of the ranks' slot
  * `slot` rows, the residual add and the norm, and W_next's activation records written into wdata for
  * srhpm_mul_mat_prequantized. One launch instead of the norm plus srhpm_mul_mat's own quantizer. Same limits as both
  * (K-quant and IQ4_XS W_next, n <= 16, d <= 16384, world <= 8). No counterpart in the reference (one device). */

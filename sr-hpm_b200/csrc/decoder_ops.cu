@@ -106,7 +106,8 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_kernel(float * x, c
 }
 
 // ---- residual add of a tensor-parallel partial sum + RMSNorm, the all-reduce done in the same kernel ------------
-// CTA i (row i): the flag barrier of allreduce.cuh, then x += the ranks' partial rows (rank order) and the norm.
+// CTA i (row i): the flag-in-word exchange of allreduce.cuh (each thread sends its values of the rank's partial row to
+// every rank, then adds the ranks' values in rank order), x += the sum, and the norm.
 __global__ void __launch_bounds__(kNormThreads) add_rms_norm_ar_kernel(float * x, const uint64_t * peers, int world,
                                                                         int rank, int slot, uint32_t * epochs,
                                                                         const float * w, float eps, float * y,
@@ -114,19 +115,25 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_ar_kernel(float * x
     pdl_launch_dependents();
     pdl_wait();  // this rank's GEMM has written its partial rows
     const int64_t i = blockIdx.x;
-    __shared__ int ok_s;
-    if (threadIdx.x == 0) ok_s = ar_row_barrier(peers, world, rank, slot, epochs, (int) i, d, status);
-    __syncthreads();
-    float * xr = x + i * d;
-    float   ss = 0.0f;
-    float4  v[4];
-    const int64_t d4 = d >> 2;
+    __shared__ uint32_t e_s;
+    const uint32_t      e  = ar_epoch(epochs, slot, (int) i, &e_s);
+    const int64_t       d4 = d >> 2;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int64_t j = threadIdx.x + (int64_t) k * kNormThreads;
+        if (j < d4) ar_push4(peers, world, rank, slot, (int) i, d, j, e);
+    }
+    float *        xr = x + i * d;
+    float          ss = 0.0f;
+    float4         v[4];
+    bool           ok = true;
+    const uint64_t t0 = global_timer_ns();
 #pragma unroll
     for (int k = 0; k < 4; k++) {
         const int64_t j = threadIdx.x + (int64_t) k * kNormThreads;
         if (j < d4) {
             float4 a = reinterpret_cast<const float4 *>(xr)[j];
-            if (ok_s) ar_add_row4(a, peers, world, slot, (int) i, d4, j);
+            ar_gather4(a, peers, world, rank, slot, (int) i, d, j, e, t0, ok, status);
             reinterpret_cast<float4 *>(xr)[j] = a;
             v[k] = a;
             ss = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, ss))));
@@ -278,7 +285,8 @@ int add_rms_norm_ar_run(srhpm_ctx * ctx, float * x, const uint64_t * peers, int 
 }
 
 size_t allreduce_buffer_bytes(int64_t d) {
-    return 2 * (size_t) kArRows * d * sizeof(float) + 2 * kArRows * kArMaxRanks * sizeof(uint32_t);
+    // the two slots of partial rows, then the receive area of 8-byte (value, epoch) words
+    return 2 * ar_part_bytes(d) + 2 * (size_t) kArRows * kArMaxRanks * d * sizeof(uint64_t);
 }
 
 int rope_kv_run(srhpm_ctx * ctx, float * qkv, int64_t ld, int n, int H, int Hkv, int hd, const int32_t * pos,

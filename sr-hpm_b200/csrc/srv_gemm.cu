@@ -258,9 +258,9 @@ __global__ void __launch_bounds__(256) swiglu_q8K_kernel(const float * __restric
 // prologue): CTA t < N: x += delta; y = x / sqrt(mean(x^2) + eps) * w (as add_rms_norm); the row of y is staged in
 // shared memory and each warp quantizes super-blocks of it into the GEMM's activation records exactly as
 // quant_q8K_kernel does (same functions); CTAs N..NT-1 write the zero padding rows; CTA 0 zeroes the split-K counters.
-// With ar.peers set, the delta is the tensor-parallel all-reduce of the ranks' partial rows instead (the flag barrier
-// and the rank-order sum of allreduce.cuh, as add_rms_norm_ar_kernel does): all-reduce, residual add, norm and the
-// next GEMM's activation records in one kernel.
+// With ar.peers set, the delta is the tensor-parallel all-reduce of the ranks' partial rows instead (the flag-in-word
+// exchange and the rank-order sum of allreduce.cuh, as add_rms_norm_ar_kernel does): all-reduce, residual add, norm
+// and the next GEMM's activation records in one kernel.
 struct NormAr {
     const uint64_t * peers;  // null: no all-reduce
     int              world, rank, slot;
@@ -283,15 +283,21 @@ __global__ void __launch_bounds__(kNormQThreads) add_rms_norm_q8K_kernel(float *
         for (int i = threadIdx.x; i < ncnt; i += blockDim.x) cnt[i] = 0;
     }
     if (t < N) {
-        float *  xr = x + (int64_t) t * d;
-        float    ss = 0.0f;
-        float4   v[4];
-        __shared__ int ok_s;
-        if (ar.peers) {
-            if (threadIdx.x == 0) {
-                ok_s = ar_row_barrier(ar.peers, ar.world, ar.rank, ar.slot, ar.epochs, t, d, ar.status);
+        float *             xr = x + (int64_t) t * d;
+        float               ss = 0.0f;
+        float4              v[4];
+        __shared__ uint32_t e_s;
+        uint32_t            e  = 0;
+        bool                ok = true;
+        uint64_t            t0 = 0;
+        if (ar.peers) {  // send this rank's values of the row to every rank first (allreduce.cuh)
+            e = ar_epoch(ar.epochs, ar.slot, t, &e_s);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int64_t j = threadIdx.x + (int64_t) k * kNormQThreads;
+                if (j < d4) ar_push4(ar.peers, ar.world, ar.rank, ar.slot, t, d, j, e);
             }
-            __syncthreads();
+            t0 = global_timer_ns();
         }
 #pragma unroll
         for (int k = 0; k < 4; k++) {
@@ -299,7 +305,7 @@ __global__ void __launch_bounds__(kNormQThreads) add_rms_norm_q8K_kernel(float *
             if (j < d4) {
                 float4 a = reinterpret_cast<const float4 *>(xr)[j];
                 if (ar.peers) {
-                    if (ok_s) ar_add_row4(a, ar.peers, ar.world, ar.slot, t, d4, j);
+                    ar_gather4(a, ar.peers, ar.world, ar.rank, ar.slot, t, d, j, e, t0, ok, ar.status);
                     reinterpret_cast<float4 *>(xr)[j] = a;
                 } else if (delta) {
                     const float4 b = reinterpret_cast<const float4 *>(delta + (int64_t) t * d)[j];

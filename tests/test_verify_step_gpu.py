@@ -276,10 +276,41 @@ def test_tensor_parallel_step_matches_one_gpu(ctx, Hkv, fused):
     assert got[2][:k] == exp[:k]
 
 
+def test_allreduce_norm_one_rank_equals_add_norm(ctx):
+    """The fused all-reduce with one rank: the rank sends its partial row to itself as (value, epoch) words and adds
+    them, so x + partial and the norm equal srhpm_add_rms_norm with the partial as delta, bit for bit, over two calls
+    per slot (the epochs advance)."""
+    lib = L.load()
+    d, n = 5120, 9
+    nbytes = int(lib.srhpm_allreduce_buffer_size(d))
+    mine = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    peers = torch.tensor([mine.data_ptr()], dtype=torch.int64, device="cuda")
+    epochs = torch.zeros(32, dtype=torch.int32, device="cuda")
+    w = 1 + 0.1 * torch.randn(d, device="cuda")
+    ptr = lambda t: t.data_ptr()
+    part = [mine[k * 16 * d * 4:(k + 1) * 16 * d * 4].view(torch.float32).view(16, d) for k in (0, 1)]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    for rep in range(4):
+        slot = rep % 2
+        part[slot][:n] = torch.randn((n, d), device="cuda", generator=g)
+        x = torch.randn((n, d), device="cuda", generator=g)
+        x2, y, y2 = x.clone(), torch.empty_like(x), torch.empty_like(x)
+        L.check(lib.srhpm_add_rms_norm_allreduce(ctx.handle, ptr(x), ptr(peers), 1, 0, slot, ptr(epochs), ptr(w),
+                                                 1e-6, ptr(y), n, d, None), "srhpm_add_rms_norm_allreduce")
+        delta = part[slot][:n].clone()
+        L.check(lib.srhpm_add_rms_norm(ctx.handle, ptr(x2), ptr(delta), ptr(w), ctypes.c_float(1e-6), ptr(y2), n, d,
+                                       None), "srhpm_add_rms_norm")
+        torch.cuda.synchronize()
+        ctx.check()
+        assert torch.equal(x, x2) and torch.equal(y, y2), rep
+    assert epochs.view(2, 16)[:, :n].tolist() == [[2] * n, [2] * n]
+
+
 def test_allreduce_norm_peer_wait_times_out(ctx):
-    """The fused all-reduce's flag wait is bounded: a second 'rank' whose flag nothing ever sets (a plain local
-    buffer standing in for the peer) ends the wait after ~2 s with an error status read on the host, and the context
-    stays usable. No GPU fault and no hang: the kernel gives up and finishes."""
+    """The fused all-reduce's wait is bounded: a second 'rank' that never sends its values (a plain local buffer
+    standing in for the peer) ends the wait after ~2 s with an error status read on the host, and the context stays
+    usable. No GPU fault and no hang: the kernel gives up and finishes."""
     import time
     lib = L.load()
     d, n = 512, 2
@@ -300,16 +331,18 @@ def test_allreduce_norm_peer_wait_times_out(ctx):
     with pytest.raises(L.SrhpmError):
         ctx.check()
     ctx.check()  # cleared: the context keeps working
-    # this rank published its epoch into both buffers' flags (slot 0, rows 0..n-1, rank 0)
+    # this rank sent its (zero) partial values with epoch 1 into both buffers' receive areas (slot 0, rows 0..n-1,
+    # source rank 0): 8-byte words, value bits low, epoch high
     off = 2 * 16 * d * 4
     for buf in (mine, fake):
-        flags = buf[off:].view(torch.int32).view(2, 16, 8)
-        assert flags[0, :n, 0].tolist() == [1] * n
+        words = buf[off:].view(torch.int32).view(2, 16, 8, d, 2)
+        assert bool((words[0, :n, 0, :, 1] == 1).all()) and bool((words[0, :n, 0, :, 0] == 0).all())
+        assert bool((words[0, :n, 1] == 0).all())  # nothing from the stand-in rank
 
 
 def test_allreduce_norm_quant_peer_wait_times_out(ctx):
-    """The fused all-reduce + norm + quantization prologue has the same bounded flag wait: against a stand-in peer
-    whose flag nothing sets it gives up after ~2 s with an error status, and the context stays usable."""
+    """The fused all-reduce + norm + quantization prologue has the same bounded wait: against a stand-in peer that
+    never sends its values it gives up after ~2 s with an error status, and the context stays usable."""
     import time
     lib = L.load()
     d, n, rows = 512, 2, 64
