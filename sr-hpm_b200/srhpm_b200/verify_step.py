@@ -197,17 +197,19 @@ class TensorParallel:
     """The collectives of a Megatron tensor-parallel step over torch.distributed.
 
     fused=True (default): the row-parallel O and down GEMMs write their partial sums into a symmetric buffer (torch
-    symmetric memory: every rank's buffer mapped on every rank), and the next RMSNorm sums the ranks' rows itself
-    over NVLink peer loads after a flag barrier (srhpm_add_rms_norm_allreduce): no separate collective launch.
+    symmetric memory: every rank's buffer mapped on every rank), and the next RMSNorm exchanges the ranks' rows over
+    NVLink as (value, epoch) words and sums them itself (srhpm_add_rms_norm_allreduce): no separate collective
+    launch.
     fused=False: an NCCL all-reduce after each of those GEMMs (128 per step for 64 layers). The vocabulary shards'
     argmax records are all-gathered with NCCL before the acceptance either way. All of it is captured in the step's
     CUDA graph."""
 
-    def __init__(self, rank, world, group=None, fused=True, fused_quant=False):
+    def __init__(self, rank, world, group=None, fused=True, fused_quant=True):
         self.rank, self.world, self.group, self.fused = rank, world, group, fused
         # fused_quant: the all-reduce norm also writes the next GEMM's activation records
-        # (srhpm_add_rms_norm_allreduce_quant). Off by default: on two B200s the separate quantizer launch measured
-        # faster (7.34 vs 7.42 ms per 27B step at k = 8, same box).
+        # (srhpm_add_rms_norm_allreduce_quant). Measured on two B200s (27B step at k = 8, one process): 6.45 ms,
+        # against 6.61 ms with the norm and a separate quantizer kernel per GEMM and 6.64 ms with GEMMs that quantize
+        # in their own grid.
         self.fused_quant = fused_quant
         self.part = self.peers = self.epochs = None
 
@@ -257,12 +259,14 @@ class VerifyStep:
     residual stream, norms and embeddings are replicated."""
 
     def __init__(self, ctx, cfg, weights, kcache, vcache, n_tokens, n_past, relax=0.0, tp=None, fuse_prologue=True,
-                 fused_quant_o=True):
+                 gemm_fused_quant=True):
         self.ctx, self.cfg, self.w = ctx, cfg, weights
         self.fuse_prologue = fuse_prologue  # RMSNorm writes the next GEMM's activation records itself
-        # the attention output projection quantizes its activations in its own grid (srhpm_mul_mat_fused_quant: one
-        # launch; the attention before it leaves the SMs free, so the grid is resident early)
-        self.fused_quant_o = fused_quant_o
+        # GEMMs without a fused prologue (the attention output projection; under tensor parallelism the QKV and
+        # gate|up GEMMs after the all-reduce norm) quantize their activations in their own grid
+        # (srhpm_mul_mat_fused_quant: one launch; the small kernel before each leaves the SMs free, so the grid is
+        # resident early)
+        self.gemm_fused_quant = gemm_fused_quant
         self.kcache, self.vcache = kcache, vcache
         self.n, self.n_past, self.relax = n_tokens, n_past, relax
         self.tp = tp if tp is not None and tp.world > 1 else None
@@ -303,7 +307,9 @@ class VerifyStep:
     def _ptr(self, t):
         return ctypes.c_void_p(t.data_ptr())
 
-    def _mm(self, W, X, Y, fused_quant=False):
+    def _mm(self, W, X, Y, fused_quant=None):
+        if fused_quant is None:
+            fused_quant = self.gemm_fused_quant
         st, ws = self.ctx.mul_mat_work_size(W, X)
         L.check(st, "srhpm_mul_mat_work_size")
         self._ws = max(self._ws, ws)
@@ -329,7 +335,8 @@ class VerifyStep:
         """Residual add + RMSNorm of the pending delta, then the GEMM of W on the normed rows into Y: one fused
         norm + activation-quantization launch and the GEMM on its records (srhpm_add_rms_norm_quant, or with the
         tensor-parallel fused all-reduce and TensorParallel.fused_quant srhpm_add_rms_norm_allreduce_quant, +
-        srhpm_mul_mat_prequantized), or the separate norm and srhpm_mul_mat (its own quantizer) otherwise."""
+        srhpm_mul_mat_prequantized), or the separate norm and then the GEMM quantizing its own activations
+        (srhpm_mul_mat_fused_quant, or srhpm_mul_mat and its quantizer kernel without gemm_fused_quant)."""
         ar = delta_slot is not None and self._fused()
         if not self.fuse_prologue or W.qtype == L.Q8_0 or (ar and not self.tp.fused_quant):
             return [self._norm(delta_slot, wnorm), self._mm(W, self.y, Y)]
@@ -422,7 +429,7 @@ class VerifyStep:
                           [h, ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(mv), None,
                            ctypes.c_float(1.0 / math.sqrt(hd)), ctypes.c_float(0.0), ctypes.c_float(0.0),
                            ctypes.byref(ov)], True))
-            calls.append(self._mm(lay["o"], self.att, self._rowpar_out(0), self.fused_quant_o))
+            calls.append(self._mm(lay["o"], self.att, self._rowpar_out(0)))
             if self.tp is not None and not self._fused():
                 calls.append(self._all_reduce(self.o))  # row-parallel O: partial sums over the rank's heads
             if "gate_up" in lay:

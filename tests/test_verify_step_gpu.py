@@ -380,10 +380,11 @@ def test_fused_norm_quant_prologue_is_exact(ctx):
     dev_w = V.DeviceWeights.from_host(cfg, w)
     outs = []
     for fuse, fq_o in ((False, False), (True, False), (True, True)):
-        # fq_o: the attention output projection quantizes its activations in its own grid (one launch instead of 2)
+        # fq_o: GEMMs without a fused prologue (here the attention output projection) quantize their activations in
+        # their own grid (one launch instead of 2)
         kcd = [torch.from_numpy(a).cuda() for a in kc]
         vcd = [torch.from_numpy(a).cuda() for a in vc]
-        step = V.VerifyStep(ctx, cfg, dev_w, kcd, vcd, len(ids), n_past, fuse_prologue=fuse, fused_quant_o=fq_o)
+        step = V.VerifyStep(ctx, cfg, dev_w, kcd, vcd, len(ids), n_past, fuse_prologue=fuse, gemm_fused_quant=fq_o)
         step.set_tokens(ids, draft)
         ctx.launch_count(reset=True)
         step.run()
