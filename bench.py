@@ -10,12 +10,14 @@ value  = algorithmic bytes (weights + activations read + outputs written) / devi
          over ranks. With N GPUs every matrix is sharded by output rows (each rank computes rows/N rows, then
          an all-gather of Y over NCCL): strong scaling.
          The timed steps replay a CUDA graph of one step (1 GPU); --eager times the calls as issued.
-e2e    = the same products through the public API with host buffers: one H2D copy of the step's activations from
+e2e    = the same products through the public API with host buffers: H2D copies of the step's activations from
          pinned host memory, the 60 products, and D2H copies of every output into pinned host memory, all timed.
-         The outputs go back in 6 chunks on a second stream as their products finish (with several ranks, after
-         each chunk's all-gather); the step's calls and copies are captured once into a CUDA graph and replayed,
-         as a serving loop runs them. The same step issued call by call from the host is reported beside it
-         (measurements.e2e_calls_issued_eagerly_gbs). The line's e2e "copies" says which ran.
+         One GPU: the activations come over in one copy per (N, K) block on a second stream, each product waiting
+         for its block, and the outputs go back in 20 chunks on that stream as their products finish; several
+         ranks: one H2D, then 6 chunks, each read back after its all-gather. The step's calls and copies are
+         captured once into a CUDA graph and replayed, as a serving loop runs them. The same step issued call by
+         call from the host is reported beside it (measurements.e2e_calls_issued_eagerly_gbs). The line's e2e
+         "copies" says which ran.
 roofline: achieved = algorithmic bytes of the step / timed step time (the quantizer kernels count against the GEMM),
          against the measured HBM copy bandwidth; per-product times for the breakdown come from a second graph with
          CUDA events between the products, replayed after the timed region.
@@ -446,26 +448,40 @@ def run_gpu(args):
         step()
         y_host.copy_(y_dev, non_blocking=True)
 
-    # one GPU: the outputs go back in chunks of consecutive products on a second stream, each chunk once its products
-    # are done, so the reads overlap the products still running; a chunk's products wait for the previous step's read
-    # of their outputs (with several ranks the outputs arrive together with the step's all-gather: serial)
+    # one GPU: the activations come over on a second stream, one copy per (N, K) activation block, and each product
+    # waits only for its own block; the outputs go back in chunks of consecutive products on the same stream, each
+    # chunk once its products are done, so the copies overlap the products still running; a chunk's products wait for
+    # the previous step's read of their outputs (with several ranks the outputs arrive together with the step's
+    # all-gather: chunks of their own below)
     copy_s = torch.cuda.Stream(dev)
-    nchunk = max(1, min(6, len(runs)))
+    nchunk = max(1, min(20 if world == 1 else 6, len(runs)))
     cb = [len(runs) * c // nchunk for c in range(nchunk + 1)]
     ybound = yoff + [y_dev.numel()]
     ran = [torch.cuda.Event() for _ in range(nchunk)]     # a chunk's products are done
     copied = [torch.cuda.Event() for _ in range(nchunk)]  # a chunk's outputs are on the host
+    first_use = {}
+    for i, (N, t, rows, K) in enumerate(ops):
+        first_use.setdefault((N, K), i)
+    key_at = {i: key for key, i in first_use.items()}     # product index -> the activation block first used there
+    h2d_ev = {key: torch.cuda.Event() for key in first_use}
 
     # captured=True: the form recorded into a CUDA graph, which replays step after step: no wait on the previous
     # step's reads (the replays are serial), and the copy stream joins the step's stream at its end
     def e2e_step_pipelined(captured=False):
         cur = torch.cuda.current_stream()
-        x_dev.copy_(x_host, non_blocking=True)
+        copy_s.wait_stream(cur)  # the previous step's products are done with the activations
+        with torch.cuda.stream(copy_s):
+            for key in sorted(first_use, key=first_use.get):
+                lo, n_el = xoff[key], key[0] * key[1]
+                x_dev[lo:lo + n_el].copy_(x_host[lo:lo + n_el], non_blocking=True)
+                h2d_ev[key].record(copy_s)
         for c in range(nchunk):
             if not captured:
                 cur.wait_event(copied[c])
-            for run in runs[cb[c]:cb[c + 1]]:
-                run()
+            for i in range(cb[c], cb[c + 1]):
+                if i in key_at:
+                    cur.wait_event(h2d_ev[key_at[i]])
+                runs[i]()
             ran[c].record(cur)
             copy_s.wait_event(ran[c])
             lo, hi = ybound[cb[c]], ybound[cb[c + 1]]
@@ -557,9 +573,9 @@ def run_gpu(args):
         try:
             e2e_eager_ms = time_e2e(e2e_step_pipelined, copied[-1])
             e2e_ms = time_e2e_graph(e2e_step_pipelined)
-            e2e_mode = (f"the step's API calls and copies as one CUDA graph, replayed: H2D of the activations, the "
-                        f"products, the outputs read back in {nchunk} chunks on a second stream as their products "
-                        f"finish")
+            e2e_mode = (f"the step's API calls and copies as one CUDA graph, replayed: H2D of the activations in "
+                        f"{len(first_use)} blocks on a second stream, each product waiting for its own block, the "
+                        f"outputs read back in {nchunk} chunks on that stream as their products finish")
         except Exception as e:  # measured the serial way instead, and said so
             torch.cuda.synchronize()
             e2e_ms = time_e2e(e2e_step_serial)

@@ -173,14 +173,14 @@ int    srhpm_flash_attn_ext_partial(srhpm_ctx * ctx, const srhpm_tensor * q, con
 int    srhpm_flash_attn_merge(srhpm_ctx * ctx, const void * parts, int n_parts, const srhpm_tensor * sinks,
                               srhpm_tensor * dst, void * stream);
 /* The same merge without a collective: every rank's record set sits at the start of its own buffer of
- * srhpm_flash_attn_peer_buffer_size(H, N) bytes, mapped on every rank (peer_buffers[j] = rank j's buffer as this rank
- * addresses it: symmetric memory), written there by srhpm_flash_attn_ext_partial. Per row, the call meets the other
- * ranks' calls at a flag barrier in those buffers (bounded: 2 s, then an error status), reads every rank's record
- * over NVLink in rank order, adds the sinks, writes dst as srhpm_flash_attn_merge does (the same arithmetic, so the
- * same result), and meets them at a second barrier once it has read them, so that no rank's next partial call
- * overwrites records a peer still reads. epochs: u32 [H * N] on this device, zero at the start, counted per call
- * identically on every rank. Every rank must make the same calls in the same order; world <= 8. No counterpart in
- * the reference (one device). */
+ * srhpm_flash_attn_peer_buffer_size(H, N) bytes, zeroed once and mapped on every rank (peer_buffers[j] = rank j's
+ * buffer as this rank addresses it: symmetric memory), written there by srhpm_flash_attn_ext_partial. Per row, the
+ * call sends its record row to every rank's buffer as 8-byte (value, epoch) words, waits (bounded: 2 s, then an error
+ * status) until every rank's words in its own buffer carry the epoch, merges them in rank order, adds the sinks and
+ * writes dst as srhpm_flash_attn_merge does (the same arithmetic, so the same result). epochs: u32 [H * N] on this
+ * device, zero at the start, counted per call identically on every rank; two receive slots alternate, so a rank's
+ * next call never overwrites words a peer still reads. Every rank must make the same calls in the same order;
+ * world <= 8. No counterpart in the reference (one device). */
 size_t srhpm_flash_attn_peer_buffer_size(int64_t n_head, int64_t n_tokens);
 int    srhpm_flash_attn_merge_peers(srhpm_ctx * ctx, const uint64_t * peer_buffers, int world, int rank,
                                     uint32_t * epochs, const srhpm_tensor * sinks, srhpm_tensor * dst, void * stream);

@@ -1,6 +1,5 @@
-// The peer-memory exchanges across the GPUs of one box: the all-reduce of the tensor-parallel decoder step (inside the
-// next RMSNorm: add_rms_norm_ar_kernel in decoder_ops.cu, add_rms_norm_q8K_kernel in srv_gemm.cu) and the flag barrier
-// of the attention's record merge over peer memory (fa_merge_peers_kernel in fa_decode.cu).
+// The peer-memory exchange across the GPUs of one box: the all-reduce of the tensor-parallel decoder step (inside the
+// next RMSNorm: add_rms_norm_ar_kernel in decoder_ops.cu, add_rms_norm_q8K_kernel in srv_gemm.cu).
 //
 // All-reduce (flag-in-word exchange). Every rank's row-parallel GEMM (attention output, FFN down) writes its partial
 // sums into slot `slot` of its own symmetric buffer (mapped on every peer): [2 slots][kArRows rows][d] f32, followed by
@@ -14,11 +13,7 @@
 // after its next exchange on the other slot, which needs this rank's words of that exchange, sent after it had read
 // the slot: two slots suffice.
 //
-// Attention record merge (flag barrier). For row i, one thread bumps this rank's epoch of the row, publishes it into
-// every peer's flag (row, rank), and waits until every peer's flag in its own buffer has reached it (bounded: 2 s,
-// then an error status); the records are then read from the peers' buffers. Ordering (PTX memory model, system
-// scope): one fence.acq_rel.sys before the relaxed flag stores (a release of the records written by the previous
-// kernel of each rank, complete at griddepcontrol.wait) and one after the polls (an acquire before the peer loads).
+// The attention's record merge over peer memory (fa_merge_peers_kernel) exchanges its records the same way.
 #pragma once
 #include <cstdint>
 
@@ -30,48 +25,8 @@ namespace srhpm {
 constexpr int kArMaxRanks = 8;
 constexpr int kArRows     = 16;
 
-__device__ __forceinline__ uint64_t global_timer_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-__device__ __forceinline__ void st_relaxed_sys(uint32_t * p, uint32_t v) {
-    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t * p) {
-    uint32_t v;
-    asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
 // bytes of one slot's partial rows
 __host__ __device__ inline size_t ar_part_bytes(int64_t d) { return (size_t) kArRows * d * sizeof(float); }
-
-// One flag round of `row` (one thread calls it): publish epoch e into flag [row][rank] of every rank's buffer (flags
-// [rows][kArMaxRanks] u32 at byte offset flag_off), then wait until every rank's flag [row][j] in this rank's buffer
-// has reached e. Release before the stores, acquire after the polls (see above). Returns false (and sets the status
-// word) when a peer's flag did not arrive within 2 s.
-__device__ inline bool peer_row_barrier(const uint64_t * peers, int world, int rank, size_t flag_off, int row,
-                                        uint32_t e, int32_t * status) {
-    const size_t fo = flag_off + ((size_t) row * kArMaxRanks + rank) * sizeof(uint32_t);
-    fence_acq_rel_sys();  // release: this rank's data before its flags
-    for (int j = 0; j < world; j++) st_relaxed_sys(reinterpret_cast<uint32_t *>(peers[j] + fo), e);
-    const uint32_t * mine = reinterpret_cast<const uint32_t *>(peers[rank] + flag_off) + (size_t) row * kArMaxRanks;
-    const uint64_t   t0   = global_timer_ns();
-    bool             ok   = true;
-    for (int j = 0; j < world && ok; j++) {
-        while ((int32_t) (ld_relaxed_sys(mine + j) - e) < 0) {
-            if (global_timer_ns() - t0 > 2000000000ull) {
-                ok = false;
-                atomicExch(status, kErrPeerWait);
-                break;
-            }
-            __nanosleep(64);
-        }
-    }
-    fence_acq_rel_sys();  // acquire: every peer's data after its flag
-    return ok;
-}
 
 // ---- all-reduce by flag-in-word exchange ------------------------------------------------------------------------
 
@@ -127,7 +82,7 @@ __device__ __forceinline__ void ar_gather4(float4 & a, const uint64_t * peers, i
                 (uint32_t) (w[3] >> 32) == e) {
                 break;
             }
-            if (!ok || global_timer_ns() - t0 > 2000000000ull) {
+            if (!ok || globaltimer_ns() - t0 > 2000000000ull) {
                 if (ok) atomicExch(status, kErrPeerWait);
                 ok = false;
                 w[0] = w[1] = w[2] = w[3] = 0;

@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(kNormThreads) add_rms_norm_ar_kernel(float * x
     float          ss = 0.0f;
     float4         v[4];
     bool           ok = true;
-    const uint64_t t0 = global_timer_ns();
+    const uint64_t t0 = globaltimer_ns();
 #pragma unroll
     for (int k = 0; k < 4; k++) {
         const int64_t j = threadIdx.x + (int64_t) k * kNormThreads;

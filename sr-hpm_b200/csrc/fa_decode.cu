@@ -1445,49 +1445,97 @@ size_t fa_part_bytes(int64_t H, int64_t N) { return fa_part_ms_bytes(H, N) + (si
 
 // ---- the record merge over peer memory ---------------------------------------------------------------------------
 // Every rank's buffer (mapped on every rank) holds its record set (fa_part_bytes(H, N), written by
-// srhpm_flash_attn_ext_partial), then two flag arrays [H * N][kArMaxRanks] u32: "ready" and "done". CTA = row
-// r = h * N + t. A flag round on "ready" (allreduce.cuh) says every rank's merge kernel has passed griddepcontrol.wait,
-// so every rank's record set is complete; the row is merged over the ranks in rank order with fa_combine_kernel's
-// arithmetic (read from the peers' buffers with uncached loads), sinks added, normalized into dst; a flag round on
-// "done" says every rank has read this row, so no rank's next partial call can overwrite records a peer still reads.
+// srhpm_flash_attn_ext_partial), then a receive area [2 slots][kArMaxRanks source ranks][H * N rows][258] of 8-byte
+// words (value bits low, epoch high): the row's 256 unnormalized outputs, then its max and sum. CTA = row
+// r = h * N + t. The CTA stores its record row, with the row's epoch, into every rank's receive area (source = this
+// rank), then reads its own until each word from each rank carries the epoch (the flag-in-word exchange of
+// allreduce.cuh: an aligned 64-bit store is single-copy atomic, so no fence or flag round is needed), merges the rows
+// in rank order with fa_combine_kernel's arithmetic, adds the sinks and normalizes into dst. Slot = epoch parity: a
+// rank sends its next-but-one exchange of a row only after this rank's words of the next one reached it, which this
+// rank sends after reading the slot, so two slots suffice.
+constexpr int kRecWords = kD + 2;
+
+__host__ __device__ inline size_t fa_recv_word(size_t set, int rows, int slot, int src, int row) {
+    return (set + 15) / 16 * 16 + ((((size_t) slot * kArMaxRanks + src) * rows + row) * kRecWords) * sizeof(uint64_t);
+}
+
+__device__ __forceinline__ uint64_t rec_word(float v, uint32_t e) {
+    return (uint64_t) __float_as_uint(v) | ((uint64_t) e << 32);
+}
+__device__ __forceinline__ void st_relaxed_sys_b64(void * p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_b64(const void * p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// the word's value once it carries epoch e (bounded: 2 s from t0, then the status word is set, ok cleared, 0)
+__device__ __forceinline__ float wait_word(const uint8_t * p, uint32_t e, uint64_t t0, bool & ok, int32_t * status) {
+    for (;;) {
+        const uint64_t w = ld_relaxed_sys_b64(p);
+        if ((uint32_t) (w >> 32) == e) return __uint_as_float((uint32_t) w);
+        if (!ok || globaltimer_ns() - t0 > 2000000000ull) {
+            if (ok) atomicExch(status, kErrPeerWait);
+            ok = false;
+            return 0.0f;
+        }
+        __nanosleep(32);
+    }
+}
+
 __global__ void __launch_bounds__(256) fa_merge_peers_kernel(const uint64_t * peers, int world, int rank,
                                                              uint32_t * epochs, int N, int H, size_t ms_bytes,
                                                              size_t set, const float * sinks, float * dst,
                                                              int64_t dnb1, int64_t dnb2, int32_t * status) {
     pdl_launch_dependents();
     pdl_wait();  // this rank's partial records are complete
-    const int    row = blockIdx.x, h = row / N, tq = row % N, rows = H * N;
-    const size_t ready_off = set, done_off = set + (size_t) rows * kArMaxRanks * sizeof(uint32_t);
-    __shared__ int      ok_s;
+    const int row = blockIdx.x, h = row / N, tq = row % N, rows = H * N, dv = threadIdx.x;
     __shared__ uint32_t e_s;
+    __shared__ int      ok_s;
     __shared__ float    w_s[kArMaxRanks], s_s[kArMaxRanks];
     __shared__ float    mf_s;
-    if (threadIdx.x == 0) {
-        const uint32_t e = ++epochs[row];
-        e_s              = e;
-        ok_s             = peer_row_barrier(peers, world, rank, ready_off, row, e, status);
-        if (ok_s) {
-            float m = -INFINITY;
-            for (int r = 0; r < world; r++) {
-                const float2 v = __ldcv(reinterpret_cast<const float2 *>(peers[r]) + row);
-                w_s[r]         = v.x;
-                s_s[r]         = v.y;
-                if (v.y != 0.0f) m = fmaxf(m, v.x);
+    if (dv == 0) e_s = ++epochs[row];
+    __syncthreads();
+    const uint32_t e = e_s;
+    const int      slot = (int) (e & 1u);
+    {  // send this rank's record row to every rank
+        const float2 ms = reinterpret_cast<const float2 *>(peers[rank])[row];
+        const float  v  = reinterpret_cast<const float *>(peers[rank] + ms_bytes)[(int64_t) row * kD + dv];
+        for (int r = 0; r < world; r++) {
+            uint8_t * q = reinterpret_cast<uint8_t *>(peers[r] + fa_recv_word(set, rows, slot, rank, row));
+            st_relaxed_sys_b64(q + (size_t) dv * sizeof(uint64_t), rec_word(v, e));
+            if (dv == 0) {
+                st_relaxed_sys_b64(q + (size_t) kD * sizeof(uint64_t), rec_word(ms.x, e));
+                st_relaxed_sys_b64(q + (size_t) (kD + 1) * sizeof(uint64_t), rec_word(ms.y, e));
             }
-            mf_s = m;
-            for (int r = 0; r < world; r++) w_s[r] = s_s[r] != 0.0f ? exp2f(w_s[r] - m) : 0.0f;
         }
     }
+    const uint8_t * mine = reinterpret_cast<const uint8_t *>(peers[rank]);
+    const uint64_t  t0   = globaltimer_ns();
+    bool            ok   = true;
+    if (dv == 0) {  // the ranks' (max, sum) pairs, their weights 2^(M_r - M)
+        float m = -INFINITY;
+        for (int r = 0; r < world; r++) {
+            const uint8_t * q = mine + fa_recv_word(set, rows, slot, r, row);
+            w_s[r]            = wait_word(q + (size_t) kD * sizeof(uint64_t), e, t0, ok, status);
+            s_s[r]            = wait_word(q + (size_t) (kD + 1) * sizeof(uint64_t), e, t0, ok, status);
+            if (s_s[r] != 0.0f) m = fmaxf(m, w_s[r]);
+        }
+        mf_s = m;
+        for (int r = 0; r < world; r++) w_s[r] = s_s[r] != 0.0f ? exp2f(w_s[r] - m) : 0.0f;
+        ok_s = ok;
+    }
     __syncthreads();
-    const int dv  = threadIdx.x;
-    float     acc = 0.0f, S = 0.0f;
+    float acc = 0.0f, S = 0.0f;
     if (ok_s) {
         const float Mf = mf_s;
         for (int r = 0; r < world; r++) {
             const float w = w_s[r];
-            const float v = __ldcv(reinterpret_cast<const float *>(peers[r] + ms_bytes) + (int64_t) row * kD + dv);
-            acc           = fmaf(w, w != 0.0f ? v : 0.0f, acc);
-            S             = fmaf(w, s_s[r], S);
+            const float v = wait_word(mine + fa_recv_word(set, rows, slot, r, row) + (size_t) dv * sizeof(uint64_t),
+                                      e, t0, ok, status);
+            acc = fmaf(w, w != 0.0f ? v : 0.0f, acc);
+            S   = fmaf(w, s_s[r], S);
         }
         if (sinks) {
             const float sk2 = sinks[h] * kLog2e;
@@ -1503,12 +1551,11 @@ __global__ void __launch_bounds__(256) fa_merge_peers_kernel(const uint64_t * pe
     const float inv = S == 0.0f ? 0.0f : 1.0f / S;
     float * out = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(dst) + h * dnb1 + tq * dnb2);
     out[dv]     = acc * inv;
-    __syncthreads();  // every thread has read the peers' row
-    if (threadIdx.x == 0 && ok_s) peer_row_barrier(peers, world, rank, done_off, row, e_s, status);
 }
 
 size_t fa_peer_buffer_bytes(int64_t H, int64_t N) {
-    return fa_part_bytes(H, N) + 2 * (size_t) (H * N) * kArMaxRanks * sizeof(uint32_t);
+    const size_t set = fa_part_bytes(H, N);
+    return (set + 15) / 16 * 16 + 2 * (size_t) kArMaxRanks * (size_t) (H * N) * kRecWords * sizeof(uint64_t);
 }
 
 int fa_merge_peers_run(srhpm_ctx * ctx, const uint64_t * peers, int world, int rank, uint32_t * epochs, int N, int H,

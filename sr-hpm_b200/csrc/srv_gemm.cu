@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(kNormQThreads) add_rms_norm_q8K_kernel(float *
                 const int64_t j = threadIdx.x + (int64_t) k * kNormQThreads;
                 if (j < d4) ar_push4(ar.peers, ar.world, ar.rank, ar.slot, t, d, j, e);
             }
-            t0 = global_timer_ns();
+            t0 = globaltimer_ns();
         }
 #pragma unroll
         for (int k = 0; k < 4; k++) {

@@ -5,7 +5,7 @@ range, the ranks' record sets are all-gathered in rank (= KV) order with one NCC
 with srhpm_flash_attn_merge into the same output flash_attn_ext gives over the whole range. This is the reference's
 chunked attention (KV chunks over CPU threads, records merged per row: patch/srhpm.patch:555-579, 779-823) with the
 devices as the chunks. Each rank reads 1/world of the cache; the exchange is H * N * 1032 bytes per rank, through
-one NCCL all-gather or read by every rank straight from the others' symmetric-memory buffers over NVLink.
+sent by every rank straight into the others' symmetric-memory buffers over NVLink, or one NCCL all-gather.
 """
 import torch
 import torch.distributed as dist
@@ -21,11 +21,12 @@ class SplitKAttention:
     rank, in the same buffer at every call (copy it to keep it past the next call). Buffers are allocated once, so
     the call can be captured in a CUDA graph. Every rank of the group must make the same calls in the same order.
 
-    exchange="nccl": the record sets are all-gathered with NCCL and merged (srhpm_flash_attn_merge).
-    exchange="peers": each rank's record set stays in its own symmetric-memory buffer and every rank merges them
-    over NVLink after a flag barrier (srhpm_flash_attn_merge_peers): no collective launch; same result."""
+    exchange="peers" (default): each rank's record set stays in its own symmetric-memory buffer; the merge kernel
+    sends every rank its record rows as (value, epoch) words over NVLink and merges what it receives
+    (srhpm_flash_attn_merge_peers): no collective launch. exchange="nccl": the record sets are all-gathered with NCCL
+    and merged (srhpm_flash_attn_merge). Same result either way."""
 
-    def __init__(self, ctx, rank, world, H, N, device, group=None, exchange="nccl"):
+    def __init__(self, ctx, rank, world, H, N, device, group=None, exchange="peers"):
         self.ctx, self.rank, self.world, self.H, self.N, self.group = ctx, rank, world, H, N, group
         self.exchange = exchange
         self.part_bytes = ctx.flash_attn_part_size(H, N)

@@ -144,7 +144,7 @@ def _nccl_worker(rank, world, port, q, k, v, mask, sinks, outdir, resq):
         for exchange in ("nccl", "peers"):
             att = SplitKAttention(ctx, rank, world, H, N, torch.device("cuda", rank), exchange=exchange)
             t0, t1 = att.range(k.shape[1])
-            for _ in range(3):  # repeated calls reuse the buffers (the peer flags count the calls)
+            for _ in range(3):  # repeated calls reuse the buffers (the epochs count the calls, the slots alternate)
                 out = att(dev(q), dev(k[:, t0:t1]), dev(v[:, t0:t1]), L.Q8_0, mask=dev(mask[:, t0:t1]),
                           sinks=dev(sinks), scale=1 / 16)
             torch.cuda.synchronize()
@@ -163,7 +163,7 @@ def _nccl_worker(rank, world, port, q, k, v, mask, sinks, outdir, resq):
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_split_over_two_gpus_nccl(ctx, tmp_path):
     """SplitKAttention over 2 GPUs: each rank holds half the cache's tokens; the record sets are all-gathered with
-    NCCL, or read from the peers' symmetric-memory buffers after a flag barrier, and merged on both ranks. Both ranks
+    NCCL, or exchanged through the ranks' symmetric-memory buffers as (value, epoch) words, and merged on both ranks. Both ranks
     and both exchanges must agree bit for bit and match the oracle over the whole range."""
     import socket
     import torch.multiprocessing as mp
@@ -203,7 +203,7 @@ def test_split_over_two_gpus_nccl(ctx, tmp_path):
 
 def test_merge_peers_single_rank_equals_merge(ctx):
     """srhpm_flash_attn_merge_peers with one rank (its own buffer as the only peer) equals srhpm_flash_attn_merge of
-    that record set bit for bit, over repeated calls (the flag epochs advance each call)."""
+    that record set bit for bit, over repeated calls (the epochs advance each call and the receive slots alternate)."""
     rng = np.random.default_rng(13)
     H, Hkv, N, L_ = 6, 2, 3, 640
     q, k, v, mask = make(rng, L.Q8_0, H, Hkv, N, L_)
@@ -220,4 +220,6 @@ def test_merge_peers_single_rank_equals_merge(ctx):
         ctx.check()
         assert np.array_equal(got, want)
     assert epochs.cpu().tolist() == [3] * (H * N)
-    assert ctx.flash_attn_peer_buffer_size(H, N) == ctx.flash_attn_part_size(H, N) + 2 * H * N * 8 * 4
+    # the record set (16-byte padded), then 2 slots x 8 source ranks x H * N rows x 258 words of 8 bytes
+    set16 = (ctx.flash_attn_part_size(H, N) + 15) // 16 * 16
+    assert ctx.flash_attn_peer_buffer_size(H, N) == set16 + 2 * 8 * H * N * 258 * 8
