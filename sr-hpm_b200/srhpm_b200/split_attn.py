@@ -1,11 +1,11 @@
 """Multi-query attention split over the KV range across the GPUs of one box (one process per GPU).
 
 Rank j holds KV tokens shard.kv_range(L, world, j) of every KV head. It runs srhpm_flash_attn_ext_partial over its
-range, the ranks' record sets are all-gathered in rank (= KV) order with one NCCL call, and every rank merges them
-with srhpm_flash_attn_merge into the same output flash_attn_ext gives over the whole range. This is the reference's
-chunked attention (KV chunks over CPU threads, records merged per row: patch/srhpm.patch:555-579, 779-823) with the
-devices as the chunks. Each rank reads 1/world of the cache; the exchange is H * N * 1032 bytes per rank, through
-sent by every rank straight into the others' symmetric-memory buffers over NVLink, or one NCCL all-gather.
+range, the ranks' record sets are exchanged, and every rank merges them in rank (= KV) order into the same output
+flash_attn_ext gives over the whole range. This is the reference's chunked attention (KV chunks over CPU threads,
+records merged per row: patch/srhpm.patch:555-579, 779-823) with the devices as the chunks. Each rank reads 1/world
+of the cache; the exchange is H * N * 1032 bytes per rank, sent by every rank straight into the others'
+symmetric-memory buffers over NVLink, or through one NCCL all-gather.
 """
 import torch
 import torch.distributed as dist
