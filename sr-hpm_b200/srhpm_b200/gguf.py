@@ -176,20 +176,19 @@ def k_columns(blocks, ggml_type, k0, k1):
     return _kc(blocks, blk, bpb, k0, k1)
 
 
-def load_decoder(gf, cfg, device="cuda", rank=0, world=1):
-    """DeviceWeights of the decoder in `gf` (a GGUFFile), the slices of tensor-parallel rank `rank` of `world`.
+def load_decoder(gf, cfg, device="cuda", rank=0, world=1, split_kv=True):
+    """DeviceWeights of the decoder in `gf` (a GGUFFile), the slices of tensor-parallel rank `rank` of `world` (split_kv:
+    as DeviceWeights.from_host).
     Matrices stay in their GGUF block layout; Q, K, V rows become one QKV matrix and gate, up one gate|up matrix
     (per rank: this rank's heads / FFN rows) when their types agree, else they stay separate GEMMs. Token embeddings
     must be F16 or F32 (srhpm_get_rows); norms F32."""
     from .ops import QuantTensor
     from .verify_step import DeviceWeights
-    from .shard import tp_layout
-    lay_tp = tp_layout(cfg.H, cfg.Hkv, cfg.n_ff, cfg.n_vocab, world, rank)
     hd = cfg.hd
+    w = DeviceWeights(cfg, device)
+    lay_tp = w._set_tp(rank, world, split_kv)
     h0, h1, g0, g1 = lay_tp["h0"], lay_tp["h1"], lay_tp["g0"], lay_tp["g1"]
     f0, f1, v0, v1 = lay_tp["f0"], lay_tp["f1"], lay_tp["v0"], lay_tp["v1"]
-    w = DeviceWeights(cfg, device)
-    w.tp = dict(lay_tp, rank=rank, world=world)
 
     def qt(blocks, ggml_type, rows, K):
         return QuantTensor.from_blocks(blocks, ggml_type, rows, K, device)
@@ -204,13 +203,14 @@ def load_decoder(gf, cfg, device="cuda", rank=0, world=1):
         p = f"blk.{l}."
         lay = {}
         tq, tk, tv = (gf.tensors[p + f"attn_{x}.weight"] for x in "qkv")
-        q = gf.data(p + "attn_q.weight")[h0 * hd:h1 * hd]
+        qa, qb = w.q_heads(l)
+        q = gf.data(p + "attn_q.weight")[qa * hd:qb * hd]
         k = gf.data(p + "attn_k.weight")[g0 * hd:g1 * hd]
         v = gf.data(p + "attn_v.weight")[g0 * hd:g1 * hd]
         if tq.type == tk.type == tv.type:
-            lay["qkv"] = qt(np.concatenate([q, k, v]), tq.type, (h1 - h0 + 2 * (g1 - g0)) * hd, cfg.d)
+            lay["qkv"] = qt(np.concatenate([q, k, v]), tq.type, (qb - qa + 2 * (g1 - g0)) * hd, cfg.d)
         else:
-            lay["q"] = qt(q, tq.type, (h1 - h0) * hd, cfg.d)
+            lay["q"] = qt(q, tq.type, (qb - qa) * hd, cfg.d)
             lay["k"] = qt(k, tk.type, (g1 - g0) * hd, cfg.d)
             lay["v"] = qt(v, tv.type, (g1 - g0) * hd, cfg.d)
         to = gf.tensors[p + "attn_output.weight"]

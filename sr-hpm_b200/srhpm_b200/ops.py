@@ -319,13 +319,13 @@ class Context:
         return out
 
     def flash_attn_peer_buffer_size(self, H, N):
-        """Bytes of one rank's buffer for flash_attn_merge_peers: the record set, then its two flag arrays."""
+        """Bytes of one rank's buffer for flash_attn_merge_peers: the record set, then its receive area."""
         return int(self.lib.srhpm_flash_attn_peer_buffer_size(H, N))
 
     def flash_attn_merge_peers(self, peers, world, rank, epochs, H, N, sinks=None, out=None, stream=None):
         """srhpm_flash_attn_merge_peers: every rank's record set at the start of its own peer buffer (peers: int64
-        device tensor of the world buffers' addresses on this device), merged in rank order after a flag barrier;
-        epochs: int32 [H * N] device counters, zero at the start. Returns out f32 [N, H, 256]."""
+        device tensor of the world buffers' addresses on this device), exchanged as (value, epoch) words and merged in
+        rank order; epochs: int32 [H * N] device counters, zero at the start. Returns out f32 [N, H, 256]."""
         if out is None:
             out = torch.empty((N, H, 256), dtype=torch.float32, device=peers.device)
         ov = _tensor_view(out, L.F32, [out.shape[2], out.shape[1], out.shape[0]],

@@ -81,7 +81,17 @@ def tp_layout(H, Hkv, n_ff, n_vocab, world, rank):
         raise ValueError("a rank's query heads must share its KV heads")
     f0, f1 = k_range(n_ff, world, rank)
     v0, v1 = vocab_range(n_vocab, world, rank)
-    return dict(h0=h0, h1=h1, g0=g0, g1=g1, f0=f0, f1=f1, v0=v0, v1=v1)
+    # KV replicas: r ranks share each KV head (1 when the KV heads split); p is this rank's place among them and
+    # [gh0, gh1) the query heads of its KV heads (all r ranks' heads)
+    r = world // Hkv if world > Hkv else 1
+    return dict(h0=h0, h1=h1, g0=g0, g1=g1, f0=f0, f1=f1, v0=v0, v1=v1, r=r, p=rank % r, gh0=g0 * G, gh1=g1 * G)
+
+
+def q_heads(lay, split):
+    """The query heads [a, b) whose rows of the QKV matrix a rank holds in one layer: its own heads, or, on a layer whose
+    attention the KV head's replicas split over the KV range (`split`: lay["r"] > 1), every query head of its KV head
+    (each replica computes all of them over its part of the tokens)."""
+    return (lay["gh0"], lay["gh1"]) if split and lay["r"] > 1 else (lay["h0"], lay["h1"])
 
 
 class PackedSlices:

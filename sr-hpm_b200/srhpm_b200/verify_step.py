@@ -27,6 +27,10 @@ class DecoderConfig:
         self.types = types or {"qkv": L.Q4_K, "o": L.Q4_K, "gate": L.Q3_K, "up": L.Q3_K, "down": L.Q4_K,
                                "head": L.Q6_K}
 
+    def full_layer(self, li):
+        """Layer li attends to the whole cache (else to the last `window` positions)."""
+        return self.window <= 0 or li % self.full_every == self.full_every - 1
+
     def as_dict(self):
         return dict(n_layer=self.n_layer, d=self.d, n_ff=self.n_ff, H=self.H, Hkv=self.Hkv, hd=self.hd,
                     n_vocab=self.n_vocab, base=self.base, eps=self.eps, window=self.window,
@@ -87,20 +91,30 @@ class DeviceWeights:
         self.out_norm = self.head = self.emb = None
         self.tp = None
 
-    def _set_tp(self, rank, world):
+    def _set_tp(self, rank, world, split_kv=True):
         from .shard import tp_layout
         self.tp = dict(tp_layout(self.cfg.H, self.cfg.Hkv, self.cfg.n_ff, self.cfg.n_vocab, world, rank), rank=rank,
                        world=world)
+        # split_kv: on full-attention layers the r ranks that share a KV head split its tokens (each attends to its
+        # part for every query head of the KV head, the records merge over the r ranks), so their QKV slices hold
+        # every query head of the KV head there
+        self.tp["split_kv"] = bool(split_kv and self.tp["r"] > 1)
         return self.tp
 
+    def q_heads(self, li):
+        """The query heads [a, b) of layer li's QKV rows on this rank (shard.q_heads)."""
+        from .shard import q_heads
+        return q_heads(self.tp, self.tp["split_kv"] and self.cfg.full_layer(li))
+
     @classmethod
-    def from_host(cls, cfg, w, device="cuda", rank=0, world=1):
+    def from_host(cls, cfg, w, device="cuda", rank=0, world=1, split_kv=True):
         """From host_weights (packed blocks of the whole model); rank / world cut one tensor-parallel rank's slices:
-        QKV rows of its query and KV heads, O columns of its heads, gate / up rows and down columns of its FFN rows,
-        head rows of its vocabulary range."""
+        QKV rows of its query and KV heads (with split_kv and replicated KV heads, every query head of its KV head on
+        full-attention layers), O columns of its heads, gate / up rows and down columns of its FFN rows, head rows of
+        its vocabulary range."""
         from .shard import k_columns
         self = cls(cfg, device)
-        tp = self._set_tp(rank, world)
+        tp = self._set_tp(rank, world, split_kv)
         hd, H, Hkv = cfg.hd, cfg.H, cfg.Hkv
         h0, h1, g0, g1, f0, f1 = tp["h0"], tp["h1"], tp["g0"], tp["g1"], tp["f0"], tp["f1"]
         t = cfg.types
@@ -110,10 +124,11 @@ class DeviceWeights:
 
         for l in range(cfg.n_layer):
             lay = {}
+            qa, qb = self.q_heads(l)
             qkv = np.asarray(w["qkv"][l]).reshape((H + 2 * Hkv) * hd, -1)
-            part = np.concatenate([qkv[h0 * hd:h1 * hd], qkv[(H + g0) * hd:(H + g1) * hd],
+            part = np.concatenate([qkv[qa * hd:qb * hd], qkv[(H + g0) * hd:(H + g1) * hd],
                                    qkv[(H + Hkv + g0) * hd:(H + Hkv + g1) * hd]])
-            lay["qkv"] = QuantTensor.from_blocks(part, t["qkv"], (h1 - h0 + 2 * (g1 - g0)) * hd, cfg.d, device)
+            lay["qkv"] = QuantTensor.from_blocks(part, t["qkv"], (qb - qa + 2 * (g1 - g0)) * hd, cfg.d, device)
             o = np.asarray(w["o"][l]).reshape(cfg.d, -1)
             lay["o"] = QuantTensor.from_blocks(kcols(o, t["o"], h0 * hd, h1 * hd), t["o"], cfg.d, (h1 - h0) * hd, device)
             # gate and up as one matrix (gate rows, then up rows): one GEMM launch, SwiGLU reads the halves
@@ -132,16 +147,17 @@ class DeviceWeights:
         return self
 
     @classmethod
-    def random(cls, cfg, device="cuda", seed=0, rank=0, world=1):
+    def random(cls, cfg, device="cuda", seed=0, rank=0, world=1, split_kv=True):
         """Random GGUF blocks of one tensor-parallel rank's slice shapes (the whole model when world = 1)."""
         self = cls(cfg, device)
-        tp = self._set_tp(rank, world)
+        tp = self._set_tp(rank, world, split_kv)
         gen = torch.Generator(device=device)
         gen.manual_seed(seed + 1000 * rank)
         hd, t = cfg.hd, cfg.types
         nh, ng, nf = tp["h1"] - tp["h0"], tp["g1"] - tp["g0"], tp["f1"] - tp["f0"]
-        for _ in range(cfg.n_layer):
-            lay = {"qkv": random_blocks_device(t["qkv"], (nh + 2 * ng) * hd, cfg.d, gen, device),
+        for l in range(cfg.n_layer):
+            qa, qb = self.q_heads(l)
+            lay = {"qkv": random_blocks_device(t["qkv"], (qb - qa + 2 * ng) * hd, cfg.d, gen, device),
                    "o": random_blocks_device(t["o"], cfg.d, nh * hd, gen, device),
                    "gate_up": random_blocks_device(t["gate"], 2 * nf, cfg.d, gen, device),
                    "down": random_blocks_device(t["down"], cfg.d, nf, gen, device)}
@@ -154,14 +170,14 @@ class DeviceWeights:
         return self
 
     @classmethod
-    def slice_of(cls, full, rank, world):
+    def slice_of(cls, full, rank, world, split_kv=True):
         """One tensor-parallel rank's slices cut on the device from the whole model `full` (world = 1 weights, fused
         qkv and gate|up): the same cuts as from_host (QKV rows of the rank's query and KV heads, O columns of its
         heads, gate / up rows and down columns of its FFN rows, head rows of its vocabulary range). Norms and
         embeddings are shared with `full`."""
         cfg = full.cfg
         self = cls(cfg, full.device)
-        tp = self._set_tp(rank, world)
+        tp = self._set_tp(rank, world, split_kv)
         hd, H, Hkv = cfg.hd, cfg.H, cfg.Hkv
         h0, h1, g0, g1, f0, f1 = tp["h0"], tp["h1"], tp["g0"], tp["g1"], tp["f0"], tp["f1"]
 
@@ -173,10 +189,11 @@ class DeviceWeights:
             part = rows2d(qt)[:, k0 // b * bs:k1 // b * bs].contiguous()
             return QuantTensor(part.view(-1), qt.qtype, qt.rows, k1 - k0)
 
-        for lay_f in full.layers:
+        for l, lay_f in enumerate(full.layers):
             lay = {}
+            qa, qb = self.q_heads(l)
             q = rows2d(lay_f["qkv"])
-            part = torch.cat([q[h0 * hd:h1 * hd], q[(H + g0) * hd:(H + g1) * hd],
+            part = torch.cat([q[qa * hd:qb * hd], q[(H + g0) * hd:(H + g1) * hd],
                               q[(H + Hkv + g0) * hd:(H + Hkv + g1) * hd]])
             lay["qkv"] = QuantTensor(part.reshape(-1), lay_f["qkv"].qtype, part.shape[0], cfg.d)
             lay["o"] = kcols(lay_f["o"], h0 * hd, h1 * hd)
@@ -232,6 +249,28 @@ class TensorParallel:
         torch.cuda.synchronize(device)
         dist.barrier(group=self.group)
 
+    def setup_attention(self, H, N, r, device):
+        """Symmetric buffers for the attention split over the r replicas of a KV head (collective: every rank calls
+        it): each rank's record set of H heads and N tokens, exchanged with its replicas by
+        srhpm_flash_attn_merge_peers; att_peers holds the r replicas' buffers (this rank at rank % r)."""
+        if getattr(self, "att_key", None) == (H, N, r):
+            return
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+        lib = L.load()
+        buf = symm.empty(int(lib.srhpm_flash_attn_peer_buffer_size(H, N)), dtype=torch.uint8, device=device)
+        buf.zero_()
+        hdl = symm.rendezvous(buf, self.group if self.group is not None else dist.group.WORLD)
+        base = self.rank // r * r
+        self._att_buf, self._att_hdl = buf, hdl
+        self.att_peers = torch.tensor([int(p) for p in hdl.buffer_ptrs[base:base + r]], dtype=torch.int64,
+                                      device=device)
+        self.att_epochs = torch.zeros(H * N, dtype=torch.int32, device=device)
+        self.att_part = buf[:int(lib.srhpm_flash_attn_part_size(H, N))]
+        self.att_key = (H, N, r)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=self.group)
+
     def all_reduce(self, t):
         import torch.distributed as dist
         dist.all_reduce(t, group=self.group)
@@ -275,6 +314,11 @@ class VerifyStep:
             raise ValueError("tensor parallelism needs the rank's weight slices")
         self.H = lay["h1"] - lay["h0"] if lay else cfg.H
         self.Hkv = lay["g1"] - lay["g0"] if lay else cfg.Hkv
+        # KV heads replicated over r ranks with their tokens split on full-attention layers: those layers compute
+        # every query head of the KV head (G of them) over this rank's part of the tokens, and the records merge over
+        # the r replicas (TensorParallel.setup_attention)
+        self.split = bool(self.tp is not None and lay and lay.get("split_kv"))
+        self.G = lay["gh1"] - lay["gh0"] if self.split else self.H
         self.n_ff = lay["f1"] - lay["f0"] if lay else cfg.n_ff
         self.vocab_offset = lay["v0"] if lay else 0
         self.V = weights.head.rows
@@ -286,8 +330,9 @@ class VerifyStep:
         self.pos = torch.arange(n_past, n_past + n, dtype=torch.int32, device=dev)
         self.x = torch.zeros((n, c.d), **f32)                              # residual stream
         self.y = torch.zeros((n, c.d), **f32)                              # normed input of a block
-        self.qkv = torch.zeros((n, (self.H + 2 * self.Hkv) * c.hd), **f32)
+        self.qkv = torch.zeros((n, (max(self.H, self.G) + 2 * self.Hkv) * c.hd), **f32)
         self.att = torch.zeros((n, self.H * c.hd), **f32)
+        self.att_all = torch.zeros((n, self.G * c.hd), **f32) if self.split else None  # every head of the KV head
         self.o = torch.zeros((n, c.d), **f32)
         self.gu = torch.zeros((n, 2 * self.n_ff), **f32)                   # gate | up
         self.h = torch.zeros((n, self.n_ff), **f32)
@@ -298,6 +343,8 @@ class VerifyStep:
             self.rec = torch.zeros((n, 16), dtype=torch.uint8, device=dev)            # srhpm_argmax_record rows
             self.rec_all = torch.zeros((self.tp.world, n, 16), dtype=torch.uint8, device=dev)
             self.tp.setup(c.d, dev)
+            if self.split:
+                self.tp.setup_attention(self.G, n, lay["r"], dev)
         self.lib = L.load()
         self._keep = []
         self._calls = []
@@ -393,43 +440,71 @@ class VerifyStep:
         L_all = self.n_past + n
         masks = {}
         for li, lay in enumerate(self.w.layers):
+            # this layer's query heads: the rank's own, or every head of its KV head on a split layer
+            split = self.split and c.full_layer(li)
+            Hq = self.G if split else H
+            qkv = self.qkv[:, :(Hq + 2 * Hkv) * hd]
             if "qkv" in lay:
-                calls += self._norm_mm(None if li == 0 else 1, lay["attn_norm"], lay["qkv"], self.qkv)
+                calls += self._norm_mm(None if li == 0 else 1, lay["attn_norm"], lay["qkv"], qkv)
             else:  # Q, K, V of different types: three GEMMs into the column ranges of the qkv rows
                 calls.append(self._norm(None if li == 0 else 1, lay["attn_norm"]))
-                calls.append(self._mm(lay["q"], self.y, self.qkv[:, :H * hd]))
-                calls.append(self._mm(lay["k"], self.y, self.qkv[:, H * hd:(H + Hkv) * hd]))
-                calls.append(self._mm(lay["v"], self.y, self.qkv[:, (H + Hkv) * hd:]))
+                calls.append(self._mm(lay["q"], self.y, qkv[:, :Hq * hd]))
+                calls.append(self._mm(lay["k"], self.y, qkv[:, Hq * hd:(Hq + Hkv) * hd]))
+                calls.append(self._mm(lay["v"], self.y, qkv[:, (Hq + Hkv) * hd:]))
             kv_full, kt = self._cache_view(self.kcache[li], 0, self.kcache[li].shape[0])
             vv_full, vt = self._cache_view(self.vcache[li], 0, self.vcache[li].shape[0])
             self._keep += [kv_full, vv_full, kt, vt]
             calls.append(("rope_kv", lib.srhpm_rope_kv,
-                          [h, self._ptr(self.qkv), self.qkv.stride(0), n, H, Hkv, hd, self._ptr(self.pos),
+                          [h, self._ptr(self.qkv), self.qkv.stride(0), n, Hq, Hkv, hd, self._ptr(self.pos),
                            ctypes.c_float(c.base), ctypes.byref(kv_full), ctypes.byref(vv_full)], False))
             # attention over the visible keys (sliding-window layers: the last `window` positions)
-            full = c.window <= 0 or li % c.full_every == c.full_every - 1
+            full = c.full_layer(li)
             start = 0 if full else max(0, self.n_past - c.window + 1)
             if (full, start) not in masks:
                 masks[(full, start)] = self._mask(full, start)
                 self._keep.append(masks[(full, start)])  # the C calls hold raw pointers into it
             mask = masks[(full, start)]
-            kv, kt2 = self._cache_view(self.kcache[li], start, L_all - start)
-            vv, vt2 = self._cache_view(self.vcache[li], start, L_all - start)
-            # q: the rotated query heads inside the qkv rows: ne [hd, n, H], token stride = row, head stride = hd
-            qv = _tensor_view(self.qkv, L.F32, [hd, n, H], [4, self.qkv.stride(0) * 4, hd * 4])
-            # dst [hd, H, n]: head stride hd, token stride H * hd -> att rows [n][H * hd]
-            ov = _tensor_view(self.att, L.F32, [hd, H, n], [4, hd * 4, self.att.stride(0) * 4])
-            mv = _tensor_view(mask, L.F16, [mask.shape[1], mask.shape[0], 1], [2, mask.stride(0) * 2])
-            self._keep += [kv, vv, kt2, vt2, qv, ov, mv]
+            t0, t1 = start, L_all
+            if split:  # this replica's part of the tokens (whole 128-token tiles)
+                from .shard import kv_range
+                lay_tp = self.w.tp
+                a, b = kv_range(L_all, lay_tp["r"], lay_tp["p"])
+                t0, t1 = start + a, start + b
+            kv, kt2 = self._cache_view(self.kcache[li], t0, t1 - t0)
+            vv, vt2 = self._cache_view(self.vcache[li], t0, t1 - t0)
+            # q: the rotated query heads inside the qkv rows: ne [hd, n, Hq], token stride = row, head stride = hd
+            qv = _tensor_view(self.qkv, L.F32, [hd, n, Hq], [4, self.qkv.stride(0) * 4, hd * 4])
+            # the mask's columns of the tokens attended to
+            mv = _tensor_view(mask[:, t0 - start:], L.F16, [t1 - t0, mask.shape[0], 1], [2, mask.stride(0) * 2])
+            self._keep += [kv, vv, kt2, vt2, qv, mv]
             sz = ctypes.c_size_t()
-            L.check(lib.srhpm_flash_attn_ext_work_size(h, ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv),
-                                                       ctypes.byref(sz)), "srhpm_flash_attn_ext_work_size")
+            if t1 > t0:
+                L.check(lib.srhpm_flash_attn_ext_work_size(h, ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv),
+                                                           ctypes.byref(sz)), "srhpm_flash_attn_ext_work_size")
             self._ws = max(self._ws, sz.value)
-            calls.append(("flash_attn_ext", lib.srhpm_flash_attn_ext,
-                          [h, ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(mv), None,
-                           ctypes.c_float(1.0 / math.sqrt(hd)), ctypes.c_float(0.0), ctypes.c_float(0.0),
-                           ctypes.byref(ov)], True))
-            calls.append(self._mm(lay["o"], self.att, self._rowpar_out(0)))
+            scale = ctypes.c_float(1.0 / math.sqrt(hd))
+            if split:
+                # the records of this part for every head of the KV head, merged over the replicas: att_all rows
+                # [n][G * hd], of which this rank's heads feed its O columns
+                tp = self.tp
+                ova = _tensor_view(self.att_all, L.F32, [hd, Hq, n], [4, hd * 4, self.att_all.stride(0) * 4])
+                self._keep.append(ova)
+                calls.append(("flash_attn_ext_partial", lib.srhpm_flash_attn_ext_partial,
+                              [h, ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(mv), scale,
+                               ctypes.c_float(0.0), ctypes.c_float(0.0), self._ptr(tp.att_part)], True))
+                calls.append(("flash_attn_merge_peers", lib.srhpm_flash_attn_merge_peers,
+                              [h, self._ptr(tp.att_peers), self.w.tp["r"], self.w.tp["p"], self._ptr(tp.att_epochs),
+                               None, ctypes.byref(ova)], False))
+                o0 = (self.w.tp["h0"] - self.w.tp["gh0"]) * hd
+                calls.append(self._mm(lay["o"], self.att_all[:, o0:o0 + H * hd], self._rowpar_out(0)))
+            else:
+                # dst [hd, H, n]: head stride hd, token stride H * hd -> att rows [n][H * hd]
+                ov = _tensor_view(self.att, L.F32, [hd, H, n], [4, hd * 4, self.att.stride(0) * 4])
+                self._keep.append(ov)
+                calls.append(("flash_attn_ext", lib.srhpm_flash_attn_ext,
+                              [h, ctypes.byref(qv), ctypes.byref(kv), ctypes.byref(vv), ctypes.byref(mv), None, scale,
+                               ctypes.c_float(0.0), ctypes.c_float(0.0), ctypes.byref(ov)], True))
+                calls.append(self._mm(lay["o"], self.att, self._rowpar_out(0)))
             if self.tp is not None and not self._fused():
                 calls.append(self._all_reduce(self.o))  # row-parallel O: partial sums over the rank's heads
             if "gate_up" in lay:

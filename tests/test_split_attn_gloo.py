@@ -149,7 +149,8 @@ def _class_worker(rank, world, port, kv_type, H, Hkv, N, L, errq):
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         dist.init_process_group("gloo", rank=rank, world_size=world)
         q, k, v, mask, sinks = inputs(kv_type, H, Hkv, N, L, seed=5)
-        att = SplitKAttention(OracleCtx(D), rank, world, H, N, torch.device("cpu"))
+        # the collective exchange (the peer exchange needs device symmetric memory)
+        att = SplitKAttention(OracleCtx(D), rank, world, H, N, torch.device("cpu"), exchange="nccl")
         att.out = torch.zeros((N, H, D), dtype=torch.float32)  # the stand-in's head size
         t0, t1 = att.range(L)
         out = att(torch.from_numpy(q), torch.from_numpy(np.ascontiguousarray(k[:, t0:t1])),

@@ -222,11 +222,14 @@ def _tp_worker(rank, world, port, cfg_kw, seed, cap, n_past, ids, draft, q, fuse
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("Hkv,fused", [(2, True), (2, False), (1, True)])
-def test_tensor_parallel_step_matches_one_gpu(ctx, Hkv, fused):
+@pytest.mark.parametrize("Hkv,fused,cap,n_past", [(2, True, 128, 100), (2, False, 128, 100), (1, True, 128, 100),
+                                                  (1, True, 512, 400)])
+def test_tensor_parallel_step_matches_one_gpu(ctx, Hkv, fused, cap, n_past):
     """Megatron TP over 2 GPUs (column-parallel QKV / gate|up / head, row-parallel O / down, vocabulary-sharded
     acceptance) against the same step on one GPU. The all-reduces run either inside the next RMSNorm over peer memory
-    (fused) or as NCCL calls; Hkv = 1 replicates the KV head on both ranks. Logits within 2e-2 (the partial sums
+    (fused) or as NCCL calls. Hkv = 1 replicates the KV head on both ranks: on the full-attention layer the two
+    replicas split its tokens (each attends to its part for all query heads, the records merge over the pair; with
+    105 tokens one replica's part is empty, with 405 each gets two tiles). Logits within 2e-2 (the partial sums
     change f32 rounding, re-quantization flips follow, as in the oracle comparison), accepted ids equal where the
     top-1 margin is clear. On each rank the step with the fused prologues (the all-reduce norm writing the next
     GEMM's activation records) gives the same logits bit for bit as the step without them."""
@@ -235,7 +238,7 @@ def test_tensor_parallel_step_matches_one_gpu(ctx, Hkv, fused):
     cfg_kw = dict(n_layer=3, d=512, n_ff=768, H=4, Hkv=Hkv, hd=256, n_vocab=1000, base=1e6, eps=1e-6, window=40,
                   full_every=2, kv_type=L.F16)
     cfg = V.DecoderConfig(**cfg_kw)
-    seed, cap, n_past, ids = 21, 128, 100, [3, 17, 250, 999, 42]
+    seed, ids = 21, [3, 17, 250, 999, 42]
     w = V.host_weights(cfg, seed=seed)
     kc, vc = _caches(cfg, cap, n_past, 512, seed + 1)
     one = _run_step(ctx, cfg, V.DeviceWeights.from_host(cfg, w), [torch.from_numpy(a).cuda() for a in kc],
