@@ -10,7 +10,8 @@ The partial O / down products are all-reduced. Logits are gathered, and the resu
 unsharded `decoder_step`. The oracle sums exact integer block dots in f64, so only f64 rounding separates the two.
 
 World sizes cover what the GPU tests cannot run here: 4 ranks with each KV head replicated on 2 of them, and 4 ranks
-with one KV head each."""
+with one KV head each; with the replicas of a KV head splitting the full-attention layer's tokens (2 and 4 replicas)
+as the GPU step does when there are more ranks than KV heads."""
 import os
 import socket
 
@@ -69,8 +70,10 @@ def caches(cfg, cap, n_past, seed=4):
     return kc, vc
 
 
-def tp_step(cfg, w, kc, vc, ids, n_past, rank, world):
-    """The rank's share of O.decoder_step; collectives over the default (gloo) group."""
+def tp_step(cfg, w, kc, vc, ids, n_past, rank, world, split=False):
+    """The rank's share of O.decoder_step; collectives over the default (gloo) group. split: on full-attention layers
+    the r replicas of a KV head (more ranks than KV heads) split its tokens: each computes the records of its part for
+    every query head of the KV head, the records are gathered and the replicas' sets merged in replica order."""
     c = cfg
     lay = shard.tp_layout(c["H"], c["Hkv"], c["n_ff"], c["n_vocab"], world, rank)
     h0, h1, g0, g1, f0, f1, v0, v1 = (lay[k] for k in ("h0", "h1", "g0", "g1", "f0", "f1", "v0", "v1"))
@@ -90,19 +93,38 @@ def tp_step(cfg, w, kc, vc, ids, n_past, rank, world):
     for l in range(c["n_layer"]):
         y = O.rms_norm(x, w["attn_norm"][l], c["eps"])
         full = w["qkv"][l]
-        wq = np.concatenate([full[h0 * hd:h1 * hd], full[(H + g0) * hd:(H + g1) * hd],
+        is_full = c["window"] <= 0 or l % c["full_every"] == c["full_every"] - 1
+        split_l = split and lay["r"] > 1 and is_full
+        qa, qb = shard.q_heads(lay, split_l)  # this layer's query heads: the rank's, or all of its KV head's
+        nq = qb - qa
+        wq = np.concatenate([full[qa * hd:qb * hd], full[(H + g0) * hd:(H + g1) * hd],
                              full[(H + Hkv + g0) * hd:(H + Hkv + g1) * hd]])
-        qkv = O.mul_mat(QT, wq, (nh + 2 * ng) * hd, d, y).astype(np.float32)
-        q = O.rope_neox(qkv[:, :nh * hd].reshape(n, nh, hd), pos, c["base"])
-        k = O.rope_neox(qkv[:, nh * hd:(nh + ng) * hd].reshape(n, ng, hd), pos, c["base"])
-        v = qkv[:, (nh + ng) * hd:].reshape(n, ng, hd)
+        qkv = O.mul_mat(QT, wq, (nq + 2 * ng) * hd, d, y).astype(np.float32)
+        q = O.rope_neox(qkv[:, :nq * hd].reshape(n, nq, hd), pos, c["base"])
+        k = O.rope_neox(qkv[:, nq * hd:(nq + ng) * hd].reshape(n, ng, hd), pos, c["base"])
+        v = qkv[:, (nq + ng) * hd:].reshape(n, ng, hd)
         kcl[l][n_past:n_past + n] = O.cache_rows(O.F16, k)
         vcl[l][n_past:n_past + n] = O.cache_rows(O.F16, v)
         start, mask = O.attn_window(l, c["full_every"], c["window"], n_past, n)
         kk = np.ascontiguousarray(kcl[l][start:n_past + n].transpose(1, 0, 2))
         vv = np.ascontiguousarray(vcl[l][start:n_past + n].transpose(1, 0, 2))
-        att = O.attention(np.ascontiguousarray(q.transpose(1, 0, 2)), O.F16, kk, vv, hd, n_past + n - start, ng,
-                          mask=mask.view(np.uint16), scale=1.0 / np.sqrt(hd))
+        qt = np.ascontiguousarray(q.transpose(1, 0, 2))
+        Lv = n_past + n - start
+        if split_l:
+            t0, t1 = shard.kv_range(Lv, lay["r"], lay["p"])
+            m, sm, acc = O.attention_partial(qt, O.F16, kk, vv, hd, Lv, ng, t0, t1, mask=mask.view(np.uint16),
+                                             scale=1.0 / np.sqrt(hd))
+            rec = torch.from_numpy(np.concatenate([m.ravel(), sm.ravel(), acc.ravel()]))
+            recs = [torch.zeros_like(rec) for _ in range(world)]
+            dist.all_gather(recs, rec)
+            base, hn = rank // lay["r"] * lay["r"], nq * n
+            mine = [recs[base + j].numpy() for j in range(lay["r"])]  # the replicas, in replica (= token) order
+            merged = O.attention_merge(np.stack([r_[:hn].reshape(nq, n) for r_ in mine]),
+                                       np.stack([r_[hn:2 * hn].reshape(nq, n) for r_ in mine]),
+                                       np.stack([r_[2 * hn:].reshape(nq, n, hd) for r_ in mine]))
+            att = np.ascontiguousarray(merged[:, h0 - qa:h1 - qa])  # [n, own heads, hd]
+        else:
+            att = O.attention(qt, O.F16, kk, vv, hd, Lv, ng, mask=mask.view(np.uint16), scale=1.0 / np.sqrt(hd))
         wo = shard.k_columns(w["o"][l], 256, 144, h0 * hd, h1 * hd)
         o = all_reduce(O.mul_mat(QT, wo, d, nh * hd, att.astype(np.float32).reshape(n, nh * hd)))
         x = (x + o.astype(np.float32)).astype(np.float32)
@@ -126,14 +148,15 @@ def tp_step(cfg, w, kc, vc, ids, n_past, rank, world):
     return torch.cat(cols, dim=1).numpy()
 
 
-def _worker(rank, world, port, H, Hkv, errq):
+def _worker(rank, world, port, H, Hkv, split, errq):
     try:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
         dist.init_process_group("gloo", rank=rank, world_size=world)
         cfg, w = make_model(H, Hkv)
-        cap, n_past, ids = 64, 40, [3, 77, 150, 299, 12]
+        # 300 past tokens: the full-attention layer's 305 tokens are 3 tiles, so with 4 replicas one part is empty
+        cap, n_past, ids = (320, 300, [3, 77, 150, 299, 12]) if split else (64, 40, [3, 77, 150, 299, 12])
         kc, vc = caches(cfg, cap, n_past)
-        got = tp_step(cfg, w, kc, vc, ids, n_past, rank, world)
+        got = tp_step(cfg, w, kc, vc, ids, n_past, rank, world, split)
         if rank == 0:
             kc1, vc1 = caches(cfg, cap, n_past)
             exp, _ = O.decoder_step(cfg, w, kc1, vc1, ids, n_past, ids[1:])
@@ -146,12 +169,15 @@ def _worker(rank, world, port, H, Hkv, errq):
         raise
 
 
-@pytest.mark.parametrize("world,H,Hkv", [(2, 4, 2), (4, 8, 2), (4, 8, 4)])
-def test_tensor_parallel_step_equals_unsharded(world, H, Hkv):
+@pytest.mark.parametrize("world,H,Hkv,split", [(2, 4, 2, False), (4, 8, 2, False), (4, 8, 4, False),
+                                                (2, 4, 1, True), (4, 8, 2, True), (4, 8, 1, True)])
+def test_tensor_parallel_step_equals_unsharded(world, H, Hkv, split):
+    """split: the KV head's replicas (2 or 4 of them) split the full-attention layer's tokens and merge their
+    records, as the GPU step does with more ranks than KV heads."""
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
     port = free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, H, Hkv, errq)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, H, Hkv, split, errq)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
