@@ -1131,6 +1131,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 // The same merge combines the record sets of several devices (each the merged record of its KV range) and, with
 // parts_out, leaves this device's merged record unnormalized for such a merge.
 __global__ void __launch_bounds__(256) fa_combine_kernel(const FaArgs a) {
+    // the next kernel (the attention output projection) may become resident and stream its first weights now; it
+    // waits for this grid before it reads the output
+    pdl_launch_dependents();
     pdl_wait();
     const int row = blockIdx.x, g = row / a.R, rr = row % a.R;
     const int h = g * a.G + rr / a.N, tq = rr % a.N;
