@@ -623,7 +623,7 @@ def run_gpu(args):
     step_tp = step_tp_q8 = None
     if world > 1 and not args.no_step:  # every rank takes part (collectives inside the step)
         try:
-            step_tp = measure_step_27b_tp(ctx, dev, rank, world)
+            step_tp = measure_step_27b_tp(ctx, dev, rank, world, ks_extra=(2, 4))
         except Exception as e:  # recorded beside the sweep rather than losing its line
             step_tp = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
         torch.cuda.empty_cache()
@@ -890,9 +890,10 @@ def _full_caches(cfg, dev, n_layer_cap, seed):
     return kc, vc
 
 
-def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0, kv_q8=False):
+def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0, kv_q8=False, ks_extra=()):
     """The 27B-class verify step (k = 8, f16 KV of 2048 tokens; kv_q8: q8_0 KV of n_past tokens, BASELINE config 5,
-    timed without the parity pass) on `world` GPUs in Megatron tensor parallelism
+    timed without the parity pass; ks_extra: shorter drafts timed first with the same weights and caches, without a
+    parity pass) on `world` GPUs in Megatron tensor parallelism
     (column-parallel QKV / gate|up / head, row-parallel O / down with the all-reduce fused into the next RMSNorm, KV
     heads split or replicated per rank, vocabulary-sharded acceptance). Every rank builds the same whole model
     (random blocks, one seed) and cuts its slices on the device (DeviceWeights.slice_of), and the same whole cache
@@ -926,35 +927,51 @@ def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0
         kc_full, vc_full = _full_caches(cfg, dev, cap, seed + 7)
         kc = [c[:, g0:g1].contiguous() for c in kc_full]
         vc = [c[:, g0:g1].contiguous() for c in vc_full]
-    step = V.VerifyStep(ctx, cfg, w, kc, vc, n, n_past, tp=V.TensorParallel(rank, world))
-    ids = torch.arange(n, dtype=torch.int32, device=dev) * 977 % cfg.n_vocab  # the same tokens on every rank
-    step.set_tokens(ids, ids[1:])
-    for _ in range(2):
-        step.run()
-    torch.cuda.synchronize()
-    s = torch.cuda.Stream(dev)
-    s.wait_stream(torch.cuda.current_stream())
-    graph = torch.cuda.CUDAGraph()
-    ctx.launch_count(reset=True)
-    with torch.cuda.stream(s):
-        with torch.cuda.graph(graph, stream=s):
-            step.run(s)
-    launches = ctx.launch_count(reset=True)
-    for _ in range(2):
-        graph.replay()
-    torch.cuda.synchronize()
-    dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        graph.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    ctx.check()
-    tt = torch.tensor([e0.elapsed_time(e1) / reps], device=dev)
-    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    ms = float(tt.item())
-    del graph  # holds NCCL calls: released before the process group
+    tp = V.TensorParallel(rank, world)
+
+    def timed(kk):
+        """The step with kk drafted tokens as one replayed CUDA graph: (step, ms max over ranks, launches per rank)."""
+        nn = kk + 1
+        st = V.VerifyStep(ctx, cfg, w, kc, vc, nn, n_past, tp=tp)
+        tok = torch.arange(nn, dtype=torch.int32, device=dev) * 977 % cfg.n_vocab  # the same tokens on every rank
+        st.set_tokens(tok, tok[1:])
+        for _ in range(2):
+            st.run()
+        torch.cuda.synchronize()
+        cs = torch.cuda.Stream(dev)
+        cs.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        ctx.launch_count(reset=True)
+        with torch.cuda.stream(cs):
+            with torch.cuda.graph(graph, stream=cs):
+                st.run(cs)
+        nl = ctx.launch_count(reset=True)
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ctx.check()
+        tt = torch.tensor([e0.elapsed_time(e1) / reps], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        del graph  # holds NCCL calls: released before the process group
+        return st, float(tt.item()), nl
+
+    out = {}
+    for kk in ks_extra:  # the shorter drafts, timed only (the same weights and caches)
+        st, ms_k, nl = timed(kk)
+        nb = step_bytes_27b(cfg, n_past, kk + 1)
+        out[f"k{kk}"] = {"ms": round(ms_k, 3), "steps_per_s": round(1e3 / ms_k, 1), "gpus": world,
+                         "GBps_per_gpu": round(nb / world / (ms_k * 1e-3) / 1e9, 1), "bytes": nb,
+                         "kernel_launches_per_rank": nl}
+        del st
+    step, ms, launches = timed(k)
+    ids = torch.arange(n, dtype=torch.int32, device=dev) * 977 % cfg.n_vocab
 
     if kv_q8:
         acc = int(step.out_n.item())
@@ -962,9 +979,10 @@ def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0
         torch.cuda.empty_cache()
         dist.barrier()
         nbytes = step_bytes_27b(cfg, n_past, n)
-        return {f"k{k}": {"ms": round(ms, 3), "steps_per_s": round(1e3 / ms, 1), "gpus": world,
-                          "GBps_per_gpu": round(nbytes / world / (ms * 1e-3) / 1e9, 1), "bytes": nbytes,
-                          "kernel_launches_per_rank": launches, "accepted": acc, "kv": f"q8_0, {n_past} past tokens"}}
+        out[f"k{k}"] = {"ms": round(ms, 3), "steps_per_s": round(1e3 / ms, 1), "gpus": world,
+                        "GBps_per_gpu": round(nbytes / world / (ms * 1e-3) / 1e9, 1), "bytes": nbytes,
+                        "kernel_launches_per_rank": launches, "accepted": acc, "kv": f"q8_0, {n_past} past tokens"}
+        return out
     # parity against the whole model on rank 0's GPU
     par = None
     ids1 = torch.zeros(n, dtype=torch.int32, device=dev)
@@ -1015,9 +1033,10 @@ def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0
     del one
     dist.barrier()
     nbytes = step_bytes_27b(cfg, n_past, n)
-    return {f"k{k}": {"ms": round(ms, 3), "steps_per_s": round(1e3 / ms, 1), "gpus": world,
-                      "GBps_per_gpu": round(nbytes / world / (ms * 1e-3) / 1e9, 1), "bytes": nbytes,
-                      "kernel_launches_per_rank": launches, "accepted": acc, "parity": par}}
+    out[f"k{k}"] = {"ms": round(ms, 3), "steps_per_s": round(1e3 / ms, 1), "gpus": world,
+                    "GBps_per_gpu": round(nbytes / world / (ms * 1e-3) / 1e9, 1), "bytes": nbytes,
+                    "kernel_launches_per_rank": launches, "accepted": acc, "parity": par}
+    return out
 
 
 def shard_vocab(n_vocab, world, j):
