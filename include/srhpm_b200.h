@@ -264,8 +264,10 @@ int srhpm_add_rms_norm_allreduce(srhpm_ctx * ctx, float * x, const uint64_t * pe
 /* srhpm_add_rms_norm_allreduce fused with the activation quantization of the GEMM that consumes y, as
  * srhpm_add_rms_norm_quant is for srhpm_add_rms_norm: the same exchange and rank-order sum of the ranks' slot
  * `slot` rows, the residual add and the norm, and W_next's activation records written into wdata for
- * srhpm_mul_mat_prequantized. One launch instead of the norm plus srhpm_mul_mat's own quantizer. Same limits as both
- * (K-quant and IQ4_XS W_next, n <= 16, d <= 16384, world <= 8). No counterpart in the reference (one device). */
+ * srhpm_mul_mat_prequantized. One launch instead of the norm plus srhpm_mul_mat's own quantizer; each row is spread
+ * over a cluster of 8 CTAs (each sends and sums a share of the columns), with results bit-identical to one CTA per
+ * row. Same limits as both (K-quant and IQ4_XS W_next, n <= 16, d <= 16384, world <= 8). No counterpart in the
+ * reference (one device). */
 int srhpm_add_rms_norm_allreduce_quant(srhpm_ctx * ctx, float * x, const uint64_t * peer_buffers, int world,
                                        int rank, int slot, uint32_t * epochs, const float * w, float eps, float * y,
                                        int n, const srhpm_tensor * W_next, void * wdata, size_t wsize, void * stream);

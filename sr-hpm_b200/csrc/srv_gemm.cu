@@ -258,9 +258,9 @@ __global__ void __launch_bounds__(256) swiglu_q8K_kernel(const float * __restric
 // prologue): CTA t < N: x += delta; y = x / sqrt(mean(x^2) + eps) * w (as add_rms_norm); the row of y is staged in
 // shared memory and each warp quantizes super-blocks of it into the GEMM's activation records exactly as
 // quant_q8K_kernel does (same functions); CTAs N..NT-1 write the zero padding rows; CTA 0 zeroes the split-K counters.
-// With ar.peers set, the delta is the tensor-parallel all-reduce of the ranks' partial rows instead (the flag-in-word
-// exchange and the rank-order sum of allreduce.cuh, as add_rms_norm_ar_kernel does): all-reduce, residual add, norm
-// and the next GEMM's activation records in one kernel.
+// add_rms_norm_ar_q8K_kernel below is the form whose delta is the tensor-parallel all-reduce of the ranks' partial
+// rows (the flag-in-word exchange and the rank-order sum of allreduce.cuh, as add_rms_norm_ar_kernel does):
+// all-reduce, residual add, norm and the next GEMM's activation records in one kernel.
 struct NormAr {
     const uint64_t * peers;  // null: no all-reduce
     int              world, rank, slot;
@@ -272,8 +272,7 @@ constexpr int kNormQThreads = 1024;
 __global__ void __launch_bounds__(kNormQThreads) add_rms_norm_q8K_kernel(float * x, const float * delta,
                                                                           const float * w, float eps, float * y,
                                                                           int N, int64_t d, int NT, uint8_t * recs,
-                                                                          int perm, int32_t * cnt, int ncnt,
-                                                                          const NormAr ar) {
+                                                                          int perm, int32_t * cnt, int ncnt) {
     pdl_launch_dependents();
     pdl_wait();
     extern __shared__ float ys[];
@@ -283,31 +282,15 @@ __global__ void __launch_bounds__(kNormQThreads) add_rms_norm_q8K_kernel(float *
         for (int i = threadIdx.x; i < ncnt; i += blockDim.x) cnt[i] = 0;
     }
     if (t < N) {
-        float *             xr = x + (int64_t) t * d;
-        float               ss = 0.0f;
-        float4              v[4];
-        __shared__ uint32_t e_s;
-        uint32_t            e  = 0;
-        bool                ok = true;
-        uint64_t            t0 = 0;
-        if (ar.peers) {  // send this rank's values of the row to every rank first (allreduce.cuh)
-            e = ar_epoch(ar.epochs, ar.slot, t, &e_s);
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const int64_t j = threadIdx.x + (int64_t) k * kNormQThreads;
-                if (j < d4) ar_push4(ar.peers, ar.world, ar.rank, ar.slot, t, d, j, e);
-            }
-            t0 = globaltimer_ns();
-        }
+        float * xr = x + (int64_t) t * d;
+        float   ss = 0.0f;
+        float4  v[4];
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             const int64_t j = threadIdx.x + (int64_t) k * kNormQThreads;
             if (j < d4) {
                 float4 a = reinterpret_cast<const float4 *>(xr)[j];
-                if (ar.peers) {
-                    ar_gather4(a, ar.peers, ar.world, ar.rank, ar.slot, t, d, j, e, t0, ok, ar.status);
-                    reinterpret_cast<float4 *>(xr)[j] = a;
-                } else if (delta) {
+                if (delta) {
                     const float4 b = reinterpret_cast<const float4 *>(delta + (int64_t) t * d)[j];
                     a.x += b.x; a.y += b.y; a.z += b.z; a.w += b.w;
                     reinterpret_cast<float4 *>(xr)[j] = a;
@@ -359,6 +342,121 @@ __global__ void __launch_bounds__(kNormQThreads) add_rms_norm_q8K_kernel(float *
         q8K_quantize_warp(v8, lane, qv, dv);
         q8K_store_record(qv, dv, recs + (size_t) sb * rec_bytes(false, NT), t, NT, lane, perm);
     }
+}
+
+// The all-reduce form of add_rms_norm_q8K_kernel, spread over a cluster of kArC CTAs per token row, so that the
+// exchange's stores to the peers and the loads of the receive area run on kArC SMs per row instead of one (a rank
+// sends (world - 1) x d x 8 bytes per row). CTA c of row t handles the float4 columns 128 c + v + 1024 k (thread v,
+// k = 0..3): the columns thread 128 c + v of the one-CTA kernel handles. So each warp is a warp of that kernel, and
+// the sum of squares is reduced in the same order (each thread's chain, the warp's butterfly, then one butterfly over
+// the 32 warp partials gathered over distributed shared memory): the rows are bit-identical to the one-CTA kernel's.
+// The super-blocks of y that a CTA quantizes (2 c + 16 k, + 1) lie inside its own columns. Every CTA reads the row's
+// epoch; CTA 0 advances it after the cluster's last barrier. Rows N..NT-1 write the zero padding records.
+constexpr int kArC  = 8;
+constexpr int kArCT = 128;
+__global__ void __cluster_dims__(kArC, 1, 1) __launch_bounds__(kArCT)
+    add_rms_norm_ar_q8K_kernel(float * x, const float * w, float eps, float * y, int N, int64_t d, int NT,
+                               uint8_t * recs, int perm, int32_t * cnt, int ncnt, const NormAr ar) {
+    pdl_launch_dependents();
+    pdl_wait();  // this rank's GEMM has written its partial rows
+    __shared__ float4   ys[4 * kArCT];  // this CTA's columns of y: [k][v]
+    __shared__ float    part[kArCT / 32];
+    __shared__ float    tot_s;
+    __shared__ uint32_t e_s;
+    const int     c = blockIdx.x, t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int64_t d4   = d >> 2;
+    const bool    real = t < N;
+    if (c == 0 && t == 0) {
+        for (int i = tid; i < ncnt; i += kArCT) cnt[i] = 0;
+    }
+    float    ss = 0.0f;
+    float4   v[4];
+    uint32_t e  = 0;
+    if (real) {
+        if (tid == 0) e_s = __ldcg(&ar.epochs[ar.slot * kArRows + t]) + 1u;
+        __syncthreads();
+        e = e_s;
+        {  // send this rank's values of the CTA's columns to every rank (ar_push4, all columns per rank in turn)
+            const float4 * part = reinterpret_cast<const float4 *>(ar.peers[ar.rank] + (size_t) ar.slot * ar_part_bytes(d)) +
+                                  (int64_t) t * d4;
+            float4 pv[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const int64_t j = kArCT * c + tid + (int64_t) k * 1024;
+                if (j < d4) pv[k] = part[j];
+            }
+            const size_t o = ar_recv_word(d, ar.slot, t, ar.rank);
+            for (int r = 0; r < ar.world; r++) {
+                uint8_t * q = reinterpret_cast<uint8_t *>(ar.peers[r] + o);
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    const int64_t j = kArCT * c + tid + (int64_t) k * 1024;
+                    if (j < d4) {
+                        st_relaxed_sys_v2(q + j * 32, ll_word(pv[k].x, e), ll_word(pv[k].y, e));
+                        st_relaxed_sys_v2(q + j * 32 + 16, ll_word(pv[k].z, e), ll_word(pv[k].w, e));
+                    }
+                }
+            }
+        }
+        float *        xr = x + (int64_t) t * d;
+        bool           ok = true;
+        const uint64_t t0 = globaltimer_ns();
+#pragma unroll
+        for (int k = 0; k < 4; k++) {
+            const int64_t j = kArCT * c + tid + (int64_t) k * 1024;
+            if (j < d4) {
+                float4 a = reinterpret_cast<const float4 *>(xr)[j];
+                ar_gather4(a, ar.peers, ar.world, ar.rank, ar.slot, t, d, j, e, t0, ok, ar.status);
+                reinterpret_cast<float4 *>(xr)[j] = a;
+                v[k] = a;
+                ss = fmaf(a.x, a.x, fmaf(a.y, a.y, fmaf(a.z, a.z, fmaf(a.w, a.w, ss))));
+            }
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) part[warp] = ss;
+    cluster_sync_all();  // every CTA's warp partials are written
+    if (warp == 0) {
+        // lane l: the partial of warp l of the one-CTA kernel = warp l % 4 of cluster CTA l / 4
+        float p = ld_dsmem_f32(mapa_shared(smem_u32(&part[lane & 3]), (uint32_t) (lane >> 2)));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
+        if (lane == 0) tot_s = p;
+    }
+    __syncthreads();
+    const float scale = 1.0f / sqrtf(tot_s / (float) d + eps);
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const int64_t j = kArCT * c + tid + (int64_t) k * 1024;
+        float4        o = make_float4(0, 0, 0, 0);
+        if (real && j < d4) {
+            const float4 ww = reinterpret_cast<const float4 *>(w)[j];
+            o.x = v[k].x * scale * ww.x;
+            o.y = v[k].y * scale * ww.y;
+            o.z = v[k].z * scale * ww.z;
+            o.w = v[k].w * scale * ww.w;
+            reinterpret_cast<float4 *>(y + (int64_t) t * d)[j] = o;
+        }
+        ys[k * kArCT + tid] = o;
+    }
+    __syncthreads();
+    const int nsb = (int) (d / QK);
+    for (int q = warp; q < 8; q += kArCT / 32) {  // the CTA's super-blocks: 2 c + 16 k + h, q = 2 k + h
+        const int k = q >> 1, h = q & 1, sb = 2 * c + 16 * k + h;
+        if (sb >= nsb) continue;
+        const float * src = reinterpret_cast<const float *>(ys + k * kArCT + h * 64) + 8 * lane;
+        const float4  a   = reinterpret_cast<const float4 *>(src)[0];
+        const float4  b   = reinterpret_cast<const float4 *>(src)[1];
+        float         v8[8];
+        v8[0] = a.x; v8[1] = a.y; v8[2] = a.z; v8[3] = a.w; v8[4] = b.x; v8[5] = b.y; v8[6] = b.z; v8[7] = b.w;
+        int   qv[8];
+        float dv;
+        q8K_quantize_warp(v8, lane, qv, dv);
+        q8K_store_record(qv, dv, recs + (size_t) sb * rec_bytes(false, NT), t, NT, lane, perm);
+    }
+    cluster_sync_all();  // no CTA exits while a peer may read its partials; every CTA has read the epoch
+    if (real && c == 0 && tid == 0) ar.epochs[ar.slot * kArRows + t] = e;
 }
 
 // q8_0 quantizer, per 32 columns (4 lanes per block): d = amax / 127 stored as f16. SIMD mode: id = 127 / amax,
@@ -1860,10 +1958,15 @@ int norm_quant_run(srhpm_ctx * ctx, int wtype, int64_t rows, int64_t K, int64_t 
         if (st != SRHPM_OK) return st;
         attr_done.fetch_or(1u << (dev & 31));
     }
-    const cudaError_t e = launch_k_pdl(add_rms_norm_q8K_kernel, dim3(NT), dim3(kNormQThreads), (size_t) K * 4, stream,
-                                       x, delta, w, eps, y, (int) N, K, NT, base + wl.recs,
-                                       record_perm(wtype), reinterpret_cast<int32_t *>(base + wl.cnt),
-                                       nrb, ar);
+    cudaError_t e;
+    if (peers) {  // a cluster of kArC CTAs per row (compile-time cluster shape)
+        e = launch_k_pdl(add_rms_norm_ar_q8K_kernel, dim3(kArC, NT), dim3(kArCT), 0, stream, x, w, eps, y, (int) N, K,
+                         NT, base + wl.recs, record_perm(wtype), reinterpret_cast<int32_t *>(base + wl.cnt), nrb, ar);
+    } else {
+        e = launch_k_pdl(add_rms_norm_q8K_kernel, dim3(NT), dim3(kNormQThreads), (size_t) K * 4, stream, x, delta, w,
+                         eps, y, (int) N, K, NT, base + wl.recs, record_perm(wtype),
+                         reinterpret_cast<int32_t *>(base + wl.cnt), nrb);
+    }
     ctx->launches.fetch_add(1);
     return cuda_status(e);
 }

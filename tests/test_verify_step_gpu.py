@@ -310,6 +310,53 @@ def test_allreduce_norm_one_rank_equals_add_norm(ctx):
     assert epochs.view(2, 16)[:, :n].tolist() == [[2] * n, [2] * n]
 
 
+@pytest.mark.parametrize("d,n,qtype", [(5120, 9, S.Q4_K), (5120, 4, S.Q3_K), (1024, 3, S.Q5_K), (16384, 16, S.IQ4_XS)])
+def test_allreduce_norm_quant_one_rank_equals_norm_quant(ctx, d, n, qtype):
+    """The fused all-reduce + norm + quantization prologue (a cluster of CTAs per row: each sends and sums a share of
+    the row's columns, the sum of squares is reduced in the one-CTA kernel's order) with one rank equals
+    srhpm_add_rms_norm_quant with the partial rows as delta, bit for bit: x, y, and the GEMM on the records
+    (srhpm_mul_mat_prequantized), over two calls per slot (the epochs advance once per call and row)."""
+    lib = L.load()
+    rows = 192
+    nbytes = int(lib.srhpm_allreduce_buffer_size(d))
+    mine = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    peers = torch.tensor([mine.data_ptr()], dtype=torch.int64, device="cuda")
+    epochs = torch.zeros(32, dtype=torch.int32, device="cuda")
+    W = S.QuantTensor.from_blocks(O.random_blocks(qtype, rows * d // 256, np.random.default_rng(d + n)), qtype, rows, d)
+    wv = W.view()
+    w = 1 + 0.1 * torch.randn(d, device="cuda")
+    ptr = lambda t: t.data_ptr()
+    part = [mine[k * 16 * d * 4:(k + 1) * 16 * d * 4].view(torch.float32).view(16, d) for k in (0, 1)]
+    g = torch.Generator(device="cuda")
+    g.manual_seed(d + n)
+    for rep in range(4):
+        slot = rep % 2
+        part[slot][:n] = torch.randn((n, d), device="cuda", generator=g)
+        x = torch.randn((n, d), device="cuda", generator=g)
+        x2, y, y2 = x.clone(), torch.empty_like(x), torch.empty_like(x)
+        st, ws = ctx.mul_mat_work_size(W, x)
+        work, work2 = (torch.empty(ws, dtype=torch.uint8, device="cuda") for _ in range(2))
+        L.check(lib.srhpm_add_rms_norm_allreduce_quant(ctx.handle, ptr(x), ptr(peers), 1, 0, slot, ptr(epochs),
+                                                       ptr(w), ctypes.c_float(1e-6), ptr(y), n, ctypes.byref(wv),
+                                                       ptr(work), work.numel(), None),
+                "srhpm_add_rms_norm_allreduce_quant")
+        delta = part[slot][:n].clone()
+        L.check(lib.srhpm_add_rms_norm_quant(ctx.handle, ptr(x2), ptr(delta), ptr(w), ctypes.c_float(1e-6), ptr(y2),
+                                             n, ctypes.byref(wv), ptr(work2), work2.numel(), None),
+                "srhpm_add_rms_norm_quant")
+        Y, Y2 = (torch.empty((n, rows), dtype=torch.float32, device="cuda") for _ in range(2))
+        for yy, ww_, buf in ((y, Y, work), (y2, Y2, work2)):
+            xv, yv = S.f32_rows_view(yy), S.f32_rows_view(ww_)
+            L.check(lib.srhpm_mul_mat_prequantized(ctx.handle, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv),
+                                                   ptr(buf), buf.numel(), None), "srhpm_mul_mat_prequantized")
+        torch.cuda.synchronize()
+        ctx.check()
+        assert torch.equal(x, x2) and torch.equal(y, y2), rep
+        assert torch.equal(Y, Y2), rep
+    assert epochs.view(2, 16)[:, :n].tolist() == [[2] * n, [2] * n]
+    assert epochs.view(2, 16)[:, n:].abs().sum().item() == 0
+
+
 def test_allreduce_norm_peer_wait_times_out(ctx):
     """The fused all-reduce's wait is bounded: a second 'rank' that never sends its values (a plain local buffer
     standing in for the peer) ends the wait after ~2 s with an error status read on the host, and the context stays
