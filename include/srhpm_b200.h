@@ -245,6 +245,15 @@ int srhpm_mul_mat_prequantized(srhpm_ctx * ctx, const srhpm_tensor * W, const sr
  * srhpm_mul_mat_prequantized. */
 int srhpm_swiglu_quant(srhpm_ctx * ctx, const float * gate, const float * up, int64_t ld_in, float * out,
                        int64_t ld_out, int n, const srhpm_tensor * W_next, void * wdata, size_t wsize, void * stream);
+/* The FFN down projection with the SwiGLU in its own prologue: Y = W . h for h = silu(gate) * up (silu(g) =
+ * g / (1 + exp(-g)), as srhpm_swiglu), gate and up f32 views of the same shape and row stride (ne[0] = K, ne[1] = n).
+ * The GEMM grid computes h for its activation super-blocks and quantizes it into the records, as
+ * srhpm_mul_mat_fused_quant does for X: the work of srhpm_swiglu_quant + srhpm_mul_mat_prequantized in one launch,
+ * h itself not stored (when the grid is too small for the prologue, the SwiGLU record kernel runs first). The records
+ * are the same bytes, so Y is bit-identical to that pair. K-quant and IQ4_XS W (Q8_0: SRHPM_UNSUPPORTED); wdata of
+ * srhpm_mul_mat_work_size(W, gate) bytes. */
+int srhpm_mul_mat_swiglu(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * gate, const srhpm_tensor * up,
+                         srhpm_tensor * Y, void * wdata, size_t wsize, void * stream);
 
 /* Tensor-parallel residual add + RMSNorm with the all-reduce inside (row-parallel GEMM -> next norm):
  * every rank's row-parallel GEMM (attention output, FFN down) writes its partial sum [n][d] f32 into slot `slot`

@@ -288,6 +288,22 @@ int srhpm_mul_mat_fused_quant(srhpm_ctx * ctx, const srhpm_tensor * W, const srh
                     nullptr, nullptr, (cudaStream_t) stream, true);
 }
 
+int srhpm_mul_mat_swiglu(srhpm_ctx * ctx, const srhpm_tensor * W, const srhpm_tensor * gate, const srhpm_tensor * up,
+                         srhpm_tensor * Y, void * wdata, size_t wsize, void * stream) {
+    if (!ctx || !Y || !up) return SRHPM_ERR_INVALID;
+    const int st = check_mul_mat(W, gate, Y);
+    if (st != SRHPM_OK) return st;
+    if (up->type != SRHPM_TYPE_F32 || up->ne[0] != gate->ne[0] || up->ne[1] != gate->ne[1] || up->ne[2] != 1 ||
+        up->ne[3] != 1 || up->nb[0] != 4 || up->nb[1] != gate->nb[1] || !up->data) {
+        return SRHPM_ERR_INVALID;
+    }
+    if (!aligned(up->data, 4)) return SRHPM_ERR_ALIGN;
+    return gemm_run_swiglu(ctx, W->type, (const uint8_t *) W->data, W->ne[1], W->ne[0], W->nb[1],
+                           (const float *) gate->data, (const float *) up->data, (int64_t) (gate->nb[1] / 4),
+                           gate->ne[1], (float *) Y->data, (int64_t) (Y->nb[1] / 4), wdata, wsize,
+                           (cudaStream_t) stream);
+}
+
 int srhpm_add_rms_norm_quant(srhpm_ctx * ctx, float * x, const float * delta, const float * w, float eps, float * y,
                              int n, const srhpm_tensor * W_next, void * wdata, size_t wsize, void * stream) {
     if (!ctx || !x || !w || !y || !W_next || n < 1 || n > 16) return SRHPM_ERR_INVALID;

@@ -1574,7 +1574,6 @@ int fa_merge_peers_run(srhpm_ctx * ctx, const uint64_t * peers, int world, int r
 int fa_merge_run(srhpm_ctx * ctx, const void * parts, int n_parts, int N, int H, const float * sinks, float * dst,
                  int64_t dnb1, int64_t dnb2, cudaStream_t stream) {
     // one "KV head" holding every head: row = h * N + t, as in the record sets
-    const int64_t rows = (int64_t) H * N;
     const size_t  set  = fa_part_bytes(H, N);
     FaArgs        a    = {};
     a.N         = N;

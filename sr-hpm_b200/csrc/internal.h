@@ -47,6 +47,11 @@ size_t gemm_work_size(int wtype, int64_t rows, int64_t K, int64_t N);
 int    gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                 const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
                 int32_t * isum, int32_t * imin, cudaStream_t stream, bool fused_quant = false);
+// the product with silu(gate) * up (rows of ld_in floats) as activations, quantized in the GEMM's own prologue (or by
+// the SwiGLU record kernel when the grid is too small); the SwiGLU output itself is not stored
+int    gemm_run_swiglu(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
+                       const float * gate, const float * up, int64_t ld_in, int64_t N, float * Y, int64_t ldy,
+                       void * wdata, size_t wsize, cudaStream_t stream);
 size_t gemm_work_size_unsplit(int wtype, int64_t rows, int64_t K, int64_t N);
 int    gemm_run_prequant(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                          int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize, cudaStream_t stream);

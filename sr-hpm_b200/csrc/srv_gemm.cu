@@ -237,7 +237,8 @@ __global__ void __launch_bounds__(256) swiglu_q8K_kernel(const float * __restric
 #pragma unroll
         for (int j = 0; j < 8; j++) v[j] = g8[j] / (1.0f + expf(-g8[j])) * u8[j];
         float * hp = h + (int64_t) t * ld_out + c0;
-        if ((reinterpret_cast<uintptr_t>(hp) & 15) == 0) {
+        if (!h) {  // the records only (srhpm_mul_mat_swiglu)
+        } else if ((reinterpret_cast<uintptr_t>(hp) & 15) == 0) {
             reinterpret_cast<float4 *>(hp)[0] = make_float4(v[0], v[1], v[2], v[3]);
             reinterpret_cast<float4 *>(hp)[1] = make_float4(v[4], v[5], v[6], v[7]);
         } else {
@@ -1170,6 +1171,8 @@ struct GemmArgs {
     // record; otherwise a separate quantizer kernel ran before this one
     int             fq;
     const float *   X;
+    const float *   X2;          // non-null: X and X2 are the SwiGLU inputs (gate, up), the records are of
+                                 // silu(X) * X2 as swiglu_q8K_kernel computes it
     int64_t         ldx;
     int             perm;        // record byte order (record_perm)
     int             q80mode;     // the context's q8_0 mode (Q8_0 weights)
@@ -1188,9 +1191,16 @@ __device__ __forceinline__ void fq_quantize(const GemmArgs & a, int warp, int la
     const int     nw = (int) gridDim.x * kNCW;
     const int     jobs = a.nsb * a.N;
     for (int j = (int) blockIdx.x * kNCW + warp; j < jobs; j += nw) {
-        const int sb = j / a.N, t = j - sb * a.N;
-        float     v[8];
-        load8(a.X + (int64_t) t * a.ldx + (int64_t) sb * QK + 8 * lane, v);
+        const int     sb = j / a.N, t = j - sb * a.N;
+        const int64_t c0 = (int64_t) t * a.ldx + (int64_t) sb * QK + 8 * lane;
+        float         v[8];
+        load8(a.X + c0, v);
+        if (a.X2) {  // h = silu(gate) * up, as swiglu_q8K_kernel
+            float u8[8];
+            load8(a.X2 + c0, u8);
+#pragma unroll
+            for (int jj = 0; jj < 8; jj++) v[jj] = v[jj] / (1.0f + expf(-v[jj])) * u8[jj];
+        }
         uint8_t * rec = const_cast<uint8_t *>(a.recs) + (size_t) sb * RB;
         if constexpr (D::Q80) {
             __half      dh;
@@ -1402,8 +1412,10 @@ __global__ void __launch_bounds__(kThreads, D::MINB) srv_gemm_kernel(const __gri
     if (a.fq) {  // warm L2 with the activation segment of this warp's first quantization job (a hint, as above)
         const int j = (int) blockIdx.x * kNCW + warp;
         if (j < a.nsb * a.N && (lane & 3) == 0) {
-            const int sb = j / a.N, t = j - sb * a.N;
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(a.X + (int64_t) t * a.ldx + (int64_t) sb * QK + 8 * lane));
+            const int     sb = j / a.N, t = j - sb * a.N;
+            const int64_t c0 = (int64_t) t * a.ldx + (int64_t) sb * QK + 8 * lane;
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(a.X + c0));
+            if (a.X2) asm volatile("prefetch.global.L2 [%0];" ::"l"(a.X2 + c0));
         }
     }
     pdl_wait();  // the split-K counters and partials are written below; the quantizer grid zeroes the counters
@@ -1636,7 +1648,11 @@ int launch_quantizer(srhpm_ctx * ctx, const GemmArgs & a, int NT, bool q80, cuda
     cfg.numAttrs                                       = 1;
     uint8_t *   recs = const_cast<uint8_t *>(a.recs);
     cudaError_t e;
-    if (q80) {
+    if (a.X2) {  // SwiGLU inputs: the SwiGLU kernel writes the records (K-quant weights; h is not stored)
+        cfg.gridDim = dim3((unsigned) (((int64_t) a.nsb * NT + 7) / 8));
+        e = cudaLaunchKernelEx(&cfg, swiglu_q8K_kernel, a.X, a.X2, a.ldx, (float *) nullptr, (int64_t) 0, a.N, a.nsb,
+                               NT, recs, a.perm, a.cnt, a.ncnt);
+    } else if (q80) {
         e = cudaLaunchKernelEx(&cfg, quant_q80_kernel<false>, a.X, a.ldx, a.N, a.nsb, NT, a.q80mode, recs,
                                (uint8_t *) nullptr, a.cnt, a.ncnt);
     } else {
@@ -1874,7 +1890,7 @@ uint32_t * sync_counter(srhpm_ctx * ctx, const void * work) {
 int gemm_run_impl(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
                   const float * X, int64_t ldx, int64_t N, float * Y, int64_t ldy, void * wdata, size_t wsize,
                   int32_t * isum, int32_t * imin, bool split, cudaStream_t stream, bool prequant = false,
-                  bool fused_ok = false) {
+                  bool fused_ok = false, const float * X2 = nullptr) {
     const WorkLayout wl = split ? work_layout(wtype, rows, K, N) : work_layout_unsplit(wtype, rows, K, N);
     if (wsize < wl.total || !wdata) return SRHPM_ERR_WORKSPACE;
     const int  nsb  = (int) (K / QK);
@@ -1888,6 +1904,7 @@ int gemm_run_impl(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, i
     GemmArgs a  = {};
     if (!prequant) {
         a.X       = X;
+        a.X2      = X2;
         a.ldx     = ldx;
         a.perm    = record_perm(wtype);
         a.q80mode = ctx->q8_0_act_mode;
@@ -1996,6 +2013,14 @@ int gemm_run(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_
              int32_t * isum, int32_t * imin, cudaStream_t stream, bool fused_quant) {
     return gemm_run_impl(ctx, wtype, W, rows, K, row_bytes, X, ldx, N, Y, ldy, wdata, wsize, isum, imin, true, stream,
                          false, fused_quant);
+}
+
+int gemm_run_swiglu(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,
+                    const float * gate, const float * up, int64_t ld_in, int64_t N, float * Y, int64_t ldy,
+                    void * wdata, size_t wsize, cudaStream_t stream) {
+    if (wtype == SRHPM_TYPE_Q8_0) return SRHPM_UNSUPPORTED;  // the SwiGLU record writer is the q8_K one
+    return gemm_run_impl(ctx, wtype, W, rows, K, row_bytes, gate, ld_in, N, Y, ldy, wdata, wsize, nullptr, nullptr,
+                         true, stream, false, true, up);
 }
 
 int gemm_run_unsplit(srhpm_ctx * ctx, int wtype, const uint8_t * W, int64_t rows, int64_t K, size_t row_bytes,

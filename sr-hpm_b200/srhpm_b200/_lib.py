@@ -54,6 +54,7 @@ _SIGNATURES = {
     "srhpm_mul_mat_work_size": (ctypes.c_int, [_T, _T, ctypes.POINTER(ctypes.c_size_t)]),
     "srhpm_mul_mat": (ctypes.c_int, [_P, _T, _T, _T, _P, ctypes.c_size_t, _P]),
     "srhpm_mul_mat_fused_quant": (ctypes.c_int, [_P, _T, _T, _T, _P, ctypes.c_size_t, _P]),
+    "srhpm_mul_mat_swiglu": (ctypes.c_int, [_P, _T, _T, _T, _T, _P, ctypes.c_size_t, _P]),
     "srhpm_mul_mat_isums": (ctypes.c_int, [_P, _T, _T, _P, _P, _P, ctypes.c_size_t, _P]),
     "srhpm_mul_mat_static": (ctypes.c_int, [_P, _T, _T, _T, _P]),
     "srhpm_quantize_rows_q8_K": (ctypes.c_int, [_P, _T, _P, _P, _P, _P, _P]),

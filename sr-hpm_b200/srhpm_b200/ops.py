@@ -179,6 +179,22 @@ class Context:
                    buf.numel(), _stream_ptr(stream)), "srhpm_mul_mat")
         return out
 
+    def mul_mat_swiglu(self, W, gate, up, out=None, stream=None, work=None):
+        """Y[N, rows] = (silu(gate) * up)[N, K] . W[rows, K]^T with the SwiGLU in the matmul grid's own prologue
+        (srhpm_mul_mat_swiglu; gate and up of the same shape and row stride, e.g. the two halves of a gate|up
+        product)."""
+        N = gate.shape[0]
+        if out is None:
+            out = torch.empty((N, W.rows), dtype=torch.float32, device=gate.device)
+        wv, gv, uv, yv = W.view(), f32_rows_view(gate), f32_rows_view(up), f32_rows_view(out)
+        st, ws = self.mul_mat_work_size(W, gate)
+        L.check(st, "srhpm_mul_mat_work_size")
+        buf = work if work is not None else self.work(ws)
+        L.check(self.lib.srhpm_mul_mat_swiglu(self.handle, ctypes.byref(wv), ctypes.byref(gv), ctypes.byref(uv),
+                                              ctypes.byref(yv), ctypes.c_void_p(buf.data_ptr()), buf.numel(),
+                                              _stream_ptr(stream)), "srhpm_mul_mat_swiglu")
+        return out
+
     def prepare_mul_mat(self, W, X, Y, work, fused_quant=False):
         """A zero-argument callable that issues srhpm_mul_mat(W, X) -> Y on the current stream with prebuilt
         arguments (the per-call host cost is one ctypes call); usable under CUDA-graph capture, since the call

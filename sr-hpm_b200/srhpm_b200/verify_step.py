@@ -298,7 +298,7 @@ class VerifyStep:
     residual stream, norms and embeddings are replicated."""
 
     def __init__(self, ctx, cfg, weights, kcache, vcache, n_tokens, n_past, relax=0.0, tp=None, fuse_prologue=True,
-                 gemm_fused_quant=True):
+                 gemm_fused_quant=True, swiglu_in_gemm=True):
         self.ctx, self.cfg, self.w = ctx, cfg, weights
         self.fuse_prologue = fuse_prologue  # RMSNorm writes the next GEMM's activation records itself
         # GEMMs without a fused prologue (the attention output projection; under tensor parallelism the QKV and
@@ -306,6 +306,9 @@ class VerifyStep:
         # (srhpm_mul_mat_fused_quant: one launch; the small kernel before each leaves the SMs free, so the grid is
         # resident early)
         self.gemm_fused_quant = gemm_fused_quant
+        # with fuse_prologue: the FFN down GEMM computes the SwiGLU of its activation super-blocks in its own grid
+        # (srhpm_mul_mat_swiglu, one launch) instead of the SwiGLU record kernel + the GEMM on the records
+        self.swiglu_in_gemm = swiglu_in_gemm
         self.kcache, self.vcache = kcache, vcache
         self.n, self.n_past, self.relax = n_tokens, n_past, relax
         self.tp = tp if tp is not None and tp.world > 1 else None
@@ -522,11 +525,17 @@ class VerifyStep:
                 self._ws = max(self._ws, ws)
                 wv, xv, yv = Wd.view(), f32_rows_view(self.h), f32_rows_view(Yd)
                 self._keep += [wv, xv, yv]
-                calls.append(("swiglu_quant", lib.srhpm_swiglu_quant,
-                              [h, self._ptr(self.gu), up_ptr, self.gu.stride(0), self._ptr(self.h), self.h.stride(0),
-                               n, ctypes.byref(wv)], True))
-                calls.append(("mul_mat_prequantized", lib.srhpm_mul_mat_prequantized,
-                              [h, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv)], True))
+                if self.swiglu_in_gemm:
+                    gv, uv = f32_rows_view(self.gu[:, :self.n_ff]), f32_rows_view(self.gu[:, self.n_ff:])
+                    self._keep += [gv, uv]
+                    calls.append(("mul_mat_swiglu", lib.srhpm_mul_mat_swiglu,
+                                  [h, ctypes.byref(wv), ctypes.byref(gv), ctypes.byref(uv), ctypes.byref(yv)], True))
+                else:
+                    calls.append(("swiglu_quant", lib.srhpm_swiglu_quant,
+                                  [h, self._ptr(self.gu), up_ptr, self.gu.stride(0), self._ptr(self.h),
+                                   self.h.stride(0), n, ctypes.byref(wv)], True))
+                    calls.append(("mul_mat_prequantized", lib.srhpm_mul_mat_prequantized,
+                                  [h, ctypes.byref(wv), ctypes.byref(xv), ctypes.byref(yv)], True))
             else:
                 calls.append(("swiglu", lib.srhpm_swiglu,
                               [h, self._ptr(self.gu), up_ptr, self.gu.stride(0), self._ptr(self.h), self.h.stride(0),

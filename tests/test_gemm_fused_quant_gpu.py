@@ -12,6 +12,7 @@ import torch
 
 import oracle as O
 import srhpm_b200 as S
+from srhpm_b200 import _lib as L
 
 pytestmark = pytest.mark.gpu
 
@@ -109,3 +110,80 @@ def test_graph_replays(ctx):
             assert np.array_equal(o.cpu().numpy(), w), rep
     del g
     ctx.check()
+
+
+SWIGLU_TYPES = [S.Q4_K, S.Q5_K, S.Q6_K, S.Q3_K, S.IQ4_XS]
+
+
+@pytest.mark.parametrize("qtype", SWIGLU_TYPES)
+@pytest.mark.parametrize("N", [1, 4, 9, 16])
+@pytest.mark.parametrize("shape", [(133, 1280), (5120, 17408), (2048, 5120)])
+def test_swiglu_in_gemm_equals_swiglu_quant(ctx, qtype, N, shape):
+    """srhpm_mul_mat_swiglu (the SwiGLU of gate and up computed and quantized in the GEMM grid's prologue) against
+    srhpm_swiglu_quant + srhpm_mul_mat_prequantized on the same halves of one gate|up product: bit-identical outputs
+    (the same records); one launch when the grid is large enough for the prologue, else the SwiGLU record kernel
+    first (two). Against the exact oracle on the SwiGLU rows the separate path stored."""
+    import ctypes
+    rows, K = shape
+    rng = np.random.default_rng(rows + K + N + qtype)
+    Wb = O.random_blocks(qtype, rows * K // O.BLOCK_ELEMS[qtype], rng).reshape(rows, -1)
+    W = S.QuantTensor.from_blocks(Wb, qtype, rows, K)
+    gu = torch.from_numpy(rng.standard_normal((N, 2 * K)).astype(np.float32)).cuda()
+    gate, up = gu[:, :K], gu[:, K:]
+    lib = L.load()
+    h = torch.empty((N, K), dtype=torch.float32, device="cuda")
+    y0 = torch.empty((N, rows), dtype=torch.float32, device="cuda")
+    st, ws = ctx.mul_mat_work_size(W, h)
+    work = torch.empty(ws, dtype=torch.uint8, device="cuda")
+    wv, hv, yv = W.view(), S.f32_rows_view(h), S.f32_rows_view(y0)
+    ptr = lambda t: ctypes.c_void_p(t.data_ptr())
+    ctx.launch_count(reset=True)
+    y1 = ctx.mul_mat_swiglu(W, gate, up)
+    torch.cuda.synchronize()
+    l1 = ctx.launch_count(reset=True)
+    L.check(lib.srhpm_swiglu_quant(ctx.handle, ptr(gu), ctypes.c_void_p(gu.data_ptr() + 4 * K), gu.stride(0), ptr(h),
+                                   h.stride(0), N, ctypes.byref(wv), ptr(work), work.numel(), None),
+            "srhpm_swiglu_quant")
+    L.check(lib.srhpm_mul_mat_prequantized(ctx.handle, ctypes.byref(wv), ctypes.byref(hv), ctypes.byref(yv),
+                                           ptr(work), work.numel(), None), "srhpm_mul_mat_prequantized")
+    torch.cuda.synchronize()
+    ctx.check()
+    assert torch.equal(y1, y0)
+    if rows >= 2048:
+        assert l1 == 1
+    else:
+        assert l1 in (1, 2)
+    sl = slice(0, 64)
+    assert rel_l2(y1.cpu().numpy()[:, sl], O.mul_mat(qtype, Wb[sl], 64, K, h.cpu().numpy())) < TOL_EXACT
+
+
+def test_swiglu_in_gemm_graph_replays_and_q8_0(ctx):
+    """The SwiGLU prologue under CUDA-graph replays (the grid counter advances), and Q8_0 weights refused."""
+    rng = np.random.default_rng(77)
+    rows, K, N = 5120, 17408, 9
+    W = S.QuantTensor.from_blocks(O.random_blocks(S.Q4_K, rows * K // 256, rng).reshape(rows, -1), S.Q4_K, rows, K)
+    gu = torch.from_numpy(rng.standard_normal((N, 2 * K)).astype(np.float32)).cuda()
+    want = ctx.mul_mat_swiglu(W, gu[:, :K], gu[:, K:]).clone()
+    out = torch.empty_like(want)
+    work = torch.empty(ctx.mul_mat_work_size(W, gu[:, :K])[1], dtype=torch.uint8, device="cuda")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ctx.mul_mat_swiglu(W, gu[:, :K], gu[:, K:], out=out, work=work, stream=s)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        ctx.mul_mat_swiglu(W, gu[:, :K], gu[:, K:], out=out, work=work)
+    for rep in range(4):
+        out.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, want), rep
+    del g
+    ctx.check()
+    W8 = S.QuantTensor.from_blocks(O.random_blocks(S.Q8_0, 64 * 1024 // 32, rng).reshape(64, -1), S.Q8_0, 64, 1024)
+    gu8 = torch.zeros((2, 2048), device="cuda")
+    with pytest.raises(L.SrhpmError) as e:
+        ctx.mul_mat_swiglu(W8, gu8[:, :1024], gu8[:, 1024:])
+    assert e.value.status == L.UNSUPPORTED

@@ -429,12 +429,13 @@ def test_fused_norm_quant_prologue_is_exact(ctx):
     kc, vc = _caches(cfg, cap, n_past, 512, 32)
     dev_w = V.DeviceWeights.from_host(cfg, w)
     outs = []
-    for fuse, fq_o in ((False, False), (True, False), (True, True)):
+    for fuse, fq_o, sw in ((False, False, False), (True, False, True), (True, True, True), (True, True, False)):
         # fq_o: GEMMs without a fused prologue (here the attention output projection) quantize their activations in
-        # their own grid (one launch instead of 2)
+        # their own grid (one launch instead of 2); sw: the down GEMM computes the SwiGLU in its own grid
         kcd = [torch.from_numpy(a).cuda() for a in kc]
         vcd = [torch.from_numpy(a).cuda() for a in vc]
-        step = V.VerifyStep(ctx, cfg, dev_w, kcd, vcd, len(ids), n_past, fuse_prologue=fuse, gemm_fused_quant=fq_o)
+        step = V.VerifyStep(ctx, cfg, dev_w, kcd, vcd, len(ids), n_past, fuse_prologue=fuse, gemm_fused_quant=fq_o,
+                            swiglu_in_gemm=sw)
         step.set_tokens(ids, draft)
         ctx.launch_count(reset=True)
         step.run()
@@ -446,10 +447,12 @@ def test_fused_norm_quant_prologue_is_exact(ctx):
         assert torch.equal(outs[0][0], o[0])
         assert all(torch.equal(a, b) for a, b in zip(outs[0][1], o[1]))
         assert outs[0][2] == o[2]
-    # kernel launches: the quantizers of the QKV, gate|up, down and head GEMMs are gone (3 per layer + 1), and with
-    # the fused output projection the O GEMM's (1 per layer) when its grid is large enough for the fused form
-    assert outs[0][3] - outs[1][3] == 3 * cfg.n_layer + 1
+    # kernel launches: the quantizers of the QKV, gate|up, down and head GEMMs are gone (3 per layer + 1), and the
+    # SwiGLU kernel too where the down GEMM's grid is large enough to compute it in its prologue (1 more per layer);
+    # with the fused output projection the O GEMM's quantizer (1 per layer) when its grid is large enough
+    assert outs[0][3] - outs[1][3] in (3 * cfg.n_layer + 1, 4 * cfg.n_layer + 1)
     assert outs[1][3] - outs[2][3] in (0, cfg.n_layer)
+    assert outs[3][3] - outs[2][3] == outs[0][3] - outs[1][3] - 3 * cfg.n_layer - 1
 
 
 @pytest.mark.parametrize("qtype", [S.Q4_K, S.Q5_K, S.Q6_K, S.Q3_K, S.IQ4_XS])
