@@ -1,5 +1,5 @@
 // The peer-memory exchange across the GPUs of one box: the all-reduce of the tensor-parallel decoder step (inside the
-// next RMSNorm: add_rms_norm_ar_kernel in decoder_ops.cu, add_rms_norm_q8K_kernel in srv_gemm.cu).
+// next RMSNorm: add_rms_norm_ar_kernel in decoder_ops.cu, add_rms_norm_ar_q8K_kernel in srv_gemm.cu).
 //
 // All-reduce (flag-in-word exchange). Every rank's row-parallel GEMM (attention output, FFN down) writes its partial
 // sums into slot `slot` of its own symmetric buffer (mapped on every peer): [2 slots][kArRows rows][d] f32, followed by

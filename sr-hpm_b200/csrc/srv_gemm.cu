@@ -378,13 +378,13 @@ __global__ void __cluster_dims__(kArC, 1, 1) __launch_bounds__(kArCT)
         __syncthreads();
         e = e_s;
         {  // send this rank's values of the CTA's columns to every rank (ar_push4, all columns per rank in turn)
-            const float4 * part = reinterpret_cast<const float4 *>(ar.peers[ar.rank] + (size_t) ar.slot * ar_part_bytes(d)) +
+            const float4 * mine = reinterpret_cast<const float4 *>(ar.peers[ar.rank] + (size_t) ar.slot * ar_part_bytes(d)) +
                                   (int64_t) t * d4;
             float4 pv[4];
 #pragma unroll
             for (int k = 0; k < 4; k++) {
                 const int64_t j = kArCT * c + tid + (int64_t) k * 1024;
-                if (j < d4) pv[k] = part[j];
+                if (j < d4) pv[k] = mine[j];
             }
             const size_t o = ar_recv_word(d, ar.slot, t, ar.rank);
             for (int r = 0; r < ar.world; r++) {
