@@ -638,7 +638,7 @@ def run_gpu(args):
             attn_split = measure_attention_split(ctx, dev, rank, world, peak)
         except Exception as e:  # recorded beside the sweep rather than losing its line
             attn_split = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
-        if 4 % world == 0:  # the 4 KV heads of config 3 split whole over 2 or 4 ranks
+        if 4 % world == 0:  # the 4 KV heads of the verify attention split whole over 2 or 4 ranks
             try:
                 attn_heads = measure_attention_kv_heads(ctx, dev, rank, world, peak)
             except Exception as e:  # recorded beside the sweep rather than losing its line
@@ -668,7 +668,7 @@ def run_gpu(args):
         if op_ms and c1:
             meas["q4_K_17408x5120_N4_us_in_sweep"] = round(sum(op_ms[i] for i in c1) / len(c1) * 1e3, 2)
         if world == 1 and not args.only:
-            meas["config1_q4_K_17408x5120_N4"] = measure_one_product(ctx, dev, host_w, host_x, (4, 12, 17408, 5120),
+            meas["single_q4_K_17408x5120_N4"] = measure_one_product(ctx, dev, host_w, host_x, (4, 12, 17408, 5120),
                                                                      peak)
             meas["sweep_N1"] = n1
         if world == 1 and not args.no_attn:
@@ -761,7 +761,7 @@ def graph_us(fn, calls, reps=20):
 
 
 def measure_one_product(ctx, dev, host_w, host_x, op, peak):
-    """One product alone (config 1 = Q4_K 17408x5120, N = 4): calls rotated over copies of its matrix that
+    """One product alone (the single product Q4_K 17408x5120, N = 4): calls rotated over copies of its matrix that
     together exceed 300 MB (no call finds its weights in L2), graph-replayed; us per call and GB/s of its bytes."""
     import torch
     import srhpm_b200 as S
@@ -891,7 +891,7 @@ def _full_caches(cfg, dev, n_layer_cap, seed):
 
 
 def measure_step_27b_tp(ctx, dev, rank, world, k=8, n_past=2048, reps=10, seed=0, kv_q8=False, ks_extra=()):
-    """The 27B-class verify step (k = 8, f16 KV of 2048 tokens; kv_q8: q8_0 KV of n_past tokens, BASELINE config 5,
+    """The 27B-class verify step (k = 8, f16 KV of 2048 tokens; kv_q8: q8_0 KV of n_past tokens, the long-context step,
     timed without the parity pass; ks_extra: shorter drafts timed first with the same weights and caches, without a
     parity pass) on `world` GPUs in Megatron tensor parallelism
     (column-parallel QKV / gate|up / head, row-parallel O / down with the all-reduce fused into the next RMSNorm, KV
@@ -1045,7 +1045,7 @@ def shard_vocab(n_vocab, world, j):
 
 
 def measure_attention(ctx, dev, peak, reps=20, lengths=(8192, 32768, 131072), N=8):
-    """Verify attention: N query rows (8: BASELINE config 3; 9: the rows of the k = 8 verify step), 24 query heads,
+    """Verify attention: N query rows (8: the 8 draft rows; 9: the rows of the k = 8 verify step), 24 query heads,
     4 KV heads, head_dim 256, causal mask among the draft rows, q8_0 K/V (N(0,1) before quantization) of L past
     tokens, Q N(0,1) / 16. Timed as CUDA-graph replays over copies of the KV cache that together exceed L2."""
     import torch
@@ -1211,7 +1211,7 @@ def measure_attention_split(ctx, dev, rank, world, peak, reps=20, lengths=(8192,
 
 
 def measure_attention_kv_heads(ctx, dev, rank, world, peak, reps=20, lengths=(8192, 32768, 131072)):
-    """The verify attention of measure_attention sharded by KV head (config 3 over 2 or 4 GPUs): rank j holds KV
+    """The verify attention of measure_attention sharded by KV head (over 2 or 4 GPUs): rank j holds KV
     heads shard.kv_heads(4, world, j) of the q8_0 cache and computes their 6 query heads each over the whole range
     (no reduction); one NCCL all-gather assembles the [N, 24, 256] output on every rank. One call = the attention
     + the all-gather, in one CUDA graph over copies of the rank's heads that together exceed L2; time = max over

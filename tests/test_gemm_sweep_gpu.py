@@ -1,8 +1,8 @@
 """The verify-GEMM sweep's own products, every output row, against the reference's kernels and the exact oracle.
 
-The benchmark's workload (BASELINE config 2 at k = 2..8): weights [5120x5120], [6144x5120], [17408x5120],
+The benchmark's workload (the verify-GEMM sweep at k = 2..8): weights [5120x5120], [6144x5120], [17408x5120],
 [5120x17408] drawn from N(0, 0.02) and quantized by the library's quantizer to Q4_K, Q5_K, Q6_K, Q8_0 and IQ4_XS,
-activations N(0, 1) with N = 2, 4 and 8 rows; config 1 (Q4_K 17408x5120, N = 4) on its own. Bars: 1e-3 relative L2
+activations N(0, 1) with N = 2, 4 and 8 rows; the single product Q4_K 17408x5120 at N = 4 on its own. Bars: 1e-3 relative L2
 against the reference's f32 kernels (patch/srhpm.patch:6119-6226 via its compute_forward scheduling; Q8_0 through
 the restated stock path), 1e-5 against the exact-integer f64 oracle, and no single output off by more than 1e-4 of
 the largest exact output (a wrong row or tile would stand out there before it moved the L2 norm)."""
@@ -62,8 +62,8 @@ def _check(ctx, ref, Wb, qtype, rows, K, N, seed):
         assert rel_l2(y, want) < TOL_REF
 
 
-def test_config1_all_rows(ctx, ref, packed):
-    """Q4_K 17408x5120, N = 4, every row."""
+def test_single_product_q4K_17408x5120_all_rows(ctx, ref, packed):
+    """The single product Q4_K 17408x5120 at N = 4, every row."""
     _check(ctx, ref, packed(S.Q4_K, 17408, 5120), S.Q4_K, 17408, 5120, 4, seed=1)
 
 
